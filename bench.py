@@ -1,0 +1,469 @@
+"""Benchmark of the B200 Gated DeltaNet token mixer.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload (one GPU): the single-token decode step of one DeltaNet
+layer at batch 64, hidden 2048, 16 key heads / 32 value heads, d_k = d_v = 128,
+bf16 activations and an fp32 recurrent state (128 MiB).  One bench step = one
+fused kernel launch that takes the step's projection outputs to the gated
+RMSNorm output, updating the recurrent state in place.  Four rotating state
+slots (4 x 134 MB) keep every step's state traffic out of the 126 MB L2.
+
+With ``--gpus N`` (torchrun, one rank per GPU) the value heads are sharded:
+rank r owns value heads [r*32/N, (r+1)*32/N) and the key heads they read; the
+token mixer needs no exchange between ranks (each (batch, head) chain is
+independent), so the total work is fixed and the scaling is strong.
+
+Also reported: the chunked-prefill workload (batch 8 x 8192 tokens) as a
+secondary object, the roofline of the dominant kernel, an end-to-end number
+through the public API with host buffers, the CPU oracle timed on the host,
+and SM clocks sampled during the timed region.
+
+``--impl reference`` times the CPU restatement of the reference path (the
+numpy oracle) on the host cores, on the same decode workload.
+"""
+from __future__ import annotations
+
+import argparse
+import glob
+import json
+import math
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+from visionstack_b200 import workloads as W  # noqa: E402
+
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the secondary prefill measurement")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-s", type=float, default=12.0, help="seconds of CPU work for the CPU baseline")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------
+# algorithmic work (per launch)
+# ----------------------------------------------------------------------------
+
+def decode_bytes(B: int, hk: int, hv: int, d: int, K: int, act_bytes: int = 2) -> int:
+    """Bytes one decode launch must move: state read+write, conv state
+    read+write, conv weights, projection outputs in, gated-norm output out."""
+    conv_ch = 2 * hk * d + hv * d
+    state = 2 * B * hv * d * d * 4
+    conv_state = 2 * B * conv_ch * (K - 1) * act_bytes
+    conv_w = conv_ch * K * act_bytes
+    inputs = B * (conv_ch + hv * d + 2 * hv) * act_bytes
+    out = B * hv * d * act_bytes
+    return state + conv_state + conv_w + inputs + out
+
+
+def prefill_flops(B: int, T: int, hv: int, d: int, C: int = 64) -> float:
+    """Contraction FLOPs of the chunked form per token and head:
+    K K^T and Q K^T (2*2*C*d), T [U | W] (2*C*2d), P v_new (2*C*d), W S, Q S,
+    K^T v_new (3*2*d*d)."""
+    return float(B) * T * hv * (2 * C * (3 * d + 2 * d) + 6 * d * d)
+
+
+def prefill_min_bytes(B: int, T: int, hk: int, hv: int, d: int, K: int = 4) -> int:
+    conv_ch = 2 * hk * d + hv * d
+    per_tok = (conv_ch + hv * d + 2 * hv + hv * d) * 2
+    return B * T * per_tok + B * hv * d * d * 4 + B * conv_ch * (K - 1) * 2
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def profiled_traffic(kernel_key: str):
+    """dram bytes per launch recorded from an ncu capture (profiles/*.md line
+    ``traffic_bytes_per_launch[<key>]: <int>``), or None."""
+    pat = re.compile(r"traffic_bytes_per_launch\[" + re.escape(kernel_key) + r"\]:\s*([0-9]+)")
+    for path in sorted(glob.glob(os.path.join(REPO, "profiles", "*.md"))):
+        with open(path) as f:
+            m = pat.search(f.read())
+        if m:
+            return int(m.group(1))
+    return None
+
+
+# ----------------------------------------------------------------------------
+# clocks during the timed region (NVML, read only)
+# ----------------------------------------------------------------------------
+
+_REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+            0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting", 0x1: "gpu_idle"}
+
+
+class ClockSampler:
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            idx = device_index
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            if vis:
+                ids = [v.strip() for v in vis.split(",") if v.strip()]
+                if device_index < len(ids) and ids[device_index].isdigit():
+                    idx = int(ids[device_index])
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self._nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+        self.period = period_s
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+                r = fn(self._h)
+                for bit, name in _REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": float(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------
+# CPU side: oracle timings (CPU baseline and the reference arm)
+# ----------------------------------------------------------------------------
+
+def cpu_decode_rate(sample_s: float):
+    """Time the oracle's decode step (numpy restatement of the reference,
+    deltanet.py:165-233 + conv + gated norm) at the full decode batch."""
+    from oracle import gdn_oracle as O
+
+    wl = W.WORKLOADS["decode"]
+    s = wl.shape
+    p = W.make_layer_params(s, wl.w_seed, "bf16")
+    rng = np.random.default_rng(wl.x_seed)
+    B = wl.batch
+    f = lambda *sh, sc=1.0: W.cast(sc * rng.standard_normal(sh).astype(np.float32), "bf16")  # noqa: E731
+    mixed, z, a, b = f(B, 1, s.conv_dim, sc=0.7), f(B, 1, s.num_v_heads, s.head_v_dim), f(B, 1, s.num_v_heads), \
+        f(B, 1, s.num_v_heads)
+    st = W.make_decode_states(wl)
+    conv, rec = st["conv"], st["recurrent"]
+    O.mixer_forward(s, mixed, z, a, b, p["conv1d.weight"], p["A_log"], p["dt_bias"], p["norm.weight"], "bf16",
+                    conv, rec, chunk=False)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        _, conv, rec, _, _ = O.mixer_forward(s, mixed, z, a, b, p["conv1d.weight"], p["A_log"], p["dt_bias"],
+                                             p["norm.weight"], "bf16", conv, rec, chunk=False)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= sample_s or n >= 200:
+            break
+    return n / el, n, el
+
+
+def cpu_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    rates = []
+    for _ in range(max(1, args.steps if args.steps < 3 else 3)):
+        r, n, el = cpu_decode_rate(max(3.0, args.cpu_sample_s / 3))
+        rates.append(r)
+    rate = statistics.median(rates)
+    line = {
+        "metric": "DeltaNet decode steps/s (B64, 16/32 heads, d128, bf16, fp32 state)",
+        "value": rate, "unit": "steps/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 / rate, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded numpy)", "impl": "reference",
+        "config": decode_config(args.gpus),
+        "cpu_baseline": {"value": rate, "unit": "steps/s", "cores": cpu_cores(), "kind": "port",
+                         "sample": f"numpy oracle decode step at B64 x 32 heads, median of {len(rates)} samples"},
+        "e2e": {"value": rate, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def decode_config(n: int):
+    return {"workload": "decode step: B64, hidden 2048, 16 k-heads / 32 v-heads, d128, conv 4",
+            "global_batch": 64, "seq_len": 1, "parallelism": f"value-head sharding x{n}" if n > 1 else "single GPU",
+            "l2": "inputs larger than L2: 4 rotating 134 MB state slots"}
+
+
+# ----------------------------------------------------------------------------
+# GPU side
+# ----------------------------------------------------------------------------
+
+def build_shard_layer(torch, rank: int, world: int, dev):
+    """Layer holding the value-head shard of rank ``rank``: its conv channels
+    (q/k of its key heads, v of its value heads), A_log, dt_bias, norm."""
+    from visionstack_b200 import Qwen3_5GatedDeltaNet, Qwen3_5TextConfig
+    from visionstack_b200.sharding import shard_params
+    s = W.SHAPE_QWEN
+    full = W.make_layer_params(s, 1, "bf16")
+    params, local = shard_params(full, s, rank, world)
+    cfg = Qwen3_5TextConfig(hidden_size=s.hidden_size, linear_num_key_heads=local.num_k_heads,
+                            linear_num_value_heads=local.num_v_heads, linear_key_head_dim=s.head_k_dim,
+                            linear_value_head_dim=s.head_v_dim)
+    m = Qwen3_5GatedDeltaNet(cfg, 0)
+    with torch.no_grad():
+        for name, p in m.named_parameters():
+            t = torch.from_numpy(params[name])
+            p.data = t if name in ("A_log", "dt_bias") else t.to(torch.bfloat16)
+    return m.to(dev), local
+
+
+def run_ours(args, rank: int, world: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from visionstack_b200 import _lib
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    lib = _lib.load()
+    m, local = build_shard_layer(torch, rank, world, dev)
+    B = 64
+    hv, hk, d = local.num_v_heads, local.num_k_heads, local.head_k_dim
+    conv_dim, vdim = local.conv_dim, local.value_dim
+    NSLOT, NIN = 4, 64
+    g = torch.Generator(device=dev)
+    g.manual_seed(2 + 1009 * rank)
+    with torch.no_grad():
+        x = torch.randn(NIN * B, W.SHAPE_QWEN.hidden_size, generator=g, device=dev).to(torch.bfloat16)
+        mixed = (x @ m.in_proj_qkv.weight.t()).view(NIN, B, 1, conv_dim)
+        z = (x @ m.in_proj_z.weight.t()).view(NIN, B, 1, vdim)
+        bb = (x @ m.in_proj_b.weight.t()).view(NIN, B, 1, hv)
+        aa = (x @ m.in_proj_a.weight.t()).view(NIN, B, 1, hv)
+        del x
+        states = [0.02 * torch.randn(B, hv, d, d, generator=g, device=dev) for _ in range(NSLOT)]
+        convs = [[torch.randn(B, conv_dim, 3, generator=g, device=dev).to(torch.bfloat16) for _ in range(2)]
+                 for _ in range(NSLOT)]
+        out = torch.empty(B, 1, vdim, dtype=torch.bfloat16, device=dev)
+
+    def step(i):
+        slot, j = i % NSLOT, i % NIN
+        cin, cout = convs[slot][(i // NSLOT) % 2], convs[slot][(i // NSLOT + 1) % 2]
+        m.mixer(mixed[j], z[j], bb[j], aa[j], conv_state=cin, rec_state=states[slot], conv_state_out=cout,
+                rec_state_out=states[slot], out=out, token_by_token=True)
+
+    K, Wm = args.steps, max(3, args.warmup)
+    stream = torch.cuda.Stream(device=dev)
+    # untimed warm-up (eager), then capture the K timed steps into one CUDA graph
+    with torch.cuda.stream(stream):
+        for i in range(Wm):
+            step(i)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(K):
+            step(Wm + i)
+    torch.cuda.synchronize(dev)
+    graph.replay()  # one untimed replay: graph upload / first-launch costs
+    torch.cuda.synchronize(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(dev.index)
+    barrier()
+    with sampler:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            graph.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    ms_total = ev0.elapsed_time(ev1)
+    t_local = torch.tensor([ms_total], device=dev)
+    if world > 1:
+        dist.all_reduce(t_local, op=dist.ReduceOp.MAX)
+    ms_total = float(t_local.item())
+    ms_step = ms_total / K
+    del graph
+
+    # end to end through the public API: H2D of the step's inputs from pinned
+    # host memory, the mixer call, D2H of the step's output, every step
+    K_e2e = min(K, 500)
+    h_in = [t[:NIN].cpu().pin_memory() for t in (mixed, z, bb, aa)]
+    d_in = [torch.empty_like(t[0]) for t in (mixed, z, bb, aa)]
+    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    h2d = sum(t[0].numel() * t.element_size() for t in h_in)
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_step(i):
+        j, slot = i % NIN, i % NSLOT
+        for dst, src in zip(d_in, h_in):
+            dst.copy_(src[j], non_blocking=True)
+        cin, cout = convs[slot][(i // NSLOT) % 2], convs[slot][(i // NSLOT + 1) % 2]
+        m.mixer(d_in[0], d_in[1], d_in[2], d_in[3], conv_state=cin, rec_state=states[slot], conv_state_out=cout,
+                rec_state_out=states[slot], out=out, token_by_token=True)
+        h_out.copy_(out, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            e2e_step(i)
+    barrier()
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for i in range(K_e2e):
+            e2e_step(i)
+        ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    t_e2e = torch.tensor([ev0.elapsed_time(ev1) / K_e2e], device=dev)
+    if world > 1:
+        dist.all_reduce(t_e2e, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t_e2e.item())
+
+    # secondary: chunked prefill (batch 8 x 8192 tokens, all heads of the shard)
+    prefill = None
+    if not args.no_prefill:
+        prefill = run_prefill(torch, dist, m, local, dev, world, barrier)
+
+    if rank != 0:
+        return
+    hbm, tflops, src = measured_peaks()
+    bytes_launch = decode_bytes(B, hk, hv, d, 4)
+    achieved = bytes_launch / (ms_step * 1e-3) / 1e9
+    traffic = profiled_traffic("decode_b64") if world == 1 else None
+    line = {
+        "metric": "DeltaNet decode steps/s (B64, 16/32 heads, d128, bf16, fp32 state)",
+        "value": 1000.0 / ms_step, "unit": "steps/s", "n_gpus": world, "steps": K, "warmup": Wm,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded torch.randn on device)", "config": decode_config(world),
+        "gpu_launches": K,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "traffic": traffic, "peak_source": src, "bytes_per_launch": bytes_launch,
+                     "kernel": "gdn::decode_kernel<128,128,256,bf16,mixer>"},
+        "e2e": {"value": 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "Qwen3_5GatedDeltaNet.mixer -> gdn_mixer_decode, pinned host buffers"},
+        "clocks": sampler.summary(),
+    }
+    if prefill is not None:
+        line["prefill"] = prefill
+    if world == 1 and not args.no_cpu_baseline:
+        rate, n, el = cpu_decode_rate(args.cpu_sample_s)
+        line["cpu_baseline"] = {"value": rate, "unit": "steps/s", "cores": cpu_cores(), "kind": "port",
+                                "sample": f"{n} decode steps of the numpy oracle at B64 x 32 heads ({el:.1f} s)"}
+    print(json.dumps(line), flush=True)
+
+
+def run_prefill(torch, dist, m, local, dev, world, barrier):
+    B, T = 8, 8192
+    hv, hk, d = local.num_v_heads, local.num_k_heads, local.head_k_dim
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    with torch.no_grad():
+        x = torch.randn(B, T, W.SHAPE_QWEN.hidden_size, generator=g, device=dev).to(torch.bfloat16)
+        mixed, z, bb, aa = m.project(x)
+        del x
+    out = torch.empty(B, T, local.value_dim, dtype=torch.bfloat16, device=dev)
+    S = torch.empty(B, hv, d, d, device=dev)
+    cs = torch.empty(B, local.conv_dim, 3, dtype=torch.bfloat16, device=dev)
+
+    def once():
+        m.mixer(mixed, z, bb, aa, conv_state_out=cs, rec_state_out=S, out=out, token_by_token=False)
+
+    for _ in range(3):
+        once()
+    reps = 5
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    ev0.record()
+    for _ in range(reps):
+        once()
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    barrier()
+    t = torch.tensor([ev0.elapsed_time(ev1) / reps], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    _, tflops, src = measured_peaks()
+    fl = prefill_flops(B, T, hv, d)
+    ach = fl / (ms * 1e-3) / 1e12
+    return {"workload": "chunked prefill: B8 x T8192, 16 k-heads / 32 v-heads (sharded), d128, bf16",
+            "tokens_per_s": B * T / (ms * 1e-3), "ms_per_launch": ms,
+            "roofline": {"bound": "tensor", "achieved": ach, "peak": tflops, "unit": "TFLOP/s",
+                         "frac": ach / tflops, "peak_source": src, "flops_per_launch": fl,
+                         "min_bytes_per_launch": prefill_min_bytes(B, T, hk, hv, d),
+                         "kernel": "gdn::prefill_kernel<128,bf16,mixer> (CUDA-core fp32)"}}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    try:
+        run_ours(args, rank, world)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

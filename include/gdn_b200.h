@@ -1,0 +1,184 @@
+/*
+ * gdn_b200.h - C ABI of the B200 (sm_100a) Gated DeltaNet token mixer.
+ *
+ * The token mixer is the part of the reference layer
+ * `Qwen3_5GatedDeltaNet.forward` (ShadowBoxer/models/qwen35/deltanet.py:447-563)
+ * between the four input projections and `out_proj`: causal depthwise conv1d
+ * + SiLU, q/k L2 normalisation, the beta / decay gates, the gated delta rule
+ * (token-by-token or chunked) and the output gated RMSNorm.  The projections
+ * and `out_proj` stay library GEMMs in the host layer.
+ *
+ * Conventions
+ *  - Every entry point returns an int32 status: GDN_OK (0) or a negative
+ *    GDN_ERR_* code.  The message of the last failure on the calling thread is
+ *    available from gdn_last_error_string().  (Same convention as the
+ *    reference's native DLL, VizInjector/src/native/vizinjector_dll.h, bound
+ *    with ctypes restype c_int32 and raised as RuntimeError by
+ *    VizInjector/python/bindings.py:298-400.)
+ *  - All tensor pointers are DEVICE pointers of the current CUDA device.
+ *    `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *  - Arguments are validated on the host before any launch; nothing traps on
+ *    the device.  Launch failures are reported as GDN_ERR_CUDA.
+ *  - Activations, projection outputs, the conv weight, the conv state and the
+ *    norm weight share one "activation dtype" (GDN_DTYPE_BF16 or
+ *    GDN_DTYPE_F32); recurrent states are always float32
+ *    [batch, num_v_heads, head_k_dim, head_v_dim] contiguous, as in the
+ *    reference cache (ShadowBoxer/models/qwen35/cache.py:17-18).
+ *  - GQA: value head h reads key head h / (num_v_heads / num_k_heads), the
+ *    mapping of `repeat_interleave` at deltanet.py:520-523.
+ */
+#ifndef GDN_B200_H
+#define GDN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_ABI_VERSION 1
+
+#define GDN_OK 0
+#define GDN_ERR_INVALID_ARG (-1)   /* null pointer, bad size or stride */
+#define GDN_ERR_UNSUPPORTED (-2)   /* shape / dtype combination not built */
+#define GDN_ERR_ALIGNMENT (-3)     /* pointer or stride misaligned */
+#define GDN_ERR_CUDA (-4)          /* a CUDA runtime call or launch failed */
+#define GDN_ERR_TOO_MANY_CHECKPOINTS (-5)
+
+#define GDN_DTYPE_F32 0
+#define GDN_DTYPE_BF16 1
+
+/* Maximum number of state checkpoints one call can record. */
+#define GDN_MAX_CHECKPOINTS 512
+/* Longest sequence the token-by-token (decode / verify) entry accepts. */
+#define GDN_MAX_DECODE_TOKENS 8
+
+/*
+ * Arguments of the fused token mixer (one layer, one call).
+ *
+ * Layout of the inputs (row-major, last dimension contiguous):
+ *   mixed_qkv   [batch, seq_len, conv_dim]  channels ordered
+ *               [q: Hk*dk | k: Hk*dk | v: Hv*dv], head-major (deltanet.py:508-514)
+ *   z           [batch, seq_len, Hv*dv]
+ *   a, b        [batch, seq_len, Hv]
+ *   conv_weight [conv_dim, conv_kernel]
+ *   A_log, dt_bias  [Hv] float32
+ *   norm_weight [dv]
+ * Outputs:
+ *   out         [batch, seq_len, Hv*dv] gated-RMSNorm output (input of out_proj)
+ *   conv_state_out [batch, conv_dim, conv_kernel-1]  raw inputs of the last
+ *               conv_kernel-1 positions, oldest first (deltanet.py:24-38)
+ *   state_out   [batch, Hv, dk, dv] float32
+ * Checkpoints (deltanet.py:479-487, 223-226, 345-388): for each local offset
+ * off = checkpoint_offsets[i] in 1..seq_len, slot i of state_checkpoints
+ * ([num_checkpoints, batch, Hv, dk, dv] float32) receives the recurrent state
+ * after `off` tokens and slot i of conv_checkpoints
+ * ([num_checkpoints, batch, conv_dim, conv_kernel-1]) the conv state after
+ * `off` tokens.  Offsets outside 1..seq_len are skipped.
+ */
+typedef struct gdn_mixer_args {
+    int32_t batch;
+    int32_t seq_len;
+    int32_t num_k_heads;
+    int32_t num_v_heads;
+    int32_t head_k_dim;
+    int32_t head_v_dim;
+    int32_t conv_kernel;
+    int32_t act_dtype;        /* GDN_DTYPE_* */
+    float norm_eps;           /* rms_norm_eps of the gated norm */
+    int32_t reserved0;
+
+    const void* mixed_qkv;    /* required */
+    int64_t mixed_stride_b;   /* elements between batch rows */
+    int64_t mixed_stride_t;   /* elements between tokens */
+    const void* z;            /* required */
+    int64_t z_stride_b;
+    int64_t z_stride_t;
+    const void* a;            /* required */
+    const void* b;            /* required */
+    int64_t ab_stride_b;      /* shared by a and b */
+    int64_t ab_stride_t;
+    const void* conv_weight;  /* required */
+    const float* A_log;       /* required */
+    const float* dt_bias;     /* required */
+    const void* norm_weight;  /* required */
+
+    const void* conv_state_in;  /* NULL: zeros (no previous state) */
+    void* conv_state_out;       /* NULL: not written; must not alias conv_state_in */
+    const float* state_in;      /* NULL: zeros */
+    float* state_out;           /* NULL: not written; may equal state_in (in-place) */
+    void* out;                  /* required */
+
+    int32_t num_checkpoints;            /* 0..GDN_MAX_CHECKPOINTS */
+    int32_t reserved1;
+    const int32_t* checkpoint_offsets;  /* HOST array of num_checkpoints local offsets */
+    float* state_checkpoints;           /* device, may be NULL when num_checkpoints == 0 */
+    void* conv_checkpoints;             /* device, may be NULL when num_checkpoints == 0 */
+} gdn_mixer_args;
+
+/* Library ABI version (GDN_ABI_VERSION). */
+int32_t gdn_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* gdn_last_error_string(void);
+
+/*
+ * Token-by-token token mixer for 1 <= seq_len <= GDN_MAX_DECODE_TOKENS: the
+ * single-token decode step and the speculative-decode verify step.
+ * Replaces deltanet.py:479-561 on the branch where _chunk_gated_delta_rule
+ * hands off to _recurrent_gated_delta_rule (deltanet.py:251-264, 165-233).
+ * One launch: conv-state shift + conv + SiLU, L2 norms, gates, decay and
+ * rank-1 delta update of the fp32 state (in place when state_out == state_in),
+ * readout, gated RMSNorm, per-token checkpoints.
+ */
+int32_t gdn_mixer_decode(const gdn_mixer_args* args, void* stream);
+
+/*
+ * Chunked token mixer for any seq_len >= 1 (prefill).  Replaces
+ * deltanet.py:479-561 on the _chunk_gated_delta_rule branch
+ * (deltanet.py:266-407): the WY/UT intra-chunk solve and the sequential
+ * inter-chunk state propagation, with conv, norms, gates and the gated RMSNorm
+ * fused in.  Needs no workspace.
+ */
+int32_t gdn_mixer_prefill(const gdn_mixer_args* args, void* stream);
+
+/*
+ * Stand-alone delta rule on already-split q/k/v, the functional boundary of
+ * _recurrent_gated_delta_rule (deltanet.py:165-233) and
+ * _chunk_gated_delta_rule (deltanet.py:236-407).
+ *   q, k   [batch, seq_len, num_heads, dk]   (num_heads = value heads: the
+ *          caller has already repeated GQA heads, as the reference does)
+ *   v      [batch, seq_len, num_heads, dv]
+ *   g, beta [batch, seq_len, num_heads]
+ * in dtype `in_dtype` (contiguous).  `out` [batch, seq_len, num_heads, dv] is
+ * written in `in_dtype`.  use_qk_l2norm != 0 applies the L2 norm of
+ * config.py:114-115; q is always scaled by dk^-1/2.  `chunked` selects the
+ * chunked algorithm (otherwise token by token, any seq_len).
+ * Checkpoint offsets are local (absolute position - past_seen_tokens).
+ */
+int32_t gdn_delta_rule(int32_t batch, int32_t seq_len, int32_t num_heads, int32_t head_k_dim,
+                       int32_t head_v_dim, int32_t in_dtype, const void* q, const void* k,
+                       const void* v, const void* g, const void* beta, const float* state_in,
+                       float* state_out, void* out, int32_t use_qk_l2norm, int32_t chunked,
+                       int32_t num_checkpoints, const int32_t* checkpoint_offsets,
+                       float* state_checkpoints, void* stream);
+
+/*
+ * Stand-alone causal depthwise conv1d + optional SiLU, the functional
+ * boundary of _causal_conv1d_fn (deltanet.py:41-90), in the reference's
+ * [batch, channels, seq_len] layout (contiguous).  Computes in the weight
+ * dtype with one rounding per tap, as the reference does.
+ *   x [batch, channels, seq_len], weight [channels, kernel],
+ *   state_in [batch, channels, kernel-1] or NULL, out like x,
+ *   state_out [batch, channels, kernel-1] or NULL.
+ */
+int32_t gdn_causal_conv1d(int32_t batch, int32_t channels, int32_t seq_len, int32_t kernel,
+                          int32_t dtype, const void* x, const void* weight, const void* state_in,
+                          void* out, void* state_out, int32_t apply_silu, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H */

@@ -1,0 +1,58 @@
+"""Tolerances and comparison helpers shared by the parity tests.
+
+Tolerances (the path's parity bar):
+* outputs in bf16: |ours - ref| <= 2e-2, or at most one bf16 ulp of the
+  reference value (2^-7 |ref|) where that ulp is larger than 2e-2 (|ref| > 2.56):
+  two correct fp32 pipelines may round a large output to neighbouring bf16
+  values;
+* outputs in fp32: |ours - ref| <= 1e-4 (layer level) / 5e-5 (mixer level);
+* recurrent states (fp32): max |ours - ref| / max |ref| <= 1e-3;
+* conv states, conv checkpoints, checkpoint keys: bit-exact.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+BF16_ABS = 2e-2
+STATE_REL = 1e-3
+
+
+def to_np(t) -> np.ndarray:
+    if hasattr(t, "detach"):
+        return t.detach().float().cpu().numpy()
+    return np.asarray(t, dtype=np.float32)
+
+
+def max_abs(a, b) -> float:
+    return float(np.max(np.abs(to_np(a).astype(np.float64) - to_np(b).astype(np.float64))))
+
+
+def rel_max(a, b) -> float:
+    b = to_np(b)
+    return max_abs(a, b) / max(1e-30, float(np.max(np.abs(b))))
+
+
+def assert_bf16_close(ours, ref, what=""):
+    o, r = to_np(ours).astype(np.float64), to_np(ref).astype(np.float64)
+    assert o.shape == r.shape, (what, o.shape, r.shape)
+    err = np.abs(o - r)
+    lim = np.maximum(BF16_ABS, np.abs(r) * 2.0 ** -7)
+    bad = err > lim
+    assert not bad.any(), (f"{what}: {int(bad.sum())} elements outside tolerance, worst err "
+                           f"{float(err.max()):.3g} (ref {float(r.flat[int(np.argmax(err))]):.3g})")
+
+
+def assert_f32_close(ours, ref, tol, what=""):
+    err = max_abs(ours, ref)
+    assert err <= tol, f"{what}: max abs err {err:.3g} > {tol}"
+
+
+def assert_state_close(ours, ref, what="", tol=STATE_REL):
+    err = rel_max(ours, ref)
+    assert err <= tol, f"{what}: state max rel err {err:.3g} > {tol}"
+
+
+def assert_bit_exact(ours, ref, what=""):
+    o, r = to_np(ours), to_np(ref)
+    assert o.shape == r.shape, (what, o.shape, r.shape)
+    assert np.array_equal(o, r), f"{what}: {int((o != r).sum())} elements differ"

@@ -1,0 +1,126 @@
+"""The C-ABI library: it loads without a GPU, exports every declared entry
+point, and rejects bad arguments on the host (no launch happens in any case
+below: every call carries at least one invalid field)."""
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+import re
+
+import pytest
+import torch
+
+from visionstack_b200 import Qwen3_5GatedDeltaNet, Qwen3_5TextConfig, _lib
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "gdn_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(gdn_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_bound_symbols():
+    assert declared_functions() == sorted(_lib.EXPORTED_SYMBOLS)
+
+
+def test_library_loads_and_exports_every_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    assert lib.gdn_version() == 1
+
+
+def _valid_args(T=1):
+    """Arguments that would pass validation; tests break one field each."""
+    a = _lib.MixerArgs()
+    a.batch, a.seq_len, a.num_k_heads, a.num_v_heads = 2, T, 2, 4
+    a.head_k_dim = a.head_v_dim = 32
+    a.conv_kernel, a.act_dtype, a.norm_eps = 4, _lib.GDN_DTYPE_BF16, 1e-6
+    conv_dim = 2 * 2 * 32 + 4 * 32
+    a.mixed_qkv, a.mixed_stride_b, a.mixed_stride_t = 0x10000, T * conv_dim, conv_dim
+    a.z, a.z_stride_b, a.z_stride_t = 0x20000, T * 128, 128
+    a.a, a.b, a.ab_stride_b, a.ab_stride_t = 0x30000, 0x31000, T * 4, 4
+    a.conv_weight, a.A_log, a.dt_bias, a.norm_weight = 0x40000, 0x41000, 0x42000, 0x43000
+    a.out = 0x50000
+    a.state_in = a.state_out = 0x60000
+    return a
+
+
+def _call(fn, args):
+    lib = _lib.load()
+    return getattr(lib, fn)(ctypes.byref(args), None)
+
+
+@pytest.mark.parametrize("fn", ["gdn_mixer_decode", "gdn_mixer_prefill"])
+@pytest.mark.parametrize("breaker,code", [
+    (lambda a: setattr(a, "batch", 0), -1),
+    (lambda a: setattr(a, "num_v_heads", 3), -1),
+    (lambda a: setattr(a, "head_v_dim", 48), -2),
+    (lambda a: setattr(a, "head_k_dim", 256), -2),
+    (lambda a: setattr(a, "conv_kernel", 5), -2),
+    (lambda a: setattr(a, "act_dtype", 7), -2),
+    (lambda a: setattr(a, "mixed_qkv", None), -1),
+    (lambda a: setattr(a, "mixed_stride_t", 10), -1),
+    (lambda a: setattr(a, "z_stride_t", 3), -1),
+    (lambda a: setattr(a, "state_in", 0x60004), -3),
+    (lambda a: setattr(a, "out", 0x50001), -3),
+    (lambda a: (setattr(a, "conv_state_in", 0x70000), setattr(a, "conv_state_out", 0x70000)), -1),
+])
+def test_mixer_validation(fn, breaker, code):
+    a = _valid_args()
+    breaker(a)
+    assert _call(fn, a) == code
+    assert _lib.load().gdn_last_error_string()
+
+
+def test_checkpoint_validation():
+    a = _valid_args(T=4)
+    offs = _lib.int_array([1, 2, 2])
+    a.num_checkpoints = 3
+    a.checkpoint_offsets = ctypes.cast(offs, ctypes.POINTER(ctypes.c_int32))
+    a.state_checkpoints, a.conv_checkpoints = 0x80000, 0x90000
+    assert _call("gdn_mixer_decode", a) == -1  # duplicate offset
+    a.num_checkpoints = _lib.GDN_MAX_CHECKPOINTS + 1
+    assert _call("gdn_mixer_prefill", a) == -5
+    a.num_checkpoints = 2
+    a.state_checkpoints = None
+    assert _call("gdn_mixer_decode", a) == -1  # slots requested without buffers
+
+
+def test_decode_rejects_long_sequences():
+    a = _valid_args(T=9)
+    a.batch = -1  # also invalid, so nothing can launch
+    assert _call("gdn_mixer_decode", a) == -1
+
+
+def test_error_raises_runtime_error():
+    with pytest.raises(_lib.GDNError):
+        _lib.check("gdn_mixer_decode", _call("gdn_mixer_decode", _lib.MixerArgs()))
+
+
+def test_functional_validation():
+    lib = _lib.load()
+    assert lib.gdn_delta_rule(1, 4, 2, 48, 48, 0, 16, 16, 16, 16, 16, None, None, 16, 1, 1, 0, None, None,
+                              None) == -2
+    assert lib.gdn_delta_rule(0, 4, 2, 32, 32, 0, 16, 16, 16, 16, 16, None, None, 16, 1, 1, 0, None, None,
+                              None) == -1
+    assert lib.gdn_causal_conv1d(1, 8, 4, 6, 0, 16, 16, None, 16, None, 1, None) == -2
+    assert lib.gdn_causal_conv1d(1, 8, 4, 4, 1, 17, 16, None, 16, None, 1, None) == -3
+
+
+def test_state_dict_matches_reference_layout():
+    with open(os.path.join(REPO, "tests", "golden", "cache.json")) as f:
+        ref = json.load(f)["state_dict"]
+    m = Qwen3_5GatedDeltaNet(Qwen3_5TextConfig(hidden_size=2048), 3)
+    ours = {k: list(v.shape) for k, v in m.state_dict().items()}
+    assert ours == ref
+
+
+def test_layer_refuses_cpu_tensors():
+    m = Qwen3_5GatedDeltaNet(Qwen3_5TextConfig(hidden_size=64, linear_num_key_heads=1, linear_num_value_heads=2,
+                                               linear_key_head_dim=32, linear_value_head_dim=32), 0)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m(torch.zeros(1, 3, 64))

@@ -1,0 +1,26 @@
+"""B200 (sm_100a) Gated DeltaNet token mixer with the reference layer's interface.
+
+Public names mirror ShadowBoxer/models/qwen35 (deltanet.py, cache.py,
+config.py).  Kernels live in ``libgdn_b200.so`` (C ABI: include/gdn_b200.h),
+loaded on first use; there is no CPU implementation in this package.
+"""
+from .cache import Qwen3_5HybridCache
+from .config import Qwen3_5RMSNormGated, Qwen3_5TextConfig
+from .deltanet import (
+    Qwen3_5GatedDeltaNet,
+    _causal_conv1d_fn,
+    _chunk_gated_delta_rule,
+    _extract_conv_state_at_offset,
+    _recurrent_gated_delta_rule,
+)
+
+__all__ = [
+    "Qwen3_5HybridCache",
+    "Qwen3_5RMSNormGated",
+    "Qwen3_5TextConfig",
+    "Qwen3_5GatedDeltaNet",
+    "_causal_conv1d_fn",
+    "_chunk_gated_delta_rule",
+    "_extract_conv_state_at_offset",
+    "_recurrent_gated_delta_rule",
+]

@@ -1,0 +1,114 @@
+"""ctypes binding of ``libgdn_b200.so`` (the C ABI in ``include/gdn_b200.h``).
+
+The binding style follows the reference's own native DLL binding: ctypes,
+``int32`` status returns, and a non-zero status raised as ``RuntimeError``
+with the library's last error string (VizInjector/python/bindings.py:298-400,
+551-729).  There is no fallback: if the library is missing or cannot be
+loaded, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libgdn_b200.so")
+
+GDN_OK = 0
+GDN_DTYPE_F32 = 0
+GDN_DTYPE_BF16 = 1
+GDN_MAX_CHECKPOINTS = 512
+GDN_MAX_DECODE_TOKENS = 8
+
+EXPORTED_SYMBOLS = (
+    "gdn_version",
+    "gdn_last_error_string",
+    "gdn_mixer_decode",
+    "gdn_mixer_prefill",
+    "gdn_delta_rule",
+    "gdn_causal_conv1d",
+)
+
+_c_void_p = ctypes.c_void_p
+_i32 = ctypes.c_int32
+_i64 = ctypes.c_int64
+
+
+class MixerArgs(ctypes.Structure):
+    """Mirror of ``gdn_mixer_args`` (include/gdn_b200.h)."""
+
+    _fields_ = [
+        ("batch", _i32), ("seq_len", _i32), ("num_k_heads", _i32), ("num_v_heads", _i32),
+        ("head_k_dim", _i32), ("head_v_dim", _i32), ("conv_kernel", _i32), ("act_dtype", _i32),
+        ("norm_eps", ctypes.c_float), ("reserved0", _i32),
+        ("mixed_qkv", _c_void_p), ("mixed_stride_b", _i64), ("mixed_stride_t", _i64),
+        ("z", _c_void_p), ("z_stride_b", _i64), ("z_stride_t", _i64),
+        ("a", _c_void_p), ("b", _c_void_p), ("ab_stride_b", _i64), ("ab_stride_t", _i64),
+        ("conv_weight", _c_void_p), ("A_log", _c_void_p), ("dt_bias", _c_void_p), ("norm_weight", _c_void_p),
+        ("conv_state_in", _c_void_p), ("conv_state_out", _c_void_p),
+        ("state_in", _c_void_p), ("state_out", _c_void_p), ("out", _c_void_p),
+        ("num_checkpoints", _i32), ("reserved1", _i32),
+        ("checkpoint_offsets", ctypes.POINTER(_i32)),
+        ("state_checkpoints", _c_void_p), ("conv_checkpoints", _c_void_p),
+    ]
+
+
+class GDNError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, fn: str, status: int, message: str):
+        super().__init__(f"{fn} failed with status {status}: {message}")
+        self.status = status
+
+
+_lock = threading.Lock()
+_lib: Optional[ctypes.CDLL] = None
+
+
+def lib_path() -> str:
+    return LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Load the shared library once; raise loudly when it is not there."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python -m visionstack_b200.build` "
+                "(nvcc, sm_100a). There is no fallback implementation.")
+        lib = ctypes.CDLL(LIB_PATH)
+        lib.gdn_version.restype = _i32
+        lib.gdn_version.argtypes = []
+        lib.gdn_last_error_string.restype = ctypes.c_char_p
+        lib.gdn_last_error_string.argtypes = []
+        lib.gdn_mixer_decode.restype = _i32
+        lib.gdn_mixer_decode.argtypes = [ctypes.POINTER(MixerArgs), _c_void_p]
+        lib.gdn_mixer_prefill.restype = _i32
+        lib.gdn_mixer_prefill.argtypes = [ctypes.POINTER(MixerArgs), _c_void_p]
+        lib.gdn_delta_rule.restype = _i32
+        lib.gdn_delta_rule.argtypes = [_i32, _i32, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p,
+                                       _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32,
+                                       ctypes.POINTER(_i32), _c_void_p, _c_void_p]
+        lib.gdn_causal_conv1d.restype = _i32
+        lib.gdn_causal_conv1d.argtypes = [_i32, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p,
+                                          _c_void_p, _c_void_p, _i32, _c_void_p]
+        _lib = lib
+        return lib
+
+
+def check(fn: str, status: int) -> None:
+    if status != GDN_OK:
+        msg = load().gdn_last_error_string()
+        raise GDNError(fn, int(status), msg.decode(errors="replace") if msg else "")
+
+
+def int_array(values) -> "ctypes.Array":
+    vals = [int(v) for v in values]
+    return (_i32 * max(1, len(vals)))(*vals)

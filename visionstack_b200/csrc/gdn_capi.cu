@@ -1,0 +1,250 @@
+// C ABI of the Gated DeltaNet kernels: host-side validation, checkpoint
+// bookkeeping, dispatch.  Every entry returns an int32 status and never lets a
+// bad argument reach the device.
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <utility>
+#include <vector>
+
+#include "gdn_kernels.cuh"
+
+namespace {
+
+thread_local char g_err[512] = {0};
+
+int32_t fail(int32_t code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int32_t ok() {
+    g_err[0] = '\0';
+    return GDN_OK;
+}
+
+int32_t cuda_status(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return ok();
+    return fail(GDN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool aligned_elem(const void* p, int dtype) {
+    const uintptr_t m = dtype == GDN_DTYPE_BF16 ? 1u : 3u;
+    return (reinterpret_cast<uintptr_t>(p) & m) == 0;
+}
+
+// Keep offsets in 1..T, sort by offset (stable in the caller's slot order),
+// reject duplicates (the reference keys checkpoints by position in a dict).
+int32_t build_ckpts(int n, const int32_t* offsets, int T, gdn::CkptList* ck) {
+    ck->n = 0;
+    if (n < 0 || n > GDN_MAX_CHECKPOINTS)
+        return fail(GDN_ERR_TOO_MANY_CHECKPOINTS, "num_checkpoints %d outside 0..%d", n, GDN_MAX_CHECKPOINTS);
+    if (n > 0 && !offsets) return fail(GDN_ERR_INVALID_ARG, "checkpoint_offsets is NULL");
+    std::vector<std::pair<int, int>> v;
+    for (int i = 0; i < n; ++i)
+        if (offsets[i] >= 1 && offsets[i] <= T) v.emplace_back(offsets[i], i);
+    std::stable_sort(v.begin(), v.end(),
+                     [](const std::pair<int, int>& a, const std::pair<int, int>& b) { return a.first < b.first; });
+    for (size_t i = 1; i < v.size(); ++i)
+        if (v[i].first == v[i - 1].first)
+            return fail(GDN_ERR_INVALID_ARG, "duplicate checkpoint offset %d", v[i].first);
+    ck->n = (int)v.size();
+    for (size_t i = 0; i < v.size(); ++i) {
+        ck->off[i] = v[i].first;
+        ck->slot[i] = v[i].second;
+    }
+    return GDN_OK;
+}
+
+bool supported_head_dims(int dk, int dv) { return dk == dv && (dk == 32 || dk == 64 || dk == 128); }
+
+int32_t validate_mixer(const gdn_mixer_args* a, gdn::MixParams* p, gdn::CkptList* ck) {
+    if (!a) return fail(GDN_ERR_INVALID_ARG, "args is NULL");
+    if (a->batch < 1 || a->seq_len < 1 || a->num_k_heads < 1 || a->num_v_heads < 1)
+        return fail(GDN_ERR_INVALID_ARG, "batch, seq_len and head counts must be >= 1");
+    if (a->num_v_heads % a->num_k_heads != 0)
+        return fail(GDN_ERR_INVALID_ARG, "num_v_heads (%d) must be a multiple of num_k_heads (%d)", a->num_v_heads,
+                    a->num_k_heads);
+    if (!supported_head_dims(a->head_k_dim, a->head_v_dim))
+        return fail(GDN_ERR_UNSUPPORTED, "head dims (%d, %d) not built: need dk == dv in {32, 64, 128}",
+                    a->head_k_dim, a->head_v_dim);
+    if (a->conv_kernel < 1 || a->conv_kernel > 4)
+        return fail(GDN_ERR_UNSUPPORTED, "conv_kernel %d not in 1..4", a->conv_kernel);
+    if (a->act_dtype != GDN_DTYPE_F32 && a->act_dtype != GDN_DTYPE_BF16)
+        return fail(GDN_ERR_UNSUPPORTED, "act_dtype %d", a->act_dtype);
+    if (!(a->norm_eps >= 0.0f)) return fail(GDN_ERR_INVALID_ARG, "norm_eps must be >= 0");
+    if (!a->mixed_qkv || !a->z || !a->a || !a->b || !a->conv_weight || !a->A_log || !a->dt_bias ||
+        !a->norm_weight || !a->out)
+        return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
+    const int64_t dk = a->head_k_dim, dv = a->head_v_dim;
+    const int64_t conv_dim = 2 * a->num_k_heads * dk + a->num_v_heads * dv;
+    const int64_t vdim = a->num_v_heads * dv;
+    const int64_t T = a->seq_len;
+    if (a->mixed_stride_t < conv_dim || a->mixed_stride_b < (T - 1) * a->mixed_stride_t + conv_dim)
+        return fail(GDN_ERR_INVALID_ARG, "mixed_qkv strides (%lld, %lld) too small for conv_dim %lld",
+                    (long long)a->mixed_stride_b, (long long)a->mixed_stride_t, (long long)conv_dim);
+    if (a->z_stride_t < vdim || a->z_stride_b < (T - 1) * a->z_stride_t + vdim)
+        return fail(GDN_ERR_INVALID_ARG, "z strides too small");
+    if (a->ab_stride_t < a->num_v_heads || a->ab_stride_b < (T - 1) * a->ab_stride_t + a->num_v_heads)
+        return fail(GDN_ERR_INVALID_ARG, "a/b strides too small");
+    const void* elem_ptrs[] = {a->mixed_qkv, a->z, a->a, a->b, a->conv_weight, a->norm_weight, a->out,
+                               a->conv_state_in, a->conv_state_out, a->conv_checkpoints};
+    for (const void* ptr : elem_ptrs)
+        if (ptr && !aligned_elem(ptr, a->act_dtype)) return fail(GDN_ERR_ALIGNMENT, "misaligned activation pointer");
+    const void* f4_ptrs[] = {a->state_in, a->state_out, a->state_checkpoints};
+    for (const void* ptr : f4_ptrs)
+        if (ptr && !aligned16(ptr)) return fail(GDN_ERR_ALIGNMENT, "state pointers must be 16-byte aligned");
+    if (!aligned_elem(a->A_log, GDN_DTYPE_F32) || !aligned_elem(a->dt_bias, GDN_DTYPE_F32))
+        return fail(GDN_ERR_ALIGNMENT, "A_log / dt_bias must be 4-byte aligned");
+    if (a->conv_state_in && a->conv_state_in == a->conv_state_out)
+        return fail(GDN_ERR_INVALID_ARG, "conv_state_out must not alias conv_state_in");
+    int32_t st = build_ckpts(a->num_checkpoints, a->checkpoint_offsets, a->seq_len, ck);
+    if (st != GDN_OK) return st;
+    if (ck->n > 0 && (!a->state_checkpoints || !a->conv_checkpoints))
+        return fail(GDN_ERR_INVALID_ARG, "checkpoints requested but state_checkpoints/conv_checkpoints is NULL");
+
+    std::memset(p, 0, sizeof(*p));
+    p->B = a->batch;
+    p->T = a->seq_len;
+    p->Hk = a->num_k_heads;
+    p->Hv = a->num_v_heads;
+    p->K = a->conv_kernel;
+    p->eps = a->norm_eps;
+    p->q_scale = (float)std::pow((double)dk, -0.5);
+    p->use_l2 = 1;
+    p->mixed = a->mixed_qkv;
+    p->ms_b = a->mixed_stride_b;
+    p->ms_t = a->mixed_stride_t;
+    p->z = a->z;
+    p->zs_b = a->z_stride_b;
+    p->zs_t = a->z_stride_t;
+    p->a = a->a;
+    p->b = a->b;
+    p->as_b = a->ab_stride_b;
+    p->as_t = a->ab_stride_t;
+    p->convw = a->conv_weight;
+    p->A_log = a->A_log;
+    p->dt_bias = a->dt_bias;
+    p->normw = a->norm_weight;
+    p->cs_in = a->conv_state_in;
+    p->cs_out = a->conv_state_out;
+    p->S_in = a->state_in;
+    p->S_out = a->state_out;
+    p->out = a->out;
+    p->S_ckpt = a->state_checkpoints;
+    p->cs_ckpt = a->conv_checkpoints;
+    return GDN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t gdn_version(void) { return GDN_ABI_VERSION; }
+
+const char* gdn_last_error_string(void) { return g_err; }
+
+int32_t gdn_mixer_decode(const gdn_mixer_args* args, void* stream) {
+    gdn::CkptList ck;
+    gdn::MixParams p;
+    int32_t st = validate_mixer(args, &p, &ck);
+    if (st != GDN_OK) return st;
+    if (args->seq_len > GDN_MAX_DECODE_TOKENS)
+        return fail(GDN_ERR_INVALID_ARG, "seq_len %d exceeds the token-by-token limit %d", args->seq_len,
+                    GDN_MAX_DECODE_TOKENS);
+    bool supported = false;
+    cudaError_t e = gdn::launch_decode(p, ck, args->head_k_dim, args->head_v_dim, args->act_dtype, true,
+                                       static_cast<cudaStream_t>(stream), &supported);
+    if (!supported) return fail(GDN_ERR_UNSUPPORTED, "no token-by-token kernel for these head dims");
+    return cuda_status(e, "gdn_mixer_decode launch");
+}
+
+int32_t gdn_mixer_prefill(const gdn_mixer_args* args, void* stream) {
+    gdn::CkptList ck;
+    gdn::MixParams p;
+    int32_t st = validate_mixer(args, &p, &ck);
+    if (st != GDN_OK) return st;
+    bool supported = false;
+    cudaError_t e = gdn::launch_prefill(p, ck, args->head_k_dim, args->act_dtype, true,
+                                        static_cast<cudaStream_t>(stream), &supported);
+    if (!supported) return fail(GDN_ERR_UNSUPPORTED, "no chunked kernel for these head dims");
+    return cuda_status(e, "gdn_mixer_prefill launch");
+}
+
+int32_t gdn_delta_rule(int32_t batch, int32_t seq_len, int32_t num_heads, int32_t head_k_dim, int32_t head_v_dim,
+                       int32_t in_dtype, const void* q, const void* k, const void* v, const void* g,
+                       const void* beta, const float* state_in, float* state_out, void* out, int32_t use_qk_l2norm,
+                       int32_t chunked, int32_t num_checkpoints, const int32_t* checkpoint_offsets,
+                       float* state_checkpoints, void* stream) {
+    if (batch < 1 || seq_len < 1 || num_heads < 1) return fail(GDN_ERR_INVALID_ARG, "sizes must be >= 1");
+    if (!supported_head_dims(head_k_dim, head_v_dim))
+        return fail(GDN_ERR_UNSUPPORTED, "head dims (%d, %d) not built: need dk == dv in {32, 64, 128}",
+                    head_k_dim, head_v_dim);
+    if (in_dtype != GDN_DTYPE_F32 && in_dtype != GDN_DTYPE_BF16)
+        return fail(GDN_ERR_UNSUPPORTED, "in_dtype %d", in_dtype);
+    if (!q || !k || !v || !g || !beta || !out) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
+    const void* elem_ptrs[] = {q, k, v, g, beta, out};
+    for (const void* ptr : elem_ptrs)
+        if (!aligned_elem(ptr, in_dtype)) return fail(GDN_ERR_ALIGNMENT, "misaligned input pointer");
+    const void* f4_ptrs[] = {state_in, state_out, state_checkpoints};
+    for (const void* ptr : f4_ptrs)
+        if (ptr && !aligned16(ptr)) return fail(GDN_ERR_ALIGNMENT, "state pointers must be 16-byte aligned");
+    gdn::CkptList ck;
+    int32_t st = build_ckpts(num_checkpoints, checkpoint_offsets, seq_len, &ck);
+    if (st != GDN_OK) return st;
+    if (ck.n > 0 && !state_checkpoints)
+        return fail(GDN_ERR_INVALID_ARG, "checkpoints requested but state_checkpoints is NULL");
+    gdn::MixParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.B = batch;
+    p.T = seq_len;
+    p.Hk = num_heads;
+    p.Hv = num_heads;
+    p.K = 1;
+    p.q_scale = (float)std::pow((double)head_k_dim, -0.5);
+    p.use_l2 = use_qk_l2norm ? 1 : 0;
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.g = g;
+    p.beta = beta;
+    p.S_in = state_in;
+    p.S_out = state_out;
+    p.out = out;
+    p.S_ckpt = state_checkpoints;
+    bool supported = false;
+    cudaError_t e;
+    if (chunked)
+        e = gdn::launch_prefill(p, ck, head_k_dim, in_dtype, false, static_cast<cudaStream_t>(stream), &supported);
+    else
+        e = gdn::launch_decode(p, ck, head_k_dim, head_v_dim, in_dtype, false, static_cast<cudaStream_t>(stream),
+                               &supported);
+    if (!supported) return fail(GDN_ERR_UNSUPPORTED, "no kernel for these head dims");
+    return cuda_status(e, "gdn_delta_rule launch");
+}
+
+int32_t gdn_causal_conv1d(int32_t batch, int32_t channels, int32_t seq_len, int32_t kernel, int32_t dtype,
+                          const void* x, const void* weight, const void* state_in, void* out, void* state_out,
+                          int32_t apply_silu, void* stream) {
+    if (batch < 1 || channels < 1 || seq_len < 1) return fail(GDN_ERR_INVALID_ARG, "sizes must be >= 1");
+    if (kernel < 1 || kernel > 4) return fail(GDN_ERR_UNSUPPORTED, "kernel %d not in 1..4", kernel);
+    if (dtype != GDN_DTYPE_F32 && dtype != GDN_DTYPE_BF16) return fail(GDN_ERR_UNSUPPORTED, "dtype %d", dtype);
+    if (!x || !weight || !out) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
+    if ((int64_t)batch * channels > (int64_t)1 << 30) return fail(GDN_ERR_INVALID_ARG, "too many rows");
+    const void* ptrs[] = {x, weight, state_in, out, state_out};
+    for (const void* ptr : ptrs)
+        if (ptr && !aligned_elem(ptr, dtype)) return fail(GDN_ERR_ALIGNMENT, "misaligned pointer");
+    if (state_in && state_in == state_out) return fail(GDN_ERR_INVALID_ARG, "state_out must not alias state_in");
+    cudaError_t e = gdn::launch_conv1d(batch, channels, seq_len, kernel, dtype, x, weight, state_in, out, state_out,
+                                       apply_silu, static_cast<cudaStream_t>(stream));
+    return cuda_status(e, "gdn_causal_conv1d launch");
+}
+
+}  // extern "C"

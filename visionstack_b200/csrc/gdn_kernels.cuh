@@ -1,0 +1,61 @@
+// Kernel parameter blocks and launcher declarations of the Gated DeltaNet
+// kernels.  The C ABI (gdn_capi.cu) validates arguments and fills these.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/gdn_b200.h"
+
+namespace gdn {
+
+// Checkpoints of one call, restricted to local offsets in 1..T and sorted by
+// offset: slot[i] is the caller's checkpoint index (the output slot) of off[i].
+struct CkptList {
+    int n;
+    int off[GDN_MAX_CHECKPOINTS];
+    int slot[GDN_MAX_CHECKPOINTS];
+};
+
+struct MixParams {
+    int B, T, Hk, Hv, K;
+    float eps;      // gated-norm epsilon
+    float q_scale;  // head_k_dim ** -0.5 rounded to float, as torch does
+    int use_l2;     // split mode: apply the q/k L2 norm
+    // fused-mixer inputs
+    const void* mixed;
+    long long ms_b, ms_t;
+    const void* z;
+    long long zs_b, zs_t;
+    const void* a;
+    const void* b;
+    long long as_b, as_t;
+    const void* convw;
+    const float* A_log;
+    const float* dt_bias;
+    const void* normw;
+    const void* cs_in;
+    void* cs_out;
+    // split-mode inputs ([B, T, H, d] / [B, T, H], contiguous)
+    const void* q;
+    const void* k;
+    const void* v;
+    const void* g;
+    const void* beta;
+    // state and outputs
+    const float* S_in;
+    float* S_out;
+    void* out;
+    float* S_ckpt;    // [n_slots, B, Hv, dk, dv]
+    void* cs_ckpt;    // [n_slots, B, conv_dim, K-1]
+};
+
+// dtype: GDN_DTYPE_*; mixer: fused conv/gates/norm (true) or split q/k/v (false).
+cudaError_t launch_decode(const MixParams& p, const CkptList& ck, int dk, int dv, int dtype, bool mixer,
+                          cudaStream_t s, bool* supported);
+cudaError_t launch_prefill(const MixParams& p, const CkptList& ck, int d, int dtype, bool mixer,
+                           cudaStream_t s, bool* supported);
+cudaError_t launch_conv1d(int B, int C, int T, int K, int dtype, const void* x, const void* w,
+                          const void* state_in, void* out, void* state_out, int silu, cudaStream_t s);
+
+}  // namespace gdn
