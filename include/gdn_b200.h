@@ -49,6 +49,14 @@ extern "C" {
 #define GDN_DTYPE_F32 0
 #define GDN_DTYPE_BF16 1
 
+/* gdn_mixer_args.flags: run the register-tile token-by-token kernel even
+ * where the bulk-copy pipelined one applies (both are exact; for testing). */
+#define GDN_FLAG_REGISTER_KERNEL 1
+
+/* Bits of the device error word (gdn_device_error). */
+#define GDN_DEVERR_TMA_TIMEOUT 0x1u
+#define GDN_DEVERR_MMA_TIMEOUT 0x2u
+
 /* Maximum number of state checkpoints one call can record. */
 #define GDN_MAX_CHECKPOINTS 512
 /* Longest sequence the token-by-token (decode / verify) entry accepts. */
@@ -87,7 +95,7 @@ typedef struct gdn_mixer_args {
     int32_t conv_kernel;
     int32_t act_dtype;        /* GDN_DTYPE_* */
     float norm_eps;           /* rms_norm_eps of the gated norm */
-    int32_t reserved0;
+    int32_t flags;            /* GDN_FLAG_* bits, 0 by default */
 
     const void* mixed_qkv;    /* required */
     int64_t mixed_stride_b;   /* elements between batch rows */
@@ -130,9 +138,20 @@ const char* gdn_last_error_string(void);
  * hands off to _recurrent_gated_delta_rule (deltanet.py:251-264, 165-233).
  * One launch: conv-state shift + conv + SiLU, L2 norms, gates, decay and
  * rank-1 delta update of the fp32 state (in place when state_out == state_in),
- * readout, gated RMSNorm, per-token checkpoints.
+ * readout, gated RMSNorm, per-token checkpoints.  When the inputs are 16-byte
+ * aligned (strides in multiples of 16 bytes) a persistent kernel streams the
+ * per-(batch, head) tiles through a bulk-copy shared-memory pipeline;
+ * otherwise a register-tile kernel runs.  Both compute the same thing.
  */
 int32_t gdn_mixer_decode(const gdn_mixer_args* args, void* stream);
+
+/*
+ * Read (and optionally clear) the sticky device error word of the current
+ * device: bounded waits inside the pipelined kernels that gave up set a
+ * GDN_DEVERR_* bit instead of hanging.  Synchronises the device.  No
+ * counterpart in the reference (it has no device code).
+ */
+int32_t gdn_device_error(uint32_t* flags_out, int32_t clear);
 
 /*
  * Chunked token mixer for any seq_len >= 1 (prefill).  Replaces

@@ -46,7 +46,7 @@ def mixer_inputs(shape: W.LayerShape, B: int, T: int, dtype: str, seed: int, wit
     return d
 
 
-def run_ours(m, shape, d, dtype, token_by_token, offsets=()):
+def run_ours(m, shape, d, dtype, token_by_token, offsets=(), register_kernel=False):
     dev = torch.device("cuda")
     t = lambda a: torch.from_numpy(a).to(dev).to(TDT[dtype])  # noqa: E731
     B, T = d["mixed"].shape[:2]
@@ -61,7 +61,8 @@ def run_ours(m, shape, d, dtype, token_by_token, offsets=()):
     cv_ck = torch.zeros((n, B, shape.conv_dim, L), dtype=TDT[dtype], device=dev) if n else None
     out = m.mixer(t(d["mixed"]), t(d["z"]), t(d["b"]), t(d["a"]), conv_state=cs, rec_state=rs,
                   conv_state_out=cs_out, rec_state_out=rs_out, checkpoint_offsets=offsets,
-                  state_checkpoints=st_ck, conv_checkpoints=cv_ck, token_by_token=token_by_token)
+                  state_checkpoints=st_ck, conv_checkpoints=cv_ck, token_by_token=token_by_token,
+                  register_kernel=register_kernel)
     torch.cuda.synchronize()
     return out, cs_out, rs_out, st_ck, cv_ck
 
@@ -88,14 +89,46 @@ def check(shape, dtype, ours, ref, offsets=(), what=""):
         assert_state_close(st_ck[i], r_st[off], f"{what} state checkpoint {off}")
 
 
+@pytest.mark.parametrize("register_kernel", [False, True])
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
 @pytest.mark.parametrize("T,offsets", [(1, (1,)), (4, (1, 2, 4)), (8, (3, 8))])
-def test_token_by_token_small(dtype, T, offsets):
+def test_token_by_token_small(dtype, T, offsets, register_kernel):
     shape = W.SHAPE_TINY
     m, params = make_layer(shape, dtype)
     d = mixer_inputs(shape, 3, T, dtype, seed=10 + T, with_state=True)
-    check(shape, dtype, run_ours(m, shape, d, dtype, True, offsets),
+    check(shape, dtype, run_ours(m, shape, d, dtype, True, offsets, register_kernel),
           run_oracle(shape, params, d, dtype, chunk=False, offsets=offsets), offsets, f"tbt T{T}")
+
+
+@pytest.mark.parametrize("d_head,T", [(64, 1), (64, 5), (128, 3)])
+def test_token_by_token_head_dims(d_head, T):
+    shape = W.LayerShape(256, 2, 4, d_head, d_head)
+    m, params = make_layer(shape, "bf16")
+    d = mixer_inputs(shape, 5, T, "bf16", seed=31 + T, with_state=True)
+    offs = tuple(range(1, T + 1))
+    check(shape, "bf16", run_ours(m, shape, d, "bf16", True, offs),
+          run_oracle(shape, params, d, "bf16", chunk=False, offsets=offs), offs, f"tbt d{d_head}")
+
+
+def test_token_by_token_unaligned_strides_fall_back():
+    """Projection outputs with a token stride that is not a multiple of 16
+    bytes cannot be bulk-copied; the register-tile kernel takes over."""
+    from visionstack_b200 import _lib
+    shape = W.SHAPE_TINY
+    m, params = make_layer(shape, "bf16")
+    d = mixer_inputs(shape, 2, 2, "bf16", seed=77, with_state=True)
+    dev = torch.device("cuda")
+    t = lambda a: torch.from_numpy(a).to(dev).to(torch.bfloat16)  # noqa: E731
+    wide = torch.zeros(2, 2, shape.conv_dim + 3, dtype=torch.bfloat16, device=dev)
+    wide[..., :shape.conv_dim] = t(d["mixed"])
+    mixed = wide[..., :shape.conv_dim]
+    assert mixed.stride(1) % 8 != 0
+    out = m.mixer(mixed, t(d["z"]), t(d["b"]), t(d["a"]), conv_state=t(d["conv_state"]),
+                  rec_state=torch.from_numpy(d["rec_state"]).to(dev), token_by_token=True)
+    torch.cuda.synchronize()
+    ref = run_oracle(shape, params, d, "bf16", chunk=False)
+    assert_bf16_close(out, ref[0], "unaligned")
+    assert _lib.device_error() == 0
 
 
 def test_token_by_token_without_state():
@@ -125,13 +158,16 @@ def test_chunked_head_dims(d_head):
           run_oracle(shape, params, d, "bf16", chunk=True, offsets=(70, 150)), (70, 150), f"d{d_head}")
 
 
-def test_decode_step_qwen_shape():
+@pytest.mark.parametrize("register_kernel", [False, True])
+def test_decode_step_qwen_shape(register_kernel):
     """One decode step at the decode benchmark's shape (B64, 16/32 heads, d128)."""
+    from visionstack_b200 import _lib
     shape = W.SHAPE_QWEN
     m, params = make_layer(shape, "bf16")
     d = mixer_inputs(shape, 64, 1, "bf16", seed=2, with_state=True)
-    check(shape, "bf16", run_ours(m, shape, d, "bf16", True), run_oracle(shape, params, d, "bf16", chunk=False),
-          what="decode B64")
+    check(shape, "bf16", run_ours(m, shape, d, "bf16", True, register_kernel=register_kernel),
+          run_oracle(shape, params, d, "bf16", chunk=False), what="decode B64")
+    assert _lib.device_error() == 0
 
 
 def test_prefill_qwen_shape():

@@ -29,7 +29,9 @@ EXPORTED_SYMBOLS = (
     "gdn_mixer_prefill",
     "gdn_delta_rule",
     "gdn_causal_conv1d",
+    "gdn_device_error",
 )
+GDN_FLAG_REGISTER_KERNEL = 1
 
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int32
@@ -42,7 +44,7 @@ class MixerArgs(ctypes.Structure):
     _fields_ = [
         ("batch", _i32), ("seq_len", _i32), ("num_k_heads", _i32), ("num_v_heads", _i32),
         ("head_k_dim", _i32), ("head_v_dim", _i32), ("conv_kernel", _i32), ("act_dtype", _i32),
-        ("norm_eps", ctypes.c_float), ("reserved0", _i32),
+        ("norm_eps", ctypes.c_float), ("flags", _i32),
         ("mixed_qkv", _c_void_p), ("mixed_stride_b", _i64), ("mixed_stride_t", _i64),
         ("z", _c_void_p), ("z_stride_b", _i64), ("z_stride_t", _i64),
         ("a", _c_void_p), ("b", _c_void_p), ("ab_stride_b", _i64), ("ab_stride_t", _i64),
@@ -99,6 +101,8 @@ def load() -> ctypes.CDLL:
         lib.gdn_causal_conv1d.restype = _i32
         lib.gdn_causal_conv1d.argtypes = [_i32, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p,
                                           _c_void_p, _c_void_p, _i32, _c_void_p]
+        lib.gdn_device_error.restype = _i32
+        lib.gdn_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32), _i32]
         _lib = lib
         return lib
 
@@ -107,6 +111,13 @@ def check(fn: str, status: int) -> None:
     if status != GDN_OK:
         msg = load().gdn_last_error_string()
         raise GDNError(fn, int(status), msg.decode(errors="replace") if msg else "")
+
+
+def device_error(clear: bool = True) -> int:
+    """Sticky device error bits (bounded waits that gave up); synchronises."""
+    v = ctypes.c_uint32(0)
+    check("gdn_device_error", load().gdn_device_error(ctypes.byref(v), 1 if clear else 0))
+    return int(v.value)
 
 
 def int_array(values) -> "ctypes.Array":

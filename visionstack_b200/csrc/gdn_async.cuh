@@ -1,0 +1,86 @@
+// Bulk asynchronous copies (TMA engine, cp.async.bulk), mbarriers and the
+// device error word used by the pipelined kernels (sm_100a inline PTX).
+//
+// Every wait on an mbarrier is bounded: after GDN_WAIT_LIMIT_NS of global
+// time it gives up, records the reason in the device error word and returns
+// false, so a kernel never spins forever.  No copy here uses cluster
+// multicast: every source is this GPU's own global memory.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/gdn_b200.h"  // GDN_DEVERR_* bits
+
+#define GDN_WAIT_LIMIT_NS 1000000000ull  // 1 s
+
+namespace gdn {
+
+// Sticky per-device error word.  Each translation unit that includes this
+// header has its own copy; it exposes a host reader (see gdn_kernels.cuh)
+// that the C ABI combines in gdn_device_error().
+static __device__ unsigned int g_device_error;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Order this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (bulk copy) accesses of the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for phase `parity` of the mbarrier; false after the limit.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, unsigned int err_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 0u && global_timer_ns() - t0 > GDN_WAIT_LIMIT_NS) {
+            atomicOr(&g_device_error, err_flag);
+            return false;
+        }
+    }
+}
+
+// One bulk copy global -> shared of `bytes` (multiple of 16, both addresses
+// 16-byte aligned), completing `bytes` of transaction count on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst_smem),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+}  // namespace gdn

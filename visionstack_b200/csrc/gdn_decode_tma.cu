@@ -1,0 +1,413 @@
+// K1 (streaming form): persistent, bulk-copy pipelined token-by-token Gated DeltaNet.
+//
+// Each CTA (one per SM) holds two independent consumer groups of 256 threads.
+// A group walks (batch row, value head) tiles; each tile's inputs - the fp32
+// state S[d][d] (one contiguous 64 KB block at d = 128), the raw projections
+// of its q/k/v channels and z for every token, its conv-state and
+// conv-weight rows - arrive in the group's shared-memory stage through bulk
+// asynchronous copies (cp.async.bulk, completion on one mbarrier).  As soon as
+// the group has moved the state into registers and run the conv, it releases
+// the stage and issues the copies of its next tile, so that copy overlaps the
+// rest of the computation.  The two groups interleave, keeping two state
+// tiles in flight per SM while the SMs do the conv / norm / delta-rule /
+// gated-norm work.  The new state leaves from registers with streaming
+// 128-bit stores (in place when state_out == state_in).
+//
+// Math per token is that of decode_kernel (gdn_decode.cu): the reference's
+// deltanet.py:41-90 (conv), :186-189 (L2 norm), :516-517 (gates),
+// :210-221 (delta rule), config.py:136-143 (gated RMSNorm).
+#include "gdn_async.cuh"
+#include "gdn_common.cuh"
+#include "gdn_kernels.cuh"
+
+namespace gdn {
+namespace dtma {
+
+constexpr int GT = 256;     // threads per consumer group
+constexpr int NG = 2;       // consumer groups per CTA
+constexpr int NT = GT * NG;
+constexpr int KC = 4;       // conv taps of the streaming kernel
+constexpr int LC = KC - 1;  // conv-state length
+
+template <int D, int TMAX, typename TA>
+struct GroupLayout {
+    static constexpr int ES = (int)sizeof(TA);
+    static constexpr int CG = D / 4, RG = GT / CG;
+    // stage: filled by bulk copies
+    static constexpr int S_BYTES = D * D * 4;
+    static constexpr int M_BYTES = TMAX * D * ES;  // one of q / k / v / z, all tokens
+    static constexpr int OFF_S = 0;
+    static constexpr int OFF_MQ = OFF_S + S_BYTES;
+    static constexpr int OFF_MK = OFF_MQ + M_BYTES;
+    static constexpr int OFF_MV = OFF_MK + M_BYTES;
+    static constexpr int OFF_Z = OFF_MV + M_BYTES;
+    static constexpr int OFF_CS = OFF_Z + M_BYTES;           // [3][D][LC]
+    static constexpr int OFF_CW = OFF_CS + 3 * D * LC * ES;  // [3][D][KC]
+    static constexpr int STAGE_END = OFF_CW + 3 * D * KC * ES;
+    // work area: private to the group, valid while the stage refills
+    static constexpr int OFF_CONV = (STAGE_END + 15) / 16 * 16;  // [TMAX][3D] f32 conv outputs q|k|v
+    static constexpr int OFF_ZF = OFF_CONV + TMAX * 3 * D * 4;   // [TMAX][D] f32
+    static constexpr int OFF_U = OFF_ZF + TMAX * D * 4;          // [D]
+    static constexpr int OFF_O = OFF_U + D * 4;                  // [D]
+    static constexpr int OFF_RED = OFF_O + D * 4;                // [2][RG][D]
+    static constexpr int OFF_GATE = OFF_RED + 2 * RG * D * 4;    // [2][TMAX]
+    static constexpr int OFF_BAR = (OFF_GATE + 2 * TMAX * 4 + 7) / 8 * 8;
+    static constexpr int BYTES = (OFF_BAR + 8 + 127) / 128 * 128;
+};
+
+__device__ __forceinline__ void group_sync(int id) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(GT) : "memory");
+}
+
+__device__ __forceinline__ bool group_any(bool pred, int id) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}\n"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(GT)
+        : "memory");
+    return r != 0;
+}
+
+template <int D, int TMAX, typename TA>
+__global__ void __launch_bounds__(NT, 1)
+    decode_tma_kernel(const MixParams p, const CkptList ck, const int num_tiles) {
+    using GL = GroupLayout<D, TMAX, TA>;
+    constexpr int CG = GL::CG, RG = GL::RG, RPT = D / RG;
+    static_assert(D % RG == 0 && RPT >= 4 && RPT % 4 == 0, "bad tiling");
+
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int grp = threadIdx.x / GT, tid = threadIdx.x % GT, lane = tid & 31;
+    const int bar_id = 1 + grp;  // named barrier of this group (0 is __syncthreads)
+    unsigned char* gbase = smem + grp * GL::BYTES;
+    float* cbuf = reinterpret_cast<float*>(gbase + GL::OFF_CONV);
+    float* zbuf = reinterpret_cast<float*>(gbase + GL::OFF_ZF);
+    float* su = reinterpret_cast<float*>(gbase + GL::OFF_U);
+    float* so = reinterpret_cast<float*>(gbase + GL::OFF_O);
+    float* red = reinterpret_cast<float*>(gbase + GL::OFF_RED);
+    float* sgate = reinterpret_cast<float*>(gbase + GL::OFF_GATE);
+    const uint32_t bar = smem_u32(gbase + GL::OFF_BAR);
+
+    const int cg = tid % CG, rg = tid / CG;
+    const int rep = p.Hv / p.Hk;
+    const int T = p.T;
+    const int conv_dim = 2 * p.Hk * D + p.Hv * D;
+    const bool has_cs = p.cs_in != nullptr;
+    const bool has_S = p.S_in != nullptr;
+    const TA* gmixed = static_cast<const TA*>(p.mixed);
+    const TA* gz = static_cast<const TA*>(p.z);
+
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    // thread 0 of the group issues every copy of one tile into the group's stage
+    auto issue = [&](int tile) {
+        const int b = tile / p.Hv, h = tile - (tile / p.Hv) * p.Hv, kh = h / rep;
+        const uint32_t mrow = D * sizeof(TA);
+        const int c0 = kh * D, c1 = p.Hk * D + kh * D, c2 = 2 * p.Hk * D + h * D;
+        uint32_t bytes = (has_S ? GL::S_BYTES : 0) + 4u * T * mrow + 3u * D * KC * sizeof(TA);
+        if (has_cs) bytes += 3u * D * LC * sizeof(TA);
+        mbar_arrive_expect_tx(bar, bytes);
+        if (has_S) bulk_load(smem_u32(gbase + GL::OFF_S), p.S_in + (size_t)tile * D * D, GL::S_BYTES, bar);
+        for (int t = 0; t < T; ++t) {
+            const TA* row = gmixed + (size_t)b * p.ms_b + (size_t)t * p.ms_t;
+            bulk_load(smem_u32(gbase + GL::OFF_MQ + t * mrow), row + c0, mrow, bar);
+            bulk_load(smem_u32(gbase + GL::OFF_MK + t * mrow), row + c1, mrow, bar);
+            bulk_load(smem_u32(gbase + GL::OFF_MV + t * mrow), row + c2, mrow, bar);
+            bulk_load(smem_u32(gbase + GL::OFF_Z + t * mrow), gz + (size_t)b * p.zs_b + (size_t)t * p.zs_t + h * D,
+                      mrow, bar);
+        }
+        const TA* cw = static_cast<const TA*>(p.convw);
+        const int chans[3] = {c0, c1, c2};
+#pragma unroll
+        for (int g = 0; g < 3; ++g) {
+            if (has_cs)
+                bulk_load(smem_u32(gbase + GL::OFF_CS + g * D * LC * (int)sizeof(TA)),
+                          static_cast<const TA*>(p.cs_in) + ((size_t)b * conv_dim + chans[g]) * LC,
+                          D * LC * sizeof(TA), bar);
+            bulk_load(smem_u32(gbase + GL::OFF_CW + g * D * KC * (int)sizeof(TA)), cw + (size_t)chans[g] * KC,
+                      D * KC * sizeof(TA), bar);
+        }
+    };
+
+    const int worker = blockIdx.x * NG + grp, nworkers = gridDim.x * NG;
+    if (tid == 0 && worker < num_tiles) issue(worker);
+
+    // gate inputs of the next tile are loaded one tile ahead into registers
+    float na = 0.f, nb = 0.f;
+    auto load_gates = [&](int tile) {
+        if (tid < T && tile < num_tiles) {
+            const int b = tile / p.Hv, h = tile - (tile / p.Hv) * p.Hv;
+            const size_t ai = (size_t)b * p.as_b + (size_t)tid * p.as_t + h;
+            na = Act<TA>::ld(static_cast<const TA*>(p.a) + ai);
+            nb = Act<TA>::ld(static_cast<const TA*>(p.b) + ai);
+        }
+    };
+    load_gates(worker);
+
+    const TA* sMQ = reinterpret_cast<const TA*>(gbase + GL::OFF_MQ);
+    const TA* sZ = reinterpret_cast<const TA*>(gbase + GL::OFF_Z);
+    const TA* sCS = reinterpret_cast<const TA*>(gbase + GL::OFF_CS);
+    const TA* sCW = reinterpret_cast<const TA*>(gbase + GL::OFF_CW);
+    const float* sS = reinterpret_cast<const float*>(gbase + GL::OFF_S);
+
+    uint32_t k = 0;
+    bool failed = false;
+    for (int tile = worker; tile < num_tiles; tile += nworkers, ++k) {
+        const int b = tile / p.Hv, h = tile - (tile / p.Hv) * p.Hv, kh = h / rep;
+        const float cur_a = na, cur_b = nb;
+        load_gates(tile + nworkers);
+        if (tid < T) {
+            sgate[tid] = Act<TA>::round(sigmoid_f(cur_b));
+            sgate[TMAX + tid] = expf(-expf(p.A_log[h]) * softplus_f(cur_a + p.dt_bias[h]));
+        }
+
+        const bool ok = mbar_wait_bounded(bar, k & 1u, GDN_DEVERR_TMA_TIMEOUT);
+        if (group_any(!ok, bar_id)) {
+            failed = true;
+            break;
+        }
+
+        // ---- consume the stage: state to registers, conv windows, conv of every token, z ----
+        float4 S[RPT];  // rows rg*RPT .. +RPT-1, columns cg*4 .. cg*4+3
+#pragma unroll
+        for (int r = 0; r < RPT; ++r)
+            S[r] = has_S ? *reinterpret_cast<const float4*>(sS + (rg * RPT + r) * D + cg * 4)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+
+        const bool own_qk = (h % rep) == 0;
+        const int cbeg = own_qk ? 0 : 2 * D;
+        {
+            // conv windows (raw inputs, bit-exact copies): final state + checkpoints
+            const int nwin = (p.cs_out ? 1 : 0) + (p.cs_ckpt ? ck.n : 0);
+            for (int w = 0; w < nwin; ++w) {
+                const bool fin = p.cs_out && w == 0;
+                const int ci_idx = p.cs_out ? w - 1 : w;
+                const int off = fin ? T : ck.off[ci_idx];
+                TA* dst = fin ? static_cast<TA*>(p.cs_out) + (size_t)b * conv_dim * LC
+                              : static_cast<TA*>(p.cs_ckpt) + ((size_t)ck.slot[ci_idx] * p.B + b) * conv_dim * LC;
+                for (int c = cbeg + tid; c < 3 * D; c += GT) {
+                    const int g = c / D, ci = c % D;
+                    const int gc = (g == 0 ? kh * D : (g == 1 ? p.Hk * D + kh * D : 2 * p.Hk * D + h * D)) + ci;
+                    const TA* mg = sMQ + g * (GL::M_BYTES / (int)sizeof(TA));
+#pragma unroll
+                    for (int i = 0; i < LC; ++i) {
+                        const int pos = off - LC + i;
+                        TA val;
+                        if (pos >= 0) val = mg[pos * D + ci];
+                        else if (has_cs) val = sCS[(g * D + ci) * LC + (LC + pos)];
+                        else val = TA(0.0f);
+                        dst[(size_t)gc * LC + i] = val;
+                    }
+                }
+            }
+        }
+        // conv + SiLU of every token, sliding a 4-tap window along the sequence;
+        // indices past the conv channels copy z (balances the two phases)
+        for (int c = tid; c < 3 * D + D; c += GT) {
+            if (c >= 3 * D) {
+                const int j = c - 3 * D;
+                for (int t = 0; t < T; ++t) zbuf[t * D + j] = Act<TA>::ld(sZ + t * D + j);
+                continue;
+            }
+            const int g = c / D, ci = c % D;
+            const TA* mg = sMQ + g * (GL::M_BYTES / (int)sizeof(TA));
+            float w[KC], win[KC];
+#pragma unroll
+            for (int j = 0; j < KC; ++j) w[j] = Act<TA>::ld(sCW + (g * D + ci) * KC + j);
+            win[0] = 0.f;
+#pragma unroll
+            for (int j = 1; j < KC; ++j) win[j] = has_cs ? Act<TA>::ld(sCS + (g * D + ci) * LC + (LC - j)) : 0.f;
+            for (int t = 0; t < T; ++t) {
+                win[0] = Act<TA>::ld(mg + t * D + ci);
+                cbuf[t * 3 * D + c] = Act<TA>::round(silu_f(conv_taps<TA>(win, w, KC, has_cs ? LC : t)));
+#pragma unroll
+                for (int j = KC - 1; j > 0; --j) win[j] = win[j - 1];
+            }
+        }
+        group_sync(bar_id);  // stage consumed: refill it with this group's next tile
+        if (tid == 0 && tile + nworkers < num_tiles) {
+            fence_proxy_async_smem();
+            issue(tile + nworkers);
+        }
+
+        int ck_i = 0;
+        for (int t = 0; t < T; ++t) {
+            const float* cq = cbuf + t * 3 * D;
+            const float* ckk = cq + D;
+            const float* cv = cq + 2 * D;
+            // norms (every warp computes them; no barrier)
+            float aq = 0.f, ak = 0.f, aqk = 0.f;
+#pragma unroll
+            for (int i = lane; i < D; i += 32) {
+                const float q = cq[i], kk = ckk[i];
+                aq = fmaf(q, q, aq);
+                ak = fmaf(kk, kk, ak);
+                aqk = fmaf(q, kk, aqk);
+            }
+            aq = warp_sum(aq);
+            ak = warp_sum(ak);
+            aqk = warp_sum(aqk);
+            const float rq = rsqrtf(aq + 1e-6f), rk = rsqrtf(ak + 1e-6f);
+            const float qk = aqk * rq * p.q_scale * rk;
+            const float beta = sgate[t], alpha = sgate[TMAX + t];
+
+            float kr[RPT], qr[RPT];
+#pragma unroll
+            for (int r4 = 0; r4 < RPT; r4 += 4) {
+                const float4 k4 = *reinterpret_cast<const float4*>(ckk + rg * RPT + r4);
+                const float4 q4 = *reinterpret_cast<const float4*>(cq + rg * RPT + r4);
+                kr[r4] = k4.x * rk; kr[r4 + 1] = k4.y * rk; kr[r4 + 2] = k4.z * rk; kr[r4 + 3] = k4.w * rk;
+                qr[r4] = (q4.x * rq) * p.q_scale; qr[r4 + 1] = (q4.y * rq) * p.q_scale;
+                qr[r4 + 2] = (q4.z * rq) * p.q_scale; qr[r4 + 3] = (q4.w * rq) * p.q_scale;
+            }
+            float4 pk = make_float4(0.f, 0.f, 0.f, 0.f), pq = pk;
+#pragma unroll
+            for (int r = 0; r < RPT; ++r) {
+                const float kv = kr[r], qv = qr[r];
+                pk.x = fmaf(kv, S[r].x, pk.x); pk.y = fmaf(kv, S[r].y, pk.y);
+                pk.z = fmaf(kv, S[r].z, pk.z); pk.w = fmaf(kv, S[r].w, pk.w);
+                pq.x = fmaf(qv, S[r].x, pq.x); pq.y = fmaf(qv, S[r].y, pq.y);
+                pq.z = fmaf(qv, S[r].z, pq.z); pq.w = fmaf(qv, S[r].w, pq.w);
+            }
+            reinterpret_cast<float4*>(red + rg * D)[cg] = pk;
+            reinterpret_cast<float4*>(red + (RG + rg) * D)[cg] = pq;
+            group_sync(bar_id);
+            // threads [0, D) reduce k.S into u; threads [D, 2D) reduce q.S into alpha q.S
+            for (int jj = tid; jj < 2 * D; jj += GT) {
+                const int j = jj % D, half = jj / D;
+                float acc = 0.f;
+#pragma unroll
+                for (int g = 0; g < RG; ++g) acc += red[(half * RG + g) * D + j];
+                if (half == 0) su[j] = beta * (cv[j] - alpha * acc);
+                else so[j] = alpha * acc;
+            }
+            group_sync(bar_id);
+
+            {
+                const float4 u4 = reinterpret_cast<const float4*>(su)[cg];
+#pragma unroll
+                for (int r = 0; r < RPT; ++r) {
+                    const float kv = kr[r];
+                    S[r].x = fmaf(kv, u4.x, alpha * S[r].x);
+                    S[r].y = fmaf(kv, u4.y, alpha * S[r].y);
+                    S[r].z = fmaf(kv, u4.z, alpha * S[r].z);
+                    S[r].w = fmaf(kv, u4.w, alpha * S[r].w);
+                }
+            }
+            while (ck_i < ck.n && ck.off[ck_i] == t + 1) {
+                if (p.S_ckpt) {
+                    float4* dst = reinterpret_cast<float4*>(p.S_ckpt + ((size_t)ck.slot[ck_i] * p.B * p.Hv + tile) *
+                                                                           (size_t)(D * D));
+#pragma unroll
+                    for (int r = 0; r < RPT; ++r) __stcs(dst + (rg * RPT + r) * CG + cg, S[r]);
+                }
+                ++ck_i;
+            }
+
+            // gated RMSNorm of token t (sum of squares recomputed by every warp);
+            // o = alpha q.S + (q.k) u
+            float ss = 0.f;
+#pragma unroll
+            for (int j = lane; j < D; j += 32) {
+                const float o = Act<TA>::round(fmaf(qk, su[j], so[j]));
+                ss = fmaf(o, o, ss);
+            }
+            ss = warp_sum(ss);
+            const float rstd = rsqrtf(ss / (float)D + p.eps);
+            const TA* normw = static_cast<const TA*>(p.normw);
+            TA* out = static_cast<TA*>(p.out) + ((size_t)b * T + t) * (size_t)(p.Hv * D) + h * D;
+            for (int j = tid; j < D; j += GT) {
+                const float o = Act<TA>::round(fmaf(qk, su[j], so[j]));
+                const float y = Act<TA>::round(Act<TA>::ldg(normw + j) * Act<TA>::round(o * rstd));
+                Act<TA>::st(out + j, y * silu_f(zbuf[t * D + j]));
+            }
+            group_sync(bar_id);  // su / so / red are rewritten by the next token or tile
+        }
+
+        if (p.S_out) {
+            float4* dst = reinterpret_cast<float4*>(p.S_out + (size_t)tile * D * D);
+#pragma unroll
+            for (int r = 0; r < RPT; ++r) __stcs(dst + (rg * RPT + r) * CG + cg, S[r]);
+        }
+    }
+
+    if (failed && tid == 0) {
+        // the copy this group waited for may still land: wait for it (bounded) before exiting
+        mbar_wait_bounded(bar, k & 1u, GDN_DEVERR_TMA_TIMEOUT);
+    }
+}
+
+template <int D, int TMAX, typename TA>
+cudaError_t launch_one(const MixParams& p, const CkptList& ck, cudaStream_t s) {
+    constexpr int bytes = NG * GroupLayout<D, TMAX, TA>::BYTES;
+    static_assert(bytes <= 232448, "shared memory budget");
+    static bool attr_set[64] = {false};
+    static int sm_count[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        e = cudaFuncSetAttribute(decode_tma_kernel<D, TMAX, TA>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e != cudaSuccess) return e;
+        e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    const int tiles = p.B * p.Hv;
+    int grid = (tiles + NG - 1) / NG;
+    if (grid > sm_count[dev]) grid = sm_count[dev];
+    decode_tma_kernel<D, TMAX, TA><<<grid, NT, bytes, s>>>(p, ck, tiles);
+    return cudaGetLastError();
+}
+
+template <typename TA>
+bool aligned_for_bulk(const MixParams& p, int d) {
+    const long long es = sizeof(TA);
+    auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    const long long conv_dim = 2LL * p.Hk * d + (long long)p.Hv * d;
+    if (!al(p.mixed) || !al(p.z) || !al(p.convw) || (p.S_in && !al(p.S_in))) return false;
+    if ((p.ms_b * es) % 16 || (p.ms_t * es) % 16 || (p.zs_b * es) % 16 || (p.zs_t * es) % 16) return false;
+    if ((d * es) % 16 || (d * KC * es) % 16) return false;
+    if (p.cs_in && (!al(p.cs_in) || (conv_dim * LC * es) % 16 || (d * LC * es) % 16)) return false;
+    return true;
+}
+
+template <typename TA>
+cudaError_t dispatch(const MixParams& p, const CkptList& ck, int d, cudaStream_t s, bool* ok) {
+    constexpr bool bf = sizeof(TA) == 2;
+    // bf16 takes any T <= 8; fp32 only the single-token step (its 8-token stages do not fit twice)
+    *ok = aligned_for_bulk<TA>(p, d) && p.K == KC && (p.T == 1 || (bf && p.T <= 8)) && (d == 128 || d == 64);
+    if (!*ok) return cudaSuccess;
+    if (p.T == 1) return d == 128 ? launch_one<128, 1, TA>(p, ck, s) : launch_one<64, 1, TA>(p, ck, s);
+    if constexpr (bf) return d == 128 ? launch_one<128, 8, TA>(p, ck, s) : launch_one<64, 8, TA>(p, ck, s);
+    *ok = false;
+    return cudaSuccess;
+}
+
+}  // namespace dtma
+
+cudaError_t launch_decode_tma(const MixParams& p, const CkptList& ck, int d, int dtype, cudaStream_t s,
+                              bool* supported) {
+    if (dtype == GDN_DTYPE_BF16) return dtma::dispatch<__nv_bfloat16>(p, ck, d, s, supported);
+    return dtma::dispatch<float>(p, ck, d, s, supported);
+}
+
+unsigned int decode_tma_device_error(bool clear) {
+    unsigned int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+    if (clear && v) {
+        const unsigned int zero = 0;
+        cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+    }
+    return v;
+}
+
+}  // namespace gdn
