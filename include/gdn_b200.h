@@ -154,6 +154,15 @@ int32_t gdn_mixer_decode(const gdn_mixer_args* args, void* stream);
 int32_t gdn_device_error(uint32_t* flags_out, int32_t clear);
 
 /*
+ * Tensor-core self-test: D[128][N] = A * B with the 5th-generation tensor
+ * core (tf32 in, fp32 out) for operand-layout combination `mode` (0..3, see
+ * gdn_umma_selftest.cu), in plain row-major fp32 device buffers.  Checks the
+ * shared-memory layouts and descriptors the chunked kernel relies on.  No
+ * counterpart in the reference.
+ */
+int32_t gdn_selftest_umma(int32_t mode, const float* A, const float* B, float* D, void* stream);
+
+/*
  * Chunked token mixer for any seq_len >= 1 (prefill).  Replaces
  * deltanet.py:479-561 on the _chunk_gated_delta_rule branch
  * (deltanet.py:266-407): the WY/UT intra-chunk solve and the sequential

@@ -223,3 +223,23 @@ def test_chunked_equals_token_by_token_at_scale():
     assert_bf16_close(torch.cat(outs, 1), out_chunk, "chunk vs decode out")
     assert_state_close(S, S_chunk, "chunk vs decode state")
     assert torch.equal(cs, cs_chunk)
+
+
+def test_mixer_plan_matches_mixer():
+    """The prepared-call API launches the same kernel with pre-bound weights."""
+    shape = W.SHAPE_QWEN
+    m, _ = make_layer(shape, "bf16")
+    d = mixer_inputs(shape, 16, 1, "bf16", seed=12, with_state=True)
+    dev = torch.device("cuda")
+    t = lambda a: torch.from_numpy(a).to(dev).to(torch.bfloat16)  # noqa: E731
+    args = (t(d["mixed"]), t(d["z"]), t(d["b"]), t(d["a"]))
+    S1 = torch.from_numpy(d["rec_state"]).to(dev)
+    S2 = S1.clone()
+    cs1, cs2 = torch.empty(16, shape.conv_dim, 3, dtype=torch.bfloat16, device=dev), \
+        torch.empty(16, shape.conv_dim, 3, dtype=torch.bfloat16, device=dev)
+    o1 = m.mixer(*args, conv_state=t(d["conv_state"]), rec_state=S1, conv_state_out=cs1, rec_state_out=S1)
+    plan = m.mixer_plan(16, 1, torch.bfloat16, dev)
+    o2 = torch.empty_like(o1)
+    plan(*args, t(d["conv_state"]), S2, cs2, S2, o2)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2) and torch.equal(S1, S2) and torch.equal(cs1, cs2)

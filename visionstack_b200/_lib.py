@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "gdn_delta_rule",
     "gdn_causal_conv1d",
     "gdn_device_error",
+    "gdn_selftest_umma",
 )
 GDN_FLAG_REGISTER_KERNEL = 1
 
@@ -101,6 +102,8 @@ def load() -> ctypes.CDLL:
         lib.gdn_causal_conv1d.restype = _i32
         lib.gdn_causal_conv1d.argtypes = [_i32, _i32, _i32, _i32, _i32, _c_void_p, _c_void_p, _c_void_p,
                                           _c_void_p, _c_void_p, _i32, _c_void_p]
+        lib.gdn_selftest_umma.restype = _i32
+        lib.gdn_selftest_umma.argtypes = [_i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p]
         lib.gdn_device_error.restype = _i32
         lib.gdn_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32), _i32]
         _lib = lib

@@ -174,10 +174,21 @@ int32_t gdn_mixer_decode(const gdn_mixer_args* args, void* stream) {
 
 int32_t gdn_device_error(uint32_t* flags_out, int32_t clear) {
     if (!flags_out) return fail(GDN_ERR_INVALID_ARG, "flags_out is NULL");
-    const unsigned int v = gdn::decode_tma_device_error(clear != 0);
-    if (v == 0xFFFFFFFFu) return fail(GDN_ERR_CUDA, "could not read the device error word");
-    *flags_out = v;
+    const unsigned int a = gdn::decode_tma_device_error(clear != 0);
+    const unsigned int b = gdn::umma_device_error(clear != 0);
+    if (a == 0xFFFFFFFFu || b == 0xFFFFFFFFu) return fail(GDN_ERR_CUDA, "could not read the device error word");
+    *flags_out = a | b;
     return ok();
+}
+
+int32_t gdn_selftest_umma(int32_t mode, const float* A, const float* B, float* D, void* stream) {
+    if (mode < 0 || mode > 3) return fail(GDN_ERR_INVALID_ARG, "mode %d not in 0..3", mode);
+    if (!A || !B || !D) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
+    const void* ptrs[] = {A, B, D};
+    for (const void* ptr : ptrs)
+        if (!aligned_elem(ptr, GDN_DTYPE_F32)) return fail(GDN_ERR_ALIGNMENT, "misaligned pointer");
+    return cuda_status(gdn::launch_umma_selftest(mode, A, B, D, static_cast<cudaStream_t>(stream)),
+                       "gdn_selftest_umma launch");
 }
 
 int32_t gdn_mixer_prefill(const gdn_mixer_args* args, void* stream) {

@@ -1,0 +1,154 @@
+// 5th-generation tensor core (tcgen05 / UMMA) helpers for sm_100a: tensor
+// memory allocation, shared-memory matrix descriptors for 128-byte swizzled
+// canonical layouts, the tf32 MMA, commit, and tensor-memory loads / stores.
+//
+// Operand layouts (fp32 / tf32 elements, 128-byte swizzle):
+//  * K-major  [rows][k]  : the k axis is cut into 32-element (128-byte) atoms;
+//    atom a holds every row's 128 bytes: byte(row, k) =
+//      (k/32)*rows*128 + (row/8)*1024 + (row%8)*128 + ((k%32/4) ^ (row%8))*16 + (k%4)*4
+//    descriptor: SBO = 1024 (8-row groups), LBO unused; one MMA k-step of 8
+//    elements (32 bytes) advances the start address by 32 bytes inside an atom.
+//    (canonical SWIZZLE_128B layout, 16-byte swizzle unit over 8-row groups)
+//  * MN-major [k][mn]    : 32-bit operands use the SWIZZLE_128B_BASE32B layout
+//    (the only MN-major layout the tf32 MMA accepts): the mn axis is cut into
+//    32-element atoms, each atom holds every k row's 128 bytes, and the 32-byte
+//    chunks of a row are swizzled over 4-row groups: byte(k, mn) =
+//      (mn/32)*krows*128 + (k/4)*512 + (k%4)*128 + ((mn%32/8) ^ (k%4))*32 + (mn%8)*4
+//    descriptor: LBO = krows*128 (next mn atom), SBO = 512 (next 4 k rows);
+//    one MMA k-step of 8 rows advances the start address by 1024 bytes.
+// Descriptor version 1, base offset 0: every operand region starts 1024-byte
+// aligned.
+#pragma once
+
+#include <stdint.h>
+
+#include "gdn_async.cuh"
+
+namespace gdn {
+namespace umma {
+
+__host__ __device__ constexpr uint32_t kmajor_off(int row, int k, int rows) {
+    return (uint32_t)((k >> 5) * rows * 128 + (row >> 3) * 1024 + (row & 7) * 128 +
+                      ((((k & 31) >> 2) ^ (row & 7)) << 4) + (k & 3) * 4);
+}
+
+__host__ __device__ constexpr uint32_t mnmajor_off(int k, int mn, int krows) {
+    return (uint32_t)((mn >> 5) * krows * 128 + (k >> 2) * 512 + (k & 3) * 128 +
+                      ((((mn & 31) >> 3) ^ (k & 3)) << 5) + (mn & 7) * 4);
+}
+
+constexpr uint32_t LAYOUT_SW128 = 2;         // K-major operands
+constexpr uint32_t LAYOUT_SW128_BASE32 = 1;  // MN-major 32-bit operands
+
+// Shared-memory matrix descriptor, version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1u << 46;  // descriptor version (sm_100)
+    d |= (uint64_t)(layout & 7u) << 61;
+    return d;
+}
+
+// Descriptor of k-step kk (8 tf32 elements) of a K-major operand with `rows` rows.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t base, int rows, int kk) {
+    return smem_desc(base + (uint32_t)((kk >> 2) * rows * 128 + (kk & 3) * 32), 16, 1024, LAYOUT_SW128);
+}
+
+// Descriptor of k-step kk (8 k rows) of an MN-major operand with `krows` k rows.
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t base, int krows, int kk) {
+    return smem_desc(base + (uint32_t)(kk * 1024), (uint32_t)(krows * 128), 512, LAYOUT_SW128_BASE32);
+}
+
+// Instruction descriptor of kind::tf32 with fp32 accumulation.
+// a_mn / b_mn: operand is MN-major (1) or K-major (0).
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, int a_mn, int b_mn) {
+    return (1u << 4)             // D format f32
+           | (2u << 7)           // A format tf32
+           | (2u << 10)          // B format tf32
+           | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
+}
+
+// ---- tensor memory ----
+// Allocation / deallocation are warp-wide (.sync.aligned): call from one full warp.
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void fence_before_sync() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc], issued by one thread.
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+
+// Arrive once on the mbarrier when every MMA issued so far by this thread completes.
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's lane (32x32b shape, warp-wide).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// TMEM address of (lane, column): lane in bits 31..16, column in 15..0.
+__device__ __forceinline__ uint32_t tmem_addr(uint32_t base, int lane, int col) {
+    return base + ((uint32_t)lane << 16) + (uint32_t)col;
+}
+
+}  // namespace umma
+}  // namespace gdn

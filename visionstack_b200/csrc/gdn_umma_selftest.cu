@@ -1,0 +1,124 @@
+// Tensor-core self-test: one CTA computes D[128][N] = A * B with kind::tf32
+// UMMA for each operand-layout combination the chunked prefill uses, so the
+// shared-memory layouts, descriptors and tensor-memory handling of
+// gdn_umma.cuh are checked against a host matmul before any model kernel
+// relies on them.
+//   mode 0: A K-major [128][128], B K-major [64][128]   (D = A B^T, N = 64)
+//   mode 1: A K-major [128][128], B MN-major [128][128] (D = A B, K = 128)
+//   mode 2: A K-major [128][64],  B MN-major [64][128]  (D = A B, K = 64)
+//   mode 3: A MN-major [64][128] (stored k-major rows of A^T), B MN-major [64][128]
+// Inputs are plain row-major fp32 in global memory: A is [M][K] for modes
+// 0-2 and [K][M] for mode 3; B is [N][K] for mode 0 and [K][N] otherwise.
+#include "gdn_kernels.cuh"
+#include "gdn_umma.cuh"
+
+namespace gdn {
+
+namespace {
+
+struct SelfTestShape {
+    int K, N, a_mn, b_mn;
+};
+
+__host__ __device__ inline SelfTestShape selftest_shape(int mode) {
+    switch (mode) {
+        case 0: return {128, 64, 0, 0};
+        case 1: return {128, 128, 0, 1};
+        case 2: return {64, 128, 0, 1};
+        default: return {64, 128, 1, 1};
+    }
+}
+
+__global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const float* __restrict__ A,
+                                                               const float* __restrict__ B, float* __restrict__ D) {
+    extern __shared__ unsigned char raw[];
+    const SelfTestShape sh = selftest_shape(mode);
+    const int M = 128, K = sh.K, N = sh.N;
+    const uint32_t raw_addr = smem_u32(raw);
+    const uint32_t pad = ((raw_addr + 1023u) & ~1023u) - raw_addr;
+    unsigned char* base = raw + pad;
+    unsigned char* sA = base;                // M*K*4 bytes
+    unsigned char* sB = base + 128 * 128 * 4;  // N*K*4 bytes
+    uint64_t* bar = reinterpret_cast<uint64_t*>(base + 2 * 128 * 128 * 4);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(base + 2 * 128 * 128 * 4 + 8);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    for (int i = tid; i < M * K; i += 128) {
+        if (!sh.a_mn) {
+            const int m = i / K, k = i % K;
+            *reinterpret_cast<float*>(sA + umma::kmajor_off(m, k, M)) = A[i];
+        } else {
+            const int k = i / M, m = i % M;
+            *reinterpret_cast<float*>(sA + umma::mnmajor_off(k, m, K)) = A[i];
+        }
+    }
+    for (int i = tid; i < N * K; i += 128) {
+        if (!sh.b_mn) {
+            const int n = i / K, k = i % K;
+            *reinterpret_cast<float*>(sB + umma::kmajor_off(n, k, N)) = B[i];
+        } else {
+            const int k = i / N, n = i % N;
+            *reinterpret_cast<float*>(sB + umma::mnmajor_off(k, n, K)) = B[i];
+        }
+    }
+    fence_proxy_async_smem();
+    if (tid == 0) {
+        mbar_init(smem_u32(bar), 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        umma::tmem_alloc(smem_u32(tslot), 128);
+        umma::tmem_relinquish();
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tbase = *tslot;
+
+    if (tid == 0) {
+        const uint32_t idesc = umma::idesc_tf32(M, N, sh.a_mn, sh.b_mn);
+        for (int kk = 0; kk < K / 8; ++kk) {
+            const uint64_t da = sh.a_mn ? umma::desc_mnmajor(smem_u32(sA), K, kk) : umma::desc_kmajor(smem_u32(sA), M, kk);
+            const uint64_t db = sh.b_mn ? umma::desc_mnmajor(smem_u32(sB), K, kk) : umma::desc_kmajor(smem_u32(sB), N, kk);
+            umma::mma_tf32(tbase, da, db, idesc, kk > 0 ? 1u : 0u);
+        }
+        umma::mma_commit(smem_u32(bar));
+    }
+    const bool ok = mbar_wait_bounded(smem_u32(bar), 0, GDN_DEVERR_MMA_TIMEOUT);
+    umma::fence_after_sync();
+    if (ok) {
+        for (int c0 = 0; c0 < N; c0 += 32) {
+            float v[32];
+            umma::tmem_ld32(umma::tmem_addr(tbase, warp * 32, c0), v);
+            umma::tmem_wait_ld();
+            const int row = warp * 32 + lane;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) D[row * N + c0 + j] = v[j];
+        }
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) umma::tmem_dealloc(tbase, 128);
+}
+
+}  // namespace
+
+cudaError_t launch_umma_selftest(int mode, const float* A, const float* B, float* D, cudaStream_t s) {
+    const int bytes = 2 * 128 * 128 * 4 + 64 + 1024;
+    cudaError_t e = cudaFuncSetAttribute(umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+    umma_selftest_kernel<<<1, 128, bytes, s>>>(mode, A, B, D);
+    return cudaGetLastError();
+}
+
+unsigned int umma_device_error(bool clear) {
+    unsigned int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+    if (clear && v) {
+        const unsigned int zero = 0;
+        cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+    }
+    return v;
+}
+
+}  // namespace gdn

@@ -300,6 +300,15 @@ class Qwen3_5GatedDeltaNet(nn.Module):
                        fn(ctypes.byref(args), _stream(dev)))
         return out
 
+    def mixer_plan(self, batch: int, seq_len: int, dtype: torch.dtype, device,
+                   token_by_token: bool = True) -> "MixerPlan":
+        """Pre-bind this layer's weights and shapes for repeated ``mixer``
+        calls (a serving decode loop): each call then only sets pointers."""
+        device = torch.device(device)
+        if device.type == "cuda" and device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        return MixerPlan(self, batch, seq_len, dtype, device, token_by_token)
+
     # -- forward -----------------------------------------------------------
     def forward(self, hidden_states: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
                 cache: Optional[Qwen3_5HybridCache] = None) -> torch.Tensor:
@@ -353,7 +362,68 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         return _linear(self.out_proj, core)
 
 
+class MixerPlan:
+    """Repeated token-mixer calls with pre-bound weights and shapes.
+
+    Built by ``Qwen3_5GatedDeltaNet.mixer_plan``.  ``__call__`` takes the
+    per-step device tensors (projection outputs, states, output) and launches
+    the same kernel as ``Qwen3_5GatedDeltaNet.mixer`` with no per-call tensor
+    conversions; the C ABI still validates every call.  The layer's
+    parameters must not be replaced while the plan is in use.
+    """
+
+    def __init__(self, layer: Qwen3_5GatedDeltaNet, batch: int, seq_len: int, dtype: torch.dtype,
+                 device: torch.device, token_by_token: bool):
+        conv_w = layer.conv1d.weight
+        if conv_w.dtype in _FP8_DTYPES:
+            conv_w = conv_w.to(dtype)
+        self._conv_w = conv_w.detach().reshape(layer.conv_dim, layer.conv_kernel_size).contiguous()
+        self._A_log = layer.A_log.detach().float().contiguous()
+        self._dt_bias = layer.dt_bias.detach().float().contiguous()
+        self._normw = layer.norm.weight.detach().contiguous()
+        for t in (self._conv_w, self._A_log, self._dt_bias, self._normw):
+            if t.device != device:
+                raise RuntimeError("layer parameters must live on the plan's device")
+        if self._conv_w.dtype != dtype or self._normw.dtype != dtype:
+            raise TypeError(f"conv/norm weights must be in the activation dtype {dtype}")
+        a = _lib.MixerArgs()
+        a.batch, a.seq_len = batch, seq_len
+        a.num_k_heads, a.num_v_heads = layer.num_k_heads, layer.num_v_heads
+        a.head_k_dim, a.head_v_dim = layer.head_k_dim, layer.head_v_dim
+        a.conv_kernel = layer.conv_kernel_size
+        a.act_dtype = _dtype_code(dtype)
+        a.norm_eps = float(layer.layer_norm_epsilon)
+        a.conv_weight, a.A_log = self._conv_w.data_ptr(), self._A_log.data_ptr()
+        a.dt_bias, a.norm_weight = self._dt_bias.data_ptr(), self._normw.data_ptr()
+        self._args = a
+        self._ref = ctypes.byref(a)
+        self._lib = _lib.load()
+        self._fn = self._lib.gdn_mixer_decode if token_by_token else self._lib.gdn_mixer_prefill
+        self._name = "gdn_mixer_decode" if token_by_token else "gdn_mixer_prefill"
+        self.device = device
+
+    def __call__(self, mixed_qkv: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: torch.Tensor,
+                 conv_state: Optional[torch.Tensor], rec_state: Optional[torch.Tensor],
+                 conv_state_out: Optional[torch.Tensor], rec_state_out: Optional[torch.Tensor],
+                 out: torch.Tensor, stream: Optional[int] = None) -> torch.Tensor:
+        g = self._args
+        g.mixed_qkv, g.mixed_stride_b, g.mixed_stride_t = mixed_qkv.data_ptr(), mixed_qkv.stride(0), \
+            mixed_qkv.stride(1)
+        g.z, g.z_stride_b, g.z_stride_t = z.data_ptr(), z.stride(0), z.stride(1)
+        g.a, g.b, g.ab_stride_b, g.ab_stride_t = a.data_ptr(), b.data_ptr(), a.stride(0), a.stride(1)
+        g.conv_state_in = None if conv_state is None else conv_state.data_ptr()
+        g.conv_state_out = None if conv_state_out is None else conv_state_out.data_ptr()
+        g.state_in = None if rec_state is None else rec_state.data_ptr()
+        g.state_out = None if rec_state_out is None else rec_state_out.data_ptr()
+        g.out = out.data_ptr()
+        st = self._fn(self._ref, torch.cuda.current_stream(self.device).cuda_stream if stream is None else stream)
+        if st:
+            _lib.check(self._name, st)
+        return out
+
+
 __all__ = [
+    "MixerPlan",
     "_extract_conv_state_at_offset",
     "_causal_conv1d_fn",
     "_recurrent_gated_delta_rule",
