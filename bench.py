@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-prefill", action="store_true", help="skip the secondary prefill measurement")
+    ap.add_argument("--no-decode", action="store_true", help="only the prefill measurement (for profiling)")
+    ap.add_argument("--prefill-batch", type=int, default=8)
+    ap.add_argument("--prefill-seq", type=int, default=8192)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-s", type=float, default=12.0, help="seconds of CPU work for the CPU baseline")
     return ap.parse_args()
@@ -272,6 +275,17 @@ def run_ours(args, rank: int, world: int) -> None:
     torch.cuda.set_device(dev)
     lib = _lib.load()
     m, local = build_shard_layer(torch, rank, world, dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    if args.no_decode:
+        pf = run_prefill(torch, dist, m, local, dev, world, barrier, args.prefill_batch, args.prefill_seq)
+        if rank == 0:
+            print(json.dumps({"prefill": pf}), flush=True)
+        return
     B = 64
     hv, hk, d = local.num_v_heads, local.num_k_heads, local.head_k_dim
     conv_dim, vdim = local.conv_dim, local.value_dim
@@ -310,11 +324,6 @@ def run_ours(args, rank: int, world: int) -> None:
     torch.cuda.synchronize(dev)
     graph.replay()  # one untimed replay: graph upload / first-launch costs
     torch.cuda.synchronize(dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
 
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(dev.index)
@@ -406,7 +415,7 @@ def run_ours(args, rank: int, world: int) -> None:
     # secondary: chunked prefill (batch 8 x 8192 tokens, all heads of the shard)
     prefill = None
     if not args.no_prefill:
-        prefill = run_prefill(torch, dist, m, local, dev, world, barrier)
+        prefill = run_prefill(torch, dist, m, local, dev, world, barrier, args.prefill_batch, args.prefill_seq)
 
     if rank != 0:
         return
@@ -437,8 +446,7 @@ def run_ours(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-def run_prefill(torch, dist, m, local, dev, world, barrier):
-    B, T = 8, 8192
+def run_prefill(torch, dist, m, local, dev, world, barrier, B=8, T=8192):
     hv, hk, d = local.num_v_heads, local.num_k_heads, local.head_k_dim
     g = torch.Generator(device=dev)
     g.manual_seed(3)
@@ -471,12 +479,12 @@ def run_prefill(torch, dist, m, local, dev, world, barrier):
     _, tflops, src = measured_peaks()
     fl = prefill_flops(B, T, hv, d)
     ach = fl / (ms * 1e-3) / 1e12
-    return {"workload": "chunked prefill: B8 x T8192, 16 k-heads / 32 v-heads (sharded), d128, bf16",
+    return {"workload": f"chunked prefill: B{B} x T{T}, 16 k-heads / 32 v-heads (sharded), d128, bf16",
             "tokens_per_s": B * T / (ms * 1e-3), "ms_per_launch": ms,
             "roofline": {"bound": "tensor", "achieved": ach, "peak": tflops, "unit": "TFLOP/s",
                          "frac": ach / tflops, "peak_source": src, "flops_per_launch": fl,
                          "min_bytes_per_launch": prefill_min_bytes(B, T, hk, hv, d),
-                         "kernel": "gdn::prefill_kernel<128,bf16,mixer> (CUDA-core fp32)"}}
+                         "kernel": "gdn::ptc::prefill_tc_kernel (tcgen05 tf32, 1 CTA per (batch, head))"}}
 
 
 def main():

@@ -50,8 +50,11 @@ extern "C" {
 #define GDN_DTYPE_BF16 1
 
 /* gdn_mixer_args.flags: run the register-tile token-by-token kernel even
- * where the bulk-copy pipelined one applies (both are exact; for testing). */
+ * where the bulk-copy pipelined one applies, and the CUDA-core chunked kernel
+ * even where the tensor-core one applies (same results up to float rounding;
+ * for testing and comparison). */
 #define GDN_FLAG_REGISTER_KERNEL 1
+#define GDN_FLAG_CUDA_CORE_PREFILL 2
 
 /* Bits of the device error word (gdn_device_error). */
 #define GDN_DEVERR_TMA_TIMEOUT 0x1u
@@ -167,7 +170,9 @@ int32_t gdn_selftest_umma(int32_t mode, const float* A, const float* B, float* D
  * deltanet.py:479-561 on the _chunk_gated_delta_rule branch
  * (deltanet.py:266-407): the WY/UT intra-chunk solve and the sequential
  * inter-chunk state propagation, with conv, norms, gates and the gated RMSNorm
- * fused in.  Needs no workspace.
+ * fused in.  Needs no workspace.  With bf16 activations, head dim 128 and
+ * 16-byte aligned z rows the contractions run on the tensor cores (tcgen05,
+ * tf32 operands, fp32 accumulation); otherwise a CUDA-core fp32 kernel runs.
  */
 int32_t gdn_mixer_prefill(const gdn_mixer_args* args, void* stream);
 

@@ -32,11 +32,13 @@ def rel_max(a, b) -> float:
     return max_abs(a, b) / max(1e-30, float(np.max(np.abs(b))))
 
 
-def assert_bf16_close(ours, ref, what=""):
+def assert_bf16_close(ours, ref, what="", scale=1.0):
+    """``scale`` = 2 compares two implementations that are each within the
+    tolerance of the reference."""
     o, r = to_np(ours).astype(np.float64), to_np(ref).astype(np.float64)
     assert o.shape == r.shape, (what, o.shape, r.shape)
     err = np.abs(o - r)
-    lim = np.maximum(BF16_ABS, np.abs(r) * 2.0 ** -7)
+    lim = scale * np.maximum(BF16_ABS, np.abs(r) * 2.0 ** -7)
     bad = err > lim
     assert not bad.any(), (f"{what}: {int(bad.sum())} elements outside tolerance, worst err "
                            f"{float(err.max()):.3g} (ref {float(r.flat[int(np.argmax(err))]):.3g})")
@@ -47,7 +49,8 @@ def assert_f32_close(ours, ref, tol, what=""):
     assert err <= tol, f"{what}: max abs err {err:.3g} > {tol}"
 
 
-def assert_state_close(ours, ref, what="", tol=STATE_REL):
+def assert_state_close(ours, ref, what="", tol=STATE_REL, scale=1.0):
+    tol = tol * scale
     err = rel_max(ours, ref)
     assert err <= tol, f"{what}: state max rel err {err:.3g} > {tol}"
 

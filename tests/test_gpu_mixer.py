@@ -220,8 +220,9 @@ def test_chunked_equals_token_by_token_at_scale():
                             rec_state=S, conv_state_out=cs_next, rec_state_out=S, token_by_token=True))
         cs = cs_next
     torch.cuda.synchronize()
-    assert_bf16_close(torch.cat(outs, 1), out_chunk, "chunk vs decode out")
-    assert_state_close(S, S_chunk, "chunk vs decode state")
+    # two implementations, each within tolerance of the reference
+    assert_bf16_close(torch.cat(outs, 1), out_chunk, "chunk vs decode out", scale=2.0)
+    assert_state_close(S, S_chunk, "chunk vs decode state", scale=2.0)
     assert torch.equal(cs, cs_chunk)
 
 
@@ -243,3 +244,39 @@ def test_mixer_plan_matches_mixer():
     plan(*args, t(d["conv_state"]), S2, cs2, S2, o2)
     torch.cuda.synchronize()
     assert torch.equal(o1, o2) and torch.equal(S1, S2) and torch.equal(cs1, cs2)
+
+
+@pytest.mark.parametrize("B,T,with_state,offsets", [
+    (2, 200, True, (1, 37, 64, 100, 128, 199, 200)),
+    (1, 64, False, (64,)),
+    (3, 7, True, (3, 7)),
+    (1, 513, False, (256, 500, 513)),
+])
+def test_tensor_core_prefill_vs_oracle(B, T, with_state, offsets):
+    """The tcgen05 chunked kernel (bf16, head dim 128) against the oracle, with
+    sub-chunk and chunk-boundary checkpoints, ragged last chunks and T < 64."""
+    from visionstack_b200 import _lib
+    shape = W.LayerShape(256, 2, 4, 128, 128)
+    m, params = make_layer(shape, "bf16")
+    d = mixer_inputs(shape, B, T, "bf16", seed=40 + T, with_state=with_state)
+    check(shape, "bf16", run_ours(m, shape, d, "bf16", False, offsets),
+          run_oracle(shape, params, d, "bf16", chunk=True, offsets=offsets), offsets, f"tc T{T}")
+    assert _lib.device_error() == 0
+
+
+def test_tensor_core_prefill_matches_cuda_core_kernel():
+    shape = W.SHAPE_QWEN
+    m, _ = make_layer(shape, "bf16")
+    d = mixer_inputs(shape, 2, 300, "bf16", seed=8, with_state=True)
+    dev = torch.device("cuda")
+    t = lambda a: torch.from_numpy(a).to(dev).to(torch.bfloat16)  # noqa: E731
+    S0 = torch.from_numpy(d["rec_state"]).to(dev)
+    outs = []
+    for cc in (False, True):
+        S = torch.empty_like(S0)
+        o = m.mixer(t(d["mixed"]), t(d["z"]), t(d["b"]), t(d["a"]), conv_state=t(d["conv_state"]), rec_state=S0,
+                    rec_state_out=S, token_by_token=False, cuda_core_prefill=cc)
+        outs.append((o, S))
+    torch.cuda.synchronize()
+    assert_bf16_close(outs[0][0], outs[1][0], "tc vs cuda-core out", scale=2.0)
+    assert_state_close(outs[0][1], outs[1][1], "tc vs cuda-core state", scale=2.0)

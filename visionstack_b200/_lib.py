@@ -33,6 +33,7 @@ EXPORTED_SYMBOLS = (
     "gdn_selftest_umma",
 )
 GDN_FLAG_REGISTER_KERNEL = 1
+GDN_FLAG_CUDA_CORE_PREFILL = 2
 
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int32

@@ -83,4 +83,16 @@ __device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, ui
         : "memory");
 }
 
+// Tiled tensor copy global -> shared of one 3-D box of `tmap` at element
+// coordinates (c0, c1, c2), completing its bytes on `bar`.  c0 * element size
+// must be a multiple of 16 bytes; out-of-range rows are filled with zeros.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst_smem, const void* tmap, int c0, int c1, int c2,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(dst_smem),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+        : "memory");
+}
+
 }  // namespace gdn

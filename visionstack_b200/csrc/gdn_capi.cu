@@ -80,7 +80,8 @@ int32_t validate_mixer(const gdn_mixer_args* a, gdn::MixParams* p, gdn::CkptList
     if (a->act_dtype != GDN_DTYPE_F32 && a->act_dtype != GDN_DTYPE_BF16)
         return fail(GDN_ERR_UNSUPPORTED, "act_dtype %d", a->act_dtype);
     if (!(a->norm_eps >= 0.0f)) return fail(GDN_ERR_INVALID_ARG, "norm_eps must be >= 0");
-    if (a->flags & ~GDN_FLAG_REGISTER_KERNEL) return fail(GDN_ERR_INVALID_ARG, "unknown flags 0x%x", a->flags);
+    if (a->flags & ~(GDN_FLAG_REGISTER_KERNEL | GDN_FLAG_CUDA_CORE_PREFILL))
+        return fail(GDN_ERR_INVALID_ARG, "unknown flags 0x%x", a->flags);
     if (!a->mixed_qkv || !a->z || !a->a || !a->b || !a->conv_weight || !a->A_log || !a->dt_bias ||
         !a->norm_weight || !a->out)
         return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
@@ -176,8 +177,10 @@ int32_t gdn_device_error(uint32_t* flags_out, int32_t clear) {
     if (!flags_out) return fail(GDN_ERR_INVALID_ARG, "flags_out is NULL");
     const unsigned int a = gdn::decode_tma_device_error(clear != 0);
     const unsigned int b = gdn::umma_device_error(clear != 0);
-    if (a == 0xFFFFFFFFu || b == 0xFFFFFFFFu) return fail(GDN_ERR_CUDA, "could not read the device error word");
-    *flags_out = a | b;
+    const unsigned int c = gdn::prefill_tc_device_error(clear != 0);
+    if (a == 0xFFFFFFFFu || b == 0xFFFFFFFFu || c == 0xFFFFFFFFu)
+        return fail(GDN_ERR_CUDA, "could not read the device error word");
+    *flags_out = a | b | c;
     return ok();
 }
 
@@ -197,8 +200,13 @@ int32_t gdn_mixer_prefill(const gdn_mixer_args* args, void* stream) {
     int32_t st = validate_mixer(args, &p, &ck);
     if (st != GDN_OK) return st;
     bool supported = false;
-    cudaError_t e = gdn::launch_prefill(p, ck, args->head_k_dim, args->act_dtype, true,
-                                        static_cast<cudaStream_t>(stream), &supported);
+    cudaError_t e = cudaSuccess;
+    if (!(args->flags & GDN_FLAG_CUDA_CORE_PREFILL))
+        e = gdn::launch_prefill_tc(p, ck, args->head_k_dim, args->act_dtype, static_cast<cudaStream_t>(stream),
+                                   &supported);
+    if (!supported)
+        e = gdn::launch_prefill(p, ck, args->head_k_dim, args->act_dtype, true, static_cast<cudaStream_t>(stream),
+                                &supported);
     if (!supported) return fail(GDN_ERR_UNSUPPORTED, "no chunked kernel for these head dims");
     return cuda_status(e, "gdn_mixer_prefill launch");
 }

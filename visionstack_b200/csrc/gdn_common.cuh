@@ -62,4 +62,16 @@ __device__ __forceinline__ float conv_taps(const float* win, const float* w, int
     return acc;
 }
 
+// The same accumulation for the 4-tap conv with the window in registers
+// (x0 = current token, x3 = three tokens back); `valid` as in conv_taps.
+template <typename TA>
+__device__ __forceinline__ float conv4_taps(float x0, float x1, float x2, float x3, float w0, float w1, float w2,
+                                            float w3, int valid) {
+    float acc = Act<TA>::round(x0 * w3);
+    if (valid >= 1) acc = Act<TA>::round(fmaf(x1, w2, acc));
+    if (valid >= 2) acc = Act<TA>::round(fmaf(x2, w1, acc));
+    if (valid >= 3) acc = Act<TA>::round(fmaf(x3, w0, acc));
+    return acc;
+}
+
 }  // namespace gdn

@@ -58,6 +58,9 @@ cudaError_t launch_decode_tma(const MixParams& p, const CkptList& ck, int d, int
 unsigned int decode_tma_device_error(bool clear);
 cudaError_t launch_umma_selftest(int mode, const float* A, const float* B, float* D, cudaStream_t s);
 unsigned int umma_device_error(bool clear);
+cudaError_t launch_prefill_tc(const MixParams& p, const CkptList& ck, int d, int dtype, cudaStream_t s,
+                              bool* supported);
+unsigned int prefill_tc_device_error(bool clear);
 cudaError_t launch_prefill(const MixParams& p, const CkptList& ck, int d, int dtype, bool mixer,
                            cudaStream_t s, bool* supported);
 cudaError_t launch_conv1d(int B, int C, int T, int K, int dtype, const void* x, const void* w,

@@ -37,6 +37,18 @@ __host__ __device__ constexpr uint32_t mnmajor_off(int k, int mn, int krows) {
                       ((((mn & 31) >> 3) ^ (k & 3)) << 5) + (mn & 7) * 4);
 }
 
+// Round an fp32 value to tf32 (10 explicit mantissa bits), nearest with ties
+// away from zero.  The tensor core drops the low 13 bits of fp32 operands, so
+// operands written through this rounding carry half the conversion error.
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+__device__ __forceinline__ float4 tf32_rna4(float4 v) {
+    return make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+}
+
 constexpr uint32_t LAYOUT_SW128 = 2;         // K-major operands
 constexpr uint32_t LAYOUT_SW128_BASE32 = 1;  // MN-major 32-bit operands
 

@@ -231,14 +231,17 @@ class Qwen3_5GatedDeltaNet(nn.Module):
               conv_state_out: Optional[torch.Tensor] = None, rec_state_out: Optional[torch.Tensor] = None,
               out: Optional[torch.Tensor] = None, checkpoint_offsets: Sequence[int] = (),
               state_checkpoints: Optional[torch.Tensor] = None, conv_checkpoints: Optional[torch.Tensor] = None,
-              token_by_token: Optional[bool] = None, register_kernel: bool = False) -> torch.Tensor:
+              token_by_token: Optional[bool] = None, register_kernel: bool = False,
+              cuda_core_prefill: bool = False) -> torch.Tensor:
         """One launch of the fused token mixer on projection outputs
         (deltanet.py:489-561): returns the gated-norm output [B, T, Hv*dv].
 
         ``token_by_token`` picks the decode kernel (T <= 8) or the chunked
         kernel; by default the reference's rule applies (a state and T <= 8).
         ``register_kernel`` forces the register-tile decode kernel instead of
-        the bulk-copy pipelined one (same results; used by the tests).
+        the bulk-copy pipelined one, ``cuda_core_prefill`` the CUDA-core
+        chunked kernel instead of the tensor-core one (same results up to
+        float rounding; used by the tests).
         """
         B, T, _ = mixed_qkv.shape
         dt = mixed_qkv.dtype
@@ -270,7 +273,8 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         args.conv_kernel = self.conv_kernel_size
         args.act_dtype = _dtype_code(dt)
         args.norm_eps = float(self.layer_norm_epsilon)
-        args.flags = _lib.GDN_FLAG_REGISTER_KERNEL if register_kernel else 0
+        args.flags = (_lib.GDN_FLAG_REGISTER_KERNEL if register_kernel else 0) | \
+            (_lib.GDN_FLAG_CUDA_CORE_PREFILL if cuda_core_prefill else 0)
         args.mixed_qkv, args.mixed_stride_b, args.mixed_stride_t = mixed_qkv.data_ptr(), mixed_qkv.stride(0), \
             mixed_qkv.stride(1)
         args.z, args.z_stride_b, args.z_stride_t = z.data_ptr(), z.stride(0), z.stride(1)
