@@ -82,7 +82,6 @@ def test_two_gpu_head_sharded_layer_matches_unsharded():
         ry = m(x, cache=cache)
         cache.past_seen_tokens = 96
         ryd = m(xd, cache=cache)
-    # the sharded sum adds the out_proj partials in another order: two roundings
     # The sharded sum adds the out_proj partials in another order, and each
     # rank's projection is a different (narrower) GEMM whose bf16 outputs may
     # differ from the full GEMM's in the last bit: outputs get two roundings of
