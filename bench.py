@@ -14,8 +14,9 @@ rank r owns value heads [r*32/N, (r+1)*32/N) and the key heads they read; the
 token mixer needs no exchange between ranks (each (batch, head) chain is
 independent), so the total work is fixed and the scaling is strong.
 
-Also reported: the chunked-prefill workload (batch 8 x 8192 tokens) as a
-secondary object, the roofline of the dominant kernel, an end-to-end number
+Also reported: the chunked-prefill workload (batch 8 x 8192 tokens) and the
+speculative verify + rollback workload (batch 16, 4-token drafts) as secondary
+objects, the roofline of the dominant kernel, an end-to-end number
 through the public API with host buffers, the CPU oracle timed on the host,
 and SM clocks sampled during the timed region.
 
@@ -56,6 +57,7 @@ def parse():
     ap.add_argument("--no-decode", action="store_true", help="only the prefill measurement (for profiling)")
     ap.add_argument("--prefill-batch", type=int, default=8)
     ap.add_argument("--prefill-seq", type=int, default=8192)
+    ap.add_argument("--no-rollback", action="store_true", help="skip the secondary rollback measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-s", type=float, default=12.0, help="seconds of CPU work for the CPU baseline")
     return ap.parse_args()
@@ -88,6 +90,21 @@ def prefill_min_bytes(B: int, T: int, hk: int, hv: int, d: int, K: int = 4) -> i
     conv_ch = 2 * hk * d + hv * d
     per_tok = (conv_ch + hv * d + 2 * hv + hv * d) * 2
     return B * T * per_tok + B * hv * d * d * 4 + B * conv_ch * (K - 1) * 2
+
+
+def rollback_bytes(B: int, hk: int, hv: int, d: int, T: int, K: int = 4, act_bytes: int = 2) -> int:
+    """Bytes one verify + accept step must move: the starting state read once,
+    the states after each of the T draft tokens written once (the slots), the
+    conv state read and T conv snapshots written, conv weights, projection
+    outputs in, gated-norm output out, slot table and accepted counts."""
+    conv_ch = 2 * hk * d + hv * d
+    state = B * hv * d * d * 4 * (1 + T)
+    conv_state = B * conv_ch * (K - 1) * act_bytes * (1 + T)
+    conv_w = conv_ch * K * act_bytes
+    inputs = B * T * (conv_ch + hv * d + 2 * hv) * act_bytes
+    out = B * T * hv * d * act_bytes
+    table = B * (T + 1) * 4 * 2 + B * 4
+    return state + conv_state + conv_w + inputs + out + table
 
 
 def measured_peaks():
@@ -417,6 +434,11 @@ def run_ours(args, rank: int, world: int) -> None:
     if not args.no_prefill:
         prefill = run_prefill(torch, dist, m, local, dev, world, barrier, args.prefill_batch, args.prefill_seq)
 
+    # secondary: speculative verify + rollback on per-row state slots
+    rollback = None
+    if not args.no_rollback:
+        rollback = run_rollback(torch, dist, m, local, dev, world, barrier)
+
     if rank != 0:
         return
     hbm, tflops, src = measured_peaks()
@@ -439,6 +461,8 @@ def run_ours(args, rank: int, world: int) -> None:
     }
     if prefill is not None:
         line["prefill"] = prefill
+    if rollback is not None:
+        line["rollback"] = rollback
     if world == 1 and not args.no_cpu_baseline:
         rate, n, el = cpu_decode_rate(args.cpu_sample_s)
         line["cpu_baseline"] = {"value": rate, "unit": "steps/s", "cores": cpu_cores(), "kind": "port",
@@ -485,6 +509,71 @@ def run_prefill(torch, dist, m, local, dev, world, barrier, B=8, T=8192):
                          "frac": ach / tflops, "peak_source": src, "flops_per_launch": fl,
                          "min_bytes_per_launch": prefill_min_bytes(B, T, hk, hv, d),
                          "kernel": "gdn::ptc::prefill_tc_kernel (tcgen05 tf32, 1 CTA per (batch, head))"}}
+
+
+def run_rollback(torch, dist, m, local, dev, world, barrier, steps=1024):
+    """Speculative-decode verify with per-row rollback: batch 16, 4-token
+    drafts, accepted counts uniform in 0..4 per row (numpy seed 5), each step =
+    one verify launch (states after every draft token into the rows' free
+    slots) + one accept launch (slot-table swap); ``steps`` steps in one CUDA
+    graph."""
+    from visionstack_b200 import StateSlots
+    wl = W.WORKLOADS["rollback"]
+    B, T = wl.batch, wl.seq_len
+    hv, hk, d = local.num_v_heads, local.num_k_heads, local.head_k_dim
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    NIN = 16
+    with torch.no_grad():
+        x = torch.randn(NIN, B, T, W.SHAPE_QWEN.hidden_size, generator=g, device=dev).to(torch.bfloat16)
+        ins = [m.project(x[i]) for i in range(NIN)]
+        del x
+    acc = torch.from_numpy(np.random.default_rng(wl.x_seed).integers(0, T + 1, size=(steps, B)).astype(np.int32))
+    acc = acc.to(dev)
+    slots = StateSlots(m, B, T, torch.bfloat16, dev)
+    slots.load(torch.randn(B, local.conv_dim, 3, generator=g, device=dev).to(torch.bfloat16),
+               0.02 * torch.randn(B, hv, d, d, generator=g, device=dev))
+    out = torch.empty(B, T, local.value_dim, dtype=torch.bfloat16, device=dev)
+
+    def step(i):
+        mixed, z, bb, aa = ins[i % NIN]
+        m.mixer_verify(mixed, z, bb, aa, slots, out=out)
+        slots.accept(acc[i % steps])
+
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for i in range(4):
+            step(i)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(steps):
+            step(i)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        graph.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    t = torch.tensor([ev0.elapsed_time(ev1) / steps], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    del graph
+    hbm, _, src = measured_peaks()
+    nbytes = rollback_bytes(B, hk, hv, d, T)
+    ach = nbytes / (ms * 1e-3) / 1e9
+    return {"workload": f"speculative verify + rollback: B{B}, {T}-token drafts, accepted ~ U{{0..{T}}} (seed "
+                        f"{wl.x_seed}), 16 k-heads / 32 v-heads (sharded), d128, bf16, {steps} steps",
+            "steps_per_s": 1000.0 / ms, "ms_per_step": ms, "gpu_launches_per_step": 2,
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                         "peak_source": src, "bytes_per_step": nbytes,
+                         "kernel": "gdn::dtma::decode_tma_kernel<128,8,bf16> with a slot table "
+                                   "+ gdn::accept_slots_kernel"}}
 
 
 def main():

@@ -59,6 +59,7 @@ extern "C" {
 /* Bits of the device error word (gdn_device_error). */
 #define GDN_DEVERR_TMA_TIMEOUT 0x1u
 #define GDN_DEVERR_MMA_TIMEOUT 0x2u
+#define GDN_DEVERR_BAD_SLOT 0x4u   /* slot-table entry or accepted count out of range */
 
 /* Maximum number of state checkpoints one call can record. */
 #define GDN_MAX_CHECKPOINTS 512
@@ -147,6 +148,44 @@ const char* gdn_last_error_string(void);
  * otherwise a register-tile kernel runs.  Both compute the same thing.
  */
 int32_t gdn_mixer_decode(const gdn_mixer_args* args, void* stream);
+
+/*
+ * Speculative-decode verify on per-row state slots: rollback without copies.
+ *
+ * The reference verifies a draft of T tokens on a cache cloned per candidate
+ * (Qwen3_5HybridCache.clone_and_expand, ShadowBoxer/models/qwen35/cache.py:156-197)
+ * that records a checkpoint after every draft token, then restores each row to
+ * the checkpoint of its accepted length by copying it out of the checkpoint
+ * dicts (select_batch_item / extract_checkpoint, cache.py:131-154, 199-244;
+ * the loop in ShadowBoxer/models/qwen35/speculative.py:778-882).  Here each
+ * batch row owns num_slots (>= seq_len + 1) state slots:
+ *   args->state_in       state pool [num_slots, batch, Hv, dk, dv] float32
+ *   args->conv_state_in  conv pool  [num_slots, batch, conv_dim, conv_kernel-1]
+ *   slot_table           [batch, num_slots] int32 (device), a permutation of
+ *                        0..num_slots-1 in every row
+ * Row b starts from pool slot slot_table[b][0]; its recurrent and conv states
+ * after t = 1..seq_len draft tokens go to pool slot slot_table[b][t].  The
+ * starting slot is never written, so a fully rejected draft costs nothing.
+ * args->state_out, conv_state_out, num_checkpoints and the checkpoint pointers
+ * must be NULL / 0.  Everything else is as for gdn_mixer_decode.  Needs the
+ * pipelined kernel's conditions (4-tap conv, head dim 64 or 128, 16-byte
+ * aligned inputs, bf16 activations or seq_len 1), else GDN_ERR_UNSUPPORTED.
+ * Table entries outside 0..num_slots-1 are never followed: the tile reads
+ * slot 0 instead, skips the write and sets GDN_DEVERR_BAD_SLOT.
+ */
+int32_t gdn_mixer_verify_slots(const gdn_mixer_args* args, const int32_t* slot_table, int32_t num_slots,
+                               void* stream);
+
+/*
+ * Accept accepted[b] (0..seq_len) draft tokens of row b after
+ * gdn_mixer_verify_slots: swaps slot_table[b][0] and slot_table[b][accepted[b]],
+ * so the row continues from its state after accepted[b] tokens (0 keeps the
+ * state from before the draft; the old starting slot becomes free).  Device
+ * int32 arrays, one small launch, no host synchronisation.  Counts outside
+ * 0..seq_len leave the row unchanged and set GDN_DEVERR_BAD_SLOT.
+ */
+int32_t gdn_accept_slots(const int32_t* accepted, int32_t* slot_table, int32_t batch, int32_t num_slots,
+                         int32_t seq_len, void* stream);
 
 /*
  * Read (and optionally clear) the sticky device error word of the current

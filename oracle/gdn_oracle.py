@@ -426,3 +426,33 @@ def mixer_forward(shape, mixed_qkv: np.ndarray, z: np.ndarray, a: np.ndarray, b:
               checkpoint_positions=list(checkpoint_offsets) or None, checkpoint_states_out=rec_cps)
     out = rms_norm_gated(o.reshape(-1, dv), z.reshape(-1, dv), norm_w, shape.rms_norm_eps, dtype)
     return out.reshape(B, T, Hv * dv), nxt, S, conv_cps, rec_cps
+
+
+def speculative_verify_rollback(shape, mixed_qkv: np.ndarray, z: np.ndarray, a: np.ndarray, b: np.ndarray,
+                                conv_w: np.ndarray, A_log: np.ndarray, dt_bias: np.ndarray, norm_w: np.ndarray,
+                                dtype: str, conv_state: np.ndarray, rec_state: np.ndarray,
+                                accepted: np.ndarray):
+    """One speculative-decode step with per-row rollback, in the reference's
+    terms: the T-token draft runs through the token-by-token mixer with a
+    checkpoint after every draft token (speculative.py:778-798 records
+    positions prev_seen+1 .. prev_seen+T; local offsets 1..T here), then row b
+    continues from the checkpoint of its accepted count a_b
+    (select_batch_item(total_valid_tokens=prev_seen + a_b), cache.py:199-244,
+    which copies conv_checkpoints / recurrent_checkpoints at that position), or
+    from the state before the draft when a_b = 0 (extract_checkpoint at
+    past_seen_tokens, cache.py:133-134, which clones the pre-draft cache).
+    Returns (gated-norm output [B, T, Hv*dv], conv state, recurrent state)."""
+    B, T, _ = mixed_qkv.shape
+    out, _, _, conv_cps, rec_cps = mixer_forward(shape, mixed_qkv, z, a, b, conv_w, A_log, dt_bias, norm_w,
+                                                 dtype, conv_state, rec_state, chunk=False,
+                                                 checkpoint_offsets=list(range(1, T + 1)))
+    new_conv = conv_state.copy()
+    new_rec = rec_state.copy()
+    for row in range(B):
+        acc = int(accepted[row])
+        if not 0 <= acc <= T:
+            raise KeyError(f"checkpoint offset {acc} not recorded")
+        if acc > 0:
+            new_conv[row] = conv_cps[acc][row]
+            new_rec[row] = rec_cps[acc][row]
+    return out, new_conv, new_rec

@@ -96,6 +96,41 @@ def test_decode_rejects_long_sequences():
     assert _call("gdn_mixer_decode", a) == -1
 
 
+def _slot_args(T=4):
+    a = _valid_args(T)
+    a.state_out = None
+    a.conv_state_in = 0x70000
+    return a
+
+
+@pytest.mark.parametrize("breaker,table,n,code", [
+    (lambda a: None, None, 5, -1),                              # no slot table
+    (lambda a: None, 0xA0002, 5, -3),                           # misaligned table
+    (lambda a: None, 0xA0000, 4, -1),                           # fewer than T + 1 slots
+    (lambda a: None, 0xA0000, 10, -1),                          # more than 9 slots
+    (lambda a: setattr(a, "state_out", 0x60000), 0xA0000, 5, -1),
+    (lambda a: setattr(a, "conv_state_in", None), 0xA0000, 5, -1),
+    (lambda a: setattr(a, "num_checkpoints", 1), 0xA0000, 5, -1),
+    (lambda a: setattr(a, "flags", _lib.GDN_FLAG_REGISTER_KERNEL), 0xA0000, 5, -2),
+    (lambda a: setattr(a, "seq_len", 9), 0xA0000, 9, -1),
+    (lambda a: setattr(a, "head_k_dim", 256), 0xA0000, 5, -2),
+])
+def test_verify_slots_validation(breaker, table, n, code):
+    a = _slot_args()
+    breaker(a)
+    assert _lib.load().gdn_mixer_verify_slots(ctypes.byref(a), table, n, None) == code
+    assert _lib.load().gdn_last_error_string()
+
+
+def test_accept_slots_validation():
+    lib = _lib.load()
+    assert lib.gdn_accept_slots(None, 0xA0000, 4, 5, 4, None) == -1
+    assert lib.gdn_accept_slots(0xB0000, 0xA0000, 0, 5, 4, None) == -1
+    assert lib.gdn_accept_slots(0xB0000, 0xA0000, 4, 4, 4, None) == -1
+    assert lib.gdn_accept_slots(0xB0000, 0xA0000, 4, 5, 0, None) == -1
+    assert lib.gdn_accept_slots(0xB0001, 0xA0000, 4, 5, 4, None) == -3
+
+
 def test_error_raises_runtime_error():
     with pytest.raises(_lib.GDNError):
         _lib.check("gdn_mixer_decode", _call("gdn_mixer_decode", _lib.MixerArgs()))

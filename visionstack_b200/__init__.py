@@ -13,12 +13,14 @@ from .deltanet import (
     _extract_conv_state_at_offset,
     _recurrent_gated_delta_rule,
 )
+from .slots import StateSlots
 
 __all__ = [
     "Qwen3_5HybridCache",
     "Qwen3_5RMSNormGated",
     "Qwen3_5TextConfig",
     "Qwen3_5GatedDeltaNet",
+    "StateSlots",
     "_causal_conv1d_fn",
     "_chunk_gated_delta_rule",
     "_extract_conv_state_at_offset",

@@ -29,11 +29,14 @@ EXPORTED_SYMBOLS = (
     "gdn_mixer_prefill",
     "gdn_delta_rule",
     "gdn_causal_conv1d",
+    "gdn_mixer_verify_slots",
+    "gdn_accept_slots",
     "gdn_device_error",
     "gdn_selftest_umma",
 )
 GDN_FLAG_REGISTER_KERNEL = 1
 GDN_FLAG_CUDA_CORE_PREFILL = 2
+GDN_DEVERR_BAD_SLOT = 0x4
 
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int32
@@ -105,6 +108,10 @@ def load() -> ctypes.CDLL:
                                           _c_void_p, _c_void_p, _i32, _c_void_p]
         lib.gdn_selftest_umma.restype = _i32
         lib.gdn_selftest_umma.argtypes = [_i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p]
+        lib.gdn_mixer_verify_slots.restype = _i32
+        lib.gdn_mixer_verify_slots.argtypes = [ctypes.POINTER(MixerArgs), _c_void_p, _i32, _c_void_p]
+        lib.gdn_accept_slots.restype = _i32
+        lib.gdn_accept_slots.argtypes = [_c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p]
         lib.gdn_device_error.restype = _i32
         lib.gdn_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32), _i32]
         _lib = lib

@@ -173,14 +173,69 @@ int32_t gdn_mixer_decode(const gdn_mixer_args* args, void* stream) {
     return cuda_status(e, "gdn_mixer_decode launch");
 }
 
+int32_t gdn_mixer_verify_slots(const gdn_mixer_args* args, const int32_t* slot_table, int32_t num_slots,
+                               void* stream) {
+    if (!args) return fail(GDN_ERR_INVALID_ARG, "args is NULL");
+    if (!slot_table) return fail(GDN_ERR_INVALID_ARG, "slot_table is NULL");
+    if ((reinterpret_cast<uintptr_t>(slot_table) & 3u) != 0) return fail(GDN_ERR_ALIGNMENT, "slot_table misaligned");
+    if (args->seq_len < 1 || args->seq_len > GDN_MAX_DECODE_TOKENS)
+        return fail(GDN_ERR_INVALID_ARG, "seq_len %d outside 1..%d", args->seq_len, GDN_MAX_DECODE_TOKENS);
+    if (num_slots < args->seq_len + 1 || num_slots > GDN_MAX_DECODE_TOKENS + 1)
+        return fail(GDN_ERR_INVALID_ARG, "num_slots %d outside seq_len + 1 (%d) .. %d", num_slots,
+                    args->seq_len + 1, GDN_MAX_DECODE_TOKENS + 1);
+    if (!args->state_in || !args->conv_state_in)
+        return fail(GDN_ERR_INVALID_ARG, "state_in and conv_state_in (the slot pools) are required");
+    if (args->state_out || args->conv_state_out || args->num_checkpoints || args->checkpoint_offsets ||
+        args->state_checkpoints || args->conv_checkpoints)
+        return fail(GDN_ERR_INVALID_ARG, "state_out, conv_state_out and checkpoint fields must be NULL / 0 "
+                                         "with a slot table");
+    if (args->flags & GDN_FLAG_REGISTER_KERNEL)
+        return fail(GDN_ERR_UNSUPPORTED, "the slot table needs the pipelined kernel");
+    gdn::CkptList ck;
+    gdn::MixParams p;
+    int32_t st = validate_mixer(args, &p, &ck);
+    if (st != GDN_OK) return st;
+    // every draft token is a checkpoint; checkpoint i (offset i + 1) goes to table column i + 1
+    ck.n = args->seq_len;
+    for (int i = 0; i < ck.n; ++i) {
+        ck.off[i] = i + 1;
+        ck.slot[i] = i + 1;
+    }
+    p.S_ckpt = const_cast<float*>(args->state_in);
+    p.cs_ckpt = const_cast<void*>(args->conv_state_in);
+    p.slot_table = slot_table;
+    p.n_slots = num_slots;
+    bool supported = false;
+    cudaError_t e = gdn::launch_decode_tma(p, ck, args->head_k_dim, args->act_dtype,
+                                           static_cast<cudaStream_t>(stream), &supported);
+    if (!supported)
+        return fail(GDN_ERR_UNSUPPORTED, "slot tables need 4-tap conv, head dim 64 or 128, 16-byte aligned inputs "
+                                         "and bf16 activations (or seq_len 1)");
+    return cuda_status(e, "gdn_mixer_verify_slots launch");
+}
+
+int32_t gdn_accept_slots(const int32_t* accepted, int32_t* slot_table, int32_t batch, int32_t num_slots,
+                         int32_t seq_len, void* stream) {
+    if (!accepted || !slot_table) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
+    if ((reinterpret_cast<uintptr_t>(accepted) & 3u) || (reinterpret_cast<uintptr_t>(slot_table) & 3u))
+        return fail(GDN_ERR_ALIGNMENT, "accepted / slot_table misaligned");
+    if (batch < 1) return fail(GDN_ERR_INVALID_ARG, "batch must be >= 1");
+    if (seq_len < 1 || num_slots < seq_len + 1)
+        return fail(GDN_ERR_INVALID_ARG, "need 1 <= seq_len < num_slots (got %d, %d)", seq_len, num_slots);
+    return cuda_status(gdn::launch_accept_slots(accepted, slot_table, batch, num_slots, seq_len,
+                                                static_cast<cudaStream_t>(stream)),
+                       "gdn_accept_slots launch");
+}
+
 int32_t gdn_device_error(uint32_t* flags_out, int32_t clear) {
     if (!flags_out) return fail(GDN_ERR_INVALID_ARG, "flags_out is NULL");
     const unsigned int a = gdn::decode_tma_device_error(clear != 0);
     const unsigned int b = gdn::umma_device_error(clear != 0);
     const unsigned int c = gdn::prefill_tc_device_error(clear != 0);
-    if (a == 0xFFFFFFFFu || b == 0xFFFFFFFFu || c == 0xFFFFFFFFu)
+    const unsigned int d = gdn::slots_device_error(clear != 0);
+    if (a == 0xFFFFFFFFu || b == 0xFFFFFFFFu || c == 0xFFFFFFFFu || d == 0xFFFFFFFFu)
         return fail(GDN_ERR_CUDA, "could not read the device error word");
-    *flags_out = a | b | c;
+    *flags_out = a | b | c | d;
     return ok();
 }
 

@@ -13,6 +13,11 @@
 // gated-norm work.  The new state leaves from registers with streaming
 // 128-bit stores (in place when state_out == state_in).
 //
+// With a slot table (gdn_mixer_verify_slots) the state and conv state of row b
+// come from pool slot slot_table[b][0] and the state after token t goes to
+// pool slot slot_table[b][t]: speculative-decode rollback becomes a swap of
+// two table entries (gdn_slots.cu) instead of a copy.
+//
 // Math per token is that of decode_kernel (gdn_decode.cu): the reference's
 // deltanet.py:41-90 (conv), :186-189 (L2 norm), :516-517 (gates),
 // :210-221 (delta rule), config.py:136-143 (gated RMSNorm).
@@ -54,6 +59,22 @@ struct GroupLayout {
     static constexpr int OFF_BAR = (OFF_GATE + 2 * TMAX * 4 + 7) / 8 * 8;
     static constexpr int BYTES = (OFF_BAR + 8 + 127) / 128 * 128;
 };
+
+// Pool slot of column `col` of row b's slot table; -1 (and the error bit) when
+// the entry is out of range, so a bad table is never followed.
+__device__ __forceinline__ int row_slot(const MixParams& p, int b, int col) {
+    const int s = __ldg(p.slot_table + (size_t)b * p.n_slots + col);
+    if (s < 0 || s >= p.n_slots) {
+        atomicOr(&g_device_error, GDN_DEVERR_BAD_SLOT);
+        return -1;
+    }
+    return s;
+}
+
+// Output slot of checkpoint i of row b: the caller's index, or the pool slot.
+__device__ __forceinline__ int ckpt_slot(const MixParams& p, const CkptList& ck, int i, int b) {
+    return p.slot_table ? row_slot(p, b, ck.slot[i]) : ck.slot[i];
+}
 
 __device__ __forceinline__ void group_sync(int id) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(GT) : "memory");
@@ -111,10 +132,16 @@ __global__ void __launch_bounds__(NT, 1)
         const int b = tile / p.Hv, h = tile - (tile / p.Hv) * p.Hv, kh = h / rep;
         const uint32_t mrow = D * sizeof(TA);
         const int c0 = kh * D, c1 = p.Hk * D + kh * D, c2 = 2 * p.Hk * D + h * D;
+        size_t slot0 = 0;  // pool slot of the starting state (slot mode)
+        if (p.slot_table) {
+            const int s0 = row_slot(p, b, 0);
+            slot0 = s0 < 0 ? 0 : (size_t)s0;
+        }
         uint32_t bytes = (has_S ? GL::S_BYTES : 0) + 4u * T * mrow + 3u * D * KC * sizeof(TA);
         if (has_cs) bytes += 3u * D * LC * sizeof(TA);
         mbar_arrive_expect_tx(bar, bytes);
-        if (has_S) bulk_load(smem_u32(gbase + GL::OFF_S), p.S_in + (size_t)tile * D * D, GL::S_BYTES, bar);
+        if (has_S)
+            bulk_load(smem_u32(gbase + GL::OFF_S), p.S_in + (slot0 * p.B * p.Hv + tile) * D * D, GL::S_BYTES, bar);
         for (int t = 0; t < T; ++t) {
             const TA* row = gmixed + (size_t)b * p.ms_b + (size_t)t * p.ms_t;
             bulk_load(smem_u32(gbase + GL::OFF_MQ + t * mrow), row + c0, mrow, bar);
@@ -129,7 +156,7 @@ __global__ void __launch_bounds__(NT, 1)
         for (int g = 0; g < 3; ++g) {
             if (has_cs)
                 bulk_load(smem_u32(gbase + GL::OFF_CS + g * D * LC * (int)sizeof(TA)),
-                          static_cast<const TA*>(p.cs_in) + ((size_t)b * conv_dim + chans[g]) * LC,
+                          static_cast<const TA*>(p.cs_in) + ((slot0 * p.B + b) * conv_dim + chans[g]) * LC,
                           D * LC * sizeof(TA), bar);
             bulk_load(smem_u32(gbase + GL::OFF_CW + g * D * KC * (int)sizeof(TA)), cw + (size_t)chans[g] * KC,
                       D * KC * sizeof(TA), bar);
@@ -190,8 +217,10 @@ __global__ void __launch_bounds__(NT, 1)
                 const bool fin = p.cs_out && w == 0;
                 const int ci_idx = p.cs_out ? w - 1 : w;
                 const int off = fin ? T : ck.off[ci_idx];
+                const int slot = fin ? 0 : ckpt_slot(p, ck, ci_idx, b);
+                if (slot < 0) continue;
                 TA* dst = fin ? static_cast<TA*>(p.cs_out) + (size_t)b * conv_dim * LC
-                              : static_cast<TA*>(p.cs_ckpt) + ((size_t)ck.slot[ci_idx] * p.B + b) * conv_dim * LC;
+                              : static_cast<TA*>(p.cs_ckpt) + ((size_t)slot * p.B + b) * conv_dim * LC;
                 for (int c = cbeg + tid; c < 3 * D; c += GT) {
                     const int g = c / D, ci = c % D;
                     const int gc = (g == 0 ? kh * D : (g == 1 ? p.Hk * D + kh * D : 2 * p.Hk * D + h * D)) + ci;
@@ -302,8 +331,9 @@ __global__ void __launch_bounds__(NT, 1)
                 }
             }
             while (ck_i < ck.n && ck.off[ck_i] == t + 1) {
-                if (p.S_ckpt) {
-                    float4* dst = reinterpret_cast<float4*>(p.S_ckpt + ((size_t)ck.slot[ck_i] * p.B * p.Hv + tile) *
+                const int slot = p.S_ckpt ? ckpt_slot(p, ck, ck_i, b) : -1;
+                if (slot >= 0) {
+                    float4* dst = reinterpret_cast<float4*>(p.S_ckpt + ((size_t)slot * p.B * p.Hv + tile) *
                                                                            (size_t)(D * D));
 #pragma unroll
                     for (int r = 0; r < RPT; ++r) __stcs(dst + (rg * RPT + r) * CG + cg, S[r]);

@@ -48,6 +48,12 @@ struct MixParams {
     void* out;
     float* S_ckpt;    // [n_slots, B, Hv, dk, dv]
     void* cs_ckpt;    // [n_slots, B, conv_dim, K-1]
+    // Per-row state slots (gdn_mixer_verify_slots): when set, S_in / S_ckpt
+    // and cs_in / cs_ckpt are the same pools [n_slots, B, ...]; row b reads
+    // pool slot slot_table[b][0] and checkpoint i goes to pool slot
+    // slot_table[b][ck.slot[i]].
+    const int* slot_table;  // [B, n_slots]
+    int n_slots;
 };
 
 // dtype: GDN_DTYPE_*; mixer: fused conv/gates/norm (true) or split q/k/v (false).
@@ -56,6 +62,8 @@ cudaError_t launch_decode(const MixParams& p, const CkptList& ck, int dk, int dv
 cudaError_t launch_decode_tma(const MixParams& p, const CkptList& ck, int d, int dtype, cudaStream_t s,
                               bool* supported);
 unsigned int decode_tma_device_error(bool clear);
+cudaError_t launch_accept_slots(const int* accepted, int* table, int B, int n_slots, int T, cudaStream_t s);
+unsigned int slots_device_error(bool clear);
 cudaError_t launch_umma_selftest(int mode, const float* A, const float* B, float* D, cudaStream_t s);
 unsigned int umma_device_error(bool clear);
 cudaError_t launch_prefill_tc(const MixParams& p, const CkptList& ck, int d, int dtype, cudaStream_t s,

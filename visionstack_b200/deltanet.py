@@ -23,6 +23,7 @@ from torch import nn
 from . import _lib
 from .cache import Qwen3_5HybridCache, is_owned, mark_owned
 from .config import _FP8_DTYPES, Qwen3_5RMSNormGated, Qwen3_5TextConfig, _linear
+from .slots import StateSlots
 
 _DTYPES = {torch.float32: _lib.GDN_DTYPE_F32, torch.bfloat16: _lib.GDN_DTYPE_BF16}
 
@@ -243,6 +244,58 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         chunked kernel instead of the tensor-core one (same results up to
         float rounding; used by the tests).
         """
+        if token_by_token is None:
+            token_by_token = rec_state is not None and mixed_qkv.shape[1] <= _lib.GDN_MAX_DECODE_TOKENS
+        flags = (_lib.GDN_FLAG_REGISTER_KERNEL if register_kernel else 0) | \
+            (_lib.GDN_FLAG_CUDA_CORE_PREFILL if cuda_core_prefill else 0)
+        args, out, keep = self._mixer_args(mixed_qkv, z, b, a, conv_state, rec_state, conv_state_out,
+                                           rec_state_out, out, flags)
+        offs = list(checkpoint_offsets)
+        arr = _lib.int_array(offs)
+        args.num_checkpoints = len(offs)
+        args.checkpoint_offsets = ctypes.cast(arr, ctypes.POINTER(ctypes.c_int32))
+        args.state_checkpoints = _ptr(state_checkpoints)
+        args.conv_checkpoints = _ptr(conv_checkpoints)
+        lib = _lib.load()
+        fn = lib.gdn_mixer_decode if token_by_token else lib.gdn_mixer_prefill
+        with torch.cuda.device(out.device):
+            _lib.check("gdn_mixer_decode" if token_by_token else "gdn_mixer_prefill",
+                       fn(ctypes.byref(args), _stream(out.device)))
+        return out
+
+    def mixer_verify(self, mixed_qkv: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: torch.Tensor,
+                     slots: "StateSlots", out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Token mixer of a speculative-decode verify step on per-row state
+        slots (``StateSlots``): each row starts from its current slot and the
+        states after every draft token land in its free slots; nothing is
+        written over the starting state.  Returns the gated-norm output
+        [B, T, Hv*dv]; follow with ``slots.accept(counts)``."""
+        B, T, _ = mixed_qkv.shape
+        if B != slots.batch or T > slots.num_slots - 1:
+            raise ValueError(f"draft of {T} tokens for {B} rows does not fit slots of {slots.batch} rows x "
+                             f"{slots.num_slots - 1} tokens")
+        if slots.conv.dtype != mixed_qkv.dtype:
+            raise TypeError(f"conv slots hold {slots.conv.dtype}, activations are {mixed_qkv.dtype}")
+        args, out, keep = self._mixer_args(mixed_qkv, z, b, a, slots.conv, slots.state, None, None, out, 0)
+        lib = _lib.load()
+        with torch.cuda.device(out.device):
+            _lib.check("gdn_mixer_verify_slots",
+                       lib.gdn_mixer_verify_slots(ctypes.byref(args), slots.table.data_ptr(), slots.num_slots,
+                                                  _stream(out.device)))
+        slots.last_len = T
+        return out
+
+    def verify(self, hidden_states: torch.Tensor, slots: "StateSlots") -> torch.Tensor:
+        """Layer output of a speculative-decode verify step: the four
+        projections, ``mixer_verify`` and ``out_proj``.  The reference runs the
+        same forward on a cache cloned per candidate with a checkpoint after
+        every draft token (speculative.py:778-798)."""
+        mixed_qkv, z, b, a = self.project(hidden_states)
+        return _linear(self.out_proj, self.mixer_verify(mixed_qkv, z, b, a, slots))
+
+    def _mixer_args(self, mixed_qkv, z, b, a, conv_state, rec_state, conv_state_out, rec_state_out, out, flags):
+        """Fill a ``gdn_mixer_args`` for one call; returns (args, out, tensors
+        that must stay alive until the launch)."""
         B, T, _ = mixed_qkv.shape
         dt = mixed_qkv.dtype
         dev = _require_cuda(mixed_qkv, z, b, a, conv_state, rec_state)
@@ -264,8 +317,6 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         normw = self.norm.weight.detach().contiguous()
         if out is None:
             out = torch.empty((B, T, self.value_dim), dtype=dt, device=dev)
-        if token_by_token is None:
-            token_by_token = rec_state is not None and T <= _lib.GDN_MAX_DECODE_TOKENS
         args = _lib.MixerArgs()
         args.batch, args.seq_len = B, T
         args.num_k_heads, args.num_v_heads = self.num_k_heads, self.num_v_heads
@@ -273,8 +324,7 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         args.conv_kernel = self.conv_kernel_size
         args.act_dtype = _dtype_code(dt)
         args.norm_eps = float(self.layer_norm_epsilon)
-        args.flags = (_lib.GDN_FLAG_REGISTER_KERNEL if register_kernel else 0) | \
-            (_lib.GDN_FLAG_CUDA_CORE_PREFILL if cuda_core_prefill else 0)
+        args.flags = flags
         args.mixed_qkv, args.mixed_stride_b, args.mixed_stride_t = mixed_qkv.data_ptr(), mixed_qkv.stride(0), \
             mixed_qkv.stride(1)
         args.z, args.z_stride_b, args.z_stride_t = z.data_ptr(), z.stride(0), z.stride(1)
@@ -291,18 +341,7 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         args.state_in = _ptr(rec_state)
         args.state_out = _ptr(rec_state_out)
         args.out = out.data_ptr()
-        offs = list(checkpoint_offsets)
-        arr = _lib.int_array(offs)
-        args.num_checkpoints = len(offs)
-        args.checkpoint_offsets = ctypes.cast(arr, ctypes.POINTER(ctypes.c_int32))
-        args.state_checkpoints = _ptr(state_checkpoints)
-        args.conv_checkpoints = _ptr(conv_checkpoints)
-        lib = _lib.load()
-        fn = lib.gdn_mixer_decode if token_by_token else lib.gdn_mixer_prefill
-        with torch.cuda.device(dev):
-            _lib.check("gdn_mixer_decode" if token_by_token else "gdn_mixer_prefill",
-                       fn(ctypes.byref(args), _stream(dev)))
-        return out
+        return args, out, (a, b, z, conv_w, A_log, dt_bias, normw, conv_state, rec_state)
 
     def mixer_plan(self, batch: int, seq_len: int, dtype: torch.dtype, device,
                    token_by_token: bool = True) -> "MixerPlan":
