@@ -197,9 +197,10 @@ int32_t gdn_device_error(uint32_t* flags_out, int32_t clear);
 
 /*
  * Tensor-core self-test: D[128][N] = A * B with the 5th-generation tensor
- * core (tf32 in, fp32 out) for operand-layout combination `mode` (0..3, see
- * gdn_umma_selftest.cu), in plain row-major fp32 device buffers.  Checks the
- * shared-memory layouts and descriptors the chunked kernel relies on.  No
+ * core (tf32 in, fp32 out) for operand-layout combination `mode` (0..6, see
+ * gdn_umma_selftest.cu; modes 4..6 read A from tensor memory), in plain
+ * row-major fp32 device buffers.  Checks the shared-memory layouts,
+ * descriptors and tensor-memory operands the chunked kernels rely on.  No
  * counterpart in the reference.
  */
 int32_t gdn_selftest_umma(int32_t mode, const float* A, const float* B, float* D, void* stream);
@@ -214,6 +215,33 @@ int32_t gdn_selftest_umma(int32_t mode, const float* A, const float* B, float* D
  * tf32 operands, fp32 accumulation); otherwise a CUDA-core fp32 kernel runs.
  */
 int32_t gdn_mixer_prefill(const gdn_mixer_args* args, void* stream);
+
+/*
+ * Device workspace, in bytes, that gdn_mixer_prefill_ws needs for these
+ * arguments: 0 when the call takes a path without workspace, a negative
+ * GDN_ERR_* code when the arguments are invalid.  At batch 8 x 8192 tokens,
+ * 16 / 32 heads of 128 this is about 2.2 GB (the conv outputs in bf16 plus a
+ * 32 KB pair of 64x64 tf32 matrices per chunk and value head).
+ */
+int64_t gdn_prefill_workspace_bytes(const gdn_mixer_args* args);
+
+/*
+ * Chunked token mixer in two kernels (prefill), same arguments, results and
+ * cache semantics as gdn_mixer_prefill.  A fully parallel preparation kernel
+ * (one CTA per batch row, key head and chunk of 64 tokens) computes what does
+ * not depend on the recurrent state - conv + SiLU, L2-norm factors, gates,
+ * and each chunk's (I + A)^-1 and masked Q K^T (deltanet.py:266-343) - into
+ * `workspace`; the sequential kernel (one CTA per batch row and value head)
+ * then carries the state through the chunks (deltanet.py:345-389) with every
+ * state product on the tensor cores.  `workspace` (device, 16-byte aligned,
+ * at least gdn_prefill_workspace_bytes, not overlapping any other argument)
+ * is scratch: nothing in it needs to be initialised or survives the call.
+ * Shapes the two-kernel form does not cover (activations other than bf16,
+ * head dims other than 128, conv_kernel != 4, num_v_heads / num_k_heads not
+ * in {1, 2, 4}, misaligned inputs) or GDN_FLAG_CUDA_CORE_PREFILL run
+ * gdn_mixer_prefill instead and ignore the workspace.
+ */
+int32_t gdn_mixer_prefill_ws(const gdn_mixer_args* args, void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
  * Stand-alone delta rule on already-split q/k/v, the functional boundary of

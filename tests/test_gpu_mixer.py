@@ -46,7 +46,7 @@ def mixer_inputs(shape: W.LayerShape, B: int, T: int, dtype: str, seed: int, wit
     return d
 
 
-def run_ours(m, shape, d, dtype, token_by_token, offsets=(), register_kernel=False):
+def run_ours(m, shape, d, dtype, token_by_token, offsets=(), register_kernel=False, fused_prefill=False):
     dev = torch.device("cuda")
     t = lambda a: torch.from_numpy(a).to(dev).to(TDT[dtype])  # noqa: E731
     B, T = d["mixed"].shape[:2]
@@ -62,7 +62,7 @@ def run_ours(m, shape, d, dtype, token_by_token, offsets=(), register_kernel=Fal
     out = m.mixer(t(d["mixed"]), t(d["z"]), t(d["b"]), t(d["a"]), conv_state=cs, rec_state=rs,
                   conv_state_out=cs_out, rec_state_out=rs_out, checkpoint_offsets=offsets,
                   state_checkpoints=st_ck, conv_checkpoints=cv_ck, token_by_token=token_by_token,
-                  register_kernel=register_kernel)
+                  register_kernel=register_kernel, fused_prefill=fused_prefill)
     torch.cuda.synchronize()
     return out, cs_out, rs_out, st_ck, cv_ck
 
@@ -246,21 +246,38 @@ def test_mixer_plan_matches_mixer():
     assert torch.equal(o1, o2) and torch.equal(S1, S2) and torch.equal(cs1, cs2)
 
 
+@pytest.mark.parametrize("fused", [False, True])
 @pytest.mark.parametrize("B,T,with_state,offsets", [
     (2, 200, True, (1, 37, 64, 100, 128, 199, 200)),
     (1, 64, False, (64,)),
     (3, 7, True, (3, 7)),
     (1, 513, False, (256, 500, 513)),
 ])
-def test_tensor_core_prefill_vs_oracle(B, T, with_state, offsets):
-    """The tcgen05 chunked kernel (bf16, head dim 128) against the oracle, with
-    sub-chunk and chunk-boundary checkpoints, ragged last chunks and T < 64."""
+def test_tensor_core_prefill_vs_oracle(B, T, with_state, offsets, fused):
+    """The tcgen05 chunked kernels (bf16, head dim 128) against the oracle, with
+    sub-chunk and chunk-boundary checkpoints, ragged last chunks and T < 64:
+    the two-kernel form (parallel preparation + sequential pass, the default)
+    and the single fused kernel."""
     from visionstack_b200 import _lib
     shape = W.LayerShape(256, 2, 4, 128, 128)
     m, params = make_layer(shape, "bf16")
     d = mixer_inputs(shape, B, T, "bf16", seed=40 + T, with_state=with_state)
-    check(shape, "bf16", run_ours(m, shape, d, "bf16", False, offsets),
+    check(shape, "bf16", run_ours(m, shape, d, "bf16", False, offsets, fused_prefill=fused),
           run_oracle(shape, params, d, "bf16", chunk=True, offsets=offsets), offsets, f"tc T{T}")
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("rep", [1, 4])
+def test_two_kernel_prefill_gqa_groupings(rep):
+    """Key heads shared by 1 or 4 value heads (the preparation pass handles
+    every value head of a key head in one CTA)."""
+    from visionstack_b200 import _lib
+    shape = W.LayerShape(256, 2, 2 * rep, 128, 128)
+    m, params = make_layer(shape, "bf16")
+    d = mixer_inputs(shape, 2, 150, "bf16", seed=60 + rep, with_state=True)
+    offs = (10, 64, 150)
+    check(shape, "bf16", run_ours(m, shape, d, "bf16", False, offs),
+          run_oracle(shape, params, d, "bf16", chunk=True, offsets=offs), offs, f"rep{rep}")
     assert _lib.device_error() == 0
 
 
@@ -272,11 +289,35 @@ def test_tensor_core_prefill_matches_cuda_core_kernel():
     t = lambda a: torch.from_numpy(a).to(dev).to(torch.bfloat16)  # noqa: E731
     S0 = torch.from_numpy(d["rec_state"]).to(dev)
     outs = []
-    for cc in (False, True):
+    for kw in ({}, {"fused_prefill": True}, {"cuda_core_prefill": True}):
         S = torch.empty_like(S0)
         o = m.mixer(t(d["mixed"]), t(d["z"]), t(d["b"]), t(d["a"]), conv_state=t(d["conv_state"]), rec_state=S0,
-                    rec_state_out=S, token_by_token=False, cuda_core_prefill=cc)
+                    rec_state_out=S, token_by_token=False, **kw)
         outs.append((o, S))
     torch.cuda.synchronize()
-    assert_bf16_close(outs[0][0], outs[1][0], "tc vs cuda-core out", scale=2.0)
-    assert_state_close(outs[0][1], outs[1][1], "tc vs cuda-core state", scale=2.0)
+    for i, name in ((1, "fused"), (2, "cuda-core")):
+        assert_bf16_close(outs[0][0], outs[i][0], f"two-kernel vs {name} out", scale=2.0)
+        assert_state_close(outs[0][1], outs[i][1], f"two-kernel vs {name} state", scale=2.0)
+
+
+def test_prefill_plan_matches_mixer():
+    """The prepared-call API on the chunked path (workspace kept by the plan)."""
+    shape = W.SHAPE_QWEN
+    m, _ = make_layer(shape, "bf16")
+    B, T = 2, 200
+    d = mixer_inputs(shape, B, T, "bf16", seed=13, with_state=True)
+    dev = torch.device("cuda")
+    t = lambda a: torch.from_numpy(a).to(dev).to(torch.bfloat16)  # noqa: E731
+    args = (t(d["mixed"]), t(d["z"]), t(d["b"]), t(d["a"]))
+    S0 = torch.from_numpy(d["rec_state"]).to(dev)
+    S1, S2 = torch.empty_like(S0), torch.empty_like(S0)
+    cs1 = torch.empty(B, shape.conv_dim, 3, dtype=torch.bfloat16, device=dev)
+    cs2 = torch.empty_like(cs1)
+    o1 = m.mixer(*args, conv_state=t(d["conv_state"]), rec_state=S0, conv_state_out=cs1, rec_state_out=S1,
+                 token_by_token=False)
+    plan = m.mixer_plan(B, T, torch.bfloat16, dev, token_by_token=False)
+    o2 = torch.empty_like(o1)
+    for _ in range(2):
+        plan(*args, t(d["conv_state"]), S0, cs2, S2, o2)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2) and torch.equal(S1, S2) and torch.equal(cs1, cs2)

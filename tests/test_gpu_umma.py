@@ -14,11 +14,13 @@ from visionstack_b200 import _lib
 
 pytestmark = pytest.mark.gpu
 
+# mode: (K, N, A MN-major, B MN-major); modes 4-6 read A from tensor memory
 SHAPES = {0: (128, 64, False, False), 1: (128, 128, False, True), 2: (64, 128, False, True),
-          3: (64, 128, True, True)}
+          3: (64, 128, True, True), 4: (128, 128, False, False), 5: (64, 64, False, False),
+          6: (64, 128, False, True)}
 
 
-@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+@pytest.mark.parametrize("mode", sorted(SHAPES))
 def test_umma_layouts(mode):
     K, N, a_mn, b_mn = SHAPES[mode]
     rng = np.random.default_rng(mode)

@@ -30,6 +30,8 @@ EXPORTED_SYMBOLS = (
     "gdn_delta_rule",
     "gdn_causal_conv1d",
     "gdn_mixer_verify_slots",
+    "gdn_prefill_workspace_bytes",
+    "gdn_mixer_prefill_ws",
     "gdn_accept_slots",
     "gdn_device_error",
     "gdn_selftest_umma",
@@ -108,6 +110,10 @@ def load() -> ctypes.CDLL:
                                           _c_void_p, _c_void_p, _i32, _c_void_p]
         lib.gdn_selftest_umma.restype = _i32
         lib.gdn_selftest_umma.argtypes = [_i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p]
+        lib.gdn_prefill_workspace_bytes.restype = _i64
+        lib.gdn_prefill_workspace_bytes.argtypes = [ctypes.POINTER(MixerArgs)]
+        lib.gdn_mixer_prefill_ws.restype = _i32
+        lib.gdn_mixer_prefill_ws.argtypes = [ctypes.POINTER(MixerArgs), _c_void_p, _i64, _c_void_p]
         lib.gdn_mixer_verify_slots.restype = _i32
         lib.gdn_mixer_verify_slots.argtypes = [ctypes.POINTER(MixerArgs), _c_void_p, _i32, _c_void_p]
         lib.gdn_accept_slots.restype = _i32

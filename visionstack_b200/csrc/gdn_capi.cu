@@ -229,18 +229,64 @@ int32_t gdn_accept_slots(const int32_t* accepted, int32_t* slot_table, int32_t b
 
 int32_t gdn_device_error(uint32_t* flags_out, int32_t clear) {
     if (!flags_out) return fail(GDN_ERR_INVALID_ARG, "flags_out is NULL");
-    const unsigned int a = gdn::decode_tma_device_error(clear != 0);
-    const unsigned int b = gdn::umma_device_error(clear != 0);
-    const unsigned int c = gdn::prefill_tc_device_error(clear != 0);
-    const unsigned int d = gdn::slots_device_error(clear != 0);
-    if (a == 0xFFFFFFFFu || b == 0xFFFFFFFFu || c == 0xFFFFFFFFu || d == 0xFFFFFFFFu)
-        return fail(GDN_ERR_CUDA, "could not read the device error word");
-    *flags_out = a | b | c | d;
+    const unsigned int words[] = {gdn::decode_tma_device_error(clear != 0), gdn::umma_device_error(clear != 0),
+                                  gdn::prefill_tc_device_error(clear != 0), gdn::slots_device_error(clear != 0),
+                                  gdn::prefill_prep_device_error(clear != 0),
+                                  gdn::prefill_seq_device_error(clear != 0)};
+    uint32_t all = 0;
+    for (unsigned int w : words) {
+        if (w == 0xFFFFFFFFu) return fail(GDN_ERR_CUDA, "could not read the device error word");
+        all |= w;
+    }
+    *flags_out = all;
     return ok();
 }
 
+int64_t gdn_prefill_workspace_bytes(const gdn_mixer_args* args) {
+    gdn::CkptList ck;
+    gdn::MixParams p;
+    const int32_t st = validate_mixer(args, &p, &ck);
+    if (st != GDN_OK) return st;
+    if ((args->flags & GDN_FLAG_CUDA_CORE_PREFILL) || !gdn::prefill_prep_supported(p, args->head_k_dim,
+                                                                                 args->act_dtype))
+        return 0;
+    size_t off[4];
+    ok();
+    return (int64_t)gdn::prefill_ws_layout(args->batch, args->seq_len, args->num_k_heads, args->num_v_heads,
+                                           args->head_k_dim, off);
+}
+
+int32_t gdn_mixer_prefill_ws(const gdn_mixer_args* args, void* workspace, int64_t workspace_bytes, void* stream) {
+    gdn::CkptList ck;
+    gdn::MixParams p;
+    int32_t st = validate_mixer(args, &p, &ck);
+    if (st != GDN_OK) return st;
+    if ((args->flags & GDN_FLAG_CUDA_CORE_PREFILL) || !gdn::prefill_prep_supported(p, args->head_k_dim,
+                                                                                 args->act_dtype))
+        return gdn_mixer_prefill(args, stream);  // needs no workspace
+    size_t off[4];
+    const size_t need = gdn::prefill_ws_layout(args->batch, args->seq_len, args->num_k_heads, args->num_v_heads,
+                                               args->head_k_dim, off);
+    if (!workspace || workspace_bytes < 0 || (size_t)workspace_bytes < need)
+        return fail(GDN_ERR_INVALID_ARG, "workspace of %lld bytes needed (got %lld)", (long long)need,
+                    (long long)workspace_bytes);
+    if (!aligned16(workspace)) return fail(GDN_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
+    unsigned char* base = static_cast<unsigned char*>(workspace);
+    gdn::PrefillWs ws;
+    ws.qkv = base + off[0];
+    ws.nrm = reinterpret_cast<float*>(base + off[1]);
+    ws.gate = reinterpret_cast<float*>(base + off[2]);
+    ws.tp = reinterpret_cast<float*>(base + off[3]);
+    ws.nc = (args->seq_len + 63) / 64;
+    ws.tp_len = ws.nc * 64;
+    cudaError_t e = gdn::launch_prefill_prep(p, ws, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_status(e, "gdn_mixer_prefill_ws preparation launch");
+    e = gdn::launch_prefill_seq(p, ck, ws, static_cast<cudaStream_t>(stream));
+    return cuda_status(e, "gdn_mixer_prefill_ws sequential launch");
+}
+
 int32_t gdn_selftest_umma(int32_t mode, const float* A, const float* B, float* D, void* stream) {
-    if (mode < 0 || mode > 3) return fail(GDN_ERR_INVALID_ARG, "mode %d not in 0..3", mode);
+    if (mode < 0 || mode > 6) return fail(GDN_ERR_INVALID_ARG, "mode %d not in 0..6", mode);
     if (!A || !B || !D) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
     const void* ptrs[] = {A, B, D};
     for (const void* ptr : ptrs)

@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include "../../include/gdn_b200.h"
+#include "gdn_prefill_ws.cuh"
 
 namespace gdn {
 
@@ -69,6 +70,12 @@ unsigned int umma_device_error(bool clear);
 cudaError_t launch_prefill_tc(const MixParams& p, const CkptList& ck, int d, int dtype, cudaStream_t s,
                               bool* supported);
 unsigned int prefill_tc_device_error(bool clear);
+// two-kernel chunked prefill: parallel preparation pass, then the sequential pass
+bool prefill_prep_supported(const MixParams& p, int d, int dtype);
+cudaError_t launch_prefill_prep(const MixParams& p, const PrefillWs& ws, cudaStream_t s);
+unsigned int prefill_prep_device_error(bool clear);
+cudaError_t launch_prefill_seq(const MixParams& p, const CkptList& ck, const PrefillWs& ws, cudaStream_t s);
+unsigned int prefill_seq_device_error(bool clear);
 cudaError_t launch_prefill(const MixParams& p, const CkptList& ck, int d, int dtype, bool mixer,
                            cudaStream_t s, bool* supported);
 cudaError_t launch_conv1d(int B, int C, int T, int K, int dtype, const void* x, const void* w,

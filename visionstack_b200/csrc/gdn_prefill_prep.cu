@@ -1,0 +1,413 @@
+// K2: parallel preparation pass of the two-kernel chunked prefill.
+//
+// One CTA per (batch row, key head kh, chunk of C = 64 tokens), every chunk at
+// once: this is the part of the chunked algorithm (deltanet.py:266-343) that
+// does not depend on the recurrent state, so it runs fully parallel and the
+// sequential kernel (gdn_prefill_seq.cu) is left with the state-touching
+// products only.  Per CTA:
+//
+//   1. raw q / k rows of key head kh and v rows of its `rep` value heads,
+//      tokens t0-3 .. t0+63, arrive by tensor-map loads (the 3 extra rows are
+//      the conv history; rows before the sequence start come from the conv
+//      state, or are absent);
+//   2. causal conv + SiLU (deltanet.py:41-90, per-tap rounding to the
+//      activation dtype), written to the workspace in bf16 - exactly the
+//      values the reference feeds to the delta rule;
+//   3. L2-norm factors rq = (|q|^2 + 1e-6)^-1/2, rk likewise (config.py:114-115);
+//   4. [K;Q] (normalised, q times dk^-1/2, rounded to tf32) in swizzled shared
+//      memory and one tcgen05 MMA: G = K K^T, P0 = Q K^T;
+//   5. per value head h of the key head: beta = sigmoid(b) rounded,
+//      g = -exp(A_log) softplus(a + dt_bias), gamma = cumsum(g)
+//      (deltanet.py:516-517, 278-281); A = tril(beta_i G_ij e^{gamma_i-gamma_j}, -1),
+//      P = P0 o e^{gamma_i-gamma_j} (j <= i), T = (I + A)^-1 by forward
+//      substitution in fp32 (the reference's triangular solve,
+//      deltanet.py:93-162, restated);
+//   6. T and P, rounded to tf32, are written as ready-made K-major 128-byte
+//      swizzled operand images that the sequential kernel copies straight
+//      into shared memory.
+//
+// Workspace (one call; sizes from gdn_prefill_workspace_bytes):
+//   qkv   bf16 [B][NC*64][conv_dim]      conv + SiLU outputs (tokens >= T are 0)
+//   nrm   fp32 [B][Hk][NC][2][64]        rq, rk
+//   gate  fp32 [B][Hv][NC][2][64]        beta, gamma (within the chunk)
+//   tp    fp32 [B][Hv][NC][2][64*64]     T image, P image
+#include "gdn_async.cuh"
+#include "gdn_common.cuh"
+#include "gdn_kernels.cuh"
+#include "gdn_prefill_ws.cuh"
+#include "gdn_tmap.h"
+#include "gdn_umma.cuh"
+
+namespace gdn {
+namespace pprep {
+
+constexpr int D = 128, C = 64, NT = 256, HIST = 3, ROWS = C + HIST;
+constexpr uint32_t GROUP_BYTES = ROWS * D * 2;  // raw rows of one 128-channel group, bf16
+constexpr int MAX_REP = 4;
+constexpr int A_STRIDE = 68;                     // floats per row of an A matrix (conflict-free row writes)
+constexpr uint32_t A_BYTES = C * A_STRIDE * 4;
+
+__host__ __device__ constexpr uint32_t region0_bytes(int rep) {
+    const uint32_t stage = (uint32_t)(2 + rep) * GROUP_BYTES;
+    const uint32_t kq = 128u * D * 4u;
+    const uint32_t am = (uint32_t)rep * A_BYTES;
+    const uint32_t m = stage > kq ? stage : kq;
+    return ((m > am ? m : am) + 1023u) & ~1023u;
+}
+// small vectors after region 0 (floats): rq[64], rk[64], beta[MAX_REP][64], gamma[MAX_REP][64]
+constexpr int V_RQ = 0, V_RK = 64, V_B = 128, V_G = 128 + 64 * MAX_REP, V_END = 128 + 128 * MAX_REP;
+__host__ __device__ constexpr uint32_t smem_bytes(int rep) { return region0_bytes(rep) + V_END * 4 + 64 + 1024; }
+
+using TA = __nv_bfloat16;
+
+__device__ __forceinline__ float bf_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
+    const __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&t);
+}
+
+__global__ void __launch_bounds__(NT, 2)
+    prefill_prep_kernel(const MixParams p, const PrefillWs ws, const __grid_constant__ CUtensorMap tm_mixed) {
+    extern __shared__ unsigned char raw[];
+    const uint32_t raw_addr = smem_u32(raw);
+    unsigned char* sm = raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+    const int rep = p.Hv / p.Hk;
+    const uint32_t R0 = region0_bytes(rep);
+    float* vec = reinterpret_cast<float*>(sm + R0);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + R0 + V_END * 4);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + R0 + V_END * 4 + 16);
+    const uint32_t bar_ld = smem_u32(&bars[0]), bar_mma = smem_u32(&bars[1]);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int NC = ws.nc;
+    const int c = blockIdx.x % NC;
+    const int bk = blockIdx.x / NC;
+    const int kh = bk % p.Hk, b = bk / p.Hk;
+    const int t0 = c * C;
+    const int T = p.T;
+    const int ngroups = 2 + rep;
+    const int conv_dim = 2 * p.Hk * D + p.Hv * D;
+    const TA* cs_in = static_cast<const TA*>(p.cs_in);
+
+    if (tid == 0) {
+        mbar_init(bar_ld, 1);
+        mbar_init(bar_mma, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        umma::tmem_alloc(smem_u32(tslot), 64);
+        umma::tmem_relinquish();
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = *tslot;
+
+    // group g: 0 = q of kh, 1 = k of kh, 2 + r = v of value head kh*rep + r
+    auto group_channel = [&](int g) -> int {
+        return g == 0 ? kh * D : (g == 1 ? p.Hk * D + kh * D : 2 * p.Hk * D + (kh * rep + g - 2) * D);
+    };
+    if (tid == 0) {
+        mbar_arrive_expect_tx(bar_ld, (uint32_t)ngroups * GROUP_BYTES);
+        for (int g = 0; g < ngroups; ++g)
+            tma_load_3d(smem_u32(sm + g * GROUP_BYTES), &tm_mixed, group_channel(g), t0 - HIST, b, bar_ld);
+    }
+    // gate inputs of every value head of this key head (threads 64r..64r+63 ->
+    // value head r, one token each), loaded while the rows arrive
+    const int g_r = tid >> 6, g_t = tid & 63;
+    float raw_a = 0.f, raw_b = 0.f;
+    if (g_r < rep && t0 + g_t < T) {
+        const size_t ai = (size_t)b * p.as_b + (size_t)(t0 + g_t) * p.as_t + kh * rep + g_r;
+        raw_a = Act<TA>::ld(static_cast<const TA*>(p.a) + ai);
+        raw_b = Act<TA>::ld(static_cast<const TA*>(p.b) + ai);
+    }
+    const bool ld_ok = mbar_wait_bounded(bar_ld, 0, GDN_DEVERR_TMA_TIMEOUT);
+    if (__syncthreads_or(!ld_ok)) {
+        // the copies may still land: wait for them (bounded) before the CTA exits
+        if (tid == 0) mbar_wait_bounded(bar_ld, 0, GDN_DEVERR_TMA_TIMEOUT);
+        __syncthreads();
+        if (warp == 0) umma::tmem_dealloc(tmem, 64);
+        return;
+    }
+
+    // ---- conv + SiLU, in place: thread -> an adjacent channel pair of one group ----
+    for (int pr = tid; pr < ngroups * (D / 2); pr += NT) {
+        const int g = pr / (D / 2), ch = (pr % (D / 2)) * 2;
+        const int gc = group_channel(g) + ch;
+        unsigned char* gbase = sm + g * GROUP_BYTES;
+        const TA* cw = static_cast<const TA*>(p.convw) + (size_t)gc * 4;
+        float w0[4], w1[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            w0[j] = Act<TA>::ldg(cw + j);
+            w1[j] = Act<TA>::ldg(cw + 4 + j);
+        }
+        // history x[-3..-1] of both channels
+        float h0[3], h1[3];
+        if (c > 0) {
+#pragma unroll
+            for (int i = 0; i < HIST; ++i) {
+                const uint32_t v = *reinterpret_cast<const uint32_t*>(gbase + i * D * 2 + ch * 2);
+                h0[i] = bf_lo(v);
+                h1[i] = bf_hi(v);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < HIST; ++i) {
+                h0[i] = cs_in ? Act<TA>::ld(cs_in + ((size_t)b * conv_dim + gc) * HIST + i) : 0.f;
+                h1[i] = cs_in ? Act<TA>::ld(cs_in + ((size_t)b * conv_dim + gc + 1) * HIST + i) : 0.f;
+            }
+        }
+        // window registers: x1 = one token back, x2, x3 = three back
+        float a1 = h0[2], a2 = h0[1], a3 = h0[0];
+        float b1 = h1[2], b2 = h1[1], b3 = h1[0];
+        __nv_bfloat16* gout = static_cast<__nv_bfloat16*>(ws.qkv) + ((size_t)b * ws.tp_len + t0) * conv_dim + gc;
+#pragma unroll 4
+        for (int t = 0; t < C; ++t) {
+            uint32_t* cell = reinterpret_cast<uint32_t*>(gbase + (t + HIST) * D * 2 + ch * 2);
+            const uint32_t xv = *cell;
+            const float x0 = bf_lo(xv), y0 = bf_hi(xv);
+            const int tg = t0 + t;
+            uint32_t outv = 0u;
+            if (tg < T) {
+                const int valid = (cs_in || c > 0) ? HIST : (tg < HIST ? tg : HIST);
+                const float ca = conv4_taps<TA>(x0, a1, a2, a3, w0[0], w0[1], w0[2], w0[3], valid);
+                const float cb = conv4_taps<TA>(y0, b1, b2, b3, w1[0], w1[1], w1[2], w1[3], valid);
+                outv = pack_bf2(__fdividef(ca, 1.0f + __expf(-ca)), __fdividef(cb, 1.0f + __expf(-cb)));
+            }
+            a3 = a2; a2 = a1; a1 = x0;
+            b3 = b2; b2 = b1; b1 = y0;
+            *cell = outv;
+            *reinterpret_cast<uint32_t*>(gout + (size_t)t * conv_dim) = outv;
+        }
+    }
+    __syncthreads();
+
+    // ---- L2-norm factors of q and k: warp per token ----
+    float* sRQ = vec + V_RQ;
+    float* sRK = vec + V_RK;
+    for (int t = warp; t < C; t += NT / 32) {
+        const uint2 qv = *reinterpret_cast<const uint2*>(sm + 0 * GROUP_BYTES + (t + HIST) * D * 2 + lane * 8);
+        const uint2 kv = *reinterpret_cast<const uint2*>(sm + 1 * GROUP_BYTES + (t + HIST) * D * 2 + lane * 8);
+        const float q0 = bf_lo(qv.x), q1 = bf_hi(qv.x), q2 = bf_lo(qv.y), q3 = bf_hi(qv.y);
+        const float k0 = bf_lo(kv.x), k1 = bf_hi(kv.x), k2 = bf_lo(kv.y), k3 = bf_hi(kv.y);
+        float sq = q0 * q0 + q1 * q1 + q2 * q2 + q3 * q3;
+        float sk = k0 * k0 + k1 * k1 + k2 * k2 + k3 * k3;
+        sq = warp_sum(sq);
+        sk = warp_sum(sk);
+        if (lane == 0) {
+            const float rq = rsqrtf(sq + 1e-6f), rk = rsqrtf(sk + 1e-6f);
+            sRQ[t] = rq;
+            sRK[t] = rk;
+            float* nrm = ws.nrm + (((size_t)b * p.Hk + kh) * NC + c) * 128;
+            nrm[t] = rq;
+            nrm[64 + t] = rk;
+        }
+    }
+    __syncthreads();
+
+    // ---- [K;Q] tf32 operand (rows 0..63 K, 64..127 Q) over the staging area ----
+    uint2 kq_raw[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+        const int idx = tid + u * NT, r = idx >> 5, c4 = (idx & 31) * 4;
+        const int g = r < C ? 1 : 0, t = r & 63;
+        kq_raw[u] = *reinterpret_cast<const uint2*>(sm + g * GROUP_BYTES + (t + HIST) * D * 2 + c4 * 2);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+        const int idx = tid + u * NT, r = idx >> 5, c4 = (idx & 31) * 4;
+        const int t = r & 63;
+        const uint2 v = kq_raw[u];
+        float4 f = make_float4(bf_lo(v.x), bf_hi(v.x), bf_lo(v.y), bf_hi(v.y));
+        if (r < C) {
+            const float s = sRK[t];
+            f = make_float4(f.x * s, f.y * s, f.z * s, f.w * s);
+        } else {
+            const float s = sRQ[t];
+            f = make_float4((f.x * s) * p.q_scale, (f.y * s) * p.q_scale, (f.z * s) * p.q_scale,
+                            (f.w * s) * p.q_scale);
+        }
+        *reinterpret_cast<float4*>(sm + umma::kmajor_off(r, c4, 128)) = umma::tf32_rna4(f);
+    }
+    fence_proxy_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+        umma::fence_after_sync();
+        const uint32_t sb = smem_u32(sm);
+        const uint32_t idesc = umma::idesc_tf32(128, 64, 0, 0);
+        for (int kk = 0; kk < D / 8; ++kk)
+            umma::mma_tf32(tmem, umma::desc_kmajor(sb, 128, kk), umma::desc_kmajor(sb, 128, kk), idesc, kk > 0);
+        umma::mma_commit(bar_mma);
+    }
+
+    // ---- gates and gamma while the MMA runs ----
+    float* sB = vec + V_B;
+    float* sG = vec + V_G;
+    if (g_r < rep) {
+        const int h = kh * rep + g_r;
+        float beta = 0.f, g = 0.f;
+        if (t0 + g_t < T) {
+            beta = Act<TA>::round(sigmoid_f(raw_b));
+            g = -expf(p.A_log[h]) * softplus_f(raw_a + p.dt_bias[h]);
+        }
+        sB[g_r * 64 + g_t] = beta;
+        sG[g_r * 64 + g_t] = g;
+    }
+    __syncthreads();
+    if (tid < rep) {
+        // sequential cumsum (the reference's torch.cumsum over the chunk)
+        float acc = 0.f;
+        float* gr = sG + tid * 64;
+        for (int t = 0; t < C; ++t) {
+            acc += gr[t];
+            gr[t] = acc;
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < rep * C; i += NT) {
+        const int r = i / C, t = i % C;
+        float* gate = ws.gate + (((size_t)b * p.Hv + kh * rep + r) * NC + c) * 128;
+        gate[t] = sB[r * 64 + t];
+        gate[64 + t] = sG[r * 64 + t];
+    }
+
+    const bool mma_ok = mbar_wait_bounded(bar_mma, 0, GDN_DEVERR_MMA_TIMEOUT);
+    umma::fence_after_sync();
+    if (__syncthreads_or(!mma_ok)) {
+        if (tid == 0) mbar_wait_bounded(bar_mma, 0, GDN_DEVERR_MMA_TIMEOUT);
+        umma::fence_before_sync();
+        __syncthreads();
+        if (warp == 0) umma::tmem_dealloc(tmem, 64);
+        return;
+    }
+
+    // ---- A (shared memory) and P (operand image) per value head from G, P0 ----
+    {
+        const int q4 = warp & 3;
+        const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
+        const bool g_rows = q4 < 2;
+        const int t = g_rows ? lane + 32 * q4 : lane + 32 * (q4 - 2);
+        float v[64];
+        {
+            float w[32];
+            umma::tmem_ld32(tmem + lane_base + 0, w);
+            umma::tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = w[j];
+            umma::tmem_ld32(tmem + lane_base + 32, w);
+            umma::tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[32 + j] = w[j];
+        }
+        for (int r = warp >> 2; r < rep; r += 2) {
+            const float* gr = sG + r * 64;
+            const float gt = gr[t];
+            if (g_rows) {
+                const float bt = sB[r * 64 + t];
+                float* arow = reinterpret_cast<float*>(sm + r * A_BYTES) + t * A_STRIDE;
+#pragma unroll
+                for (int j = 0; j < C; j += 4) {
+                    float4 a;
+                    a.x = j + 0 < t ? (bt * v[j + 0]) * __expf(gt - gr[j + 0]) : 0.f;
+                    a.y = j + 1 < t ? (bt * v[j + 1]) * __expf(gt - gr[j + 1]) : 0.f;
+                    a.z = j + 2 < t ? (bt * v[j + 2]) * __expf(gt - gr[j + 2]) : 0.f;
+                    a.w = j + 3 < t ? (bt * v[j + 3]) * __expf(gt - gr[j + 3]) : 0.f;
+                    *reinterpret_cast<float4*>(arow + j) = a;
+                }
+            } else {
+                unsigned char* img = reinterpret_cast<unsigned char*>(
+                    ws.tp + ((((size_t)b * p.Hv + kh * rep + r) * NC + c) * 2 + 1) * (C * C));
+#pragma unroll
+                for (int j = 0; j < C; j += 4) {
+                    float4 a;
+                    a.x = j + 0 <= t ? umma::tf32_rna(v[j + 0] * __expf(gt - gr[j + 0])) : 0.f;
+                    a.y = j + 1 <= t ? umma::tf32_rna(v[j + 1] * __expf(gt - gr[j + 1])) : 0.f;
+                    a.z = j + 2 <= t ? umma::tf32_rna(v[j + 2] * __expf(gt - gr[j + 2])) : 0.f;
+                    a.w = j + 3 <= t ? umma::tf32_rna(v[j + 3] * __expf(gt - gr[j + 3])) : 0.f;
+                    *reinterpret_cast<float4*>(img + umma::kmajor_off(t, j, C)) = a;
+                }
+            }
+        }
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+
+    // ---- T = (I + A)^-1 by forward substitution: two warps per value head ----
+    // lane l of warp 2r + hf owns column j = 32 hf + l of T; row i of T is
+    // e_i - sum_{k<i} A[i][k] T[k] (T[k][j] = 0 for k < j).
+    if (warp < 2 * rep) {
+        const int r = warp >> 1, hf = warp & 1, j = 32 * hf + lane;
+        const float* A = reinterpret_cast<const float*>(sm + r * A_BYTES);
+        float x[C];
+#pragma unroll
+        for (int i = 0; i < C; ++i) {
+            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+            const int k0 = hf ? 32 : 0;  // rows above the column block are zero
+#pragma unroll
+            for (int k = 0; k < i; k += 4) {
+                if (k + 3 < k0) continue;
+                const float4 a = *reinterpret_cast<const float4*>(A + i * A_STRIDE + k);
+                if (k + 0 < i && k + 0 >= k0) s0 = fmaf(a.x, x[k + 0], s0);
+                if (k + 1 < i && k + 1 >= k0) s1 = fmaf(a.y, x[k + 1], s1);
+                if (k + 2 < i && k + 2 >= k0) s2 = fmaf(a.z, x[k + 2], s2);
+                if (k + 3 < i && k + 3 >= k0) s3 = fmaf(a.w, x[k + 3], s3);
+            }
+            x[i] = (i == j ? 1.f : 0.f) - ((s0 + s1) + (s2 + s3));
+        }
+        unsigned char* img = reinterpret_cast<unsigned char*>(
+            ws.tp + (((size_t)b * p.Hv + kh * rep + r) * NC + c) * 2 * (C * C));
+#pragma unroll
+        for (int i = 0; i < C; ++i) *reinterpret_cast<float*>(img + umma::kmajor_off(i, j, C)) = umma::tf32_rna(x[i]);
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) umma::tmem_dealloc(tmem, 64);
+}
+
+}  // namespace pprep
+
+bool prefill_prep_supported(const MixParams& p, int d, int dtype) {
+    const int rep = p.Hk > 0 ? p.Hv / p.Hk : 0;
+    auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    return dtype == GDN_DTYPE_BF16 && d == 128 && p.K == 4 && (rep == 1 || rep == 2 || rep == 4) && al(p.mixed) &&
+           (p.ms_b % 8) == 0 && (p.ms_t % 8) == 0 && al(p.z) && (p.zs_b % 8) == 0 && (p.zs_t % 8) == 0;
+}
+
+cudaError_t launch_prefill_prep(const MixParams& p, const PrefillWs& ws, cudaStream_t s) {
+    const int rep = p.Hv / p.Hk;
+    const uint64_t conv_dim = 2ull * p.Hk * 128 + (uint64_t)p.Hv * 128;
+    CUtensorMap tm_mixed;
+    if (!encode_tmap_3d_bf16(&tm_mixed, p.mixed, conv_dim, (uint64_t)p.T, (uint64_t)p.B, (uint64_t)p.ms_t * 2,
+                             (uint64_t)p.ms_b * 2, 128, pprep::ROWS))
+        return cudaErrorInvalidValue;
+    const int bytes = (int)pprep::smem_bytes(rep);
+    static int attr_bytes[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (attr_bytes[dev] < bytes) {
+        e = cudaFuncSetAttribute(pprep::prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e != cudaSuccess) return e;
+        attr_bytes[dev] = bytes;
+    }
+    const int grid = p.B * p.Hk * ws.nc;
+    pprep::prefill_prep_kernel<<<grid, pprep::NT, bytes, s>>>(p, ws, tm_mixed);
+    return cudaGetLastError();
+}
+
+unsigned int prefill_prep_device_error(bool clear) {
+    unsigned int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+    if (clear && v) {
+        const unsigned int zero = 0;
+        cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+    }
+    return v;
+}
+
+}  // namespace gdn

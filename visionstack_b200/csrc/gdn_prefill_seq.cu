@@ -1,0 +1,525 @@
+// K3 (two-kernel form): the sequential inter-chunk pass of the chunked
+// prefill, after gdn_prefill_prep.cu has produced every chunk's conv outputs,
+// norm factors, gates and T / P operand images.
+//
+// One CTA per (batch row, value head) chain walks its chunks of C = 64 tokens.
+// The state lives in tensor memory, TRANSPOSED: lane = value dim dv, column =
+// key dim dk, so that it is directly the A operand of the next MMA (tcgen05
+// reads A from tensor memory).  Two copies: the fp32 master and its tf32
+// (round-to-nearest) operand copy.  Per chunk, with K, Q the normalised k and
+// q rows (q times dk^-1/2), V the v rows, beta and gamma = cumsum(g) of the
+// chunk, T = (I + A)^-1 and P = (Q K^T) o e^{gamma_i - gamma_j} (j <= i):
+//
+//   MMA-b  [Y^T | O1^T] = S^T [K;Q]^T                  (M128 N128 K128, A from TMEM)
+//   CUDA   Z^T = beta (V - e^gamma Y)^T                 (to TMEM)
+//   MMA-c  v_new^T = Z^T T^T                            (M128 N64  K64,  A from TMEM)
+//   CUDA   v_new^T and (e^{gamma_C - gamma} v_new)^T, tf32 (to TMEM)
+//   MMA-d  D^T = v_new^T P^T                            (M128 N64  K64)
+//   MMA-e  dS^T = (e^{gamma_C - gamma} v_new)^T K        (M128 N128 K64)
+//   CUDA   S^T <- e^{gamma_C} S^T + dS^T (master and operand copy), boundary
+//          checkpoints, final state; in parallel, the output rows
+//          O = e^gamma O1 + D through the gated RMSNorm
+//
+// i.e. the reference's v_new = U - W S with U = T (beta V), W = T (beta K e^gamma)
+// and O = (Q e^gamma) S + P v_new, S' = e^{gamma_C} S + (K e^{gamma_C-gamma})^T v_new
+// (deltanet.py:323-389), regrouped and transposed.  Inputs of the next chunk
+// stream in by tensor-map / bulk copies while the current one computes.
+#include "gdn_async.cuh"
+#include "gdn_common.cuh"
+#include "gdn_conv_windows.cuh"
+#include "gdn_kernels.cuh"
+#include "gdn_prefill_ws.cuh"
+#include "gdn_tmap.h"
+#include "gdn_umma.cuh"
+
+namespace gdn {
+namespace pseq {
+
+constexpr int D = 128, C = 64, NT = 256;
+// shared memory (bytes from the 1024-aligned base)
+constexpr uint32_t R_KQ = 0;        // [K;Q] K-major [128][dk] tf32, 64 KB (B of MMA-b)
+constexpr uint32_t R_KM = 65536;    // K MN-major [tok][dk] tf32, 32 KB (B of MMA-e)
+constexpr uint32_t R_TP = 98304;    // T image, P image (16 KB each; B of MMA-c / MMA-d)
+constexpr uint32_t R_QS = 131072;   // q rows bf16 [64][128]
+constexpr uint32_t R_KS = 147456;   // k rows
+constexpr uint32_t R_VS = 163840;   // v rows
+constexpr uint32_t R_ZS = 180224;   // z rows
+constexpr uint32_t R_VEC = 196608;  // rq[64] rk[64] beta[64] gamma[64] as loaded
+constexpr uint32_t R_SCR = R_VEC + 1024;
+constexpr int S_B = 0, S_G = 64, S_EG = 128, S_EF = 192, S_F = 256, S_NW = 320, S_PART = 448, S_RSTD = 704,
+              S_END = 768;  // floats
+constexpr uint32_t R_BAR = R_SCR + S_END * 4;
+constexpr uint32_t SMEM_BYTES = R_BAR + 64 + 1024;
+// tensor memory columns
+constexpr uint32_t C_MS = 0, C_OP = 128, C_YO = 256, C_Z = 384, C_V = 448, T_COLS = 512;
+
+using TA = __nv_bfloat16;
+
+__device__ __forceinline__ float bf_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+__device__ __forceinline__ float bf_at(const unsigned char* base, int idx) {
+    return __uint_as_float((uint32_t)(*reinterpret_cast<const uint16_t*>(base + 2 * idx)) << 16);
+}
+
+__device__ __forceinline__ void wg_sync(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+
+__global__ void __launch_bounds__(NT, 1)
+    prefill_seq_kernel(const MixParams p, const CkptList ck, const PrefillWs ws,
+                       const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_z) {
+    extern __shared__ unsigned char raw[];
+    const uint32_t raw_addr = smem_u32(raw);
+    unsigned char* sm = raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+    const uint32_t sb = smem_u32(sm);
+    float* scr = reinterpret_cast<float*>(sm + R_SCR);
+    float* sB = scr + S_B;
+    float* sG = scr + S_G;
+    float* sEG = scr + S_EG;
+    float* sEF = scr + S_EF;
+    float* sF = scr + S_F;
+    float* sNW = scr + S_NW;
+    float* sPart = scr + S_PART;
+    float* sRstd = scr + S_RSTD;
+    const float* vec = reinterpret_cast<const float*>(sm + R_VEC);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + R_BAR);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + R_BAR + 48);
+    const uint32_t bar_qk = smem_u32(&bars[0]), bar_v = smem_u32(&bars[1]), bar_z = smem_u32(&bars[2]),
+                   bar_tp = smem_u32(&bars[3]), bar_mma = smem_u32(&bars[4]);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int wg = warp >> 2, q4 = warp & 3;
+    const int dv = 32 * q4 + lane;                       // this thread's tensor-memory lane
+    const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
+    const int bh = blockIdx.x;
+    const int b = bh / p.Hv, h = bh - (bh / p.Hv) * p.Hv;
+    const int rep = p.Hv / p.Hk, kh = h / rep;
+    const int T = p.T, NC = ws.nc;
+
+    if (tid == 0) {
+        for (int i = 0; i < 5; ++i) mbar_init(smem_u32(&bars[i]), 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        umma::tmem_alloc(smem_u32(tslot), T_COLS);
+        umma::tmem_relinquish();
+    }
+    write_conv_windows<TA, D, D, NT>(p, ck, b, h, kh, rep);
+    if (tid < D) sNW[tid] = Act<TA>::ldg(static_cast<const TA*>(p.normw) + tid);
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = *tslot;
+
+    // initial state, transposed: lane dv, column dk (warpgroup wg: dk 64 wg .. 64 wg + 63)
+    for (int c0 = 64 * wg; c0 < 64 * wg + 64; c0 += 32) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = p.S_in ? __ldcs(p.S_in + ((size_t)bh * D + c0 + j) * D + dv) : 0.f;
+        umma::tmem_st32(tmem + lane_base + C_MS + c0, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = umma::tf32_rna(v[j]);
+        umma::tmem_st32(tmem + lane_base + C_OP + c0, v);
+    }
+    umma::tmem_wait_st();
+
+    const int v_ch = 2 * p.Hk * D + h * D;
+    auto issue_qk = [&](int cc) {
+        mbar_arrive_expect_tx(bar_qk, 2u * C * D * 2u + 1024u);
+        tma_load_3d(sb + R_QS, &tm_qkv, kh * D, cc * C, b, bar_qk);
+        tma_load_3d(sb + R_KS, &tm_qkv, p.Hk * D + kh * D, cc * C, b, bar_qk);
+        bulk_load(sb + R_VEC, ws.nrm + (((size_t)b * p.Hk + kh) * NC + cc) * 128, 512, bar_qk);
+        bulk_load(sb + R_VEC + 512, ws.gate + (((size_t)b * p.Hv + h) * NC + cc) * 128, 512, bar_qk);
+    };
+    auto issue_v = [&](int cc) {
+        mbar_arrive_expect_tx(bar_v, (uint32_t)C * D * 2u);
+        tma_load_3d(sb + R_VS, &tm_qkv, v_ch, cc * C, b, bar_v);
+    };
+    auto issue_z = [&](int cc) {
+        mbar_arrive_expect_tx(bar_z, (uint32_t)C * D * 2u);
+        tma_load_3d(sb + R_ZS, &tm_z, h * D, cc * C, b, bar_z);
+    };
+    auto issue_tp = [&](int cc) {
+        mbar_arrive_expect_tx(bar_tp, 2u * C * C * 4u);
+        bulk_load(sb + R_TP, ws.tp + (((size_t)b * p.Hv + h) * NC + cc) * (2 * C * C), 2u * C * C * 4u, bar_tp);
+    };
+    // copies issued / waited per barrier (issuing thread tracks issues; waits are uniform)
+    int n_qk = 0, n_v = 0, n_z = 0, n_tp = 0;
+    if (tid == 0) {
+        issue_qk(0);
+        issue_v(0);
+        issue_tp(0);
+        n_qk = n_v = n_tp = 1;
+    }
+    if (tid == 128) {
+        issue_z(0);
+        n_z = 1;
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+
+    const uint32_t idesc_b = umma::idesc_tf32(128, 128, 0, 0);
+    const uint32_t idesc_c = umma::idesc_tf32(128, 64, 0, 0);
+    const uint32_t idesc_e = umma::idesc_tf32(128, 128, 0, 1);
+    uint32_t mma_phase = 0;
+    int w_qk = 0, w_v = 0, w_z = 0, w_tp = 0;  // completed waits
+    bool failed = false, mma_pending = false;
+    int ck_i = 0;
+    auto mma_wait = [&]() -> bool {
+        const bool ok = mbar_wait_bounded(bar_mma, mma_phase & 1u, GDN_DEVERR_MMA_TIMEOUT);
+        ++mma_phase;
+        umma::fence_after_sync();
+        return !__syncthreads_or(!ok);
+    };
+    auto wait_all = [&](uint32_t bar, int& count) -> bool {
+        const bool ok = mbar_wait_bounded(bar, (uint32_t)count & 1u, GDN_DEVERR_TMA_TIMEOUT);
+        ++count;
+        return !__syncthreads_or(!ok);
+    };
+
+    for (int c = 0; c < NC; ++c) {
+        const int t0 = c * C;
+        // ---------------- 1. operands of the chunk ----------------
+        if (!wait_all(bar_qk, w_qk)) {
+            failed = true;
+            break;
+        }
+        if (tid < C) {
+            const float gC = vec[192 + C - 1], gt = vec[192 + tid];
+            sB[tid] = vec[128 + tid];
+            sG[tid] = gt;
+            sEG[tid] = expf(gt);
+            sEF[tid] = expf(gC - gt);
+        }
+#pragma unroll 4
+        for (int u = 0; u < 16; ++u) {
+            const int idx = tid + u * NT, r = idx >> 5, c4 = (idx & 31) * 4, t = r & 63;
+            const uint2 raw2 =
+                *reinterpret_cast<const uint2*>(sm + (r < C ? R_KS : R_QS) + t * D * 2 + c4 * 2);
+            float4 f = make_float4(bf_lo(raw2.x), bf_hi(raw2.x), bf_lo(raw2.y), bf_hi(raw2.y));
+            if (r < C) {
+                const float s = vec[64 + t];
+                f = make_float4(f.x * s, f.y * s, f.z * s, f.w * s);
+                *reinterpret_cast<float4*>(sm + R_KM + umma::mnmajor_off(t, c4, C)) = umma::tf32_rna4(f);
+            } else {
+                const float s = vec[t];
+                f = make_float4((f.x * s) * p.q_scale, (f.y * s) * p.q_scale, (f.z * s) * p.q_scale,
+                                (f.w * s) * p.q_scale);
+            }
+            *reinterpret_cast<float4*>(sm + R_KQ + umma::kmajor_off(r, c4, 128)) = umma::tf32_rna4(f);
+        }
+        fence_proxy_async_smem();
+        umma::fence_before_sync();
+        __syncthreads();
+        // checkpoints strictly inside this chunk keep the k rows (and rk) until step 5
+        const bool has_sub = ck_i < ck.n && ck.off[ck_i] > t0 && ck.off[ck_i] - t0 < C;
+        // ---------------- 2. MMA-b; next chunk's q/k copies ----------------
+        if (tid == 0) {
+            umma::fence_after_sync();
+            for (int kk = 0; kk < D / 8; ++kk)
+                umma::mma_tf32_ta(tmem + C_YO, tmem + C_OP + kk * 8, umma::desc_kmajor(sb + R_KQ, 128, kk), idesc_b,
+                                  kk > 0);
+            umma::mma_commit(bar_mma);
+            if (c + 1 < NC && !has_sub) {
+                issue_qk(c + 1);
+                ++n_qk;
+            }
+        }
+        mma_pending = true;
+        if (!mma_wait()) {
+            failed = true;
+            break;
+        }
+        mma_pending = false;
+        if (!wait_all(bar_v, w_v)) {
+            failed = true;
+            break;
+        }
+        // ---------------- 3. Z^T = beta (V - e^gamma Y)^T ----------------
+        if (wg == 0) {
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                float y[32];
+                umma::tmem_ld32(tmem + lane_base + C_YO + 32 * hf, y);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int t = 32 * hf + j;
+                    const float vv = bf_at(sm + R_VS, t * D + dv);
+                    y[j] = umma::tf32_rna(sB[t] * (vv - sEG[t] * y[j]));
+                }
+                umma::tmem_st32(tmem + lane_base + C_Z + 32 * hf, y);
+            }
+            umma::tmem_wait_st();
+        }
+        umma::fence_before_sync();
+        __syncthreads();
+        // ---------------- 4. MMA-c: v_new^T = Z^T T^T; next chunk's v copy ----------------
+        if (!wait_all(bar_tp, w_tp)) {
+            failed = true;
+            break;
+        }
+        if (tid == 0) {
+            umma::fence_after_sync();
+            for (int kk = 0; kk < C / 8; ++kk)
+                umma::mma_tf32_ta(tmem + C_V, tmem + C_Z + kk * 8, umma::desc_kmajor(sb + R_TP, C, kk), idesc_c,
+                                  kk > 0);
+            umma::mma_commit(bar_mma);
+            if (c + 1 < NC) {
+                fence_proxy_async_smem();
+                issue_v(c + 1);
+                ++n_v;
+            }
+        }
+        mma_pending = true;
+        if (!mma_wait()) {
+            failed = true;
+            break;
+        }
+        mma_pending = false;
+        // ---------------- 5a. sub-chunk checkpoints (fp32 v_new, fp32 K, state before the update) ----------------
+        // S_s = e^{gamma_{s-1}} S + sum_{t<s} e^{gamma_{s-1}-gamma_t} k_t^T v_new_t (deltanet.py:375-388)
+        while (ck_i < ck.n && ck.off[ck_i] > t0 && ck.off[ck_i] - t0 < C) {
+            const int s_off = ck.off[ck_i] - t0;
+            if (tid < C) sF[tid] = tid < s_off ? expf(sG[s_off - 1] - sG[tid]) : 0.f;
+            __syncthreads();
+            const float es = expf(sG[s_off - 1]);
+            float wv[C];
+            {
+                float v[32];
+                umma::tmem_ld32(tmem + lane_base + C_V, v);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) wv[j] = v[j] * sF[j];
+                umma::tmem_ld32(tmem + lane_base + C_V + 32, v);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) wv[32 + j] = v[j] * sF[32 + j];
+            }
+            float* dst = p.S_ckpt + ((size_t)ck.slot[ck_i] * p.B * p.Hv + bh) * (size_t)(D * D);
+#pragma unroll 1
+            for (int c0 = 64 * wg; c0 < 64 * wg + 64; c0 += 32) {
+                float m[32];
+                umma::tmem_ld32(tmem + lane_base + C_MS + c0, m);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) m[j] *= es;
+#pragma unroll
+                for (int t = 0; t < C; ++t) {
+                    const float wt = wv[t] * vec[64 + t];  // v_new * decay * rk
+                    const uint4* krow = reinterpret_cast<const uint4*>(sm + R_KS + t * D * 2 + c0 * 2);
+#pragma unroll
+                    for (int j8 = 0; j8 < 4; ++j8) {
+                        const uint4 k8 = krow[j8];
+                        const uint32_t kw[4] = {k8.x, k8.y, k8.z, k8.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            m[8 * j8 + 2 * e] = fmaf(wt, bf_lo(kw[e]), m[8 * j8 + 2 * e]);
+                            m[8 * j8 + 2 * e + 1] = fmaf(wt, bf_hi(kw[e]), m[8 * j8 + 2 * e + 1]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) __stcs(dst + (size_t)(c0 + j) * D + dv, m[j]);
+            }
+            __syncthreads();
+            ++ck_i;
+        }
+        if (tid == 0 && has_sub && c + 1 < NC) {
+            fence_proxy_async_smem();
+            issue_qk(c + 1);
+            ++n_qk;
+        }
+        // ---------------- 5b. v_new^T (tf32) and its e^{gamma_C - gamma} scaled copy ----------------
+        if (wg == 0) {
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                float v[32], w[32];
+                umma::tmem_ld32(tmem + lane_base + C_V + 32 * hf, v);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int t = 32 * hf + j;
+                    w[j] = umma::tf32_rna(v[j] * sEF[t]);
+                    v[j] = umma::tf32_rna(v[j]);
+                }
+                umma::tmem_st32(tmem + lane_base + C_V + 32 * hf, v);
+                umma::tmem_st32(tmem + lane_base + C_Z + 32 * hf, w);
+            }
+            umma::tmem_wait_st();
+        }
+        umma::fence_before_sync();
+        __syncthreads();
+        // ---------------- 6. MMA-d (D^T = v_new^T P^T), MMA-e (dS^T) ----------------
+        if (tid == 0) {
+            umma::fence_after_sync();
+            for (int kk = 0; kk < C / 8; ++kk)
+                umma::mma_tf32_ta(tmem + C_YO, tmem + C_V + kk * 8, umma::desc_kmajor(sb + R_TP + C * C * 4, C, kk),
+                                  idesc_c, kk > 0);
+            for (int kk = 0; kk < C / 8; ++kk)
+                umma::mma_tf32_ta(tmem + C_OP, tmem + C_Z + kk * 8, umma::desc_mnmajor(sb + R_KM, C, kk), idesc_e,
+                                  kk > 0);
+            umma::mma_commit(bar_mma);
+        }
+        mma_pending = true;
+        if (!mma_wait()) {
+            failed = true;
+            break;
+        }
+        mma_pending = false;
+        if (tid == 0 && c + 1 < NC) {
+            fence_proxy_async_smem();
+            issue_tp(c + 1);
+            ++n_tp;
+        }
+        // ---------------- 7. state update (warpgroup 0) || output rows (warpgroup 1) ----------------
+        if (wg == 0) {
+            const float ec = sEG[C - 1];
+            const bool last = c == NC - 1;
+#pragma unroll 1
+            for (int c0 = 0; c0 < D; c0 += 32) {
+                float m[32], d[32];
+                umma::tmem_ld32(tmem + lane_base + C_MS + c0, m);
+                umma::tmem_ld32(tmem + lane_base + C_OP + c0, d);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) m[j] = fmaf(m[j], ec, d[j]);
+                umma::tmem_st32(tmem + lane_base + C_MS + c0, m);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) d[j] = umma::tf32_rna(m[j]);
+                umma::tmem_st32(tmem + lane_base + C_OP + c0, d);
+                for (int w = ck_i; w < ck.n && ck.off[w] - t0 == C; ++w) {
+                    float* dst = p.S_ckpt + ((size_t)ck.slot[w] * p.B * p.Hv + bh) * (size_t)(D * D);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) __stcs(dst + (size_t)(c0 + j) * D + dv, m[j]);
+                }
+                if (last && p.S_out) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) __stcs(p.S_out + ((size_t)bh * D + c0 + j) * D + dv, m[j]);
+                }
+            }
+            umma::tmem_wait_st();
+        } else {
+            // O[t][dv] = e^{gamma_t} O1 + D, rounded; gated RMSNorm over dv (the 128 lanes)
+            float o[C];
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                float o1[32], dd[32];
+                umma::tmem_ld32(tmem + lane_base + C_YO + 64 + 32 * hf, o1);
+                umma::tmem_ld32(tmem + lane_base + C_YO + 32 * hf, dd);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) o[32 * hf + j] = Act<TA>::round(fmaf(sEG[32 * hf + j], o1[j], dd[j]));
+            }
+            // per-token sums of squares over this warp's 32 lanes: halving exchange,
+            // ending with tokens tb, tb + 1 in this lane
+            float sq[C];
+#pragma unroll
+            for (int t = 0; t < C; ++t) sq[t] = o[t] * o[t];
+#pragma unroll
+            for (int st = 0; st < 5; ++st) {
+                const int s = 16 >> st, half = 32 >> st;  // exchange distance, values kept after this step
+                const bool up = (lane & s) != 0;
+#pragma unroll
+                for (int k = 0; k < half; ++k) {
+                    const float send = up ? sq[k] : sq[k + half];
+                    const float keep = up ? sq[k + half] : sq[k];
+                    sq[k] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+                }
+            }
+            const int tb = ((lane >> 4) & 1) * 32 + ((lane >> 3) & 1) * 16 + ((lane >> 2) & 1) * 8 +
+                           ((lane >> 1) & 1) * 4 + (lane & 1) * 2;
+            sPart[q4 * C + tb] = sq[0];
+            sPart[q4 * C + tb + 1] = sq[1];
+            wg_sync(1);
+            if (q4 == 0) {
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    const int t = tb + k;
+                    const float ss = (sPart[t] + sPart[C + t]) + (sPart[2 * C + t] + sPart[3 * C + t]);
+                    sRstd[t] = rsqrtf(ss / (float)D + p.eps);
+                }
+            }
+            const bool zok = mbar_wait_bounded(bar_z, (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            ++w_z;
+            wg_sync(1);
+            const float nw = sNW[dv];
+            TA* out = static_cast<TA*>(p.out) + ((size_t)b * T + t0) * (size_t)(p.Hv * D) + h * D + dv;
+            if (zok) {
+#pragma unroll
+                for (int t = 0; t < C; ++t) {
+                    if (t0 + t < T) {
+                        const float y = Act<TA>::round(nw * Act<TA>::round(o[t] * sRstd[t]));
+                        const float zz = bf_at(sm + R_ZS, t * D + dv);
+                        out[(size_t)t * (p.Hv * D)] = __float2bfloat16_rn(y * __fdividef(zz, 1.0f + __expf(-zz)));
+                    }
+                }
+            } else {
+                failed = true;
+            }
+            wg_sync(1);
+            if (tid == 128 && c + 1 < NC && zok) {
+                fence_proxy_async_smem();
+                issue_z(c + 1);
+                ++n_z;
+            }
+        }
+        while (ck_i < ck.n && ck.off[ck_i] - t0 == C) ++ck_i;
+        umma::fence_before_sync();
+        if (__syncthreads_or(failed)) {
+            failed = true;
+            break;
+        }
+        umma::fence_after_sync();
+    }
+
+    if (failed) {
+        // let copies and MMAs still in flight finish (bounded) before the CTA exits
+        if (tid == 0) {
+            for (; w_qk < n_qk; ++w_qk) mbar_wait_bounded(bar_qk, (uint32_t)w_qk & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            for (; w_v < n_v; ++w_v) mbar_wait_bounded(bar_v, (uint32_t)w_v & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            for (; w_tp < n_tp; ++w_tp) mbar_wait_bounded(bar_tp, (uint32_t)w_tp & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            if (mma_pending) mbar_wait_bounded(bar_mma, (mma_phase - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
+        }
+        if (tid == 128)
+            for (; w_z < n_z; ++w_z) mbar_wait_bounded(bar_z, (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) umma::tmem_dealloc(tmem, T_COLS);
+}
+
+}  // namespace pseq
+
+cudaError_t launch_prefill_seq(const MixParams& p, const CkptList& ck, const PrefillWs& ws, cudaStream_t s) {
+    const uint64_t conv_dim = 2ull * p.Hk * 128 + (uint64_t)p.Hv * 128;
+    CUtensorMap tm_qkv, tm_z;
+    if (!encode_tmap_3d_bf16(&tm_qkv, ws.qkv, conv_dim, (uint64_t)ws.tp_len, (uint64_t)p.B, conv_dim * 2,
+                             conv_dim * 2 * (uint64_t)ws.tp_len, 128, pseq::C) ||
+        !encode_tmap_3d_bf16(&tm_z, p.z, (uint64_t)p.Hv * 128, (uint64_t)p.T, (uint64_t)p.B, (uint64_t)p.zs_t * 2,
+                             (uint64_t)p.zs_b * 2, 128, pseq::C))
+        return cudaErrorInvalidValue;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        e = cudaFuncSetAttribute(pseq::prefill_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)pseq::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    pseq::prefill_seq_kernel<<<p.B * p.Hv, pseq::NT, pseq::SMEM_BYTES, s>>>(p, ck, ws, tm_qkv, tm_z);
+    return cudaGetLastError();
+}
+
+unsigned int prefill_seq_device_error(bool clear) {
+    unsigned int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+    if (clear && v) {
+        const unsigned int zero = 0;
+        cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+    }
+    return v;
+}
+
+}  // namespace gdn

@@ -7,8 +7,11 @@
 //   mode 1: A K-major [128][128], B MN-major [128][128] (D = A B, K = 128)
 //   mode 2: A K-major [128][64],  B MN-major [64][128]  (D = A B, K = 64)
 //   mode 3: A MN-major [64][128] (stored k-major rows of A^T), B MN-major [64][128]
-// Inputs are plain row-major fp32 in global memory: A is [M][K] for modes
-// 0-2 and [K][M] for mode 3; B is [N][K] for mode 0 and [K][N] otherwise.
+//   mode 4: A in tensor memory [128][128], B K-major [128][128] (D = A B^T, N = 128)
+//   mode 5: A in tensor memory [128][64],  B K-major [64][64]   (D = A B^T, N = 64)
+//   mode 6: A in tensor memory [128][64],  B MN-major [64][128] (D = A B, K = 64)
+// Inputs are plain row-major fp32 in global memory: A is [M][K] except for
+// mode 3 ([K][M]); B is [N][K] for K-major B and [K][N] for MN-major B.
 #include "gdn_kernels.cuh"
 #include "gdn_umma.cuh"
 
@@ -17,15 +20,18 @@ namespace gdn {
 namespace {
 
 struct SelfTestShape {
-    int K, N, a_mn, b_mn;
+    int K, N, a_mn, b_mn, a_tmem;
 };
 
 __host__ __device__ inline SelfTestShape selftest_shape(int mode) {
     switch (mode) {
-        case 0: return {128, 64, 0, 0};
-        case 1: return {128, 128, 0, 1};
-        case 2: return {64, 128, 0, 1};
-        default: return {64, 128, 1, 1};
+        case 0: return {128, 64, 0, 0, 0};
+        case 1: return {128, 128, 0, 1, 0};
+        case 2: return {64, 128, 0, 1, 0};
+        case 3: return {64, 128, 1, 1, 0};
+        case 4: return {128, 128, 0, 0, 1};
+        case 5: return {64, 64, 0, 0, 1};
+        default: return {64, 128, 0, 1, 1};
     }
 }
 
@@ -43,7 +49,7 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const f
     uint32_t* tslot = reinterpret_cast<uint32_t*>(base + 2 * 128 * 128 * 4 + 8);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-    for (int i = tid; i < M * K; i += 128) {
+    for (int i = tid; i < M * K && !sh.a_tmem; i += 128) {
         if (!sh.a_mn) {
             const int m = i / K, k = i % K;
             *reinterpret_cast<float*>(sA + umma::kmajor_off(m, k, M)) = A[i];
@@ -67,20 +73,40 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const f
         fence_mbar_init();
     }
     if (warp == 0) {
-        umma::tmem_alloc(smem_u32(tslot), 128);
+        umma::tmem_alloc(smem_u32(tslot), 256);
         umma::tmem_relinquish();
     }
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
     const uint32_t tbase = *tslot;
+    constexpr int A_COL = 128;  // A operand columns when A lives in tensor memory
+    if (sh.a_tmem) {
+        // row m of A -> lane m (warp w writes lanes 32w..32w+31), columns A_COL + k
+        const int row = warp * 32 + lane;
+        for (int c0 = 0; c0 < K; c0 += 32) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = A[row * K + c0 + j];
+            umma::tmem_st32(umma::tmem_addr(tbase, warp * 32, A_COL + c0), v);
+        }
+        umma::tmem_wait_st();
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
 
     if (tid == 0) {
         const uint32_t idesc = umma::idesc_tf32(M, N, sh.a_mn, sh.b_mn);
         for (int kk = 0; kk < K / 8; ++kk) {
-            const uint64_t da = sh.a_mn ? umma::desc_mnmajor(smem_u32(sA), K, kk) : umma::desc_kmajor(smem_u32(sA), M, kk);
             const uint64_t db = sh.b_mn ? umma::desc_mnmajor(smem_u32(sB), K, kk) : umma::desc_kmajor(smem_u32(sB), N, kk);
-            umma::mma_tf32(tbase, da, db, idesc, kk > 0 ? 1u : 0u);
+            if (sh.a_tmem) {
+                umma::mma_tf32_ta(tbase, tbase + A_COL + kk * 8, db, idesc, kk > 0 ? 1u : 0u);
+            } else {
+                const uint64_t da =
+                    sh.a_mn ? umma::desc_mnmajor(smem_u32(sA), K, kk) : umma::desc_kmajor(smem_u32(sA), M, kk);
+                umma::mma_tf32(tbase, da, db, idesc, kk > 0 ? 1u : 0u);
+            }
         }
         umma::mma_commit(smem_u32(bar));
     }
@@ -98,7 +124,7 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const f
     }
     umma::fence_before_sync();
     __syncthreads();
-    if (warp == 0) umma::tmem_dealloc(tbase, 128);
+    if (warp == 0) umma::tmem_dealloc(tbase, 256);
 }
 
 }  // namespace

@@ -62,6 +62,14 @@ def _stream(dev: torch.device) -> int:
 # Functional boundary (deltanet.py:24-407)
 # ---------------------------------------------------------------------------
 
+def _workspace(lib, args, device: torch.device) -> Optional[torch.Tensor]:
+    """Scratch of the two-kernel chunked prefill (None when the call needs none)."""
+    n = lib.gdn_prefill_workspace_bytes(ctypes.byref(args))
+    if n < 0:
+        _lib.check("gdn_prefill_workspace_bytes", int(n))
+    return torch.empty(int(n), dtype=torch.uint8, device=device) if n > 0 else None
+
+
 def _extract_conv_state_at_offset(mixed_qkv: torch.Tensor, prev_conv_state: Optional[torch.Tensor],
                                   local_offset: int, state_len: int = 3) -> torch.Tensor:
     """Raw inputs of positions [off - state_len, off) of a [B, C, T] tensor,
@@ -233,15 +241,18 @@ class Qwen3_5GatedDeltaNet(nn.Module):
               out: Optional[torch.Tensor] = None, checkpoint_offsets: Sequence[int] = (),
               state_checkpoints: Optional[torch.Tensor] = None, conv_checkpoints: Optional[torch.Tensor] = None,
               token_by_token: Optional[bool] = None, register_kernel: bool = False,
-              cuda_core_prefill: bool = False) -> torch.Tensor:
+              cuda_core_prefill: bool = False, fused_prefill: bool = False) -> torch.Tensor:
         """One launch of the fused token mixer on projection outputs
         (deltanet.py:489-561): returns the gated-norm output [B, T, Hv*dv].
 
         ``token_by_token`` picks the decode kernel (T <= 8) or the chunked
         kernel; by default the reference's rule applies (a state and T <= 8).
-        ``register_kernel`` forces the register-tile decode kernel instead of
-        the bulk-copy pipelined one, ``cuda_core_prefill`` the CUDA-core
-        chunked kernel instead of the tensor-core one (same results up to
+        The chunked form runs as two kernels (a parallel preparation pass into
+        a workspace from torch's caching allocator, then the sequential
+        pass).  ``register_kernel`` forces the register-tile decode kernel
+        instead of the bulk-copy pipelined one, ``fused_prefill`` the
+        single-kernel tensor-core chunked form (no workspace),
+        ``cuda_core_prefill`` the CUDA-core chunked kernel (same results up to
         float rounding; used by the tests).
         """
         if token_by_token is None:
@@ -257,10 +268,16 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         args.state_checkpoints = _ptr(state_checkpoints)
         args.conv_checkpoints = _ptr(conv_checkpoints)
         lib = _lib.load()
-        fn = lib.gdn_mixer_decode if token_by_token else lib.gdn_mixer_prefill
         with torch.cuda.device(out.device):
-            _lib.check("gdn_mixer_decode" if token_by_token else "gdn_mixer_prefill",
-                       fn(ctypes.byref(args), _stream(out.device)))
+            if token_by_token:
+                _lib.check("gdn_mixer_decode", lib.gdn_mixer_decode(ctypes.byref(args), _stream(out.device)))
+            elif fused_prefill:
+                _lib.check("gdn_mixer_prefill", lib.gdn_mixer_prefill(ctypes.byref(args), _stream(out.device)))
+            else:
+                ws = _workspace(lib, args, out.device)
+                _lib.check("gdn_mixer_prefill_ws",
+                           lib.gdn_mixer_prefill_ws(ctypes.byref(args), None if ws is None else ws.data_ptr(),
+                                                    0 if ws is None else ws.numel(), _stream(out.device)))
         return out
 
     def mixer_verify(self, mixed_qkv: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: torch.Tensor,
@@ -441,8 +458,8 @@ class MixerPlan:
         self._args = a
         self._ref = ctypes.byref(a)
         self._lib = _lib.load()
-        self._fn = self._lib.gdn_mixer_decode if token_by_token else self._lib.gdn_mixer_prefill
-        self._name = "gdn_mixer_decode" if token_by_token else "gdn_mixer_prefill"
+        self._token_by_token = token_by_token
+        self._ws: Optional[torch.Tensor] = None
         self.device = device
 
     def __call__(self, mixed_qkv: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: torch.Tensor,
@@ -459,9 +476,20 @@ class MixerPlan:
         g.state_in = None if rec_state is None else rec_state.data_ptr()
         g.state_out = None if rec_state_out is None else rec_state_out.data_ptr()
         g.out = out.data_ptr()
-        st = self._fn(self._ref, torch.cuda.current_stream(self.device).cuda_stream if stream is None else stream)
+        sh = torch.cuda.current_stream(self.device).cuda_stream if stream is None else stream
+        if self._token_by_token:
+            st = self._lib.gdn_mixer_decode(self._ref, sh)
+            if st:
+                _lib.check("gdn_mixer_decode", st)
+            return out
+        if self._ws is None:
+            self._ws = _workspace(self._lib, g, self.device)
+            if self._ws is None:
+                self._ws = torch.empty(0, dtype=torch.uint8, device=self.device)
+        st = self._lib.gdn_mixer_prefill_ws(self._ref, self._ws.data_ptr() if self._ws.numel() else None,
+                                            self._ws.numel(), sh)
         if st:
-            _lib.check(self._name, st)
+            _lib.check("gdn_mixer_prefill_ws", st)
         return out
 
 
