@@ -67,6 +67,37 @@ __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t*>(&t);
 }
 
+// Round a pair of values to bf16 (one packed conversion) and back to float.
+__device__ __forceinline__ void round2(float& a, float& b) {
+    const uint32_t u = pack_bf2(a, b);
+    a = bf_lo(u);
+    b = bf_hi(u);
+}
+
+// Column j of T = (I + A)^-1 (A strictly lower triangular, row stride
+// A_STRIDE) by forward substitution: T[i][j] = [i == j] - sum_{k<i} A[i][k] T[k][j].
+// K0 = 32 for columns j >= 32, whose rows above 32 are zero.
+template <int K0>
+__device__ __forceinline__ void tri_inverse_column(const float* A, int j, float (&x)[C]) {
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+        if (i < K0) {
+            x[i] = 0.f;
+            continue;
+        }
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+        for (int k = K0; k < i; k += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(A + i * A_STRIDE + k);
+            s0 = fmaf(a.x, x[k], s0);
+            if (k + 1 < i) s1 = fmaf(a.y, x[k + 1], s1);
+            if (k + 2 < i) s2 = fmaf(a.z, x[k + 2], s2);
+            if (k + 3 < i) s3 = fmaf(a.w, x[k + 3], s3);
+        }
+        x[i] = (i == j ? 1.f : 0.f) - ((s0 + s1) + (s2 + s3));
+    }
+}
+
 __global__ void __launch_bounds__(NT, 2)
     prefill_prep_kernel(const MixParams p, const PrefillWs ws, const __grid_constant__ CUtensorMap tm_mixed) {
     extern __shared__ unsigned char raw[];
@@ -159,10 +190,11 @@ __global__ void __launch_bounds__(NT, 2)
                 h1[i] = cs_in ? Act<TA>::ld(cs_in + ((size_t)b * conv_dim + gc + 1) * HIST + i) : 0.f;
             }
         }
-        // window registers: x1 = one token back, x2, x3 = three back
+        // window registers: x1 = one token back, x2, x3 = three back (channel pair a, b)
         float a1 = h0[2], a2 = h0[1], a3 = h0[0];
         float b1 = h1[2], b2 = h1[1], b3 = h1[0];
         __nv_bfloat16* gout = static_cast<__nv_bfloat16*>(ws.qkv) + ((size_t)b * ws.tp_len + t0) * conv_dim + gc;
+        const bool full_window = cs_in != nullptr || c > 0;  // every token has 3 predecessors
 #pragma unroll 4
         for (int t = 0; t < C; ++t) {
             uint32_t* cell = reinterpret_cast<uint32_t*>(gbase + (t + HIST) * D * 2 + ch * 2);
@@ -171,9 +203,24 @@ __global__ void __launch_bounds__(NT, 2)
             const int tg = t0 + t;
             uint32_t outv = 0u;
             if (tg < T) {
-                const int valid = (cs_in || c > 0) ? HIST : (tg < HIST ? tg : HIST);
-                const float ca = conv4_taps<TA>(x0, a1, a2, a3, w0[0], w0[1], w0[2], w0[3], valid);
-                const float cb = conv4_taps<TA>(y0, b1, b2, b3, w1[0], w1[1], w1[2], w1[3], valid);
+                // taps newest first, one rounding per tap (deltanet.py:66-80)
+                float ca = x0 * w0[3], cb = y0 * w1[3];
+                round2(ca, cb);
+                if (full_window || tg >= 1) {
+                    ca = fmaf(a1, w0[2], ca);
+                    cb = fmaf(b1, w1[2], cb);
+                    round2(ca, cb);
+                }
+                if (full_window || tg >= 2) {
+                    ca = fmaf(a2, w0[1], ca);
+                    cb = fmaf(b2, w1[1], cb);
+                    round2(ca, cb);
+                }
+                if (full_window || tg >= 3) {
+                    ca = fmaf(a3, w0[0], ca);
+                    cb = fmaf(b3, w1[0], cb);
+                    round2(ca, cb);
+                }
                 outv = pack_bf2(__fdividef(ca, 1.0f + __expf(-ca)), __fdividef(cb, 1.0f + __expf(-cb)));
             }
             a3 = a2; a2 = a1; a1 = x0;
@@ -343,21 +390,8 @@ __global__ void __launch_bounds__(NT, 2)
         const int r = warp >> 1, hf = warp & 1, j = 32 * hf + lane;
         const float* A = reinterpret_cast<const float*>(sm + r * A_BYTES);
         float x[C];
-#pragma unroll
-        for (int i = 0; i < C; ++i) {
-            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-            const int k0 = hf ? 32 : 0;  // rows above the column block are zero
-#pragma unroll
-            for (int k = 0; k < i; k += 4) {
-                if (k + 3 < k0) continue;
-                const float4 a = *reinterpret_cast<const float4*>(A + i * A_STRIDE + k);
-                if (k + 0 < i && k + 0 >= k0) s0 = fmaf(a.x, x[k + 0], s0);
-                if (k + 1 < i && k + 1 >= k0) s1 = fmaf(a.y, x[k + 1], s1);
-                if (k + 2 < i && k + 2 >= k0) s2 = fmaf(a.z, x[k + 2], s2);
-                if (k + 3 < i && k + 3 >= k0) s3 = fmaf(a.w, x[k + 3], s3);
-            }
-            x[i] = (i == j ? 1.f : 0.f) - ((s0 + s1) + (s2 + s3));
-        }
+        if (hf == 0) tri_inverse_column<0>(A, j, x);
+        else tri_inverse_column<32>(A, j, x);
         unsigned char* img = reinterpret_cast<unsigned char*>(
             ws.tp + (((size_t)b * p.Hv + kh * rep + r) * NC + c) * 2 * (C * C));
 #pragma unroll

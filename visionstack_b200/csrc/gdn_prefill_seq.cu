@@ -147,11 +147,8 @@ __global__ void __launch_bounds__(NT, 1)
         issue_qk(0);
         issue_v(0);
         issue_tp(0);
-        n_qk = n_v = n_tp = 1;
-    }
-    if (tid == 128) {
         issue_z(0);
-        n_z = 1;
+        n_qk = n_v = n_tp = n_z = 1;
     }
     umma::fence_before_sync();
     __syncthreads();
@@ -233,21 +230,18 @@ __global__ void __launch_bounds__(NT, 1)
             failed = true;
             break;
         }
-        // ---------------- 3. Z^T = beta (V - e^gamma Y)^T ----------------
-        if (wg == 0) {
+        // ---------------- 3. Z^T = beta (V - e^gamma Y)^T (warpgroup wg: tokens 32 wg ..) ----------------
+        {
+            float y[32];
+            umma::tmem_ld32(tmem + lane_base + C_YO + 32 * wg, y);
+            umma::tmem_wait_ld();
 #pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                float y[32];
-                umma::tmem_ld32(tmem + lane_base + C_YO + 32 * hf, y);
-                umma::tmem_wait_ld();
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int t = 32 * hf + j;
-                    const float vv = bf_at(sm + R_VS, t * D + dv);
-                    y[j] = umma::tf32_rna(sB[t] * (vv - sEG[t] * y[j]));
-                }
-                umma::tmem_st32(tmem + lane_base + C_Z + 32 * hf, y);
+            for (int j = 0; j < 32; ++j) {
+                const int t = 32 * wg + j;
+                const float vv = bf_at(sm + R_VS, t * D + dv);
+                y[j] = umma::tf32_rna(sB[t] * (vv - sEG[t] * y[j]));
             }
+            umma::tmem_st32(tmem + lane_base + C_Z + 32 * wg, y);
             umma::tmem_wait_st();
         }
         umma::fence_before_sync();
@@ -328,22 +322,19 @@ __global__ void __launch_bounds__(NT, 1)
             issue_qk(c + 1);
             ++n_qk;
         }
-        // ---------------- 5b. v_new^T (tf32) and its e^{gamma_C - gamma} scaled copy ----------------
-        if (wg == 0) {
+        // ---------------- 5b. v_new^T (tf32) and its e^{gamma_C - gamma} scaled copy (tokens 32 wg ..) ----------------
+        {
+            float v[32], w[32];
+            umma::tmem_ld32(tmem + lane_base + C_V + 32 * wg, v);
+            umma::tmem_wait_ld();
 #pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                float v[32], w[32];
-                umma::tmem_ld32(tmem + lane_base + C_V + 32 * hf, v);
-                umma::tmem_wait_ld();
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int t = 32 * hf + j;
-                    w[j] = umma::tf32_rna(v[j] * sEF[t]);
-                    v[j] = umma::tf32_rna(v[j]);
-                }
-                umma::tmem_st32(tmem + lane_base + C_V + 32 * hf, v);
-                umma::tmem_st32(tmem + lane_base + C_Z + 32 * hf, w);
+            for (int j = 0; j < 32; ++j) {
+                const int t = 32 * wg + j;
+                w[j] = umma::tf32_rna(v[j] * sEF[t]);
+                v[j] = umma::tf32_rna(v[j]);
             }
+            umma::tmem_st32(tmem + lane_base + C_V + 32 * wg, v);
+            umma::tmem_st32(tmem + lane_base + C_Z + 32 * wg, w);
             umma::tmem_wait_st();
         }
         umma::fence_before_sync();
@@ -370,12 +361,12 @@ __global__ void __launch_bounds__(NT, 1)
             issue_tp(c + 1);
             ++n_tp;
         }
-        // ---------------- 7. state update (warpgroup 0) || output rows (warpgroup 1) ----------------
-        if (wg == 0) {
+        // ---------------- 7. state update (columns 64 wg ..) then output rows (tokens 32 wg ..) ----------------
+        {
             const float ec = sEG[C - 1];
             const bool last = c == NC - 1;
 #pragma unroll 1
-            for (int c0 = 0; c0 < D; c0 += 32) {
+            for (int c0 = 64 * wg; c0 < 64 * wg + 64; c0 += 32) {
                 float m[32], d[32];
                 umma::tmem_ld32(tmem + lane_base + C_MS + c0, m);
                 umma::tmem_ld32(tmem + lane_base + C_OP + c0, d);
@@ -396,27 +387,27 @@ __global__ void __launch_bounds__(NT, 1)
                     for (int j = 0; j < 32; ++j) __stcs(p.S_out + ((size_t)bh * D + c0 + j) * D + dv, m[j]);
                 }
             }
-            umma::tmem_wait_st();
-        } else {
+        }
+        {
             // O[t][dv] = e^{gamma_t} O1 + D, rounded; gated RMSNorm over dv (the 128 lanes)
-            float o[C];
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
+            const int tw = 32 * wg;  // this warpgroup's tokens tw .. tw + 31
+            float o[32];
+            {
                 float o1[32], dd[32];
-                umma::tmem_ld32(tmem + lane_base + C_YO + 64 + 32 * hf, o1);
-                umma::tmem_ld32(tmem + lane_base + C_YO + 32 * hf, dd);
+                umma::tmem_ld32(tmem + lane_base + C_YO + 64 + tw, o1);
+                umma::tmem_ld32(tmem + lane_base + C_YO + tw, dd);
                 umma::tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) o[32 * hf + j] = Act<TA>::round(fmaf(sEG[32 * hf + j], o1[j], dd[j]));
+                for (int j = 0; j < 32; ++j) o[j] = Act<TA>::round(fmaf(sEG[tw + j], o1[j], dd[j]));
             }
-            // per-token sums of squares over this warp's 32 lanes: halving exchange,
-            // ending with tokens tb, tb + 1 in this lane
-            float sq[C];
+            // per-token sums of squares over this warp's 32 lanes: halving exchange
+            // that leaves token tw + lane in this lane
+            float sq[32];
 #pragma unroll
-            for (int t = 0; t < C; ++t) sq[t] = o[t] * o[t];
+            for (int j = 0; j < 32; ++j) sq[j] = o[j] * o[j];
 #pragma unroll
             for (int st = 0; st < 5; ++st) {
-                const int s = 16 >> st, half = 32 >> st;  // exchange distance, values kept after this step
+                const int s = 16 >> st, half = 16 >> st;  // exchange distance = values kept after this step
                 const bool up = (lane & s) != 0;
 #pragma unroll
                 for (int k = 0; k < half; ++k) {
@@ -425,42 +416,37 @@ __global__ void __launch_bounds__(NT, 1)
                     sq[k] = keep + __shfl_xor_sync(0xffffffffu, send, s);
                 }
             }
-            const int tb = ((lane >> 4) & 1) * 32 + ((lane >> 3) & 1) * 16 + ((lane >> 2) & 1) * 8 +
-                           ((lane >> 1) & 1) * 4 + (lane & 1) * 2;
-            sPart[q4 * C + tb] = sq[0];
-            sPart[q4 * C + tb + 1] = sq[1];
-            wg_sync(1);
+            sPart[q4 * C + tw + lane] = sq[0];
+            wg_sync(1 + wg);
             if (q4 == 0) {
-#pragma unroll
-                for (int k = 0; k < 2; ++k) {
-                    const int t = tb + k;
-                    const float ss = (sPart[t] + sPart[C + t]) + (sPart[2 * C + t] + sPart[3 * C + t]);
-                    sRstd[t] = rsqrtf(ss / (float)D + p.eps);
-                }
+                const int t = tw + lane;
+                const float ss = (sPart[t] + sPart[C + t]) + (sPart[2 * C + t] + sPart[3 * C + t]);
+                sRstd[t] = rsqrtf(ss / (float)D + p.eps);
             }
             const bool zok = mbar_wait_bounded(bar_z, (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
             ++w_z;
-            wg_sync(1);
+            wg_sync(1 + wg);
             const float nw = sNW[dv];
-            TA* out = static_cast<TA*>(p.out) + ((size_t)b * T + t0) * (size_t)(p.Hv * D) + h * D + dv;
+            TA* out = static_cast<TA*>(p.out) + ((size_t)b * T + t0 + tw) * (size_t)(p.Hv * D) + h * D + dv;
             if (zok) {
 #pragma unroll
-                for (int t = 0; t < C; ++t) {
-                    if (t0 + t < T) {
-                        const float y = Act<TA>::round(nw * Act<TA>::round(o[t] * sRstd[t]));
-                        const float zz = bf_at(sm + R_ZS, t * D + dv);
-                        out[(size_t)t * (p.Hv * D)] = __float2bfloat16_rn(y * __fdividef(zz, 1.0f + __expf(-zz)));
+                for (int j = 0; j < 32; ++j) {
+                    if (t0 + tw + j < T) {
+                        const float y = Act<TA>::round(nw * Act<TA>::round(o[j] * sRstd[tw + j]));
+                        const float zz = bf_at(sm + R_ZS, (tw + j) * D + dv);
+                        out[(size_t)j * (p.Hv * D)] = __float2bfloat16_rn(y * __fdividef(zz, 1.0f + __expf(-zz)));
                     }
                 }
             } else {
                 failed = true;
             }
-            wg_sync(1);
-            if (tid == 128 && c + 1 < NC && zok) {
-                fence_proxy_async_smem();
-                issue_z(c + 1);
-                ++n_z;
-            }
+        }
+        umma::fence_before_sync();
+        __syncthreads();
+        if (tid == 0 && c + 1 < NC && !failed) {
+            fence_proxy_async_smem();
+            issue_z(c + 1);
+            ++n_z;
         }
         while (ck_i < ck.n && ck.off[ck_i] - t0 == C) ++ck_i;
         umma::fence_before_sync();
@@ -478,9 +464,8 @@ __global__ void __launch_bounds__(NT, 1)
             for (; w_v < n_v; ++w_v) mbar_wait_bounded(bar_v, (uint32_t)w_v & 1u, GDN_DEVERR_TMA_TIMEOUT);
             for (; w_tp < n_tp; ++w_tp) mbar_wait_bounded(bar_tp, (uint32_t)w_tp & 1u, GDN_DEVERR_TMA_TIMEOUT);
             if (mma_pending) mbar_wait_bounded(bar_mma, (mma_phase - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
-        }
-        if (tid == 128)
             for (; w_z < n_z; ++w_z) mbar_wait_bounded(bar_z, (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
+        }
     }
     umma::fence_before_sync();
     __syncthreads();
