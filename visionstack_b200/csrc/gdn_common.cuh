@@ -29,6 +29,16 @@ struct Act<__nv_bfloat16> {
     static __device__ __forceinline__ float round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 };
 
+// Nearest bf16 (ties to even) of a finite fp32 value, as fp32, in integer
+// arithmetic (the same value as __float2bfloat16_rn, without the conversion
+// pipe): add 0x7FFF plus the lowest kept bit, clear the low 16 bits.
+__device__ __forceinline__ float bf16_round_alu(float x) {
+    const uint32_t u = __float_as_uint(x);
+    return __uint_as_float((u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u);
+}
+// The bf16 bit pattern of a value already rounded by bf16_round_alu.
+__device__ __forceinline__ uint16_t bf16_bits(float rounded) { return (uint16_t)(__float_as_uint(rounded) >> 16); }
+
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 // torch.nn.functional.softplus(beta=1, threshold=20)

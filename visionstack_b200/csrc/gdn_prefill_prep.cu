@@ -50,7 +50,7 @@ constexpr uint32_t A_BYTES = C * A_STRIDE * 4;
 __host__ __device__ constexpr uint32_t region0_bytes(int rep) {
     const uint32_t stage = (uint32_t)(2 + rep) * GROUP_BYTES;
     const uint32_t kq = 128u * D * 4u;
-    const uint32_t am = (uint32_t)rep * A_BYTES;
+    const uint32_t am = 2u * (uint32_t)rep * A_BYTES;  // A and T matrices of every value head
     const uint32_t m = stage > kq ? stage : kq;
     return ((m > am ? m : am) + 1023u) & ~1023u;
 }
@@ -74,20 +74,15 @@ __device__ __forceinline__ void round2(float& a, float& b) {
     b = bf_hi(u);
 }
 
-// Column j of T = (I + A)^-1 (A strictly lower triangular, row stride
-// A_STRIDE) by forward substitution: T[i][j] = [i == j] - sum_{k<i} A[i][k] T[k][j].
-// K0 = 32 for columns j >= 32, whose rows above 32 are zero.
-template <int K0>
-__device__ __forceinline__ void tri_inverse_column(const float* A, int j, float (&x)[C]) {
+// Column j of the inverse of the unit lower triangular 32x32 block I + A
+// (A strictly lower triangular, row stride A_STRIDE) by forward substitution:
+// X[i][j] = [i == j] - sum_{k<i} A[i][k] X[k][j] (X[k][j] = 0 for k < j).
+__device__ __forceinline__ void tri_inverse_block32(const float* A, int j, float (&x)[32]) {
 #pragma unroll
-    for (int i = 0; i < C; ++i) {
-        if (i < K0) {
-            x[i] = 0.f;
-            continue;
-        }
+    for (int i = 0; i < 32; ++i) {
         float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
-        for (int k = K0; k < i; k += 4) {
+        for (int k = 0; k < i; k += 4) {
             const float4 a = *reinterpret_cast<const float4*>(A + i * A_STRIDE + k);
             s0 = fmaf(a.x, x[k], s0);
             if (k + 1 < i) s1 = fmaf(a.y, x[k + 1], s1);
@@ -96,6 +91,35 @@ __device__ __forceinline__ void tri_inverse_column(const float* A, int j, float 
         }
         x[i] = (i == j ? 1.f : 0.f) - ((s0 + s1) + (s2 + s3));
     }
+}
+
+// out[i][jb..jb+7] (+)= sign * sum_k L[i][k] R[k][jb..jb+7] over 32 k, row stride A_STRIDE.
+__device__ __forceinline__ void block_row8(const float* L, const float* R, int i, int jb, float* out, float sign) {
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll
+    for (int k = 0; k < 32; k += 4) {
+        const float4 a = *reinterpret_cast<const float4*>(L + i * A_STRIDE + k);
+        const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            const float4 r0 = *reinterpret_cast<const float4*>(R + (k + kk) * A_STRIDE + jb);
+            const float4 r1 = *reinterpret_cast<const float4*>(R + (k + kk) * A_STRIDE + jb + 4);
+            acc[0] = fmaf(av[kk], r0.x, acc[0]);
+            acc[1] = fmaf(av[kk], r0.y, acc[1]);
+            acc[2] = fmaf(av[kk], r0.z, acc[2]);
+            acc[3] = fmaf(av[kk], r0.w, acc[3]);
+            acc[4] = fmaf(av[kk], r1.x, acc[4]);
+            acc[5] = fmaf(av[kk], r1.y, acc[5]);
+            acc[6] = fmaf(av[kk], r1.z, acc[6]);
+            acc[7] = fmaf(av[kk], r1.w, acc[7]);
+        }
+    }
+    *reinterpret_cast<float4*>(out + i * A_STRIDE + jb) =
+        make_float4(sign * acc[0], sign * acc[1], sign * acc[2], sign * acc[3]);
+    *reinterpret_cast<float4*>(out + i * A_STRIDE + jb + 4) =
+        make_float4(sign * acc[4], sign * acc[5], sign * acc[6], sign * acc[7]);
 }
 
 __global__ void __launch_bounds__(NT, 2)
@@ -383,19 +407,42 @@ __global__ void __launch_bounds__(NT, 2)
     umma::fence_before_sync();
     __syncthreads();
 
-    // ---- T = (I + A)^-1 by forward substitution: two warps per value head ----
-    // lane l of warp 2r + hf owns column j = 32 hf + l of T; row i of T is
-    // e_i - sum_{k<i} A[i][k] T[k] (T[k][j] = 0 for k < j).
+    // ---- T = (I + A)^-1 in 32x32 blocks (the doubling merge of deltanet.py:146-160) ----
+    // T11, T22 by forward substitution (one warp per block, lane = column), then
+    // X = A21 T11 (parked in T's zero upper-right block) and T21 = -T22 X.
+    float* Tall = reinterpret_cast<float*>(sm + rep * A_BYTES);  // T of value head r at Tall + r * C * A_STRIDE
     if (warp < 2 * rep) {
-        const int r = warp >> 1, hf = warp & 1, j = 32 * hf + lane;
+        const int r = warp >> 1, o = 32 * (warp & 1);
+        const float* A = reinterpret_cast<const float*>(sm + r * A_BYTES) + o * A_STRIDE + o;
+        float* Tr = Tall + r * C * A_STRIDE + o * A_STRIDE + o;
+        float x[32];
+        tri_inverse_block32(A, lane, x);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) Tr[i * A_STRIDE + lane] = x[i];
+    }
+    __syncthreads();
+    for (int u = tid; u < rep * 128; u += NT) {
+        const int r = u >> 7, i = (u & 127) >> 2, jb = (u & 3) * 8;
         const float* A = reinterpret_cast<const float*>(sm + r * A_BYTES);
-        float x[C];
-        if (hf == 0) tri_inverse_column<0>(A, j, x);
-        else tri_inverse_column<32>(A, j, x);
+        float* Tr = Tall + r * C * A_STRIDE;
+        block_row8(A + 32 * A_STRIDE, Tr, i, jb, Tr + 32, 1.f);  // X[i][jb..] = A21 T11
+    }
+    __syncthreads();
+    for (int u = tid; u < rep * 128; u += NT) {
+        const int r = u >> 7, i = (u & 127) >> 2, jb = (u & 3) * 8;
+        float* Tr = Tall + r * C * A_STRIDE;
+        block_row8(Tr + 32 * A_STRIDE + 32, Tr + 32, i, jb, Tr + 32 * A_STRIDE, -1.f);  // T21 = -T22 X
+    }
+    __syncthreads();
+    // T image (tf32, zero above the diagonal)
+    for (int u = tid; u < rep * C * (C / 4); u += NT) {
+        const int r = u / (C * C / 4), w = u % (C * C / 4), i = w >> 4, j = (w & 15) * 4;
+        const float4 v = *reinterpret_cast<const float4*>(Tall + r * C * A_STRIDE + i * A_STRIDE + j);
+        const float4 o = make_float4(j + 0 <= i ? umma::tf32_rna(v.x) : 0.f, j + 1 <= i ? umma::tf32_rna(v.y) : 0.f,
+                                     j + 2 <= i ? umma::tf32_rna(v.z) : 0.f, j + 3 <= i ? umma::tf32_rna(v.w) : 0.f);
         unsigned char* img = reinterpret_cast<unsigned char*>(
             ws.tp + (((size_t)b * p.Hv + kh * rep + r) * NC + c) * 2 * (C * C));
-#pragma unroll
-        for (int i = 0; i < C; ++i) *reinterpret_cast<float*>(img + umma::kmajor_off(i, j, C)) = umma::tf32_rna(x[i]);
+        *reinterpret_cast<float4*>(img + umma::kmajor_off(i, j, C)) = o;
     }
     umma::fence_before_sync();
     __syncthreads();

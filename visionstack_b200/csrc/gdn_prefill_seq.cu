@@ -398,7 +398,7 @@ __global__ void __launch_bounds__(NT, 1)
                 umma::tmem_ld32(tmem + lane_base + C_YO + tw, dd);
                 umma::tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) o[j] = Act<TA>::round(fmaf(sEG[tw + j], o1[j], dd[j]));
+                for (int j = 0; j < 32; ++j) o[j] = bf16_round_alu(fmaf(sEG[tw + j], o1[j], dd[j]));
             }
             // per-token sums of squares over this warp's 32 lanes: halving exchange
             // that leaves token tw + lane in this lane
@@ -432,9 +432,10 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     if (t0 + tw + j < T) {
-                        const float y = Act<TA>::round(nw * Act<TA>::round(o[j] * sRstd[tw + j]));
+                        const float y = bf16_round_alu(nw * bf16_round_alu(o[j] * sRstd[tw + j]));
                         const float zz = bf_at(sm + R_ZS, (tw + j) * D + dv);
-                        out[(size_t)j * (p.Hv * D)] = __float2bfloat16_rn(y * __fdividef(zz, 1.0f + __expf(-zz)));
+                        reinterpret_cast<uint16_t*>(out)[(size_t)j * (p.Hv * D)] =
+                            bf16_bits(bf16_round_alu(y * __fdividef(zz, 1.0f + __expf(-zz))));
                     }
                 }
             } else {
