@@ -61,6 +61,11 @@ extern "C" {
 #define GDN_DEVERR_MMA_TIMEOUT 0x2u
 #define GDN_DEVERR_BAD_SLOT 0x4u   /* slot-table entry or accepted count out of range */
 
+/* Size of the library's fixed device scratch used by gdn_mixer_prefill_noalloc
+ * (64 MiB per device: the two-kernel prefill's workspace for about 1.9k
+ * tokens x 16 / 32 heads of 128). */
+#define GDN_STATIC_SCRATCH_BYTES (64ll << 20)
+
 /* Maximum number of state checkpoints one call can record. */
 #define GDN_MAX_CHECKPOINTS 512
 /* Longest sequence the token-by-token (decode / verify) entry accepts. */
@@ -242,6 +247,23 @@ int64_t gdn_prefill_workspace_bytes(const gdn_mixer_args* args);
  * gdn_mixer_prefill instead and ignore the workspace.
  */
 int32_t gdn_mixer_prefill_ws(const gdn_mixer_args* args, void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * gdn_mixer_prefill_ws with the workspace taken from a fixed scratch array
+ * of this library (GDN_STATIC_SCRATCH_BYTES per device, address looked up
+ * once per device with cudaGetSymbolAddress): the call allocates no device
+ * memory, for callers that have no device allocator of their own (a C or FFI
+ * host without PyTorch, which would otherwise need a cudaMalloc / cudaFree
+ * pair - each synchronising the device - around every call).  Calls that need
+ * more than GDN_STATIC_SCRATCH_BYTES of workspace (gdn_prefill_workspace_bytes)
+ * are rejected with GDN_ERR_INVALID_ARG.  Every call on a device shares the
+ * one scratch array: calls that can run at the same time on a device
+ * (different streams, or host threads without ordering between them) race
+ * on it and must be serialised by the caller.  Nothing in the scratch needs
+ * to be zero or survives a call.  No counterpart in the reference (its
+ * PyTorch path takes its temporaries from torch's allocator).
+ */
+int32_t gdn_mixer_prefill_noalloc(const gdn_mixer_args* args, void* stream);
 
 /*
  * Stand-alone delta rule on already-split q/k/v, the functional boundary of

@@ -32,6 +32,7 @@ EXPORTED_SYMBOLS = (
     "gdn_mixer_verify_slots",
     "gdn_prefill_workspace_bytes",
     "gdn_mixer_prefill_ws",
+    "gdn_mixer_prefill_noalloc",
     "gdn_accept_slots",
     "gdn_device_error",
     "gdn_selftest_umma",
@@ -39,6 +40,7 @@ EXPORTED_SYMBOLS = (
 GDN_FLAG_REGISTER_KERNEL = 1
 GDN_FLAG_CUDA_CORE_PREFILL = 2
 GDN_DEVERR_BAD_SLOT = 0x4
+GDN_STATIC_SCRATCH_BYTES = 64 << 20
 
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int32
@@ -114,6 +116,8 @@ def load() -> ctypes.CDLL:
         lib.gdn_prefill_workspace_bytes.argtypes = [ctypes.POINTER(MixerArgs)]
         lib.gdn_mixer_prefill_ws.restype = _i32
         lib.gdn_mixer_prefill_ws.argtypes = [ctypes.POINTER(MixerArgs), _c_void_p, _i64, _c_void_p]
+        lib.gdn_mixer_prefill_noalloc.restype = _i32
+        lib.gdn_mixer_prefill_noalloc.argtypes = [ctypes.POINTER(MixerArgs), _c_void_p]
         lib.gdn_mixer_verify_slots.restype = _i32
         lib.gdn_mixer_verify_slots.argtypes = [ctypes.POINTER(MixerArgs), _c_void_p, _i32, _c_void_p]
         lib.gdn_accept_slots.restype = _i32

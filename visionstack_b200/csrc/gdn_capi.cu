@@ -381,4 +381,18 @@ int32_t gdn_causal_conv1d(int32_t batch, int32_t channels, int32_t seq_len, int3
     return cuda_status(e, "gdn_causal_conv1d launch");
 }
 
+int32_t gdn_mixer_prefill_noalloc(const gdn_mixer_args* args, void* stream) {
+    const int64_t need = gdn_prefill_workspace_bytes(args);
+    if (need < 0) return (int32_t)need;  // invalid arguments, message already set
+    if (need > GDN_STATIC_SCRATCH_BYTES)
+        return fail(GDN_ERR_INVALID_ARG, "needs %lld bytes of scratch; the static scratch holds %lld",
+                    (long long)need, (long long)GDN_STATIC_SCRATCH_BYTES);
+    void* scratch = nullptr;
+    if (need > 0) {
+        const cudaError_t e = gdn::static_prefill_scratch(&scratch);
+        if (e != cudaSuccess) return cuda_status(e, "address of the static prefill scratch");
+    }
+    return gdn_mixer_prefill_ws(args, scratch, need > 0 ? (int64_t)GDN_STATIC_SCRATCH_BYTES : 0, stream);
+}
+
 }  // extern "C"

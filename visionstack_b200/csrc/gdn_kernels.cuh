@@ -76,6 +76,8 @@ cudaError_t launch_prefill_prep(const MixParams& p, const PrefillWs& ws, cudaStr
 unsigned int prefill_prep_device_error(bool clear);
 cudaError_t launch_prefill_seq(const MixParams& p, const CkptList& ck, const PrefillWs& ws, cudaStream_t s);
 unsigned int prefill_seq_device_error(bool clear);
+// address of the fixed prefill scratch on the current device (looked up once per device)
+cudaError_t static_prefill_scratch(void** addr);
 cudaError_t launch_prefill(const MixParams& p, const CkptList& ck, int d, int dtype, bool mixer,
                            cudaStream_t s, bool* supported);
 cudaError_t launch_conv1d(int B, int C, int T, int K, int dtype, const void* x, const void* w,
