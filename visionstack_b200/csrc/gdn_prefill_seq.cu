@@ -17,13 +17,20 @@
 //   MMA-d  D^T = v_new^T P^T                            (M128 N64  K64)
 //   MMA-e  dS^T = (e^{gamma_C - gamma} v_new)^T K        (M128 N128 K64)
 //   CUDA   S^T <- e^{gamma_C} S^T + dS^T (master and operand copy), boundary
-//          checkpoints, final state; in parallel, the output rows
-//          O = e^gamma O1 + D through the gated RMSNorm
+//          checkpoints, final state
+//   CUDA   output rows O = e^gamma O1 + D through the gated RMSNorm
 //
 // i.e. the reference's v_new = U - W S with U = T (beta V), W = T (beta K e^gamma)
 // and O = (Q e^gamma) S + P v_new, S' = e^{gamma_C} S + (K e^{gamma_C-gamma})^T v_new
-// (deltanet.py:323-389), regrouped and transposed.  Inputs of the next chunk
-// stream in by tensor-map / bulk copies while the current one computes.
+// (deltanet.py:323-389), regrouped and transposed.
+//
+// 16 warps in two roles.  Warpgroups 0-1 carry the state: operand staging,
+// the MMAs (thread 0 issues them and every copy), Z, v_new, the state update.
+// Warpgroups 2-3 turn the previous chunk's O into output rows while the state
+// path moves on: they copy O out of tensor memory as soon as MMA-d completes
+// (mbarrier o_ready, a second commit of that MMA), release those columns
+// (mbarrier o_free, which the next MMA-b waits for), then normalise and store.
+// Inputs of the next chunk stream in by tensor-map / bulk copies meanwhile.
 #include "gdn_async.cuh"
 #include "gdn_common.cuh"
 #include "gdn_conv_windows.cuh"
@@ -35,7 +42,7 @@
 namespace gdn {
 namespace pseq {
 
-constexpr int D = 128, C = 64, NT = 256;
+constexpr int D = 128, C = 64, NT = 512, NMAIN = 256;
 // shared memory (bytes from the 1024-aligned base)
 constexpr uint32_t R_KQ = 0;        // [K;Q] K-major [128][dk] tf32, 64 KB (B of MMA-b)
 constexpr uint32_t R_KM = 65536;    // K MN-major [tok][dk] tf32, 32 KB (B of MMA-e)
@@ -46,10 +53,11 @@ constexpr uint32_t R_VS = 163840;   // v rows
 constexpr uint32_t R_ZS = 180224;   // z rows
 constexpr uint32_t R_VEC = 196608;  // rq[64] rk[64] beta[64] gamma[64] as loaded
 constexpr uint32_t R_SCR = R_VEC + 1024;
-constexpr int S_B = 0, S_G = 64, S_EG = 128, S_EF = 192, S_F = 256, S_NW = 320, S_PART = 448, S_RSTD = 704,
-              S_END = 768;  // floats
+// scratch floats: per chunk parity p, beta / gamma / e^gamma / e^{gamma_C - gamma} at S_V + 256 p
+constexpr int S_V = 0, S_F = 512, S_NW = 576, S_PART = 704, S_RSTD = 960, S_END = 1024;
+constexpr int V_B = 0, V_G = 64, V_EG = 128, V_EF = 192;
 constexpr uint32_t R_BAR = R_SCR + S_END * 4;
-constexpr uint32_t SMEM_BYTES = R_BAR + 64 + 1024;
+constexpr uint32_t SMEM_BYTES = R_BAR + 128 + 1024;
 // tensor memory columns
 constexpr uint32_t C_MS = 0, C_OP = 128, C_YO = 256, C_Z = 384, C_V = 448, T_COLS = 512;
 
@@ -60,8 +68,44 @@ __device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 
 __device__ __forceinline__ float bf_at(const unsigned char* base, int idx) {
     return __uint_as_float((uint32_t)(*reinterpret_cast<const uint16_t*>(base + 2 * idx)) << 16);
 }
+// a pair of values rounded to bf16 (nearest, ties to even) with one packed
+// conversion; the packed bits in *bits
+__device__ __forceinline__ void round2_bf16(float& a, float& b, uint32_t* bits = nullptr) {
+    const __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(&t);
+    a = bf_lo(u);
+    b = bf_hi(u);
+    if (bits) *bits = u;
+}
+// round to 11 significant bits (tf32) on the fp32 pipe: Veltkamp's split with
+// 2^13 + 1 (nearest); the explicitly rounded operators keep the compiler from
+// contracting it into an fma
+__device__ __forceinline__ float tf32_rn(float x) {
+    const float t = __fmul_rn(x, 8193.0f);
+    return __fsub_rn(t, __fsub_rn(t, x));
+}
+__device__ __forceinline__ float4 tf32_rn4(float4 v) {
+    return make_float4(tf32_rn(v.x), tf32_rn(v.y), tf32_rn(v.z), tf32_rn(v.w));
+}
 
-__device__ __forceinline__ void wg_sync(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+// named barriers: 1 = state warpgroups (256 threads), 2 / 3 = output warpgroup
+// 0 / 1 (128 threads each), 4 = both output warpgroups (256)
+__device__ __forceinline__ void nb_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ bool nb_any(bool pred, int id, int n) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}\n"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(n)
+        : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
 
 __global__ void __launch_bounds__(NT, 1)
     prefill_seq_kernel(const MixParams p, const CkptList ck, const PrefillWs ws,
@@ -71,23 +115,21 @@ __global__ void __launch_bounds__(NT, 1)
     unsigned char* sm = raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
     const uint32_t sb = smem_u32(sm);
     float* scr = reinterpret_cast<float*>(sm + R_SCR);
-    float* sB = scr + S_B;
-    float* sG = scr + S_G;
-    float* sEG = scr + S_EG;
-    float* sEF = scr + S_EF;
     float* sF = scr + S_F;
     float* sNW = scr + S_NW;
     float* sPart = scr + S_PART;
     float* sRstd = scr + S_RSTD;
     const float* vec = reinterpret_cast<const float*>(sm + R_VEC);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + R_BAR);
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + R_BAR + 48);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + R_BAR + 96);
     const uint32_t bar_qk = smem_u32(&bars[0]), bar_v = smem_u32(&bars[1]), bar_z = smem_u32(&bars[2]),
-                   bar_tp = smem_u32(&bars[3]), bar_mma = smem_u32(&bars[4]);
+                   bar_tp = smem_u32(&bars[3]), bar_mma = smem_u32(&bars[4]), bar_ordy = smem_u32(&bars[5]),
+                   bar_ofree = smem_u32(&bars[6]);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int wg = warp >> 2, q4 = warp & 3;
-    const int dv = 32 * q4 + lane;                       // this thread's tensor-memory lane
+    const bool main_grp = tid < NMAIN;
+    const int dv = 32 * q4 + lane;  // this thread's tensor-memory lane
     const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
     const int bh = blockIdx.x;
     const int b = bh / p.Hv, h = bh - (bh / p.Hv) * p.Hv;
@@ -95,7 +137,8 @@ __global__ void __launch_bounds__(NT, 1)
     const int T = p.T, NC = ws.nc;
 
     if (tid == 0) {
-        for (int i = 0; i < 5; ++i) mbar_init(smem_u32(&bars[i]), 1);
+        for (int i = 0; i < 6; ++i) mbar_init(smem_u32(&bars[i]), 1);
+        mbar_init(bar_ofree, NT - NMAIN);
         fence_mbar_init();
     }
     if (warp == 0) {
@@ -109,17 +152,18 @@ __global__ void __launch_bounds__(NT, 1)
     umma::fence_after_sync();
     const uint32_t tmem = *tslot;
 
-    // initial state, transposed: lane dv, column dk (warpgroup wg: dk 64 wg .. 64 wg + 63)
-    for (int c0 = 64 * wg; c0 < 64 * wg + 64; c0 += 32) {
+    // initial state, transposed: lane dv, column dk (warpgroup wg: dk 32 wg .. 32 wg + 31)
+    {
+        const int c0 = 32 * wg;
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = p.S_in ? __ldcs(p.S_in + ((size_t)bh * D + c0 + j) * D + dv) : 0.f;
         umma::tmem_st32(tmem + lane_base + C_MS + c0, v);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = umma::tf32_rna(v[j]);
+        for (int j = 0; j < 32; ++j) v[j] = tf32_rn(v[j]);
         umma::tmem_st32(tmem + lane_base + C_OP + c0, v);
+        umma::tmem_wait_st();
     }
-    umma::tmem_wait_st();
 
     const int v_ch = 2 * p.Hk * D + h * D;
     auto issue_qk = [&](int cc) {
@@ -141,256 +185,304 @@ __global__ void __launch_bounds__(NT, 1)
         mbar_arrive_expect_tx(bar_tp, 2u * C * C * 4u);
         bulk_load(sb + R_TP, ws.tp + (((size_t)b * p.Hv + h) * NC + cc) * (2 * C * C), 2u * C * C * 4u, bar_tp);
     };
-    // copies issued / waited per barrier (issuing thread tracks issues; waits are uniform)
+    // copies issued (by their issuing thread) and waits completed (uniform in a group)
     int n_qk = 0, n_v = 0, n_z = 0, n_tp = 0;
+    int w_qk = 0, w_v = 0, w_z = 0, w_tp = 0;
     if (tid == 0) {
         issue_qk(0);
         issue_v(0);
         issue_tp(0);
+        n_qk = n_v = n_tp = 1;
+    }
+    if (tid == NMAIN) {
         issue_z(0);
-        n_qk = n_v = n_tp = n_z = 1;
+        n_z = 1;
     }
     umma::fence_before_sync();
     __syncthreads();
 
-    const uint32_t idesc_b = umma::idesc_tf32(128, 128, 0, 0);
-    const uint32_t idesc_c = umma::idesc_tf32(128, 64, 0, 0);
-    const uint32_t idesc_e = umma::idesc_tf32(128, 128, 0, 1);
-    uint32_t mma_phase = 0;
-    int w_qk = 0, w_v = 0, w_z = 0, w_tp = 0;  // completed waits
-    bool failed = false, mma_pending = false;
-    int ck_i = 0;
-    auto mma_wait = [&]() -> bool {
-        const bool ok = mbar_wait_bounded(bar_mma, mma_phase & 1u, GDN_DEVERR_MMA_TIMEOUT);
-        ++mma_phase;
-        umma::fence_after_sync();
-        return !__syncthreads_or(!ok);
-    };
-    auto wait_all = [&](uint32_t bar, int& count) -> bool {
-        const bool ok = mbar_wait_bounded(bar, (uint32_t)count & 1u, GDN_DEVERR_TMA_TIMEOUT);
-        ++count;
-        return !__syncthreads_or(!ok);
-    };
-
-    for (int c = 0; c < NC; ++c) {
-        const int t0 = c * C;
-        // ---------------- 1. operands of the chunk ----------------
-        if (!wait_all(bar_qk, w_qk)) {
-            failed = true;
-            break;
-        }
-        if (tid < C) {
-            const float gC = vec[192 + C - 1], gt = vec[192 + tid];
-            sB[tid] = vec[128 + tid];
-            sG[tid] = gt;
-            sEG[tid] = expf(gt);
-            sEF[tid] = expf(gC - gt);
-        }
-#pragma unroll 4
+    bool failed = false;
+    if (main_grp) {
+        // ======================= state path (warpgroups 0-1) =======================
+        const uint32_t idesc_b = umma::idesc_tf32(128, 128, 0, 0);
+        const uint32_t idesc_c = umma::idesc_tf32(128, 64, 0, 0);
+        const uint32_t idesc_e = umma::idesc_tf32(128, 128, 0, 1);
+        uint32_t mma_phase = 0;
+        int n_ofree = 0;  // o_free phases waited (thread 0)
+        bool mma_pending = false;
+        int ck_i = 0;
+        // operand staging offsets of this thread (the same every chunk): [K;Q] row r,
+        // columns c4..c4+3 for r = (tid + 256 u) / 32; rows r < 64 also go to K MN-major
+        uint32_t off_kq[16], off_km[8];
+#pragma unroll
         for (int u = 0; u < 16; ++u) {
-            const int idx = tid + u * NT, r = idx >> 5, c4 = (idx & 31) * 4, t = r & 63;
-            const uint2 raw2 =
-                *reinterpret_cast<const uint2*>(sm + (r < C ? R_KS : R_QS) + t * D * 2 + c4 * 2);
-            float4 f = make_float4(bf_lo(raw2.x), bf_hi(raw2.x), bf_lo(raw2.y), bf_hi(raw2.y));
-            if (r < C) {
-                const float s = vec[64 + t];
-                f = make_float4(f.x * s, f.y * s, f.z * s, f.w * s);
-                *reinterpret_cast<float4*>(sm + R_KM + umma::mnmajor_off(t, c4, C)) = umma::tf32_rna4(f);
-            } else {
-                const float s = vec[t];
-                f = make_float4((f.x * s) * p.q_scale, (f.y * s) * p.q_scale, (f.z * s) * p.q_scale,
-                                (f.w * s) * p.q_scale);
-            }
-            *reinterpret_cast<float4*>(sm + R_KQ + umma::kmajor_off(r, c4, 128)) = umma::tf32_rna4(f);
+            const int idx = tid + u * NMAIN, r = idx >> 5, c4 = (idx & 31) * 4;
+            off_kq[u] = R_KQ + umma::kmajor_off(r, c4, 128);
+            if (u < 8) off_km[u] = R_KM + umma::mnmajor_off(r, c4, C);
         }
-        fence_proxy_async_smem();
-        umma::fence_before_sync();
-        __syncthreads();
-        // checkpoints strictly inside this chunk keep the k rows (and rk) until step 5
-        const bool has_sub = ck_i < ck.n && ck.off[ck_i] > t0 && ck.off[ck_i] - t0 < C;
-        // ---------------- 2. MMA-b; next chunk's q/k copies ----------------
-        if (tid == 0) {
+        auto mma_wait = [&]() -> bool {
+            const bool ok = mbar_wait_bounded(bar_mma, mma_phase & 1u, GDN_DEVERR_MMA_TIMEOUT);
+            ++mma_phase;
             umma::fence_after_sync();
-            for (int kk = 0; kk < D / 8; ++kk)
-                umma::mma_tf32_ta(tmem + C_YO, tmem + C_OP + kk * 8, umma::desc_kmajor(sb + R_KQ, 128, kk), idesc_b,
-                                  kk > 0);
-            umma::mma_commit(bar_mma);
-            if (c + 1 < NC && !has_sub) {
+            return !nb_any(!ok, 1, NMAIN);
+        };
+        auto wait_main = [&](uint32_t bar, int& count) -> bool {
+            const bool ok = mbar_wait_bounded(bar, (uint32_t)count & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            ++count;
+            return !nb_any(!ok, 1, NMAIN);
+        };
+        for (int c = 0; c < NC; ++c) {
+            const int t0 = c * C;
+            float* sv = scr + S_V + 256 * (c & 1);
+            // ---------------- 1. operands of the chunk ----------------
+            if (!wait_main(bar_qk, w_qk)) {
+                failed = true;
+                break;
+            }
+            if (tid < C) {
+                const float gC = vec[192 + C - 1], gt = vec[192 + tid];
+                sv[V_B + tid] = vec[128 + tid];
+                sv[V_G + tid] = gt;
+                sv[V_EG + tid] = expf(gt);
+                sv[V_EF + tid] = expf(gC - gt);
+            }
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const int idx = tid + u * NMAIN, r = idx >> 5, c4 = (idx & 31) * 4, t = r & 63;
+                const uint2 raw2 = *reinterpret_cast<const uint2*>(sm + (u < 8 ? R_KS : R_QS) + t * D * 2 + c4 * 2);
+                float4 f = make_float4(bf_lo(raw2.x), bf_hi(raw2.x), bf_lo(raw2.y), bf_hi(raw2.y));
+                if (u < 8) {
+                    const float s = vec[64 + t];
+                    f = tf32_rn4(make_float4(f.x * s, f.y * s, f.z * s, f.w * s));
+                    *reinterpret_cast<float4*>(sm + off_km[u]) = f;
+                } else {
+                    const float s = vec[t];
+                    f = tf32_rn4(make_float4((f.x * s) * p.q_scale, (f.y * s) * p.q_scale, (f.z * s) * p.q_scale,
+                                             (f.w * s) * p.q_scale));
+                }
+                *reinterpret_cast<float4*>(sm + off_kq[u]) = f;
+            }
+            fence_proxy_async_smem();
+            umma::fence_before_sync();
+            nb_sync(1, NMAIN);
+            // checkpoints strictly inside this chunk keep the k rows (and rk) until step 5
+            const bool has_sub = ck_i < ck.n && ck.off[ck_i] > t0 && ck.off[ck_i] - t0 < C;
+            // ---------------- 2. MMA-b (after the output warps released O of the last chunk) ----------------
+            bool free_ok = true;
+            if (tid == 0) {
+                if (c > 0) {
+                    free_ok = mbar_wait_bounded(bar_ofree, (uint32_t)n_ofree & 1u, GDN_DEVERR_MMA_TIMEOUT);
+                    ++n_ofree;
+                }
+                umma::fence_after_sync();
+                if (free_ok) {
+                    for (int kk = 0; kk < D / 8; ++kk)
+                        umma::mma_tf32_ta(tmem + C_YO, tmem + C_OP + kk * 8, umma::desc_kmajor(sb + R_KQ, 128, kk),
+                                          idesc_b, kk > 0);
+                    umma::mma_commit(bar_mma);
+                    mma_pending = true;
+                    if (c + 1 < NC && !has_sub) {
+                        issue_qk(c + 1);
+                        ++n_qk;
+                    }
+                }
+            }
+            if (nb_any(!free_ok, 1, NMAIN)) {
+                failed = true;
+                break;
+            }
+            if (!mma_wait()) {
+                failed = true;
+                break;
+            }
+            mma_pending = false;
+            if (!wait_main(bar_v, w_v)) {
+                failed = true;
+                break;
+            }
+            // ---------------- 3. Z^T = beta (V - e^gamma Y)^T (warpgroup wg: tokens 32 wg ..) ----------------
+            {
+                float y[32];
+                umma::tmem_ld32(tmem + lane_base + C_YO + 32 * wg, y);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int t = 32 * wg + j;
+                    const float vv = bf_at(sm + R_VS, t * D + dv);
+                    y[j] = tf32_rn(sv[V_B + t] * (vv - sv[V_EG + t] * y[j]));
+                }
+                umma::tmem_st32(tmem + lane_base + C_Z + 32 * wg, y);
+                umma::tmem_wait_st();
+            }
+            umma::fence_before_sync();
+            nb_sync(1, NMAIN);
+            // ---------------- 4. MMA-c: v_new^T = Z^T T^T; next chunk's v copy ----------------
+            if (!wait_main(bar_tp, w_tp)) {
+                failed = true;
+                break;
+            }
+            if (tid == 0) {
+                umma::fence_after_sync();
+                for (int kk = 0; kk < C / 8; ++kk)
+                    umma::mma_tf32_ta(tmem + C_V, tmem + C_Z + kk * 8, umma::desc_kmajor(sb + R_TP, C, kk), idesc_c,
+                                      kk > 0);
+                umma::mma_commit(bar_mma);
+                mma_pending = true;
+                if (c + 1 < NC) {
+                    fence_proxy_async_smem();
+                    issue_v(c + 1);
+                    ++n_v;
+                }
+            }
+            if (!mma_wait()) {
+                failed = true;
+                break;
+            }
+            mma_pending = false;
+            // ---------------- 5a. sub-chunk checkpoints (fp32 v_new, fp32 K, state before the update) ----------------
+            // S_s = e^{gamma_{s-1}} S + sum_{t<s} e^{gamma_{s-1}-gamma_t} k_t^T v_new_t (deltanet.py:375-388)
+            while (ck_i < ck.n && ck.off[ck_i] > t0 && ck.off[ck_i] - t0 < C) {
+                const int s_off = ck.off[ck_i] - t0;
+                if (tid < C) sF[tid] = tid < s_off ? expf(sv[V_G + s_off - 1] - sv[V_G + tid]) : 0.f;
+                nb_sync(1, NMAIN);
+                const float es = expf(sv[V_G + s_off - 1]);
+                float* dst = p.S_ckpt + ((size_t)ck.slot[ck_i] * p.B * p.Hv + bh) * (size_t)(D * D);
+#pragma unroll 1
+                for (int hb = 0; hb < 2; ++hb) {  // 32 key columns at a time
+                    const int cb = 64 * wg + 32 * hb;
+                    float m[32];
+                    umma::tmem_ld32(tmem + lane_base + C_MS + cb, m);
+                    umma::tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) m[j] *= es;
+#pragma unroll 1
+                    for (int th = 0; th < 2; ++th) {  // 32 tokens at a time
+                        float wv[32];
+                        umma::tmem_ld32(tmem + lane_base + C_V + 32 * th, wv);
+                        umma::tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) wv[j] *= sF[32 * th + j] * vec[64 + 32 * th + j];  // decay, rk
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int t = 32 * th + j;
+                            const uint4* krow = reinterpret_cast<const uint4*>(sm + R_KS + t * D * 2 + cb * 2);
+#pragma unroll
+                            for (int j8 = 0; j8 < 4; ++j8) {
+                                const uint4 k8 = krow[j8];
+                                const uint32_t kw[4] = {k8.x, k8.y, k8.z, k8.w};
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    m[8 * j8 + 2 * e] = fmaf(wv[j], bf_lo(kw[e]), m[8 * j8 + 2 * e]);
+                                    m[8 * j8 + 2 * e + 1] = fmaf(wv[j], bf_hi(kw[e]), m[8 * j8 + 2 * e + 1]);
+                                }
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) __stcs(dst + (size_t)(cb + j) * D + dv, m[j]);
+                }
+                nb_sync(1, NMAIN);
+                ++ck_i;
+            }
+            if (tid == 0 && has_sub && c + 1 < NC) {
+                fence_proxy_async_smem();
                 issue_qk(c + 1);
                 ++n_qk;
             }
-        }
-        mma_pending = true;
-        if (!mma_wait()) {
-            failed = true;
-            break;
-        }
-        mma_pending = false;
-        if (!wait_all(bar_v, w_v)) {
-            failed = true;
-            break;
-        }
-        // ---------------- 3. Z^T = beta (V - e^gamma Y)^T (warpgroup wg: tokens 32 wg ..) ----------------
-        {
-            float y[32];
-            umma::tmem_ld32(tmem + lane_base + C_YO + 32 * wg, y);
-            umma::tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int t = 32 * wg + j;
-                const float vv = bf_at(sm + R_VS, t * D + dv);
-                y[j] = umma::tf32_rna(sB[t] * (vv - sEG[t] * y[j]));
-            }
-            umma::tmem_st32(tmem + lane_base + C_Z + 32 * wg, y);
-            umma::tmem_wait_st();
-        }
-        umma::fence_before_sync();
-        __syncthreads();
-        // ---------------- 4. MMA-c: v_new^T = Z^T T^T; next chunk's v copy ----------------
-        if (!wait_all(bar_tp, w_tp)) {
-            failed = true;
-            break;
-        }
-        if (tid == 0) {
-            umma::fence_after_sync();
-            for (int kk = 0; kk < C / 8; ++kk)
-                umma::mma_tf32_ta(tmem + C_V, tmem + C_Z + kk * 8, umma::desc_kmajor(sb + R_TP, C, kk), idesc_c,
-                                  kk > 0);
-            umma::mma_commit(bar_mma);
-            if (c + 1 < NC) {
-                fence_proxy_async_smem();
-                issue_v(c + 1);
-                ++n_v;
-            }
-        }
-        mma_pending = true;
-        if (!mma_wait()) {
-            failed = true;
-            break;
-        }
-        mma_pending = false;
-        // ---------------- 5a. sub-chunk checkpoints (fp32 v_new, fp32 K, state before the update) ----------------
-        // S_s = e^{gamma_{s-1}} S + sum_{t<s} e^{gamma_{s-1}-gamma_t} k_t^T v_new_t (deltanet.py:375-388)
-        while (ck_i < ck.n && ck.off[ck_i] > t0 && ck.off[ck_i] - t0 < C) {
-            const int s_off = ck.off[ck_i] - t0;
-            if (tid < C) sF[tid] = tid < s_off ? expf(sG[s_off - 1] - sG[tid]) : 0.f;
-            __syncthreads();
-            const float es = expf(sG[s_off - 1]);
-            float wv[C];
+            // ---------------- 5b. v_new^T (tf32) and its e^{gamma_C - gamma} scaled copy (tokens 32 wg ..) ----------------
             {
-                float v[32];
-                umma::tmem_ld32(tmem + lane_base + C_V, v);
+                float v[32], w[32];
+                umma::tmem_ld32(tmem + lane_base + C_V + 32 * wg, v);
                 umma::tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) wv[j] = v[j] * sF[j];
-                umma::tmem_ld32(tmem + lane_base + C_V + 32, v);
-                umma::tmem_wait_ld();
-#pragma unroll
-                for (int j = 0; j < 32; ++j) wv[32 + j] = v[j] * sF[32 + j];
+                for (int j = 0; j < 32; ++j) {
+                    const int t = 32 * wg + j;
+                    w[j] = tf32_rn(v[j] * sv[V_EF + t]);
+                    v[j] = tf32_rn(v[j]);
+                }
+                umma::tmem_st32(tmem + lane_base + C_V + 32 * wg, v);
+                umma::tmem_st32(tmem + lane_base + C_Z + 32 * wg, w);
+                umma::tmem_wait_st();
             }
-            float* dst = p.S_ckpt + ((size_t)ck.slot[ck_i] * p.B * p.Hv + bh) * (size_t)(D * D);
+            umma::fence_before_sync();
+            nb_sync(1, NMAIN);
+            // ---------------- 6. MMA-d (D^T = v_new^T P^T), MMA-e (dS^T) ----------------
+            if (tid == 0) {
+                umma::fence_after_sync();
+                for (int kk = 0; kk < C / 8; ++kk)
+                    umma::mma_tf32_ta(tmem + C_YO, tmem + C_V + kk * 8,
+                                      umma::desc_kmajor(sb + R_TP + C * C * 4, C, kk), idesc_c, kk > 0);
+                for (int kk = 0; kk < C / 8; ++kk)
+                    umma::mma_tf32_ta(tmem + C_OP, tmem + C_Z + kk * 8, umma::desc_mnmajor(sb + R_KM, C, kk), idesc_e,
+                                      kk > 0);
+                umma::mma_commit(bar_mma);
+                umma::mma_commit(bar_ordy);  // O of this chunk is complete for the output warps
+                mma_pending = true;
+            }
+            if (!mma_wait()) {
+                failed = true;
+                break;
+            }
+            mma_pending = false;
+            if (tid == 0 && c + 1 < NC) {
+                fence_proxy_async_smem();
+                issue_tp(c + 1);
+                ++n_tp;
+            }
+            // ---------------- 7. state update (key columns 64 wg ..), checkpoints, final state ----------------
+            {
+                const float ec = sv[V_EG + C - 1];
+                const bool last = c == NC - 1;
 #pragma unroll 1
-            for (int c0 = 64 * wg; c0 < 64 * wg + 64; c0 += 32) {
-                float m[32];
-                umma::tmem_ld32(tmem + lane_base + C_MS + c0, m);
-                umma::tmem_wait_ld();
+                for (int c0 = 64 * wg; c0 < 64 * wg + 64; c0 += 32) {
+                    float m[32], d[32];
+                    umma::tmem_ld32(tmem + lane_base + C_MS + c0, m);
+                    umma::tmem_ld32(tmem + lane_base + C_OP + c0, d);
+                    umma::tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) m[j] *= es;
+                    for (int j = 0; j < 32; ++j) m[j] = fmaf(m[j], ec, d[j]);
+                    umma::tmem_st32(tmem + lane_base + C_MS + c0, m);
 #pragma unroll
-                for (int t = 0; t < C; ++t) {
-                    const float wt = wv[t] * vec[64 + t];  // v_new * decay * rk
-                    const uint4* krow = reinterpret_cast<const uint4*>(sm + R_KS + t * D * 2 + c0 * 2);
+                    for (int j = 0; j < 32; ++j) d[j] = tf32_rn(m[j]);
+                    umma::tmem_st32(tmem + lane_base + C_OP + c0, d);
+                    for (int w = ck_i; w < ck.n && ck.off[w] - t0 == C; ++w) {
+                        float* dst = p.S_ckpt + ((size_t)ck.slot[w] * p.B * p.Hv + bh) * (size_t)(D * D);
 #pragma unroll
-                    for (int j8 = 0; j8 < 4; ++j8) {
-                        const uint4 k8 = krow[j8];
-                        const uint32_t kw[4] = {k8.x, k8.y, k8.z, k8.w};
+                        for (int j = 0; j < 32; ++j) __stcs(dst + (size_t)(c0 + j) * D + dv, m[j]);
+                    }
+                    if (last && p.S_out) {
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            m[8 * j8 + 2 * e] = fmaf(wt, bf_lo(kw[e]), m[8 * j8 + 2 * e]);
-                            m[8 * j8 + 2 * e + 1] = fmaf(wt, bf_hi(kw[e]), m[8 * j8 + 2 * e + 1]);
-                        }
+                        for (int j = 0; j < 32; ++j) __stcs(p.S_out + ((size_t)bh * D + c0 + j) * D + dv, m[j]);
                     }
                 }
-#pragma unroll
-                for (int j = 0; j < 32; ++j) __stcs(dst + (size_t)(c0 + j) * D + dv, m[j]);
+                umma::tmem_wait_st();
             }
-            __syncthreads();
-            ++ck_i;
-        }
-        if (tid == 0 && has_sub && c + 1 < NC) {
-            fence_proxy_async_smem();
-            issue_qk(c + 1);
-            ++n_qk;
-        }
-        // ---------------- 5b. v_new^T (tf32) and its e^{gamma_C - gamma} scaled copy (tokens 32 wg ..) ----------------
-        {
-            float v[32], w[32];
-            umma::tmem_ld32(tmem + lane_base + C_V + 32 * wg, v);
-            umma::tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int t = 32 * wg + j;
-                w[j] = umma::tf32_rna(v[j] * sEF[t]);
-                v[j] = umma::tf32_rna(v[j]);
-            }
-            umma::tmem_st32(tmem + lane_base + C_V + 32 * wg, v);
-            umma::tmem_st32(tmem + lane_base + C_Z + 32 * wg, w);
-            umma::tmem_wait_st();
-        }
-        umma::fence_before_sync();
-        __syncthreads();
-        // ---------------- 6. MMA-d (D^T = v_new^T P^T), MMA-e (dS^T) ----------------
-        if (tid == 0) {
+            while (ck_i < ck.n && ck.off[ck_i] - t0 == C) ++ck_i;
+            umma::fence_before_sync();
+            nb_sync(1, NMAIN);
             umma::fence_after_sync();
-            for (int kk = 0; kk < C / 8; ++kk)
-                umma::mma_tf32_ta(tmem + C_YO, tmem + C_V + kk * 8, umma::desc_kmajor(sb + R_TP + C * C * 4, C, kk),
-                                  idesc_c, kk > 0);
-            for (int kk = 0; kk < C / 8; ++kk)
-                umma::mma_tf32_ta(tmem + C_OP, tmem + C_Z + kk * 8, umma::desc_mnmajor(sb + R_KM, C, kk), idesc_e,
-                                  kk > 0);
-            umma::mma_commit(bar_mma);
         }
-        mma_pending = true;
-        if (!mma_wait()) {
-            failed = true;
-            break;
+        if (failed && tid == 0) {
+            // let copies and MMAs in flight finish (bounded) before the CTA exits
+            for (; w_qk < n_qk; ++w_qk) mbar_wait_bounded(bar_qk, (uint32_t)w_qk & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            for (; w_v < n_v; ++w_v) mbar_wait_bounded(bar_v, (uint32_t)w_v & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            for (; w_tp < n_tp; ++w_tp) mbar_wait_bounded(bar_tp, (uint32_t)w_tp & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            if (mma_pending) mbar_wait_bounded(bar_mma, (mma_phase - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
         }
-        mma_pending = false;
-        if (tid == 0 && c + 1 < NC) {
-            fence_proxy_async_smem();
-            issue_tp(c + 1);
-            ++n_tp;
-        }
-        // ---------------- 7. state update (columns 64 wg ..) then output rows (tokens 32 wg ..) ----------------
-        {
-            const float ec = sEG[C - 1];
-            const bool last = c == NC - 1;
-#pragma unroll 1
-            for (int c0 = 64 * wg; c0 < 64 * wg + 64; c0 += 32) {
-                float m[32], d[32];
-                umma::tmem_ld32(tmem + lane_base + C_MS + c0, m);
-                umma::tmem_ld32(tmem + lane_base + C_OP + c0, d);
-                umma::tmem_wait_ld();
-#pragma unroll
-                for (int j = 0; j < 32; ++j) m[j] = fmaf(m[j], ec, d[j]);
-                umma::tmem_st32(tmem + lane_base + C_MS + c0, m);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) d[j] = umma::tf32_rna(m[j]);
-                umma::tmem_st32(tmem + lane_base + C_OP + c0, d);
-                for (int w = ck_i; w < ck.n && ck.off[w] - t0 == C; ++w) {
-                    float* dst = p.S_ckpt + ((size_t)ck.slot[w] * p.B * p.Hv + bh) * (size_t)(D * D);
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) __stcs(dst + (size_t)(c0 + j) * D + dv, m[j]);
-                }
-                if (last && p.S_out) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) __stcs(p.S_out + ((size_t)bh * D + c0 + j) * D + dv, m[j]);
-                }
+    } else {
+        // ======================= output rows (warpgroups 2-3) =======================
+        const int owg = wg - 2, tw = 32 * owg;  // this warpgroup's tokens tw .. tw + 31
+        const float nw = sNW[dv];
+        for (int c = 0; c < NC; ++c) {
+            const int t0 = c * C;
+            const float* sv = scr + S_V + 256 * (c & 1);
+            const bool rdy = mbar_wait_bounded(bar_ordy, (uint32_t)c & 1u, GDN_DEVERR_MMA_TIMEOUT);
+            if (nb_any(!rdy, 4, NT - NMAIN)) {
+                failed = true;
+                break;
             }
-        }
-        {
-            // O[t][dv] = e^{gamma_t} O1 + D, rounded; gated RMSNorm over dv (the 128 lanes)
-            const int tw = 32 * wg;  // this warpgroup's tokens tw .. tw + 31
+            umma::fence_after_sync();
+            // O[t][dv] = e^{gamma_t} O1 + D
             float o[32];
             {
                 float o1[32], dd[32];
@@ -398,8 +490,12 @@ __global__ void __launch_bounds__(NT, 1)
                 umma::tmem_ld32(tmem + lane_base + C_YO + tw, dd);
                 umma::tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) o[j] = bf16_round_alu(fmaf(sEG[tw + j], o1[j], dd[j]));
+                for (int j = 0; j < 32; ++j) o[j] = fmaf(sv[V_EG + tw + j], o1[j], dd[j]);
             }
+            umma::fence_before_sync();
+            mbar_arrive(bar_ofree);  // these tensor-memory columns may be overwritten now
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) round2_bf16(o[j], o[j + 1]);
             // per-token sums of squares over this warp's 32 lanes: halving exchange
             // that leaves token tw + lane in this lane
             float sq[32];
@@ -417,7 +513,7 @@ __global__ void __launch_bounds__(NT, 1)
                 }
             }
             sPart[q4 * C + tw + lane] = sq[0];
-            wg_sync(1 + wg);
+            nb_sync(2 + owg, 128);
             if (q4 == 0) {
                 const int t = tw + lane;
                 const float ss = (sPart[t] + sPart[C + t]) + (sPart[2 * C + t] + sPart[3 * C + t]);
@@ -425,48 +521,45 @@ __global__ void __launch_bounds__(NT, 1)
             }
             const bool zok = mbar_wait_bounded(bar_z, (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
             ++w_z;
-            wg_sync(1 + wg);
-            const float nw = sNW[dv];
-            TA* out = static_cast<TA*>(p.out) + ((size_t)b * T + t0 + tw) * (size_t)(p.Hv * D) + h * D + dv;
+            nb_sync(2 + owg, 128);
+            uint16_t* out = reinterpret_cast<uint16_t*>(static_cast<TA*>(p.out)) +
+                            ((size_t)b * T + t0 + tw) * (size_t)(p.Hv * D) + h * D + dv;
             if (zok) {
+                float y[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    if (t0 + tw + j < T) {
-                        const float y = bf16_round_alu(nw * bf16_round_alu(o[j] * sRstd[tw + j]));
-                        const float zz = bf_at(sm + R_ZS, (tw + j) * D + dv);
-                        reinterpret_cast<uint16_t*>(out)[(size_t)j * (p.Hv * D)] =
-                            bf16_bits(bf16_round_alu(y * __fdividef(zz, 1.0f + __expf(-zz))));
-                    }
+                for (int j = 0; j < 32; ++j) y[j] = o[j] * sRstd[tw + j];
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) round2_bf16(y[j], y[j + 1]);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) y[j] *= nw;
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) round2_bf16(y[j], y[j + 1]);
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const float z0 = bf_at(sm + R_ZS, (tw + j) * D + dv);
+                    const float z1 = bf_at(sm + R_ZS, (tw + j + 1) * D + dv);
+                    float a0 = y[j] * __fdividef(z0, 1.0f + __expf(-z0));
+                    float a1 = y[j + 1] * __fdividef(z1, 1.0f + __expf(-z1));
+                    uint32_t bits;
+                    round2_bf16(a0, a1, &bits);
+                    if (t0 + tw + j < T) out[(size_t)j * (p.Hv * D)] = (uint16_t)(bits & 0xFFFFu);
+                    if (t0 + tw + j + 1 < T) out[(size_t)(j + 1) * (p.Hv * D)] = (uint16_t)(bits >> 16);
                 }
-            } else {
+            }
+            // z rows consumed by both output warpgroups: refill with the next chunk's
+            nb_sync(4, NT - NMAIN);
+            if (tid == NMAIN && c + 1 < NC && zok) {
+                fence_proxy_async_smem();
+                issue_z(c + 1);
+                ++n_z;
+            }
+            if (nb_any(!zok, 4, NT - NMAIN)) {
                 failed = true;
+                break;
             }
         }
-        umma::fence_before_sync();
-        __syncthreads();
-        if (tid == 0 && c + 1 < NC && !failed) {
-            fence_proxy_async_smem();
-            issue_z(c + 1);
-            ++n_z;
-        }
-        while (ck_i < ck.n && ck.off[ck_i] - t0 == C) ++ck_i;
-        umma::fence_before_sync();
-        if (__syncthreads_or(failed)) {
-            failed = true;
-            break;
-        }
-        umma::fence_after_sync();
-    }
-
-    if (failed) {
-        // let copies and MMAs still in flight finish (bounded) before the CTA exits
-        if (tid == 0) {
-            for (; w_qk < n_qk; ++w_qk) mbar_wait_bounded(bar_qk, (uint32_t)w_qk & 1u, GDN_DEVERR_TMA_TIMEOUT);
-            for (; w_v < n_v; ++w_v) mbar_wait_bounded(bar_v, (uint32_t)w_v & 1u, GDN_DEVERR_TMA_TIMEOUT);
-            for (; w_tp < n_tp; ++w_tp) mbar_wait_bounded(bar_tp, (uint32_t)w_tp & 1u, GDN_DEVERR_TMA_TIMEOUT);
-            if (mma_pending) mbar_wait_bounded(bar_mma, (mma_phase - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
+        if (failed && tid == NMAIN)
             for (; w_z < n_z; ++w_z) mbar_wait_bounded(bar_z, (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
-        }
     }
     umma::fence_before_sync();
     __syncthreads();
