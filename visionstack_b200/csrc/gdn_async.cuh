@@ -95,4 +95,27 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst_smem, const void* tmap,
         : "memory");
 }
 
+// Tiled tensor copy shared -> global of one 3-D box of `tmap` at element
+// coordinates (c0, c1, c2) (c0 * element size a multiple of 16 bytes, no
+// negative coordinates), tracked by this thread's bulk-async group.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, uint32_t src_smem, int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(tmap), "r"(c0),
+        "r"(c1), "r"(c2), "r"(src_smem)
+        : "memory");
+}
+// One bulk copy shared -> global of `bytes` (multiple of 16, both addresses
+// 16-byte aligned), tracked by this thread's bulk-async group.
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src_smem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src_smem), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed bulk store of this thread has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until every committed bulk store of this thread has completed.
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 }  // namespace gdn

@@ -46,16 +46,20 @@ constexpr uint32_t GROUP_BYTES = ROWS * D * 2;  // raw rows of one 128-channel g
 constexpr int MAX_REP = 4;
 constexpr int A_STRIDE = 68;                     // floats per row of an A matrix (conflict-free row writes)
 constexpr uint32_t A_BYTES = C * A_STRIDE * 4;
+constexpr uint32_t IMG_BYTES = C * C * 4;        // one 64x64 tf32 operand image
 
 __host__ __device__ constexpr uint32_t region0_bytes(int rep) {
     const uint32_t stage = (uint32_t)(2 + rep) * GROUP_BYTES;
     const uint32_t kq = 128u * D * 4u;
-    const uint32_t am = 2u * (uint32_t)rep * A_BYTES;  // A and T matrices of every value head
+    // A and T matrices and the P operand image of every value head
+    const uint32_t am = 2u * (uint32_t)rep * A_BYTES + (uint32_t)rep * IMG_BYTES;
     const uint32_t m = stage > kq ? stage : kq;
     return ((m > am ? m : am) + 1023u) & ~1023u;
 }
-// small vectors after region 0 (floats): rq[64], rk[64], beta[MAX_REP][64], gamma[MAX_REP][64]
-constexpr int V_RQ = 0, V_RK = 64, V_B = 128, V_G = 128 + 64 * MAX_REP, V_END = 128 + 128 * MAX_REP;
+// small vectors after region 0 (floats): rq[64], rk[64], then per value head r
+// beta, gamma, e^gamma, e^-gamma [MAX_REP][64]
+constexpr int V_RQ = 0, V_RK = 64, V_B = 128, V_G = V_B + 64 * MAX_REP, V_EG = V_G + 64 * MAX_REP,
+              V_ENG = V_EG + 64 * MAX_REP, V_END = V_ENG + 64 * MAX_REP;
 __host__ __device__ constexpr uint32_t smem_bytes(int rep) { return region0_bytes(rep) + V_END * 4 + 64 + 1024; }
 
 using TA = __nv_bfloat16;
@@ -73,7 +77,6 @@ __device__ __forceinline__ void round2(float& a, float& b) {
     a = bf_lo(u);
     b = bf_hi(u);
 }
-
 // Column j of the inverse of the unit lower triangular 32x32 block I + A
 // (A strictly lower triangular, row stride A_STRIDE) by forward substitution:
 // X[i][j] = [i == j] - sum_{k<i} A[i][k] X[k][j] (X[k][j] = 0 for k < j).
@@ -123,7 +126,8 @@ __device__ __forceinline__ void block_row8(const float* L, const float* R, int i
 }
 
 __global__ void __launch_bounds__(NT, 2)
-    prefill_prep_kernel(const MixParams p, const PrefillWs ws, const __grid_constant__ CUtensorMap tm_mixed) {
+    prefill_prep_kernel(const MixParams p, const PrefillWs ws, const __grid_constant__ CUtensorMap tm_mixed,
+                        const __grid_constant__ CUtensorMap tm_qkv) {
     extern __shared__ unsigned char raw[];
     const uint32_t raw_addr = smem_u32(raw);
     unsigned char* sm = raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -217,7 +221,6 @@ __global__ void __launch_bounds__(NT, 2)
         // window registers: x1 = one token back, x2, x3 = three back (channel pair a, b)
         float a1 = h0[2], a2 = h0[1], a3 = h0[0];
         float b1 = h1[2], b2 = h1[1], b3 = h1[0];
-        __nv_bfloat16* gout = static_cast<__nv_bfloat16*>(ws.qkv) + ((size_t)b * ws.tp_len + t0) * conv_dim + gc;
         const bool full_window = cs_in != nullptr || c > 0;  // every token has 3 predecessors
 #pragma unroll 4
         for (int t = 0; t < C; ++t) {
@@ -250,14 +253,22 @@ __global__ void __launch_bounds__(NT, 2)
             a3 = a2; a2 = a1; a1 = x0;
             b3 = b2; b2 = b1; b1 = y0;
             *cell = outv;
-            *reinterpret_cast<uint32_t*>(gout + (size_t)t * conv_dim) = outv;
         }
+    }
+    // conv outputs (staging rows 3..66 of every group) to the workspace: one tensor store per group
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+        for (int g = 0; g < ngroups; ++g)
+            tma_store_3d(&tm_qkv, smem_u32(sm + g * GROUP_BYTES + HIST * D * 2), group_channel(g), t0, b);
+        bulk_commit_group();
     }
     __syncthreads();
 
     // ---- L2-norm factors of q and k: warp per token ----
     float* sRQ = vec + V_RQ;
     float* sRK = vec + V_RK;
+#pragma unroll
     for (int t = warp; t < C; t += NT / 32) {
         const uint2 qv = *reinterpret_cast<const uint2*>(sm + 0 * GROUP_BYTES + (t + HIST) * D * 2 + lane * 8);
         const uint2 kv = *reinterpret_cast<const uint2*>(sm + 1 * GROUP_BYTES + (t + HIST) * D * 2 + lane * 8);
@@ -279,6 +290,7 @@ __global__ void __launch_bounds__(NT, 2)
     __syncthreads();
 
     // ---- [K;Q] tf32 operand (rows 0..63 K, 64..127 Q) over the staging area ----
+    if (tid == 0) bulk_wait_group_read0();  // the conv-output stores have read the staging rows
     uint2 kq_raw[16];
 #pragma unroll
     for (int u = 0; u < 16; ++u) {
@@ -330,17 +342,33 @@ __global__ void __launch_bounds__(NT, 2)
     }
     __syncthreads();
     if (tid < rep) {
-        // sequential cumsum (the reference's torch.cumsum over the chunk)
+        // sequential cumsum (the reference's torch.cumsum over the chunk), in registers
+        float4* gr = reinterpret_cast<float4*>(sG + tid * 64);
+        float4 g4[C / 4];
+#pragma unroll
+        for (int i = 0; i < C / 4; ++i) g4[i] = gr[i];
         float acc = 0.f;
-        float* gr = sG + tid * 64;
-        for (int t = 0; t < C; ++t) {
-            acc += gr[t];
-            gr[t] = acc;
+#pragma unroll
+        for (int i = 0; i < C / 4; ++i) {
+            acc += g4[i].x;
+            g4[i].x = acc;
+            acc += g4[i].y;
+            g4[i].y = acc;
+            acc += g4[i].z;
+            g4[i].z = acc;
+            acc += g4[i].w;
+            g4[i].w = acc;
         }
+#pragma unroll
+        for (int i = 0; i < C / 4; ++i) gr[i] = g4[i];
     }
     __syncthreads();
+    float* sEG = vec + V_EG;
+    float* sENG = vec + V_ENG;
     for (int i = tid; i < rep * C; i += NT) {
         const int r = i / C, t = i % C;
+        sEG[i] = expf(sG[i]);
+        sENG[i] = expf(-sG[i]);
         float* gate = ws.gate + (((size_t)b * p.Hv + kh * rep + r) * NC + c) * 128;
         gate[t] = sB[r * 64 + t];
         gate[64 + t] = sG[r * 64 + t];
@@ -349,7 +377,10 @@ __global__ void __launch_bounds__(NT, 2)
     const bool mma_ok = mbar_wait_bounded(bar_mma, 0, GDN_DEVERR_MMA_TIMEOUT);
     umma::fence_after_sync();
     if (__syncthreads_or(!mma_ok)) {
-        if (tid == 0) mbar_wait_bounded(bar_mma, 0, GDN_DEVERR_MMA_TIMEOUT);
+        if (tid == 0) {
+            mbar_wait_bounded(bar_mma, 0, GDN_DEVERR_MMA_TIMEOUT);
+            bulk_wait_group0();
+        }
         umma::fence_before_sync();
         __syncthreads();
         if (warp == 0) umma::tmem_dealloc(tmem, 64);
@@ -377,35 +408,47 @@ __global__ void __launch_bounds__(NT, 2)
         for (int r = warp >> 2; r < rep; r += 2) {
             const float* gr = sG + r * 64;
             const float gt = gr[t];
+            // decay e^{gamma_t - gamma_j}: as e^{gamma_t} e^{-gamma_j} when neither factor can
+            // leave the normal range (gamma >= -80 over the chunk), else one exp per pair
+            const bool split = gr[C - 1] >= -80.f;
+            const float egt = sEG[r * 64 + t];
+            const float* eng = sENG + r * 64;
+            auto decay = [&](int j) -> float { return split ? egt * eng[j] : __expf(gt - gr[j]); };
             if (g_rows) {
                 const float bt = sB[r * 64 + t];
                 float* arow = reinterpret_cast<float*>(sm + r * A_BYTES) + t * A_STRIDE;
 #pragma unroll
                 for (int j = 0; j < C; j += 4) {
                     float4 a;
-                    a.x = j + 0 < t ? (bt * v[j + 0]) * __expf(gt - gr[j + 0]) : 0.f;
-                    a.y = j + 1 < t ? (bt * v[j + 1]) * __expf(gt - gr[j + 1]) : 0.f;
-                    a.z = j + 2 < t ? (bt * v[j + 2]) * __expf(gt - gr[j + 2]) : 0.f;
-                    a.w = j + 3 < t ? (bt * v[j + 3]) * __expf(gt - gr[j + 3]) : 0.f;
+                    a.x = j + 0 < t ? (bt * v[j + 0]) * decay(j + 0) : 0.f;
+                    a.y = j + 1 < t ? (bt * v[j + 1]) * decay(j + 1) : 0.f;
+                    a.z = j + 2 < t ? (bt * v[j + 2]) * decay(j + 2) : 0.f;
+                    a.w = j + 3 < t ? (bt * v[j + 3]) * decay(j + 3) : 0.f;
                     *reinterpret_cast<float4*>(arow + j) = a;
                 }
             } else {
-                unsigned char* img = reinterpret_cast<unsigned char*>(
-                    ws.tp + ((((size_t)b * p.Hv + kh * rep + r) * NC + c) * 2 + 1) * (C * C));
+                unsigned char* img = sm + 2 * rep * A_BYTES + r * IMG_BYTES;
 #pragma unroll
                 for (int j = 0; j < C; j += 4) {
                     float4 a;
-                    a.x = j + 0 <= t ? umma::tf32_rna(v[j + 0] * __expf(gt - gr[j + 0])) : 0.f;
-                    a.y = j + 1 <= t ? umma::tf32_rna(v[j + 1] * __expf(gt - gr[j + 1])) : 0.f;
-                    a.z = j + 2 <= t ? umma::tf32_rna(v[j + 2] * __expf(gt - gr[j + 2])) : 0.f;
-                    a.w = j + 3 <= t ? umma::tf32_rna(v[j + 3] * __expf(gt - gr[j + 3])) : 0.f;
+                    a.x = j + 0 <= t ? umma::tf32_rna(v[j + 0] * decay(j + 0)) : 0.f;
+                    a.y = j + 1 <= t ? umma::tf32_rna(v[j + 1] * decay(j + 1)) : 0.f;
+                    a.z = j + 2 <= t ? umma::tf32_rna(v[j + 2] * decay(j + 2)) : 0.f;
+                    a.w = j + 3 <= t ? umma::tf32_rna(v[j + 3] * decay(j + 3)) : 0.f;
                     *reinterpret_cast<float4*>(img + umma::kmajor_off(t, j, C)) = a;
                 }
             }
         }
     }
+    fence_proxy_async_smem();
     umma::fence_before_sync();
     __syncthreads();
+    if (tid == 0) {  // P images to the workspace
+        for (int r = 0; r < rep; ++r)
+            bulk_store(ws.tp + ((((size_t)b * p.Hv + kh * rep + r) * NC + c) * 2 + 1) * (C * C),
+                       smem_u32(sm + 2 * rep * A_BYTES + r * IMG_BYTES), IMG_BYTES);
+        bulk_commit_group();
+    }
 
     // ---- T = (I + A)^-1 in 32x32 blocks (the doubling merge of deltanet.py:146-160) ----
     // T11, T22 by forward substitution (one warp per block, lane = column), then
@@ -434,16 +477,23 @@ __global__ void __launch_bounds__(NT, 2)
         block_row8(Tr + 32 * A_STRIDE + 32, Tr + 32, i, jb, Tr + 32 * A_STRIDE, -1.f);  // T21 = -T22 X
     }
     __syncthreads();
-    // T image (tf32, zero above the diagonal)
+    // T images (tf32, zero above the diagonal) over the dead A matrices, then to the workspace
     for (int u = tid; u < rep * C * (C / 4); u += NT) {
         const int r = u / (C * C / 4), w = u % (C * C / 4), i = w >> 4, j = (w & 15) * 4;
         const float4 v = *reinterpret_cast<const float4*>(Tall + r * C * A_STRIDE + i * A_STRIDE + j);
         const float4 o = make_float4(j + 0 <= i ? umma::tf32_rna(v.x) : 0.f, j + 1 <= i ? umma::tf32_rna(v.y) : 0.f,
                                      j + 2 <= i ? umma::tf32_rna(v.z) : 0.f, j + 3 <= i ? umma::tf32_rna(v.w) : 0.f);
-        unsigned char* img = reinterpret_cast<unsigned char*>(
-            ws.tp + (((size_t)b * p.Hv + kh * rep + r) * NC + c) * 2 * (C * C));
-        *reinterpret_cast<float4*>(img + umma::kmajor_off(i, j, C)) = o;
+        *reinterpret_cast<float4*>(sm + r * A_BYTES + umma::kmajor_off(i, j, C)) = o;
     }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+        for (int r = 0; r < rep; ++r)
+            bulk_store(ws.tp + (((size_t)b * p.Hv + kh * rep + r) * NC + c) * 2 * (C * C), smem_u32(sm + r * A_BYTES),
+                       IMG_BYTES);
+        bulk_commit_group();
+    }
+    if (tid == 0) bulk_wait_group0();  // conv-output stores complete before the CTA exits
     umma::fence_before_sync();
     __syncthreads();
     if (warp == 0) umma::tmem_dealloc(tmem, 64);
@@ -465,6 +515,10 @@ cudaError_t launch_prefill_prep(const MixParams& p, const PrefillWs& ws, cudaStr
     if (!encode_tmap_3d_bf16(&tm_mixed, p.mixed, conv_dim, (uint64_t)p.T, (uint64_t)p.B, (uint64_t)p.ms_t * 2,
                              (uint64_t)p.ms_b * 2, 128, pprep::ROWS))
         return cudaErrorInvalidValue;
+    CUtensorMap tm_qkv;
+    if (!encode_tmap_3d_bf16(&tm_qkv, ws.qkv, conv_dim, (uint64_t)ws.tp_len, (uint64_t)p.B, conv_dim * 2,
+                             conv_dim * 2 * (uint64_t)ws.tp_len, 128, pprep::C))
+        return cudaErrorInvalidValue;
     const int bytes = (int)pprep::smem_bytes(rep);
     static int attr_bytes[64] = {0};
     int dev = 0;
@@ -477,7 +531,7 @@ cudaError_t launch_prefill_prep(const MixParams& p, const PrefillWs& ws, cudaStr
         attr_bytes[dev] = bytes;
     }
     const int grid = p.B * p.Hk * ws.nc;
-    pprep::prefill_prep_kernel<<<grid, pprep::NT, bytes, s>>>(p, ws, tm_mixed);
+    pprep::prefill_prep_kernel<<<grid, pprep::NT, bytes, s>>>(p, ws, tm_mixed, tm_qkv);
     return cudaGetLastError();
 }
 

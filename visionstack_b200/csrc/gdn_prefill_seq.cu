@@ -204,9 +204,12 @@ __global__ void __launch_bounds__(NT, 1)
     bool failed = false;
     if (main_grp) {
         // ======================= state path (warpgroups 0-1) =======================
-        const uint32_t idesc_b = umma::idesc_tf32(128, 128, 0, 0);
         const uint32_t idesc_c = umma::idesc_tf32(128, 64, 0, 0);
         const uint32_t idesc_e = umma::idesc_tf32(128, 128, 0, 1);
+        // B-operand descriptors at k-step 0 (the operand regions never move)
+        const uint32_t idesc_b = umma::idesc_tf32(128, 128, 0, 0);
+        const uint64_t d_kq = umma::desc_kmajor0(sb + R_KQ), d_t = umma::desc_kmajor0(sb + R_TP),
+                       d_p = umma::desc_kmajor0(sb + R_TP + C * C * 4), d_km = umma::desc_mnmajor0(sb + R_KM, C);
         uint32_t mma_phase = 0;
         int n_ofree = 0;  // o_free phases waited (thread 0)
         bool mma_pending = false;
@@ -276,9 +279,10 @@ __global__ void __launch_bounds__(NT, 1)
                 }
                 umma::fence_after_sync();
                 if (free_ok) {
+#pragma unroll
                     for (int kk = 0; kk < D / 8; ++kk)
-                        umma::mma_tf32_ta(tmem + C_YO, tmem + C_OP + kk * 8, umma::desc_kmajor(sb + R_KQ, 128, kk),
-                                          idesc_b, kk > 0);
+                        umma::mma_tf32_ta(tmem + C_YO, tmem + C_OP + kk * 8,
+                                          umma::desc_add(d_kq, umma::kmajor_kstep(kk, 128)), idesc_b, kk > 0);
                     umma::mma_commit(bar_mma);
                     mma_pending = true;
                     if (c + 1 < NC && !has_sub) {
@@ -323,9 +327,10 @@ __global__ void __launch_bounds__(NT, 1)
             }
             if (tid == 0) {
                 umma::fence_after_sync();
+#pragma unroll
                 for (int kk = 0; kk < C / 8; ++kk)
-                    umma::mma_tf32_ta(tmem + C_V, tmem + C_Z + kk * 8, umma::desc_kmajor(sb + R_TP, C, kk), idesc_c,
-                                      kk > 0);
+                    umma::mma_tf32_ta(tmem + C_V, tmem + C_Z + kk * 8, umma::desc_add(d_t, umma::kmajor_kstep(kk, C)),
+                                      idesc_c, kk > 0);
                 umma::mma_commit(bar_mma);
                 mma_pending = true;
                 if (c + 1 < NC) {
@@ -409,12 +414,14 @@ __global__ void __launch_bounds__(NT, 1)
             // ---------------- 6. MMA-d (D^T = v_new^T P^T), MMA-e (dS^T) ----------------
             if (tid == 0) {
                 umma::fence_after_sync();
+#pragma unroll
                 for (int kk = 0; kk < C / 8; ++kk)
-                    umma::mma_tf32_ta(tmem + C_YO, tmem + C_V + kk * 8,
-                                      umma::desc_kmajor(sb + R_TP + C * C * 4, C, kk), idesc_c, kk > 0);
+                    umma::mma_tf32_ta(tmem + C_YO, tmem + C_V + kk * 8, umma::desc_add(d_p, umma::kmajor_kstep(kk, C)),
+                                      idesc_c, kk > 0);
+#pragma unroll
                 for (int kk = 0; kk < C / 8; ++kk)
-                    umma::mma_tf32_ta(tmem + C_OP, tmem + C_Z + kk * 8, umma::desc_mnmajor(sb + R_KM, C, kk), idesc_e,
-                                      kk > 0);
+                    umma::mma_tf32_ta(tmem + C_OP, tmem + C_Z + kk * 8, umma::desc_add(d_km, umma::mnmajor_kstep(kk)),
+                                      idesc_e, kk > 0);
                 umma::mma_commit(bar_mma);
                 umma::mma_commit(bar_ordy);  // O of this chunk is complete for the output warps
                 mma_pending = true;

@@ -76,6 +76,22 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t base, int krows, int k
     return smem_desc(base + (uint32_t)(kk * 1024), (uint32_t)(krows * 128), 512, LAYOUT_SW128_BASE32);
 }
 
+// Byte offset of k-step kk inside a K-major operand with `rows` rows, and of an
+// MN-major operand: added (>> 4) to the descriptor's start-address field, so a
+// loop over k-steps needs one descriptor and an add per step.
+__host__ __device__ constexpr uint32_t kmajor_kstep(int kk, int rows) {
+    return (uint32_t)((kk >> 2) * rows * 128 + (kk & 3) * 32);
+}
+__host__ __device__ constexpr uint32_t mnmajor_kstep(int kk) { return (uint32_t)(kk * 1024); }
+// Descriptors of a K-major / MN-major operand at k-step 0 (start of a k loop).
+__device__ __forceinline__ uint64_t desc_kmajor0(uint32_t base) { return smem_desc(base, 16, 1024, LAYOUT_SW128); }
+__device__ __forceinline__ uint64_t desc_mnmajor0(uint32_t base, int krows) {
+    return smem_desc(base, (uint32_t)(krows * 128), 512, LAYOUT_SW128_BASE32);
+}
+// desc0 advanced by `bytes` (the start address field is 16-byte units in the low 14 bits;
+// operands here lie below 256 KB of shared memory, so the field cannot overflow).
+__device__ __forceinline__ uint64_t desc_add(uint64_t desc0, uint32_t bytes) { return desc0 + (bytes >> 4); }
+
 // Instruction descriptor of kind::tf32 with fp32 accumulation.
 // a_mn / b_mn: operand is MN-major (1) or K-major (0).
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, int a_mn, int b_mn) {
