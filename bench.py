@@ -12,7 +12,10 @@ slots (4 x 134 MB) keep every step's state traffic out of the 126 MB L2.
 With ``--gpus N`` (torchrun, one rank per GPU) the value heads are sharded:
 rank r owns value heads [r*32/N, (r+1)*32/N) and the key heads they read; the
 token mixer needs no exchange between ranks (each (batch, head) chain is
-independent), so the total work is fixed and the scaling is strong.
+independent).  The global batch grows with N (64 N decode rows, 8 N prefill
+rows, 16 N rollback rows), so every GPU keeps the single-GPU amount of work
+(weak scaling), and ``value`` is the whole job's rate in units of the
+single-GPU workload (B64 decode steps per second).
 
 Also reported: the chunked-prefill workload (batch 8 x 8192 tokens) and the
 speculative verify + rollback workload (batch 16, 4-token drafts) as secondary
@@ -243,7 +246,7 @@ def run_reference(args, rank: int, world: int) -> None:
     line = {
         "metric": "DeltaNet decode steps/s (B64, 16/32 heads, d128, bf16, fp32 state)",
         "value": rate, "unit": "steps/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 / rate, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "ms_per_step": 1000.0 / rate, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (seeded numpy)", "impl": "reference",
         "config": decode_config(args.gpus),
         "cpu_baseline": {"value": rate, "unit": "steps/s", "cores": cpu_cores(), "kind": "port",
@@ -254,8 +257,9 @@ def run_reference(args, rank: int, world: int) -> None:
 
 
 def decode_config(n: int):
-    return {"workload": "decode step: B64, hidden 2048, 16 k-heads / 32 v-heads, d128, conv 4",
-            "global_batch": 64, "seq_len": 1, "parallelism": f"value-head sharding x{n}" if n > 1 else "single GPU",
+    return {"workload": "decode step: B64 per GPU, hidden 2048, 16 k-heads / 32 v-heads, d128, conv 4",
+            "global_batch": 64 * n, "seq_len": 1,
+            "parallelism": f"value-head sharding x{n}, batch {64 * n} (64 per GPU)" if n > 1 else "single GPU",
             "l2": "inputs larger than L2: 4 rotating 134 MB state slots"}
 
 
@@ -299,11 +303,11 @@ def run_ours(args, rank: int, world: int) -> None:
         torch.cuda.synchronize(dev)
 
     if args.no_decode:
-        pf = run_prefill(torch, dist, m, local, dev, world, barrier, args.prefill_batch, args.prefill_seq)
+        pf = run_prefill(torch, dist, m, local, dev, world, barrier, args.prefill_batch * world, args.prefill_seq)
         if rank == 0:
             print(json.dumps({"prefill": pf}), flush=True)
         return
-    B = 64
+    B = 64 * world  # global batch: every rank has all rows for its value heads
     hv, hk, d = local.num_v_heads, local.num_k_heads, local.head_k_dim
     conv_dim, vdim = local.conv_dim, local.value_dim
     NSLOT, NIN = 4, 64
@@ -432,7 +436,8 @@ def run_ours(args, rank: int, world: int) -> None:
     # secondary: chunked prefill (batch 8 x 8192 tokens, all heads of the shard)
     prefill = None
     if not args.no_prefill:
-        prefill = run_prefill(torch, dist, m, local, dev, world, barrier, args.prefill_batch, args.prefill_seq)
+        prefill = run_prefill(torch, dist, m, local, dev, world, barrier, args.prefill_batch * world,
+                              args.prefill_seq)
 
     # secondary: speculative verify + rollback on per-row state slots
     rollback = None
@@ -447,14 +452,14 @@ def run_ours(args, rank: int, world: int) -> None:
     traffic = profiled_traffic("decode_b64") if world == 1 else None
     line = {
         "metric": "DeltaNet decode steps/s (B64, 16/32 heads, d128, bf16, fp32 state)",
-        "value": 1000.0 / ms_step, "unit": "steps/s", "n_gpus": world, "steps": K, "warmup": Wm,
-        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "value": world * 1000.0 / ms_step, "unit": "steps/s", "n_gpus": world, "steps": K, "warmup": Wm,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (seeded torch.randn on device)", "config": decode_config(world),
         "gpu_launches": K,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "traffic": traffic, "peak_source": src, "bytes_per_launch": bytes_launch,
                      "kernel": "gdn::dtma::decode_tma_kernel<128,1,bf16> (2 groups x 256 threads, 1 CTA/SM)"},
-        "e2e": {"value": 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+        "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "Qwen3_5GatedDeltaNet.mixer_plan -> gdn_mixer_decode; packed pinned host inputs, "
                         "H2D and D2H on two copy streams, double-buffered"},
         "clocks": sampler.summary(),
@@ -519,7 +524,7 @@ def run_rollback(torch, dist, m, local, dev, world, barrier, steps=1024):
     graph."""
     from visionstack_b200 import StateSlots
     wl = W.WORKLOADS["rollback"]
-    B, T = wl.batch, wl.seq_len
+    B, T = wl.batch * world, wl.seq_len  # global batch, 16 rows per GPU-equivalent
     hv, hk, d = local.num_v_heads, local.num_k_heads, local.head_k_dim
     g = torch.Generator(device=dev)
     g.manual_seed(5)
@@ -569,7 +574,8 @@ def run_rollback(torch, dist, m, local, dev, world, barrier, steps=1024):
     ach = nbytes / (ms * 1e-3) / 1e9
     return {"workload": f"speculative verify + rollback: B{B}, {T}-token drafts, accepted ~ U{{0..{T}}} (seed "
                         f"{wl.x_seed}), 16 k-heads / 32 v-heads (sharded), d128, bf16, {steps} steps",
-            "steps_per_s": 1000.0 / ms, "ms_per_step": ms, "gpu_launches_per_step": 2,
+            "steps_per_s": world * 1000.0 / ms, "unit": "B16 steps/s (whole job)", "ms_per_step": ms,
+            "gpu_launches_per_step": 2,
             "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
                          "peak_source": src, "bytes_per_step": nbytes,
                          "kernel": "gdn::dtma::decode_tma_kernel<128,8,bf16> with a slot table "
