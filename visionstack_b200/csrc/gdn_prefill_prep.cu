@@ -191,68 +191,53 @@ __global__ void __launch_bounds__(NT, 2)
     }
 
     // ---- conv + SiLU, in place: thread -> an adjacent channel pair of one group ----
+    // Taps newest first with one bf16 rounding per tap (deltanet.py:66-80), on packed channel
+    // pairs: the first tap is a bf16x2 multiply (the reference's rounded product), the others
+    // bf16x2 fused multiply-adds.  The reference adds in fp32 and then rounds to bf16; the
+    // product of two bf16 values and a bf16 accumulator always sum exactly in fp32 unless their
+    // magnitudes differ by more than 2^8 (accumulator larger) or 2^16 (product larger), so the
+    // two roundings agree except when such a sum also lands exactly on a bf16 tie.
     for (int pr = tid; pr < ngroups * (D / 2); pr += NT) {
         const int g = pr / (D / 2), ch = (pr % (D / 2)) * 2;
         const int gc = group_channel(g) + ch;
         unsigned char* gbase = sm + g * GROUP_BYTES;
         const TA* cw = static_cast<const TA*>(p.convw) + (size_t)gc * 4;
-        float w0[4], w1[4];
+        __nv_bfloat162 w[4];  // tap j of both channels
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            w0[j] = Act<TA>::ldg(cw + j);
-            w1[j] = Act<TA>::ldg(cw + 4 + j);
-        }
-        // history x[-3..-1] of both channels
-        float h0[3], h1[3];
+        for (int j = 0; j < 4; ++j) w[j] = __halves2bfloat162(cw[j], cw[4 + j]);
+        // history x[-3..-1] of both channels, packed like the rows
+        __nv_bfloat162 x1, x2, x3;
         if (c > 0) {
-#pragma unroll
-            for (int i = 0; i < HIST; ++i) {
-                const uint32_t v = *reinterpret_cast<const uint32_t*>(gbase + i * D * 2 + ch * 2);
-                h0[i] = bf_lo(v);
-                h1[i] = bf_hi(v);
-            }
+            x3 = *reinterpret_cast<const __nv_bfloat162*>(gbase + 0 * D * 2 + ch * 2);
+            x2 = *reinterpret_cast<const __nv_bfloat162*>(gbase + 1 * D * 2 + ch * 2);
+            x1 = *reinterpret_cast<const __nv_bfloat162*>(gbase + 2 * D * 2 + ch * 2);
         } else {
-#pragma unroll
-            for (int i = 0; i < HIST; ++i) {
-                h0[i] = cs_in ? Act<TA>::ld(cs_in + ((size_t)b * conv_dim + gc) * HIST + i) : 0.f;
-                h1[i] = cs_in ? Act<TA>::ld(cs_in + ((size_t)b * conv_dim + gc + 1) * HIST + i) : 0.f;
-            }
+            const TA zero = __float2bfloat16_rn(0.f);
+            const TA* sa = cs_in ? cs_in + ((size_t)b * conv_dim + gc) * HIST : nullptr;
+            const TA* sb2 = cs_in ? cs_in + ((size_t)b * conv_dim + gc + 1) * HIST : nullptr;
+            x3 = __halves2bfloat162(sa ? sa[0] : zero, sb2 ? sb2[0] : zero);
+            x2 = __halves2bfloat162(sa ? sa[1] : zero, sb2 ? sb2[1] : zero);
+            x1 = __halves2bfloat162(sa ? sa[2] : zero, sb2 ? sb2[2] : zero);
         }
-        // window registers: x1 = one token back, x2, x3 = three back (channel pair a, b)
-        float a1 = h0[2], a2 = h0[1], a3 = h0[0];
-        float b1 = h1[2], b2 = h1[1], b3 = h1[0];
         const bool full_window = cs_in != nullptr || c > 0;  // every token has 3 predecessors
 #pragma unroll 4
         for (int t = 0; t < C; ++t) {
-            uint32_t* cell = reinterpret_cast<uint32_t*>(gbase + (t + HIST) * D * 2 + ch * 2);
-            const uint32_t xv = *cell;
-            const float x0 = bf_lo(xv), y0 = bf_hi(xv);
+            __nv_bfloat162* cell = reinterpret_cast<__nv_bfloat162*>(gbase + (t + HIST) * D * 2 + ch * 2);
+            const __nv_bfloat162 x0 = *cell;
             const int tg = t0 + t;
             uint32_t outv = 0u;
             if (tg < T) {
-                // taps newest first, one rounding per tap (deltanet.py:66-80)
-                float ca = x0 * w0[3], cb = y0 * w1[3];
-                round2(ca, cb);
-                if (full_window || tg >= 1) {
-                    ca = fmaf(a1, w0[2], ca);
-                    cb = fmaf(b1, w1[2], cb);
-                    round2(ca, cb);
-                }
-                if (full_window || tg >= 2) {
-                    ca = fmaf(a2, w0[1], ca);
-                    cb = fmaf(b2, w1[1], cb);
-                    round2(ca, cb);
-                }
-                if (full_window || tg >= 3) {
-                    ca = fmaf(a3, w0[0], ca);
-                    cb = fmaf(b3, w1[0], cb);
-                    round2(ca, cb);
-                }
+                __nv_bfloat162 acc = __hmul2(x0, w[3]);
+                if (full_window || tg >= 1) acc = __hfma2(x1, w[2], acc);
+                if (full_window || tg >= 2) acc = __hfma2(x2, w[1], acc);
+                if (full_window || tg >= 3) acc = __hfma2(x3, w[0], acc);
+                const float ca = __low2float(acc), cb = __high2float(acc);
                 outv = pack_bf2(__fdividef(ca, 1.0f + __expf(-ca)), __fdividef(cb, 1.0f + __expf(-cb)));
             }
-            a3 = a2; a2 = a1; a1 = x0;
-            b3 = b2; b2 = b1; b1 = y0;
-            *cell = outv;
+            x3 = x2;
+            x2 = x1;
+            x1 = x0;
+            *reinterpret_cast<uint32_t*>(cell) = outv;
         }
     }
     // conv outputs (staging rows 3..66 of every group) to the workspace: one tensor store per group
