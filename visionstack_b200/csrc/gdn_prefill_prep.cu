@@ -250,21 +250,40 @@ __global__ void __launch_bounds__(NT, 2)
     }
     __syncthreads();
 
-    // ---- L2-norm factors of q and k: warp per token ----
+    // ---- L2-norm factors of q and k: warp per token (8 tokens per warp, loads first) ----
     float* sRQ = vec + V_RQ;
     float* sRK = vec + V_RK;
+    {
+        constexpr int TPW = C / (NT / 32);  // tokens per warp
+        float sq[TPW], sk[TPW];
 #pragma unroll
-    for (int t = warp; t < C; t += NT / 32) {
-        const uint2 qv = *reinterpret_cast<const uint2*>(sm + 0 * GROUP_BYTES + (t + HIST) * D * 2 + lane * 8);
-        const uint2 kv = *reinterpret_cast<const uint2*>(sm + 1 * GROUP_BYTES + (t + HIST) * D * 2 + lane * 8);
-        const float q0 = bf_lo(qv.x), q1 = bf_hi(qv.x), q2 = bf_lo(qv.y), q3 = bf_hi(qv.y);
-        const float k0 = bf_lo(kv.x), k1 = bf_hi(kv.x), k2 = bf_lo(kv.y), k3 = bf_hi(kv.y);
-        float sq = q0 * q0 + q1 * q1 + q2 * q2 + q3 * q3;
-        float sk = k0 * k0 + k1 * k1 + k2 * k2 + k3 * k3;
-        sq = warp_sum(sq);
-        sk = warp_sum(sk);
-        if (lane == 0) {
-            const float rq = rsqrtf(sq + 1e-6f), rk = rsqrtf(sk + 1e-6f);
+        for (int i = 0; i < TPW; ++i) {
+            const int t = warp + i * (NT / 32);
+            const uint2 qv = *reinterpret_cast<const uint2*>(sm + 0 * GROUP_BYTES + (t + HIST) * D * 2 + lane * 8);
+            const uint2 kv = *reinterpret_cast<const uint2*>(sm + 1 * GROUP_BYTES + (t + HIST) * D * 2 + lane * 8);
+            const float q0 = bf_lo(qv.x), q1 = bf_hi(qv.x), q2 = bf_lo(qv.y), q3 = bf_hi(qv.y);
+            const float k0 = bf_lo(kv.x), k1 = bf_hi(kv.x), k2 = bf_lo(kv.y), k3 = bf_hi(kv.y);
+            sq[i] = q0 * q0 + q1 * q1 + q2 * q2 + q3 * q3;
+            sk[i] = k0 * k0 + k1 * k1 + k2 * k2 + k3 * k3;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int i = 0; i < TPW; ++i) {
+                sq[i] += __shfl_xor_sync(0xffffffffu, sq[i], o);
+                sk[i] += __shfl_xor_sync(0xffffffffu, sk[i], o);
+            }
+        }
+        if (lane < TPW) {
+            // lane i publishes token warp + 8 i (register index by a select chain, no local memory)
+            float a = sq[0], k = sk[0];
+#pragma unroll
+            for (int i = 1; i < TPW; ++i) {
+                a = lane == i ? sq[i] : a;
+                k = lane == i ? sk[i] : k;
+            }
+            const int t = warp + lane * (NT / 32);
+            const float rq = rsqrtf(a + 1e-6f), rk = rsqrtf(k + 1e-6f);
             sRQ[t] = rq;
             sRK[t] = rk;
             float* nrm = ws.nrm + (((size_t)b * p.Hk + kh) * NC + c) * 128;
@@ -373,23 +392,13 @@ __global__ void __launch_bounds__(NT, 2)
     }
 
     // ---- A (shared memory) and P (operand image) per value head from G, P0 ----
+    // 32 columns at a time; every shared-memory operand of a half is read into
+    // registers before the half's stores, so loads never wait behind stores.
     {
         const int q4 = warp & 3;
         const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
         const bool g_rows = q4 < 2;
         const int t = g_rows ? lane + 32 * q4 : lane + 32 * (q4 - 2);
-        float v[64];
-        {
-            float w[32];
-            umma::tmem_ld32(tmem + lane_base + 0, w);
-            umma::tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = w[j];
-            umma::tmem_ld32(tmem + lane_base + 32, w);
-            umma::tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[32 + j] = w[j];
-        }
         for (int r = warp >> 2; r < rep; r += 2) {
             const float* gr = sG + r * 64;
             const float gt = gr[t];
@@ -397,30 +406,57 @@ __global__ void __launch_bounds__(NT, 2)
             // leave the normal range (gamma >= -80 over the chunk), else one exp per pair
             const bool split = gr[C - 1] >= -80.f;
             const float egt = sEG[r * 64 + t];
-            const float* eng = sENG + r * 64;
-            auto decay = [&](int j) -> float { return split ? egt * eng[j] : __expf(gt - gr[j]); };
-            if (g_rows) {
-                const float bt = sB[r * 64 + t];
-                float* arow = reinterpret_cast<float*>(sm + r * A_BYTES) + t * A_STRIDE;
+            const float bt = sB[r * 64 + t];
+            float* arow = reinterpret_cast<float*>(sm + r * A_BYTES) + t * A_STRIDE;
+            unsigned char* img = sm + 2 * rep * A_BYTES + r * IMG_BYTES;
 #pragma unroll
-                for (int j = 0; j < C; j += 4) {
-                    float4 a;
-                    a.x = j + 0 < t ? (bt * v[j + 0]) * decay(j + 0) : 0.f;
-                    a.y = j + 1 < t ? (bt * v[j + 1]) * decay(j + 1) : 0.f;
-                    a.z = j + 2 < t ? (bt * v[j + 2]) * decay(j + 2) : 0.f;
-                    a.w = j + 3 < t ? (bt * v[j + 3]) * decay(j + 3) : 0.f;
-                    *reinterpret_cast<float4*>(arow + j) = a;
+            for (int hf = 0; hf < 2; ++hf) {
+                float v[32], dec[32];
+                umma::tmem_ld32(tmem + lane_base + 32 * hf, v);
+                if (split) {
+                    const float4* e4 = reinterpret_cast<const float4*>(sENG + r * 64 + 32 * hf);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const float4 e = e4[q];
+                        dec[4 * q] = egt * e.x;
+                        dec[4 * q + 1] = egt * e.y;
+                        dec[4 * q + 2] = egt * e.z;
+                        dec[4 * q + 3] = egt * e.w;
+                    }
+                } else {
+                    const float4* g4 = reinterpret_cast<const float4*>(gr + 32 * hf);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const float4 e = g4[q];
+                        dec[4 * q] = __expf(gt - e.x);
+                        dec[4 * q + 1] = __expf(gt - e.y);
+                        dec[4 * q + 2] = __expf(gt - e.z);
+                        dec[4 * q + 3] = __expf(gt - e.w);
+                    }
                 }
-            } else {
-                unsigned char* img = sm + 2 * rep * A_BYTES + r * IMG_BYTES;
+                umma::tmem_wait_ld();
+                if (g_rows) {
 #pragma unroll
-                for (int j = 0; j < C; j += 4) {
-                    float4 a;
-                    a.x = j + 0 <= t ? umma::tf32_rna(v[j + 0] * decay(j + 0)) : 0.f;
-                    a.y = j + 1 <= t ? umma::tf32_rna(v[j + 1] * decay(j + 1)) : 0.f;
-                    a.z = j + 2 <= t ? umma::tf32_rna(v[j + 2] * decay(j + 2)) : 0.f;
-                    a.w = j + 3 <= t ? umma::tf32_rna(v[j + 3] * decay(j + 3)) : 0.f;
-                    *reinterpret_cast<float4*>(img + umma::kmajor_off(t, j, C)) = a;
+                    for (int jj = 0; jj < 32; jj += 4) {
+                        const int j = 32 * hf + jj;
+                        float4 a;
+                        a.x = j + 0 < t ? (bt * v[jj + 0]) * dec[jj + 0] : 0.f;
+                        a.y = j + 1 < t ? (bt * v[jj + 1]) * dec[jj + 1] : 0.f;
+                        a.z = j + 2 < t ? (bt * v[jj + 2]) * dec[jj + 2] : 0.f;
+                        a.w = j + 3 < t ? (bt * v[jj + 3]) * dec[jj + 3] : 0.f;
+                        *reinterpret_cast<float4*>(arow + j) = a;
+                    }
+                } else {
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj += 4) {
+                        const int j = 32 * hf + jj;
+                        float4 a;
+                        a.x = j + 0 <= t ? umma::tf32_rna(v[jj + 0] * dec[jj + 0]) : 0.f;
+                        a.y = j + 1 <= t ? umma::tf32_rna(v[jj + 1] * dec[jj + 1]) : 0.f;
+                        a.z = j + 2 <= t ? umma::tf32_rna(v[jj + 2] * dec[jj + 2]) : 0.f;
+                        a.w = j + 3 <= t ? umma::tf32_rna(v[jj + 3] * dec[jj + 3]) : 0.f;
+                        *reinterpret_cast<float4*>(img + umma::kmajor_off(t, j, C)) = a;
+                    }
                 }
             }
         }
