@@ -526,7 +526,8 @@ bool prefill_prep_supported(const MixParams& p, int d, int dtype) {
     const int rep = p.Hk > 0 ? p.Hv / p.Hk : 0;
     auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
     return dtype == GDN_DTYPE_BF16 && d == 128 && p.K == 4 && (rep == 1 || rep == 2 || rep == 4) && al(p.mixed) &&
-           (p.ms_b % 8) == 0 && (p.ms_t % 8) == 0 && al(p.z) && (p.zs_b % 8) == 0 && (p.zs_t % 8) == 0;
+           (p.ms_b % 8) == 0 && (p.ms_t % 8) == 0 && al(p.z) && (p.zs_b % 8) == 0 && (p.zs_t % 8) == 0 &&
+           al(p.out);
 }
 
 cudaError_t launch_prefill_prep(const MixParams& p, const PrefillWs& ws, cudaStream_t s) {

@@ -109,7 +109,8 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 
 __global__ void __launch_bounds__(NT, 1)
     prefill_seq_kernel(const MixParams p, const CkptList ck, const PrefillWs ws,
-                       const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_z) {
+                       const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_z,
+                       const __grid_constant__ CUtensorMap tm_out) {
     extern __shared__ unsigned char raw[];
     const uint32_t raw_addr = smem_u32(raw);
     unsigned char* sm = raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -249,20 +250,25 @@ __global__ void __launch_bounds__(NT, 1)
                 sv[V_EG + tid] = expf(gt);
                 sv[V_EF + tid] = expf(gC - gt);
             }
+            // every raw q / k value and norm factor of this thread first (no load behind a store)
+            uint2 raws[16];
+            float scl[16];
 #pragma unroll
             for (int u = 0; u < 16; ++u) {
                 const int idx = tid + u * NMAIN, r = idx >> 5, c4 = (idx & 31) * 4, t = r & 63;
-                const uint2 raw2 = *reinterpret_cast<const uint2*>(sm + (u < 8 ? R_KS : R_QS) + t * D * 2 + c4 * 2);
+                raws[u] = *reinterpret_cast<const uint2*>(sm + (u < 8 ? R_KS : R_QS) + t * D * 2 + c4 * 2);
+                scl[u] = u < 8 ? vec[64 + t] : vec[t];
+            }
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const uint2 raw2 = raws[u];
                 float4 f = make_float4(bf_lo(raw2.x), bf_hi(raw2.x), bf_lo(raw2.y), bf_hi(raw2.y));
-                if (u < 8) {
-                    const float s = vec[64 + t];
-                    f = tf32_rn4(make_float4(f.x * s, f.y * s, f.z * s, f.w * s));
-                    *reinterpret_cast<float4*>(sm + off_km[u]) = f;
-                } else {
-                    const float s = vec[t];
-                    f = tf32_rn4(make_float4((f.x * s) * p.q_scale, (f.y * s) * p.q_scale, (f.z * s) * p.q_scale,
-                                             (f.w * s) * p.q_scale));
-                }
+                const float s = scl[u];
+                f = make_float4(f.x * s, f.y * s, f.z * s, f.w * s);
+                if (u >= 8)  // q: (q * rq) * dk^-1/2, the reference's order
+                    f = make_float4(f.x * p.q_scale, f.y * p.q_scale, f.z * p.q_scale, f.w * p.q_scale);
+                f = tf32_rn4(f);
+                if (u < 8) *reinterpret_cast<float4*>(sm + off_km[u]) = f;
                 *reinterpret_cast<float4*>(sm + off_kq[u]) = f;
             }
             fence_proxy_async_smem();
@@ -529,12 +535,17 @@ __global__ void __launch_bounds__(NT, 1)
             const bool zok = mbar_wait_bounded(bar_z, (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
             ++w_z;
             nb_sync(2 + owg, 128);
-            uint16_t* out = reinterpret_cast<uint16_t*>(static_cast<TA*>(p.out)) +
-                            ((size_t)b * T + t0 + tw) * (size_t)(p.Hv * D) + h * D + dv;
-            if (zok) {
-                float y[32];
+            // the rows are assembled in the z tile's place ([64 tokens][128] bf16) and leave by one
+            // tensor store, so every z value is read before the tile is overwritten
+            float y[32], zv[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) y[j] = o[j] * sRstd[tw + j];
+            for (int j = 0; j < 32; ++j) {
+                y[j] = o[j] * sRstd[tw + j];
+                zv[j] = zok ? bf_at(sm + R_ZS, (tw + j) * D + dv) : 0.f;
+            }
+            nb_sync(4, NT - NMAIN);
+            uint16_t* tile = reinterpret_cast<uint16_t*>(sm + R_ZS) + tw * D + dv;
+            if (zok) {
 #pragma unroll
                 for (int j = 0; j < 32; j += 2) round2_bf16(y[j], y[j + 1]);
 #pragma unroll
@@ -543,22 +554,28 @@ __global__ void __launch_bounds__(NT, 1)
                 for (int j = 0; j < 32; j += 2) round2_bf16(y[j], y[j + 1]);
 #pragma unroll
                 for (int j = 0; j < 32; j += 2) {
-                    const float z0 = bf_at(sm + R_ZS, (tw + j) * D + dv);
-                    const float z1 = bf_at(sm + R_ZS, (tw + j + 1) * D + dv);
+                    const float z0 = zv[j], z1 = zv[j + 1];
                     float a0 = y[j] * __fdividef(z0, 1.0f + __expf(-z0));
                     float a1 = y[j + 1] * __fdividef(z1, 1.0f + __expf(-z1));
                     uint32_t bits;
                     round2_bf16(a0, a1, &bits);
-                    if (t0 + tw + j < T) out[(size_t)j * (p.Hv * D)] = (uint16_t)(bits & 0xFFFFu);
-                    if (t0 + tw + j + 1 < T) out[(size_t)(j + 1) * (p.Hv * D)] = (uint16_t)(bits >> 16);
+                    tile[j * D] = (uint16_t)(bits & 0xFFFFu);
+                    tile[(j + 1) * D] = (uint16_t)(bits >> 16);
                 }
             }
-            // z rows consumed by both output warpgroups: refill with the next chunk's
+            fence_proxy_async_smem();
             nb_sync(4, NT - NMAIN);
-            if (tid == NMAIN && c + 1 < NC && zok) {
-                fence_proxy_async_smem();
-                issue_z(c + 1);
-                ++n_z;
+            if (tid == NMAIN) {
+                if (zok) {
+                    // rows past the sequence end fall outside the tensor map and are not written
+                    tma_store_3d(&tm_out, sb + R_ZS, h * D, t0, b);
+                    bulk_commit_group();
+                    bulk_wait_group_read0();  // the tile is read: the next z rows may land there
+                }
+                if (c + 1 < NC && zok) {
+                    issue_z(c + 1);
+                    ++n_z;
+                }
             }
             if (nb_any(!zok, 4, NT - NMAIN)) {
                 failed = true;
@@ -567,6 +584,7 @@ __global__ void __launch_bounds__(NT, 1)
         }
         if (failed && tid == NMAIN)
             for (; w_z < n_z; ++w_z) mbar_wait_bounded(bar_z, (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
+        if (tid == NMAIN) bulk_wait_group0();  // output rows written before the CTA exits
     }
     umma::fence_before_sync();
     __syncthreads();
@@ -577,11 +595,13 @@ __global__ void __launch_bounds__(NT, 1)
 
 cudaError_t launch_prefill_seq(const MixParams& p, const CkptList& ck, const PrefillWs& ws, cudaStream_t s) {
     const uint64_t conv_dim = 2ull * p.Hk * 128 + (uint64_t)p.Hv * 128;
-    CUtensorMap tm_qkv, tm_z;
+    CUtensorMap tm_qkv, tm_z, tm_out;
     if (!encode_tmap_3d_bf16(&tm_qkv, ws.qkv, conv_dim, (uint64_t)ws.tp_len, (uint64_t)p.B, conv_dim * 2,
                              conv_dim * 2 * (uint64_t)ws.tp_len, 128, pseq::C) ||
         !encode_tmap_3d_bf16(&tm_z, p.z, (uint64_t)p.Hv * 128, (uint64_t)p.T, (uint64_t)p.B, (uint64_t)p.zs_t * 2,
-                             (uint64_t)p.zs_b * 2, 128, pseq::C))
+                             (uint64_t)p.zs_b * 2, 128, pseq::C) ||
+        !encode_tmap_3d_bf16(&tm_out, p.out, (uint64_t)p.Hv * 128, (uint64_t)p.T, (uint64_t)p.B,
+                             (uint64_t)p.Hv * 128 * 2, (uint64_t)p.Hv * 128 * 2 * (uint64_t)p.T, 128, pseq::C))
         return cudaErrorInvalidValue;
     static bool attr_set[64] = {false};
     int dev = 0;
@@ -594,7 +614,7 @@ cudaError_t launch_prefill_seq(const MixParams& p, const CkptList& ck, const Pre
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
-    pseq::prefill_seq_kernel<<<p.B * p.Hv, pseq::NT, pseq::SMEM_BYTES, s>>>(p, ck, ws, tm_qkv, tm_z);
+    pseq::prefill_seq_kernel<<<p.B * p.Hv, pseq::NT, pseq::SMEM_BYTES, s>>>(p, ck, ws, tm_qkv, tm_z, tm_out);
     return cudaGetLastError();
 }
 
