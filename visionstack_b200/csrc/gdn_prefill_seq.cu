@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(NT, 1)
     uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + R_BAR + 96);
     const uint32_t bar_qk = smem_u32(&bars[0]), bar_v = smem_u32(&bars[1]), bar_z = smem_u32(&bars[2]),
                    bar_tp = smem_u32(&bars[3]), bar_mma = smem_u32(&bars[4]), bar_ordy = smem_u32(&bars[5]),
-                   bar_ofree = smem_u32(&bars[6]);
+                   bar_ofree = smem_u32(&bars[6]), bar_bdone = smem_u32(&bars[7]), bar_staged = smem_u32(&bars[8]);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int wg = warp >> 2, q4 = warp & 3;
@@ -135,11 +135,13 @@ __global__ void __launch_bounds__(NT, 1)
     const int bh = blockIdx.x;
     const int b = bh / p.Hv, h = bh - (bh / p.Hv) * p.Hv;
     const int rep = p.Hv / p.Hk, kh = h / rep;
-    const int T = p.T, NC = ws.nc;
+    const int NC = ws.nc;
 
     if (tid == 0) {
         for (int i = 0; i < 6; ++i) mbar_init(smem_u32(&bars[i]), 1);
         mbar_init(bar_ofree, NT - NMAIN);
+        mbar_init(bar_bdone, 1);
+        mbar_init(bar_staged, NT - NMAIN);
         fence_mbar_init();
     }
     if (warp == 0) {
@@ -188,7 +190,7 @@ __global__ void __launch_bounds__(NT, 1)
     };
     // copies issued (by their issuing thread) and waits completed (uniform in a group)
     int n_qk = 0, n_v = 0, n_z = 0, n_tp = 0;
-    int w_qk = 0, w_v = 0, w_z = 0, w_tp = 0;
+    int w_qk = 0, w_v = 0, w_z = 0, w_tp = 0, w_st = 0;
     if (tid == 0) {
         issue_qk(0);
         issue_v(0);
@@ -215,15 +217,6 @@ __global__ void __launch_bounds__(NT, 1)
         int n_ofree = 0;  // o_free phases waited (thread 0)
         bool mma_pending = false;
         int ck_i = 0;
-        // operand staging offsets of this thread (the same every chunk): [K;Q] row r,
-        // columns c4..c4+3 for r = (tid + 256 u) / 32; rows r < 64 also go to K MN-major
-        uint32_t off_kq[16], off_km[8];
-#pragma unroll
-        for (int u = 0; u < 16; ++u) {
-            const int idx = tid + u * NMAIN, r = idx >> 5, c4 = (idx & 31) * 4;
-            off_kq[u] = R_KQ + umma::kmajor_off(r, c4, 128);
-            if (u < 8) off_km[u] = R_KM + umma::mnmajor_off(r, c4, C);
-        }
         auto mma_wait = [&]() -> bool {
             const bool ok = mbar_wait_bounded(bar_mma, mma_phase & 1u, GDN_DEVERR_MMA_TIMEOUT);
             ++mma_phase;
@@ -238,42 +231,11 @@ __global__ void __launch_bounds__(NT, 1)
         for (int c = 0; c < NC; ++c) {
             const int t0 = c * C;
             float* sv = scr + S_V + 256 * (c & 1);
-            // ---------------- 1. operands of the chunk ----------------
-            if (!wait_main(bar_qk, w_qk)) {
+            // ---------------- 1. operands of the chunk (staged by the output warps) ----------------
+            if (!wait_main(bar_staged, w_st)) {
                 failed = true;
                 break;
             }
-            if (tid < C) {
-                const float gC = vec[192 + C - 1], gt = vec[192 + tid];
-                sv[V_B + tid] = vec[128 + tid];
-                sv[V_G + tid] = gt;
-                sv[V_EG + tid] = expf(gt);
-                sv[V_EF + tid] = expf(gC - gt);
-            }
-            // every raw q / k value and norm factor of this thread first (no load behind a store)
-            uint2 raws[16];
-            float scl[16];
-#pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const int idx = tid + u * NMAIN, r = idx >> 5, c4 = (idx & 31) * 4, t = r & 63;
-                raws[u] = *reinterpret_cast<const uint2*>(sm + (u < 8 ? R_KS : R_QS) + t * D * 2 + c4 * 2);
-                scl[u] = u < 8 ? vec[64 + t] : vec[t];
-            }
-#pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const uint2 raw2 = raws[u];
-                float4 f = make_float4(bf_lo(raw2.x), bf_hi(raw2.x), bf_lo(raw2.y), bf_hi(raw2.y));
-                const float s = scl[u];
-                f = make_float4(f.x * s, f.y * s, f.z * s, f.w * s);
-                if (u >= 8)  // q: (q * rq) * dk^-1/2, the reference's order
-                    f = make_float4(f.x * p.q_scale, f.y * p.q_scale, f.z * p.q_scale, f.w * p.q_scale);
-                f = tf32_rn4(f);
-                if (u < 8) *reinterpret_cast<float4*>(sm + off_km[u]) = f;
-                *reinterpret_cast<float4*>(sm + off_kq[u]) = f;
-            }
-            fence_proxy_async_smem();
-            umma::fence_before_sync();
-            nb_sync(1, NMAIN);
             // checkpoints strictly inside this chunk keep the k rows (and rk) until step 5
             const bool has_sub = ck_i < ck.n && ck.off[ck_i] > t0 && ck.off[ck_i] - t0 < C;
             // ---------------- 2. MMA-b (after the output warps released O of the last chunk) ----------------
@@ -290,6 +252,7 @@ __global__ void __launch_bounds__(NT, 1)
                         umma::mma_tf32_ta(tmem + C_YO, tmem + C_OP + kk * 8,
                                           umma::desc_add(d_kq, umma::kmajor_kstep(kk, 128)), idesc_b, kk > 0);
                     umma::mma_commit(bar_mma);
+                    umma::mma_commit(bar_bdone);  // [K;Q] may be restaged for the next chunk
                     mma_pending = true;
                     if (c + 1 < NC && !has_sub) {
                         issue_qk(c + 1);
@@ -477,18 +440,86 @@ __global__ void __launch_bounds__(NT, 1)
         }
         if (failed && tid == 0) {
             // let copies and MMAs in flight finish (bounded) before the CTA exits
-            for (; w_qk < n_qk; ++w_qk) mbar_wait_bounded(bar_qk, (uint32_t)w_qk & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            // q/k copies are waited for by the output warps: wait for the last one issued
+            if (n_qk > 0) mbar_wait_bounded(bar_qk, (uint32_t)(n_qk - 1) & 1u, GDN_DEVERR_TMA_TIMEOUT);
             for (; w_v < n_v; ++w_v) mbar_wait_bounded(bar_v, (uint32_t)w_v & 1u, GDN_DEVERR_TMA_TIMEOUT);
             for (; w_tp < n_tp; ++w_tp) mbar_wait_bounded(bar_tp, (uint32_t)w_tp & 1u, GDN_DEVERR_TMA_TIMEOUT);
             if (mma_pending) mbar_wait_bounded(bar_mma, (mma_phase - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
         }
     } else {
-        // ======================= output rows (warpgroups 2-3) =======================
+        // ======================= output rows and operand staging (warpgroups 2-3) =======================
         const int owg = wg - 2, tw = 32 * owg;  // this warpgroup's tokens tw .. tw + 31
+        const int otid = tid - NMAIN;
         const float nw = sNW[dv];
-        for (int c = 0; c < NC; ++c) {
+        // chunk cc's vectors (beta, gamma, e^gamma, e^{gamma_C - gamma}) from the loaded rows
+        auto stage_vectors = [&](int cc) {
+            float* sv = scr + S_V + 256 * (cc & 1);
+            if (otid < C) {
+                const float gC = vec[192 + C - 1], gt = vec[192 + otid];
+                sv[V_B + otid] = vec[128 + otid];
+                sv[V_G + otid] = gt;
+                sv[V_EG + otid] = expf(gt);
+                sv[V_EF + otid] = expf(gC - gt);
+            }
+        };
+        // [K;Q] rows (K: k * rk, Q: (q * rq) * dk^-1/2, tf32) of the loaded chunk; with
+        // km, the K rows also go to the K MN-major operand
+        auto stage_rows = [&](bool kq, bool km) {
+            uint2 raws[16];
+            float scl[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {  // every shared operand first (no load behind a store)
+                const int idx = otid + u * (NT - NMAIN), r = idx >> 5, c4 = (idx & 31) * 4, t = r & 63;
+                if (u < 8 || kq) {
+                    raws[u] = *reinterpret_cast<const uint2*>(sm + (u < 8 ? R_KS : R_QS) + t * D * 2 + c4 * 2);
+                    scl[u] = u < 8 ? vec[64 + t] : vec[t];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                if (!(u < 8 || kq)) continue;
+                const int idx = otid + u * (NT - NMAIN), r = idx >> 5, c4 = (idx & 31) * 4;
+                const uint2 raw2 = raws[u];
+                float4 f = make_float4(bf_lo(raw2.x), bf_hi(raw2.x), bf_lo(raw2.y), bf_hi(raw2.y));
+                const float sc = scl[u];
+                f = make_float4(f.x * sc, f.y * sc, f.z * sc, f.w * sc);
+                if (u >= 8)  // q: (q * rq) * dk^-1/2, the reference's order
+                    f = make_float4(f.x * p.q_scale, f.y * p.q_scale, f.z * p.q_scale, f.w * p.q_scale);
+                f = tf32_rn4(f);
+                if (u < 8 && km) *reinterpret_cast<float4*>(sm + R_KM + umma::mnmajor_off(r, c4, C)) = f;
+                if (kq) *reinterpret_cast<float4*>(sm + R_KQ + umma::kmajor_off(r, c4, 128)) = f;
+            }
+            fence_proxy_async_smem();
+        };
+        int n_bdone = 0;
+        // the first chunk's operands
+        {
+            const bool ok = mbar_wait_bounded(bar_qk, (uint32_t)w_qk & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            ++w_qk;
+            if (!nb_any(!ok, 4, NT - NMAIN)) {
+                stage_vectors(0);
+                stage_rows(true, true);
+                mbar_arrive(bar_staged);
+            } else {
+                failed = true;
+            }
+        }
+        for (int c = 0; c < NC && !failed; ++c) {
             const int t0 = c * C;
             const float* sv = scr + S_V + 256 * (c & 1);
+            if (c + 1 < NC) {
+                // [K;Q] of the next chunk once MMA-b of this one has read the operand region
+                const bool bd = mbar_wait_bounded(bar_bdone, (uint32_t)n_bdone & 1u, GDN_DEVERR_MMA_TIMEOUT);
+                ++n_bdone;
+                const bool lq = bd && mbar_wait_bounded(bar_qk, (uint32_t)w_qk & 1u, GDN_DEVERR_TMA_TIMEOUT);
+                ++w_qk;
+                if (nb_any(!lq, 4, NT - NMAIN)) {
+                    failed = true;
+                    break;
+                }
+                stage_vectors(c + 1);
+                stage_rows(true, false);
+            }
             const bool rdy = mbar_wait_bounded(bar_ordy, (uint32_t)c & 1u, GDN_DEVERR_MMA_TIMEOUT);
             if (nb_any(!rdy, 4, NT - NMAIN)) {
                 failed = true;
@@ -507,6 +538,11 @@ __global__ void __launch_bounds__(NT, 1)
             }
             umma::fence_before_sync();
             mbar_arrive(bar_ofree);  // these tensor-memory columns may be overwritten now
+            if (c + 1 < NC) {
+                // K MN-major of the next chunk: MMA-e of this one (before o_ready) has read it
+                stage_rows(false, true);
+                mbar_arrive(bar_staged);
+            }
 #pragma unroll
             for (int j = 0; j < 32; j += 2) round2_bf16(o[j], o[j + 1]);
             // per-token sums of squares over this warp's 32 lanes: halving exchange
