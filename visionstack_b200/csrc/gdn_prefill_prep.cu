@@ -51,8 +51,8 @@ constexpr uint32_t IMG_BYTES = C * C * 4;        // one 64x64 tf32 operand image
 __host__ __device__ constexpr uint32_t region0_bytes(int rep) {
     const uint32_t stage = (uint32_t)(2 + rep) * GROUP_BYTES;
     const uint32_t kq = 128u * D * 4u;
-    // A and T matrices and the P operand image of every value head
-    const uint32_t am = 2u * (uint32_t)rep * A_BYTES + (uint32_t)rep * IMG_BYTES;
+    // per value head: the A matrix (inverted in place into T) and one operand image (P, then T)
+    const uint32_t am = (uint32_t)rep * (A_BYTES + IMG_BYTES);
     const uint32_t m = stage > kq ? stage : kq;
     return ((m > am ? m : am) + 1023u) & ~1023u;
 }
@@ -125,7 +125,7 @@ __device__ __forceinline__ void block_row8(const float* L, const float* R, int i
         make_float4(sign * acc[4], sign * acc[5], sign * acc[6], sign * acc[7]);
 }
 
-__global__ void __launch_bounds__(NT, 2)
+__global__ void __launch_bounds__(NT, 3)
     prefill_prep_kernel(const MixParams p, const PrefillWs ws, const __grid_constant__ CUtensorMap tm_mixed,
                         const __grid_constant__ CUtensorMap tm_qkv) {
     extern __shared__ unsigned char raw[];
@@ -408,7 +408,7 @@ __global__ void __launch_bounds__(NT, 2)
             const float egt = sEG[r * 64 + t];
             const float bt = sB[r * 64 + t];
             float* arow = reinterpret_cast<float*>(sm + r * A_BYTES) + t * A_STRIDE;
-            unsigned char* img = sm + 2 * rep * A_BYTES + r * IMG_BYTES;
+            unsigned char* img = sm + rep * A_BYTES + r * IMG_BYTES;
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 float v[32], dec[32];
@@ -467,14 +467,15 @@ __global__ void __launch_bounds__(NT, 2)
     if (tid == 0) {  // P images to the workspace
         for (int r = 0; r < rep; ++r)
             bulk_store(ws.tp + ((((size_t)b * p.Hv + kh * rep + r) * NC + c) * 2 + 1) * (C * C),
-                       smem_u32(sm + 2 * rep * A_BYTES + r * IMG_BYTES), IMG_BYTES);
+                       smem_u32(sm + rep * A_BYTES + r * IMG_BYTES), IMG_BYTES);
         bulk_commit_group();
     }
 
     // ---- T = (I + A)^-1 in 32x32 blocks (the doubling merge of deltanet.py:146-160) ----
-    // T11, T22 by forward substitution (one warp per block, lane = column), then
-    // X = A21 T11 (parked in T's zero upper-right block) and T21 = -T22 X.
-    float* Tall = reinterpret_cast<float*>(sm + rep * A_BYTES);  // T of value head r at Tall + r * C * A_STRIDE
+    // In place over A: T11, T22 by forward substitution (one warp per block, lane = column,
+    // written back after the block's rows are read), X = A21 T11 (parked in the zero upper-right
+    // block), then T21 = -T22 X over the dead A21.
+    float* Tall = reinterpret_cast<float*>(sm);  // A, then T, of value head r at Tall + r * C * A_STRIDE
     if (warp < 2 * rep) {
         const int r = warp >> 1, o = 32 * (warp & 1);
         const float* A = reinterpret_cast<const float*>(sm + r * A_BYTES) + o * A_STRIDE + o;
@@ -497,21 +498,22 @@ __global__ void __launch_bounds__(NT, 2)
         float* Tr = Tall + r * C * A_STRIDE;
         block_row8(Tr + 32 * A_STRIDE + 32, Tr + 32, i, jb, Tr + 32 * A_STRIDE, -1.f);  // T21 = -T22 X
     }
+    if (tid == 0) bulk_wait_group_read0();  // the P images are read: their space takes the T images
     __syncthreads();
-    // T images (tf32, zero above the diagonal) over the dead A matrices, then to the workspace
+    // T images (tf32, zero above the diagonal), then to the workspace
     for (int u = tid; u < rep * C * (C / 4); u += NT) {
         const int r = u / (C * C / 4), w = u % (C * C / 4), i = w >> 4, j = (w & 15) * 4;
         const float4 v = *reinterpret_cast<const float4*>(Tall + r * C * A_STRIDE + i * A_STRIDE + j);
         const float4 o = make_float4(j + 0 <= i ? umma::tf32_rna(v.x) : 0.f, j + 1 <= i ? umma::tf32_rna(v.y) : 0.f,
                                      j + 2 <= i ? umma::tf32_rna(v.z) : 0.f, j + 3 <= i ? umma::tf32_rna(v.w) : 0.f);
-        *reinterpret_cast<float4*>(sm + r * A_BYTES + umma::kmajor_off(i, j, C)) = o;
+        *reinterpret_cast<float4*>(sm + rep * A_BYTES + r * IMG_BYTES + umma::kmajor_off(i, j, C)) = o;
     }
     fence_proxy_async_smem();
     __syncthreads();
     if (tid == 0) {
         for (int r = 0; r < rep; ++r)
-            bulk_store(ws.tp + (((size_t)b * p.Hv + kh * rep + r) * NC + c) * 2 * (C * C), smem_u32(sm + r * A_BYTES),
-                       IMG_BYTES);
+            bulk_store(ws.tp + (((size_t)b * p.Hv + kh * rep + r) * NC + c) * 2 * (C * C),
+                       smem_u32(sm + rep * A_BYTES + r * IMG_BYTES), IMG_BYTES);
         bulk_commit_group();
     }
     if (tid == 0) bulk_wait_group0();  // conv-output stores complete before the CTA exits
