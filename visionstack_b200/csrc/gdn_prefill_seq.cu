@@ -239,22 +239,24 @@ __global__ void __launch_bounds__(NT, 1)
             // checkpoints strictly inside this chunk keep the k rows (and rk) until step 5
             const bool has_sub = ck_i < ck.n && ck.off[ck_i] > t0 && ck.off[ck_i] - t0 < C;
             // ---------------- 2. MMA-b (after the output warps released O of the last chunk) ----------------
+            // (warp 0 issues every MMA: elect.sync picks lane 0, which also issues the copies)
             bool free_ok = true;
-            if (tid == 0) {
+            if (warp == 0) {
                 if (c > 0) {
                     free_ok = mbar_wait_bounded(bar_ofree, (uint32_t)n_ofree & 1u, GDN_DEVERR_MMA_TIMEOUT);
                     ++n_ofree;
                 }
                 umma::fence_after_sync();
+                free_ok = __all_sync(0xffffffffu, free_ok);
                 if (free_ok) {
 #pragma unroll
                     for (int kk = 0; kk < D / 8; ++kk)
-                        umma::mma_tf32_ta(tmem + C_YO, tmem + C_OP + kk * 8,
-                                          umma::desc_add(d_kq, umma::kmajor_kstep(kk, 128)), idesc_b, kk > 0);
-                    umma::mma_commit(bar_mma);
-                    umma::mma_commit(bar_bdone);  // [K;Q] may be restaged for the next chunk
+                        umma::mma_tf32_ta_elect(tmem + C_YO, tmem + C_OP + kk * 8,
+                                                umma::desc_add(d_kq, umma::kmajor_kstep(kk, 128)), idesc_b, kk > 0);
+                    umma::mma_commit_elect(bar_mma);
+                    umma::mma_commit_elect(bar_bdone);  // [K;Q] may be restaged for the next chunk
                     mma_pending = true;
-                    if (c + 1 < NC && !has_sub) {
+                    if (lane == 0 && c + 1 < NC && !has_sub) {
                         issue_qk(c + 1);
                         ++n_qk;
                     }
@@ -294,15 +296,15 @@ __global__ void __launch_bounds__(NT, 1)
                 failed = true;
                 break;
             }
-            if (tid == 0) {
+            if (warp == 0) {
                 umma::fence_after_sync();
 #pragma unroll
                 for (int kk = 0; kk < C / 8; ++kk)
-                    umma::mma_tf32_ta(tmem + C_V, tmem + C_Z + kk * 8, umma::desc_add(d_t, umma::kmajor_kstep(kk, C)),
-                                      idesc_c, kk > 0);
-                umma::mma_commit(bar_mma);
+                    umma::mma_tf32_ta_elect(tmem + C_V, tmem + C_Z + kk * 8,
+                                            umma::desc_add(d_t, umma::kmajor_kstep(kk, C)), idesc_c, kk > 0);
+                umma::mma_commit_elect(bar_mma);
                 mma_pending = true;
-                if (c + 1 < NC) {
+                if (lane == 0 && c + 1 < NC) {
                     fence_proxy_async_smem();
                     issue_v(c + 1);
                     ++n_v;
@@ -381,18 +383,18 @@ __global__ void __launch_bounds__(NT, 1)
             umma::fence_before_sync();
             nb_sync(1, NMAIN);
             // ---------------- 6. MMA-d (D^T = v_new^T P^T), MMA-e (dS^T) ----------------
-            if (tid == 0) {
+            if (warp == 0) {
                 umma::fence_after_sync();
 #pragma unroll
                 for (int kk = 0; kk < C / 8; ++kk)
-                    umma::mma_tf32_ta(tmem + C_YO, tmem + C_V + kk * 8, umma::desc_add(d_p, umma::kmajor_kstep(kk, C)),
-                                      idesc_c, kk > 0);
+                    umma::mma_tf32_ta_elect(tmem + C_YO, tmem + C_V + kk * 8,
+                                            umma::desc_add(d_p, umma::kmajor_kstep(kk, C)), idesc_c, kk > 0);
 #pragma unroll
                 for (int kk = 0; kk < C / 8; ++kk)
-                    umma::mma_tf32_ta(tmem + C_OP, tmem + C_Z + kk * 8, umma::desc_add(d_km, umma::mnmajor_kstep(kk)),
-                                      idesc_e, kk > 0);
-                umma::mma_commit(bar_mma);
-                umma::mma_commit(bar_ordy);  // O of this chunk is complete for the output warps
+                    umma::mma_tf32_ta_elect(tmem + C_OP, tmem + C_Z + kk * 8,
+                                            umma::desc_add(d_km, umma::mnmajor_kstep(kk)), idesc_e, kk > 0);
+                umma::mma_commit_elect(bar_mma);
+                umma::mma_commit_elect(bar_ordy);  // O of this chunk is complete for the output warps
                 mma_pending = true;
             }
             if (!mma_wait()) {
