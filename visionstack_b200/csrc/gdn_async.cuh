@@ -86,6 +86,10 @@ __device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, ui
 // Tiled tensor copy global -> shared of one 3-D box of `tmap` at element
 // coordinates (c0, c1, c2), completing its bytes on `bar`.  c0 * element size
 // must be a multiple of 16 bytes; out-of-range rows are filled with zeros.
+// Bring a kernel-parameter tensor map into the descriptor cache ahead of its first copy.
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
 __device__ __forceinline__ void tma_load_3d(uint32_t dst_smem, const void* tmap, int c0, int c1, int c2,
                                             uint32_t bar) {
     asm volatile(

@@ -88,7 +88,8 @@ __device__ __forceinline__ float4 tf32_rn4(float4 v) {
     return make_float4(tf32_rn(v.x), tf32_rn(v.y), tf32_rn(v.z), tf32_rn(v.w));
 }
 
-// named barriers: 1 = state warpgroups (256 threads), 2 / 3 = output warpgroup
+// named barriers: 1 = state warpgroups (256 threads; warps 1-7 may only arrive
+// while warp 0 waits), 2 / 3 = output warpgroup
 // 0 / 1 (128 threads each), 4 = both output warpgroups (256)
 __device__ __forceinline__ void nb_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 __device__ __forceinline__ bool nb_any(bool pred, int id, int n) {
@@ -103,6 +104,7 @@ __device__ __forceinline__ bool nb_any(bool pred, int id, int n) {
         : "memory");
     return r != 0;
 }
+__device__ __forceinline__ void nb_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -143,6 +145,9 @@ __global__ void __launch_bounds__(NT, 1)
         mbar_init(bar_bdone, 1);
         mbar_init(bar_staged, NT - NMAIN);
         fence_mbar_init();
+        prefetch_tmap(&tm_qkv);
+        prefetch_tmap(&tm_z);
+        prefetch_tmap(&tm_out);
     }
     if (warp == 0) {
         umma::tmem_alloc(smem_u32(tslot), T_COLS);
@@ -214,67 +219,63 @@ __global__ void __launch_bounds__(NT, 1)
         const uint64_t d_kq = umma::desc_kmajor0(sb + R_KQ), d_t = umma::desc_kmajor0(sb + R_TP),
                        d_p = umma::desc_kmajor0(sb + R_TP + C * C * 4), d_km = umma::desc_mnmajor0(sb + R_KM, C);
         uint32_t mma_phase = 0;
-        int n_ofree = 0;  // o_free phases waited (thread 0)
+        int n_ofree = 0;  // o_free phases waited (warp 0)
         bool mma_pending = false;
         int ck_i = 0;
-        auto mma_wait = [&]() -> bool {
+        // A bounded wait that runs out marks this thread bad; the threads agree on it once per
+        // chunk (the closing barrier) and leave together.  Until then a bad thread keeps going
+        // on stale data: every address it touches is fixed by the chunk index, never by data.
+        bool bad = false;
+        auto mma_wait = [&]() {
             const bool ok = mbar_wait_bounded(bar_mma, mma_phase & 1u, GDN_DEVERR_MMA_TIMEOUT);
             ++mma_phase;
             umma::fence_after_sync();
-            return !nb_any(!ok, 1, NMAIN);
+            bad |= !ok;
+            if (ok) mma_pending = false;
         };
-        auto wait_main = [&](uint32_t bar, int& count) -> bool {
-            const bool ok = mbar_wait_bounded(bar, (uint32_t)count & 1u, GDN_DEVERR_TMA_TIMEOUT);
+        auto wait_copy = [&](uint32_t bar, int& count) {
+            bad |= !mbar_wait_bounded(bar, (uint32_t)count & 1u, GDN_DEVERR_TMA_TIMEOUT);
             ++count;
-            return !nb_any(!ok, 1, NMAIN);
+        };
+        // the tensor-memory stores of all 256 threads before warp 0 issues the next MMA; the
+        // other warps only arrive (they next wait for that MMA, so none can run a phase ahead)
+        auto stores_to_warp0 = [&]() {
+            umma::fence_before_sync();
+            if (warp == 0)
+                nb_sync(1, NMAIN);
+            else
+                nb_arrive(1, NMAIN);
         };
         for (int c = 0; c < NC; ++c) {
             const int t0 = c * C;
             float* sv = scr + S_V + 256 * (c & 1);
             // ---------------- 1. operands of the chunk (staged by the output warps) ----------------
-            if (!wait_main(bar_staged, w_st)) {
-                failed = true;
-                break;
-            }
+            wait_copy(bar_staged, w_st);
             // checkpoints strictly inside this chunk keep the k rows (and rk) until step 5
             const bool has_sub = ck_i < ck.n && ck.off[ck_i] > t0 && ck.off[ck_i] - t0 < C;
             // ---------------- 2. MMA-b (after the output warps released O of the last chunk) ----------------
             // (warp 0 issues every MMA: elect.sync picks lane 0, which also issues the copies)
-            bool free_ok = true;
             if (warp == 0) {
                 if (c > 0) {
-                    free_ok = mbar_wait_bounded(bar_ofree, (uint32_t)n_ofree & 1u, GDN_DEVERR_MMA_TIMEOUT);
+                    bad |= !mbar_wait_bounded(bar_ofree, (uint32_t)n_ofree & 1u, GDN_DEVERR_MMA_TIMEOUT);
                     ++n_ofree;
                 }
+                __syncwarp();
                 umma::fence_after_sync();
-                free_ok = __all_sync(0xffffffffu, free_ok);
-                if (free_ok) {
 #pragma unroll
-                    for (int kk = 0; kk < D / 8; ++kk)
-                        umma::mma_tf32_ta_elect(tmem + C_YO, tmem + C_OP + kk * 8,
-                                                umma::desc_add(d_kq, umma::kmajor_kstep(kk, 128)), idesc_b, kk > 0);
-                    umma::mma_commit_elect(bar_mma);
-                    umma::mma_commit_elect(bar_bdone);  // [K;Q] may be restaged for the next chunk
-                    mma_pending = true;
-                    if (lane == 0 && c + 1 < NC && !has_sub) {
-                        issue_qk(c + 1);
-                        ++n_qk;
-                    }
+                for (int kk = 0; kk < D / 8; ++kk)
+                    umma::mma_tf32_ta_elect(tmem + C_YO, tmem + C_OP + kk * 8,
+                                            umma::desc_add(d_kq, umma::kmajor_kstep(kk, 128)), idesc_b, kk > 0);
+                umma::mma_commit_elect(bar_mma);
+                umma::mma_commit_elect(bar_bdone);  // [K;Q] may be restaged for the next chunk
+                mma_pending = true;
+                if (lane == 0 && c + 1 < NC && !has_sub) {
+                    issue_qk(c + 1);
+                    ++n_qk;
                 }
             }
-            if (nb_any(!free_ok, 1, NMAIN)) {
-                failed = true;
-                break;
-            }
-            if (!mma_wait()) {
-                failed = true;
-                break;
-            }
-            mma_pending = false;
-            if (!wait_main(bar_v, w_v)) {
-                failed = true;
-                break;
-            }
+            mma_wait();
+            wait_copy(bar_v, w_v);
             // ---------------- 3. Z^T = beta (V - e^gamma Y)^T (warpgroup wg: tokens 32 wg ..) ----------------
             {
                 float y[32];
@@ -289,14 +290,11 @@ __global__ void __launch_bounds__(NT, 1)
                 umma::tmem_st32(tmem + lane_base + C_Z + 32 * wg, y);
                 umma::tmem_wait_st();
             }
-            umma::fence_before_sync();
-            nb_sync(1, NMAIN);
+            stores_to_warp0();
             // ---------------- 4. MMA-c: v_new^T = Z^T T^T; next chunk's v copy ----------------
-            if (!wait_main(bar_tp, w_tp)) {
-                failed = true;
-                break;
-            }
             if (warp == 0) {
+                wait_copy(bar_tp, w_tp);
+                __syncwarp();
                 umma::fence_after_sync();
 #pragma unroll
                 for (int kk = 0; kk < C / 8; ++kk)
@@ -304,17 +302,13 @@ __global__ void __launch_bounds__(NT, 1)
                                             umma::desc_add(d_t, umma::kmajor_kstep(kk, C)), idesc_c, kk > 0);
                 umma::mma_commit_elect(bar_mma);
                 mma_pending = true;
-                if (lane == 0 && c + 1 < NC) {
+                if (lane == 0 && c + 1 < NC) {  // every thread has read the v rows (the barrier above)
                     fence_proxy_async_smem();
                     issue_v(c + 1);
                     ++n_v;
                 }
             }
-            if (!mma_wait()) {
-                failed = true;
-                break;
-            }
-            mma_pending = false;
+            mma_wait();
             // ---------------- 5a. sub-chunk checkpoints (fp32 v_new, fp32 K, state before the update) ----------------
             // S_s = e^{gamma_{s-1}} S + sum_{t<s} e^{gamma_{s-1}-gamma_t} k_t^T v_new_t (deltanet.py:375-388)
             while (ck_i < ck.n && ck.off[ck_i] > t0 && ck.off[ck_i] - t0 < C) {
@@ -380,8 +374,7 @@ __global__ void __launch_bounds__(NT, 1)
                 umma::tmem_st32(tmem + lane_base + C_Z + 32 * wg, w);
                 umma::tmem_wait_st();
             }
-            umma::fence_before_sync();
-            nb_sync(1, NMAIN);
+            stores_to_warp0();
             // ---------------- 6. MMA-d (D^T = v_new^T P^T), MMA-e (dS^T) ----------------
             if (warp == 0) {
                 umma::fence_after_sync();
@@ -397,11 +390,7 @@ __global__ void __launch_bounds__(NT, 1)
                 umma::mma_commit_elect(bar_ordy);  // O of this chunk is complete for the output warps
                 mma_pending = true;
             }
-            if (!mma_wait()) {
-                failed = true;
-                break;
-            }
-            mma_pending = false;
+            mma_wait();
             if (tid == 0 && c + 1 < NC) {
                 fence_proxy_async_smem();
                 issue_tp(c + 1);
@@ -437,7 +426,10 @@ __global__ void __launch_bounds__(NT, 1)
             }
             while (ck_i < ck.n && ck.off[ck_i] - t0 == C) ++ck_i;
             umma::fence_before_sync();
-            nb_sync(1, NMAIN);
+            if (nb_any(bad, 1, NMAIN)) {
+                failed = true;
+                break;
+            }
             umma::fence_after_sync();
         }
         if (failed && tid == 0) {
