@@ -6,31 +6,34 @@
 // The state lives in tensor memory, TRANSPOSED: lane = value dim dv, column =
 // key dim dk, so that it is directly the A operand of the next MMA (tcgen05
 // reads A from tensor memory).  Two copies: the fp32 master and its tf32
-// (round-to-nearest) operand copy.  Per chunk, with K, Q the normalised k and
-// q rows (q times dk^-1/2), V the v rows, beta and gamma = cumsum(g) of the
-// chunk, T = (I + A)^-1 and P = (Q K^T) o e^{gamma_i - gamma_j} (j <= i):
+// (round-to-nearest) operand copy.  Per chunk, with k, q the raw bf16 rows
+// (exact as tf32 operands; the norm factors rk, rq and dk^-1/2 are applied per
+// token outside the MMAs), V the v rows, beta and gamma = cumsum(g) of the
+// chunk, T = (I + A)^-1 and P = (Q K^T) o e^{gamma_i - gamma_j} (j <= i) of the
+// normalised rows:
 //
-//   MMA-b  [Y^T | O1^T] = S^T [K;Q]^T                  (M128 N128 K128, A from TMEM)
-//   CUDA   Z^T = beta (V - e^gamma Y)^T                 (to TMEM)
+//   MMA-b  [Y^T | O1^T] = S^T [k;q]^T                  (M128 N128 K128, A from TMEM)
+//   CUDA   Z^T = beta (V - e^gamma rk Y)^T              (to TMEM)
 //   MMA-c  v_new^T = Z^T T^T                            (M128 N64  K64,  A from TMEM)
-//   CUDA   v_new^T and (e^{gamma_C - gamma} v_new)^T, tf32 (to TMEM)
+//   CUDA   v_new^T and (e^{gamma_C - gamma} rk v_new)^T, tf32 (to TMEM)
 //   MMA-d  D^T = v_new^T P^T                            (M128 N64  K64)
-//   MMA-e  dS^T = (e^{gamma_C - gamma} v_new)^T K        (M128 N128 K64)
+//   MMA-e  dS^T = (e^{gamma_C - gamma} rk v_new)^T k     (M128 N128 K64)
 //   CUDA   S^T <- e^{gamma_C} S^T + dS^T (master and operand copy), boundary
 //          checkpoints, final state
-//   CUDA   output rows O = e^gamma O1 + D through the gated RMSNorm
+//   CUDA   output rows O = e^gamma rq dk^-1/2 O1 + D through the gated RMSNorm
 //
 // i.e. the reference's v_new = U - W S with U = T (beta V), W = T (beta K e^gamma)
 // and O = (Q e^gamma) S + P v_new, S' = e^{gamma_C} S + (K e^{gamma_C-gamma})^T v_new
 // (deltanet.py:323-389), regrouped and transposed.
 //
-// 16 warps in two roles.  Warpgroups 0-1 carry the state: operand staging,
-// the MMAs (thread 0 issues them and every copy), Z, v_new, the state update.
-// Warpgroups 2-3 turn the previous chunk's O into output rows while the state
-// path moves on: they copy O out of tensor memory as soon as MMA-d completes
-// (mbarrier o_ready, a second commit of that MMA), release those columns
-// (mbarrier o_free, which the next MMA-b waits for), then normalise and store.
-// Inputs of the next chunk stream in by tensor-map / bulk copies meanwhile.
+// 16 warps in two roles.  Warpgroups 0-1 carry the state: the MMAs (warp 0
+// issues them), Z, v_new, the state update.  Warpgroups 2-3 stage the next
+// chunk's [k;q] and k operands (mbarriers b_done: MMA-b has read [k;q];
+// staged: both operands ready), issue the input copies, and turn the previous
+// chunk's O into output rows while the state path moves on: they copy O out
+// of tensor memory as soon as MMA-d completes (mbarrier o_ready, a second
+// commit of that MMA), release those columns (mbarrier o_free, which the next
+// MMA-b waits for), then normalise and store.
 #include "gdn_async.cuh"
 #include "gdn_common.cuh"
 #include "gdn_conv_windows.cuh"
@@ -53,9 +56,10 @@ constexpr uint32_t R_VS = 163840;   // v rows
 constexpr uint32_t R_ZS = 180224;   // z rows
 constexpr uint32_t R_VEC = 196608;  // rq[64] rk[64] beta[64] gamma[64] as loaded
 constexpr uint32_t R_SCR = R_VEC + 1024;
-// scratch floats: per chunk parity p, beta / gamma / e^gamma / e^{gamma_C - gamma} at S_V + 256 p
-constexpr int S_V = 0, S_F = 512, S_NW = 576, S_PART = 704, S_RSTD = 960, S_END = 1024;
-constexpr int V_B = 0, V_G = 64, V_EG = 128, V_EF = 192;
+// scratch floats: per chunk parity p, at S_V + 384 p, the per-token vectors beta, gamma,
+// e^gamma rk, e^{gamma_C - gamma} rk, e^gamma rq dk^-1/2 and the scalar e^{gamma_C}
+constexpr int S_V = 0, S_F = 768, S_NW = 832, S_PART = 960, S_RSTD = 1216, S_END = 1280;
+constexpr int V_B = 0, V_G = 64, V_EK = 128, V_EF = 192, V_EQ = 256, V_EC = 320;
 constexpr uint32_t R_BAR = R_SCR + S_END * 4;
 constexpr uint32_t SMEM_BYTES = R_BAR + 128 + 1024;
 // tensor memory columns
@@ -125,6 +129,8 @@ __global__ void __launch_bounds__(NT, 1)
     const float* vec = reinterpret_cast<const float*>(sm + R_VEC);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + R_BAR);
     uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + R_BAR + 96);
+    // copies issued (qk, v, tp) and copies waited for (qk, v, tp), for the drain at exit
+    int* n_cp = reinterpret_cast<int*>(sm + R_BAR + 100);
     const uint32_t bar_qk = smem_u32(&bars[0]), bar_v = smem_u32(&bars[1]), bar_z = smem_u32(&bars[2]),
                    bar_tp = smem_u32(&bars[3]), bar_mma = smem_u32(&bars[4]), bar_ordy = smem_u32(&bars[5]),
                    bar_ofree = smem_u32(&bars[6]), bar_bdone = smem_u32(&bars[7]), bar_staged = smem_u32(&bars[8]);
@@ -144,6 +150,7 @@ __global__ void __launch_bounds__(NT, 1)
         mbar_init(bar_ofree, NT - NMAIN);
         mbar_init(bar_bdone, 1);
         mbar_init(bar_staged, NT - NMAIN);
+        for (int i = 0; i < 6; ++i) n_cp[i] = 0;
         fence_mbar_init();
         prefetch_tmap(&tm_qkv);
         prefetch_tmap(&tm_z);
@@ -174,7 +181,10 @@ __global__ void __launch_bounds__(NT, 1)
     }
 
     const int v_ch = 2 * p.Hk * D + h * D;
+    // Each input region is reloaded only after every reader of the previous chunk's copy is done
+    // (and that copy was waited for), so one copy per barrier is in flight at a time.
     auto issue_qk = [&](int cc) {
+        atomicAdd(&n_cp[0], 1);
         mbar_arrive_expect_tx(bar_qk, 2u * C * D * 2u + 1024u);
         tma_load_3d(sb + R_QS, &tm_qkv, kh * D, cc * C, b, bar_qk);
         tma_load_3d(sb + R_KS, &tm_qkv, p.Hk * D + kh * D, cc * C, b, bar_qk);
@@ -182,6 +192,7 @@ __global__ void __launch_bounds__(NT, 1)
         bulk_load(sb + R_VEC + 512, ws.gate + (((size_t)b * p.Hv + h) * NC + cc) * 128, 512, bar_qk);
     };
     auto issue_v = [&](int cc) {
+        atomicAdd(&n_cp[1], 1);
         mbar_arrive_expect_tx(bar_v, (uint32_t)C * D * 2u);
         tma_load_3d(sb + R_VS, &tm_qkv, v_ch, cc * C, b, bar_v);
     };
@@ -190,17 +201,23 @@ __global__ void __launch_bounds__(NT, 1)
         tma_load_3d(sb + R_ZS, &tm_z, h * D, cc * C, b, bar_z);
     };
     auto issue_tp = [&](int cc) {
+        atomicAdd(&n_cp[2], 1);
         mbar_arrive_expect_tx(bar_tp, 2u * C * C * 4u);
         bulk_load(sb + R_TP, ws.tp + (((size_t)b * p.Hv + h) * NC + cc) * (2 * C * C), 2u * C * C * 4u, bar_tp);
     };
-    // copies issued (by their issuing thread) and waits completed (uniform in a group)
-    int n_qk = 0, n_v = 0, n_z = 0, n_tp = 0;
+    // a chunk with a checkpoint strictly inside keeps its k rows until the state path's step 5a
+    auto sub_in = [&](int cc) {
+        for (int i = 0; i < ck.n; ++i)
+            if (ck.off[i] > cc * C && ck.off[i] - cc * C < C) return true;
+        return false;
+    };
+    // copies waited for (uniform in the waiting group); z copies issued
+    int n_z = 0;
     int w_qk = 0, w_v = 0, w_z = 0, w_tp = 0, w_st = 0;
     if (tid == 0) {
         issue_qk(0);
         issue_v(0);
         issue_tp(0);
-        n_qk = n_v = n_tp = 1;
     }
     if (tid == NMAIN) {
         issue_z(0);
@@ -209,6 +226,11 @@ __global__ void __launch_bounds__(NT, 1)
     umma::fence_before_sync();
     __syncthreads();
 
+    // Input copies: thread 0 issues every chunk's first ones and, for a chunk with a checkpoint
+    // strictly inside, the next q/k rows after step 5a; the output group's first thread issues
+    // the rest once the readers are done: v and T/P of chunk c + 1 when MMA-d of chunk c
+    // completes (o_ready: Z and MMA-c of chunk c are then done too), q/k rows of chunk c + 2
+    // when the output group has staged chunk c + 1.
     bool failed = false;
     if (main_grp) {
         // ======================= state path (warpgroups 0-1) =======================
@@ -234,8 +256,9 @@ __global__ void __launch_bounds__(NT, 1)
             if (ok) mma_pending = false;
         };
         auto wait_copy = [&](uint32_t bar, int& count) {
-            bad |= !mbar_wait_bounded(bar, (uint32_t)count & 1u, GDN_DEVERR_TMA_TIMEOUT);
-            ++count;
+            const bool ok = mbar_wait_bounded(bar, (uint32_t)count & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            bad |= !ok;
+            count += ok;
         };
         // the tensor-memory stores of all 256 threads before warp 0 issues the next MMA; the
         // other warps only arrive (they next wait for that MMA, so none can run a phase ahead)
@@ -248,7 +271,7 @@ __global__ void __launch_bounds__(NT, 1)
         };
         for (int c = 0; c < NC; ++c) {
             const int t0 = c * C;
-            float* sv = scr + S_V + 256 * (c & 1);
+            float* sv = scr + S_V + 384 * (c & 1);
             // ---------------- 1. operands of the chunk (staged by the output warps) ----------------
             wait_copy(bar_staged, w_st);
             // checkpoints strictly inside this chunk keep the k rows (and rk) until step 5
@@ -269,10 +292,6 @@ __global__ void __launch_bounds__(NT, 1)
                 umma::mma_commit_elect(bar_mma);
                 umma::mma_commit_elect(bar_bdone);  // [K;Q] may be restaged for the next chunk
                 mma_pending = true;
-                if (lane == 0 && c + 1 < NC && !has_sub) {
-                    issue_qk(c + 1);
-                    ++n_qk;
-                }
             }
             mma_wait();
             wait_copy(bar_v, w_v);
@@ -285,7 +304,7 @@ __global__ void __launch_bounds__(NT, 1)
                 for (int j = 0; j < 32; ++j) {
                     const int t = 32 * wg + j;
                     const float vv = bf_at(sm + R_VS, t * D + dv);
-                    y[j] = tf32_rn(sv[V_B + t] * (vv - sv[V_EG + t] * y[j]));
+                    y[j] = tf32_rn(sv[V_B + t] * (vv - sv[V_EK + t] * y[j]));
                 }
                 umma::tmem_st32(tmem + lane_base + C_Z + 32 * wg, y);
                 umma::tmem_wait_st();
@@ -302,11 +321,6 @@ __global__ void __launch_bounds__(NT, 1)
                                             umma::desc_add(d_t, umma::kmajor_kstep(kk, C)), idesc_c, kk > 0);
                 umma::mma_commit_elect(bar_mma);
                 mma_pending = true;
-                if (lane == 0 && c + 1 < NC) {  // every thread has read the v rows (the barrier above)
-                    fence_proxy_async_smem();
-                    issue_v(c + 1);
-                    ++n_v;
-                }
             }
             mma_wait();
             // ---------------- 5a. sub-chunk checkpoints (fp32 v_new, fp32 K, state before the update) ----------------
@@ -357,7 +371,6 @@ __global__ void __launch_bounds__(NT, 1)
             if (tid == 0 && has_sub && c + 1 < NC) {
                 fence_proxy_async_smem();
                 issue_qk(c + 1);
-                ++n_qk;
             }
             // ---------------- 5b. v_new^T (tf32) and its e^{gamma_C - gamma} scaled copy (tokens 32 wg ..) ----------------
             {
@@ -391,14 +404,9 @@ __global__ void __launch_bounds__(NT, 1)
                 mma_pending = true;
             }
             mma_wait();
-            if (tid == 0 && c + 1 < NC) {
-                fence_proxy_async_smem();
-                issue_tp(c + 1);
-                ++n_tp;
-            }
             // ---------------- 7. state update (key columns 64 wg ..), checkpoints, final state ----------------
             {
-                const float ec = sv[V_EG + C - 1];
+                const float ec = sv[V_EC];
                 const bool last = c == NC - 1;
 #pragma unroll 1
                 for (int c0 = 64 * wg; c0 < 64 * wg + 64; c0 += 32) {
@@ -432,56 +440,49 @@ __global__ void __launch_bounds__(NT, 1)
             }
             umma::fence_after_sync();
         }
-        if (failed && tid == 0) {
-            // let copies and MMAs in flight finish (bounded) before the CTA exits
-            // q/k copies are waited for by the output warps: wait for the last one issued
-            if (n_qk > 0) mbar_wait_bounded(bar_qk, (uint32_t)(n_qk - 1) & 1u, GDN_DEVERR_TMA_TIMEOUT);
-            for (; w_v < n_v; ++w_v) mbar_wait_bounded(bar_v, (uint32_t)w_v & 1u, GDN_DEVERR_TMA_TIMEOUT);
-            for (; w_tp < n_tp; ++w_tp) mbar_wait_bounded(bar_tp, (uint32_t)w_tp & 1u, GDN_DEVERR_TMA_TIMEOUT);
-            if (mma_pending) mbar_wait_bounded(bar_mma, (mma_phase - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
+        if (tid == 0) {
+            n_cp[4] = w_v;
+            n_cp[5] = w_tp;
+            // an MMA in flight finishes (bounded) before the CTA exits
+            if (failed && mma_pending) mbar_wait_bounded(bar_mma, (mma_phase - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
         }
     } else {
         // ======================= output rows and operand staging (warpgroups 2-3) =======================
         const int owg = wg - 2, tw = 32 * owg;  // this warpgroup's tokens tw .. tw + 31
         const int otid = tid - NMAIN;
         const float nw = sNW[dv];
-        // chunk cc's vectors (beta, gamma, e^gamma, e^{gamma_C - gamma}) from the loaded rows
+        // chunk cc's per-token vectors from the loaded rows (rq, rk, beta, gamma): the norm
+        // factors ride on the vectors, so the operand rows stay the exact bf16 values
         auto stage_vectors = [&](int cc) {
-            float* sv = scr + S_V + 256 * (cc & 1);
+            float* sv = scr + S_V + 384 * (cc & 1);
             if (otid < C) {
-                const float gC = vec[192 + C - 1], gt = vec[192 + otid];
+                const float gC = vec[192 + C - 1], gt = vec[192 + otid], rk = vec[64 + otid];
+                const float eg = expf(gt);
                 sv[V_B + otid] = vec[128 + otid];
                 sv[V_G + otid] = gt;
-                sv[V_EG + otid] = expf(gt);
-                sv[V_EF + otid] = expf(gC - gt);
+                sv[V_EK + otid] = eg * rk;
+                sv[V_EF + otid] = expf(gC - gt) * rk;
+                sv[V_EQ + otid] = eg * (vec[otid] * p.q_scale);
+                if (otid == 0) sv[V_EC] = expf(gC);
             }
         };
-        // [K;Q] rows (K: k * rk, Q: (q * rq) * dk^-1/2, tf32) of the loaded chunk; with
+        // [K;Q] rows of the loaded chunk as tf32 operands (bf16 values are exact in tf32); with
         // km, the K rows also go to the K MN-major operand
         auto stage_rows = [&](bool kq, bool km) {
             uint2 raws[16];
-            float scl[16];
 #pragma unroll
             for (int u = 0; u < 16; ++u) {  // every shared operand first (no load behind a store)
                 const int idx = otid + u * (NT - NMAIN), r = idx >> 5, c4 = (idx & 31) * 4, t = r & 63;
-                if (u < 8 || kq) {
-                    raws[u] = *reinterpret_cast<const uint2*>(sm + (u < 8 ? R_KS : R_QS) + t * D * 2 + c4 * 2);
-                    scl[u] = u < 8 ? vec[64 + t] : vec[t];
-                }
+                if (u < 8 || kq) raws[u] = *reinterpret_cast<const uint2*>(sm + (u < 8 ? R_KS : R_QS) + t * D * 2 + c4 * 2);
             }
 #pragma unroll
             for (int u = 0; u < 16; ++u) {
                 if (!(u < 8 || kq)) continue;
                 const int idx = otid + u * (NT - NMAIN), r = idx >> 5, c4 = (idx & 31) * 4;
                 const uint2 raw2 = raws[u];
-                float4 f = make_float4(bf_lo(raw2.x), bf_hi(raw2.x), bf_lo(raw2.y), bf_hi(raw2.y));
-                const float sc = scl[u];
-                f = make_float4(f.x * sc, f.y * sc, f.z * sc, f.w * sc);
-                if (u >= 8)  // q: (q * rq) * dk^-1/2, the reference's order
-                    f = make_float4(f.x * p.q_scale, f.y * p.q_scale, f.z * p.q_scale, f.w * p.q_scale);
-                f = tf32_rn4(f);
-                if (u < 8 && km) *reinterpret_cast<float4*>(sm + R_KM + umma::mnmajor_off(r, c4, C)) = f;
-                if (kq) *reinterpret_cast<float4*>(sm + R_KQ + umma::kmajor_off(r, c4, 128)) = f;
+                const uint4 f = make_uint4(raw2.x << 16, raw2.x & 0xFFFF0000u, raw2.y << 16, raw2.y & 0xFFFF0000u);
+                if (u < 8 && km) *reinterpret_cast<uint4*>(sm + R_KM + umma::mnmajor_off(r, c4, C)) = f;
+                if (kq) *reinterpret_cast<uint4*>(sm + R_KQ + umma::kmajor_off(r, c4, 128)) = f;
             }
             fence_proxy_async_smem();
         };
@@ -489,24 +490,32 @@ __global__ void __launch_bounds__(NT, 1)
         // the first chunk's operands
         {
             const bool ok = mbar_wait_bounded(bar_qk, (uint32_t)w_qk & 1u, GDN_DEVERR_TMA_TIMEOUT);
-            ++w_qk;
+            w_qk += ok;
             if (!nb_any(!ok, 4, NT - NMAIN)) {
                 stage_vectors(0);
                 stage_rows(true, true);
                 mbar_arrive(bar_staged);
+                nb_sync(4, NT - NMAIN);  // every output thread has read the rows of chunk 0
+                if (tid == NMAIN && NC > 1 && !sub_in(0)) {
+                    fence_proxy_async_smem();
+                    issue_qk(1);
+                }
             } else {
                 failed = true;
             }
         }
         for (int c = 0; c < NC && !failed; ++c) {
             const int t0 = c * C;
-            const float* sv = scr + S_V + 256 * (c & 1);
+            const float* sv = scr + S_V + 384 * (c & 1);
             if (c + 1 < NC) {
                 // [K;Q] of the next chunk once MMA-b of this one has read the operand region
                 const bool bd = mbar_wait_bounded(bar_bdone, (uint32_t)n_bdone & 1u, GDN_DEVERR_MMA_TIMEOUT);
                 ++n_bdone;
-                const bool lq = bd && mbar_wait_bounded(bar_qk, (uint32_t)w_qk & 1u, GDN_DEVERR_TMA_TIMEOUT);
-                ++w_qk;
+                bool lq = false;
+                if (bd) {
+                    lq = mbar_wait_bounded(bar_qk, (uint32_t)w_qk & 1u, GDN_DEVERR_TMA_TIMEOUT);
+                    w_qk += lq;
+                }
                 if (nb_any(!lq, 4, NT - NMAIN)) {
                     failed = true;
                     break;
@@ -519,6 +528,11 @@ __global__ void __launch_bounds__(NT, 1)
                 failed = true;
                 break;
             }
+            if (tid == NMAIN && c + 1 < NC) {  // MMA-c and MMA-d of chunk c are complete, Z has read v
+                fence_proxy_async_smem();
+                issue_v(c + 1);
+                issue_tp(c + 1);
+            }
             umma::fence_after_sync();
             // O[t][dv] = e^{gamma_t} O1 + D
             float o[32];
@@ -528,7 +542,7 @@ __global__ void __launch_bounds__(NT, 1)
                 umma::tmem_ld32(tmem + lane_base + C_YO + tw, dd);
                 umma::tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) o[j] = fmaf(sv[V_EG + tw + j], o1[j], dd[j]);
+                for (int j = 0; j < 32; ++j) o[j] = fmaf(sv[V_EQ + tw + j], o1[j], dd[j]);
             }
             umma::fence_before_sync();
             mbar_arrive(bar_ofree);  // these tensor-memory columns may be overwritten now
@@ -574,6 +588,10 @@ __global__ void __launch_bounds__(NT, 1)
                 zv[j] = zok ? bf_at(sm + R_ZS, (tw + j) * D + dv) : 0.f;
             }
             nb_sync(4, NT - NMAIN);
+            if (tid == NMAIN && c + 2 < NC && !sub_in(c + 1)) {  // every output thread has staged chunk c + 1
+                fence_proxy_async_smem();
+                issue_qk(c + 2);
+            }
             uint16_t* tile = reinterpret_cast<uint16_t*>(sm + R_ZS) + tw * D + dv;
             if (zok) {
 #pragma unroll
@@ -614,10 +632,20 @@ __global__ void __launch_bounds__(NT, 1)
         }
         if (failed && tid == NMAIN)
             for (; w_z < n_z; ++w_z) mbar_wait_bounded(bar_z, (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
-        if (tid == NMAIN) bulk_wait_group0();  // output rows written before the CTA exits
+        if (tid == NMAIN) {
+            bulk_wait_group0();  // output rows written before the CTA exits
+            n_cp[3] = w_qk;
+        }
     }
     umma::fence_before_sync();
     __syncthreads();
+    if (tid == 0) {
+        // input copies still in flight (a wait ran out) land before the CTA exits (bounded)
+        const uint32_t bar_cp[3] = {bar_qk, bar_v, bar_tp};
+        for (int i = 0; i < 3; ++i)
+            for (int k = n_cp[3 + i]; k < n_cp[i]; ++k)
+                mbar_wait_bounded(bar_cp[i], (uint32_t)k & 1u, GDN_DEVERR_TMA_TIMEOUT);
+    }
     if (warp == 0) umma::tmem_dealloc(tmem, T_COLS);
 }
 
