@@ -528,11 +528,6 @@ __global__ void __launch_bounds__(NT, 1)
                 failed = true;
                 break;
             }
-            if (tid == NMAIN && c + 1 < NC) {  // MMA-c and MMA-d of chunk c are complete, Z has read v
-                fence_proxy_async_smem();
-                issue_v(c + 1);
-                issue_tp(c + 1);
-            }
             umma::fence_after_sync();
             // O[t][dv] = e^{gamma_t} O1 + D
             float o[32];
@@ -550,6 +545,10 @@ __global__ void __launch_bounds__(NT, 1)
                 // K MN-major of the next chunk: MMA-e of this one (before o_ready) has read it
                 stage_rows(false, true);
                 mbar_arrive(bar_staged);
+                if (tid == NMAIN) {  // MMA-c and MMA-d of chunk c are complete, Z has read v
+                    issue_v(c + 1);
+                    issue_tp(c + 1);
+                }
             }
 #pragma unroll
             for (int j = 0; j < 32; j += 2) round2_bf16(o[j], o[j + 1]);
