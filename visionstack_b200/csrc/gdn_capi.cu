@@ -286,7 +286,7 @@ int32_t gdn_mixer_prefill_ws(const gdn_mixer_args* args, void* workspace, int64_
 }
 
 int32_t gdn_selftest_umma(int32_t mode, const float* A, const float* B, float* D, void* stream) {
-    if (mode < 0 || mode > 6) return fail(GDN_ERR_INVALID_ARG, "mode %d not in 0..6", mode);
+    if (mode < 0 || mode > 8) return fail(GDN_ERR_INVALID_ARG, "mode %d not in 0..8", mode);
     if (!A || !B || !D) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
     const void* ptrs[] = {A, B, D};
     for (const void* ptr : ptrs)

@@ -18,6 +18,19 @@
 //    one MMA k-step of 8 rows advances the start address by 1024 bytes.
 // Descriptor version 1, base offset 0: every operand region starts 1024-byte
 // aligned.
+//
+// 16-bit (bf16) operands, 128-byte swizzle (the layout a TMA copy with
+// CU_TENSOR_MAP_SWIZZLE_128B writes for a box 64 elements wide):
+//  * K-major  [rows][k]  : atom = 64 k-elements (128 bytes) of every row:
+//      byte(row, k) = (k/64)*rows*128 + (row/8)*1024 + (row%8)*128 +
+//                     ((k%64/8) ^ (row%8))*16 + (k%8)*2
+//    descriptor as for tf32 (SBO = 1024); one MMA k-step of 16 elements is
+//    again 32 bytes inside an atom.
+//  * MN-major [k][mn]    : the same bytes read the other way: atom = 64
+//    mn-elements of 8 k rows; descriptor LBO = stride between 64-element mn
+//    atoms, SBO = 1024 (next 8 k rows); a k-step of 16 rows is 2048 bytes.
+//  * in tensor memory (A of kind::f16): row m = lane m, column c holds the
+//    pair k = 2c (low half) and 2c + 1 (high half).
 #pragma once
 
 #include <stdint.h>
@@ -30,6 +43,15 @@ namespace umma {
 __host__ __device__ constexpr uint32_t kmajor_off(int row, int k, int rows) {
     return (uint32_t)((k >> 5) * rows * 128 + (row >> 3) * 1024 + (row & 7) * 128 +
                       ((((k & 31) >> 2) ^ (row & 7)) << 4) + (k & 3) * 4);
+}
+
+__host__ __device__ constexpr uint32_t kmajor_off16(int row, int k, int rows) {
+    return (uint32_t)((k >> 6) * rows * 128 + (row >> 3) * 1024 + (row & 7) * 128 +
+                      ((((k & 63) >> 3) ^ (row & 7)) << 4) + (k & 7) * 2);
+}
+__host__ __device__ constexpr uint32_t mnmajor_off16(int k, int mn, uint32_t mn_atom_stride) {
+    return (uint32_t)((mn >> 6) * mn_atom_stride + (k >> 3) * 1024 + (k & 7) * 128 +
+                      ((((mn & 63) >> 3) ^ (k & 7)) << 4) + (mn & 7) * 2);
 }
 
 __host__ __device__ constexpr uint32_t mnmajor_off(int k, int mn, int krows) {
@@ -91,6 +113,21 @@ __device__ __forceinline__ uint64_t desc_mnmajor0(uint32_t base, int krows) {
 // desc0 advanced by `bytes` (the start address field is 16-byte units in the low 14 bits;
 // operands here lie below 256 KB of shared memory, so the field cannot overflow).
 __device__ __forceinline__ uint64_t desc_add(uint64_t desc0, uint32_t bytes) { return desc0 + (bytes >> 4); }
+
+// MN-major 16-bit operand at k-step 0; a k-step (16 rows) adds 2048 bytes.
+__device__ __forceinline__ uint64_t desc_mnmajor16_0(uint32_t base, uint32_t mn_atom_stride) {
+    return smem_desc(base, mn_atom_stride, 1024, LAYOUT_SW128);
+}
+__host__ __device__ constexpr uint32_t mnmajor16_kstep(int kk) { return (uint32_t)(kk * 2048); }
+
+// Instruction descriptor of kind::f16 with bf16 operands and fp32 accumulation.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int a_mn, int b_mn) {
+    return (1u << 4)             // D format f32
+           | (1u << 7)           // A format bf16
+           | (1u << 10)          // B format bf16
+           | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
+}
 
 // Instruction descriptor of kind::tf32 with fp32 accumulation.
 // a_mn / b_mn: operand is MN-major (1) or K-major (0).
@@ -163,6 +200,28 @@ __device__ __forceinline__ void mma_commit_elect(uint32_t bar) {
         "{\n\t.reg .pred e;\n\t"
         "elect.sync _|e, 0xffffffff;\n\t"
         "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(bar)
+        : "memory");
+}
+
+// kind::f16 with bf16 operands, A from tensor memory (packed pairs), from one
+// thread / from a converged warp through elect.sync.
+__device__ __forceinline__ void mma_bf16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+__device__ __forceinline__ void mma_bf16_ta_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                  uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
         : "memory");
 }
 

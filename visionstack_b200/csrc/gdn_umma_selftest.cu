@@ -10,8 +10,16 @@
 //   mode 4: A in tensor memory [128][128], B K-major [128][128] (D = A B^T, N = 128)
 //   mode 5: A in tensor memory [128][64],  B K-major [64][64]   (D = A B^T, N = 64)
 //   mode 6: A in tensor memory [128][64],  B MN-major [64][128] (D = A B, K = 64)
+// and kind::f16 with bf16 operands (inputs rounded to bf16 on the device; A
+// packed in pairs in tensor memory, B in the 16-bit 128-byte swizzle a TMA copy
+// writes, in regions laid out like the sequential prefill kernel's [k;q] rows):
+//   mode 7: A in tensor memory [128][128], B K-major [128][128] (D = A B^T, N = 128)
+//   mode 8: A in tensor memory [128][64],  B MN-major [64][128] (D = A B, K = 64;
+//           64-element mn atoms 16 KB apart)
 // Inputs are plain row-major fp32 in global memory: A is [M][K] except for
 // mode 3 ([K][M]); B is [N][K] for K-major B and [K][N] for MN-major B.
+#include <cuda_bf16.h>
+
 #include "gdn_kernels.cuh"
 #include "gdn_umma.cuh"
 
@@ -20,18 +28,21 @@ namespace gdn {
 namespace {
 
 struct SelfTestShape {
-    int K, N, a_mn, b_mn, a_tmem;
+    int K, N, a_mn, b_mn, a_tmem, bf16;
 };
+constexpr uint32_t MN_ATOM16 = 16384;  // mode 8: stride between 64-element mn atoms
 
 __host__ __device__ inline SelfTestShape selftest_shape(int mode) {
     switch (mode) {
-        case 0: return {128, 64, 0, 0, 0};
-        case 1: return {128, 128, 0, 1, 0};
-        case 2: return {64, 128, 0, 1, 0};
-        case 3: return {64, 128, 1, 1, 0};
-        case 4: return {128, 128, 0, 0, 1};
-        case 5: return {64, 64, 0, 0, 1};
-        default: return {64, 128, 0, 1, 1};
+        case 0: return {128, 64, 0, 0, 0, 0};
+        case 1: return {128, 128, 0, 1, 0, 0};
+        case 2: return {64, 128, 0, 1, 0, 0};
+        case 3: return {64, 128, 1, 1, 0, 0};
+        case 4: return {128, 128, 0, 0, 1, 0};
+        case 5: return {64, 64, 0, 0, 1, 0};
+        case 6: return {64, 128, 0, 1, 1, 0};
+        case 7: return {128, 128, 0, 0, 1, 1};
+        default: return {64, 128, 0, 1, 1, 1};
     }
 }
 
@@ -58,7 +69,17 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const f
             *reinterpret_cast<float*>(sA + umma::mnmajor_off(k, m, K)) = A[i];
         }
     }
-    for (int i = tid; i < N * K; i += 128) {
+    for (int i = tid; i < N * K && sh.bf16; i += 128) {
+        const __nv_bfloat16 v = __float2bfloat16_rn(B[i]);
+        if (!sh.b_mn) {
+            const int n = i / K, k = i % K;
+            *reinterpret_cast<__nv_bfloat16*>(sB + umma::kmajor_off16(n, k, N)) = v;
+        } else {
+            const int k = i / N, n = i % N;
+            *reinterpret_cast<__nv_bfloat16*>(sB + umma::mnmajor_off16(k, n, MN_ATOM16)) = v;
+        }
+    }
+    for (int i = tid; i < N * K && !sh.bf16; i += 128) {
         if (!sh.b_mn) {
             const int n = i / K, k = i % K;
             *reinterpret_cast<float*>(sB + umma::kmajor_off(n, k, N)) = B[i];
@@ -81,7 +102,20 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const f
     umma::fence_after_sync();
     const uint32_t tbase = *tslot;
     constexpr int A_COL = 128;  // A operand columns when A lives in tensor memory
-    if (sh.a_tmem) {
+    if (sh.a_tmem && sh.bf16) {
+        // row m of A -> lane m, column A_COL + c holds the bf16 pair k = 2c, 2c + 1
+        const int row = warp * 32 + lane;
+        for (int c0 = 0; c0 < K / 2; c0 += 32) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const __nv_bfloat162 pr = __floats2bfloat162_rn(A[row * K + 2 * (c0 + j)], A[row * K + 2 * (c0 + j) + 1]);
+                v[j] = __uint_as_float(*reinterpret_cast<const uint32_t*>(&pr));
+            }
+            umma::tmem_st32(umma::tmem_addr(tbase, warp * 32, A_COL + c0), v);
+        }
+        umma::tmem_wait_st();
+    } else if (sh.a_tmem) {
         // row m of A -> lane m (warp w writes lanes 32w..32w+31), columns A_COL + k
         const int row = warp * 32 + lane;
         for (int c0 = 0; c0 < K; c0 += 32) {
@@ -96,7 +130,15 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const f
     __syncthreads();
     umma::fence_after_sync();
 
-    if (tid == 0) {
+    if (tid == 0 && sh.bf16) {
+        const uint32_t idesc = umma::idesc_bf16(M, N, 0, sh.b_mn);
+        const uint64_t d0 = sh.b_mn ? umma::desc_mnmajor16_0(smem_u32(sB), MN_ATOM16) : umma::desc_kmajor0(smem_u32(sB));
+        for (int kk = 0; kk < K / 16; ++kk) {
+            const uint32_t step = sh.b_mn ? umma::mnmajor16_kstep(kk) : umma::kmajor_kstep(kk, N);
+            umma::mma_bf16_ta(tbase, tbase + A_COL + kk * 8, umma::desc_add(d0, step), idesc, kk > 0 ? 1u : 0u);
+        }
+        umma::mma_commit(smem_u32(bar));
+    } else if (tid == 0) {
         const uint32_t idesc = umma::idesc_tf32(M, N, sh.a_mn, sh.b_mn);
         for (int kk = 0; kk < K / 8; ++kk) {
             const uint64_t db = sh.b_mn ? umma::desc_mnmajor(smem_u32(sB), K, kk) : umma::desc_kmajor(smem_u32(sB), N, kk);
