@@ -47,17 +47,18 @@ namespace pseq {
 
 constexpr int D = 128, C = 64, NT = 512, NMAIN = 256;
 // shared memory (bytes from the 1024-aligned base)
-constexpr uint32_t R_KQ = 0;        // [K;Q] K-major [128][dk] tf32, 64 KB (B of MMA-b)
-constexpr uint32_t R_KM = 65536;    // K MN-major [tok][dk] tf32, 32 KB (B of MMA-e)
-constexpr uint32_t R_TP = 98304;    // T image, P image (16 KB each; B of MMA-c / MMA-d)
-constexpr uint32_t R_QS = 131072;   // q rows bf16 [64][128]
-constexpr uint32_t R_KS = 147456;   // k rows
-constexpr uint32_t R_VS = 163840;   // v rows
-constexpr uint32_t R_ZS = 180224;   // z rows
-constexpr uint32_t R_VEC = 196608;  // rq[64] rk[64] beta[64] gamma[64] as loaded
-constexpr uint32_t R_SCR = R_VEC + 1024;
+// [k;q] rows of a chunk, two buffers (chunk parity): the bf16 rows as the
+// 128-byte swizzled operand a TMA copy writes, 128 rows (k tokens 0..63, q
+// tokens 64..127) by dk in two 64-element atoms 16 KB apart: K-major B of
+// MMA-b, and its k rows MN-major B of MMA-e
+constexpr uint32_t R_QK = 0, QK_BYTES = 32768;
+constexpr uint32_t R_TP = 65536;    // T image, P image (16 KB each, tf32; B of MMA-c / MMA-d)
+constexpr uint32_t R_VS = 98304;    // v rows bf16 [64][128]
+constexpr uint32_t R_ZS = 114688;   // z rows (then the output rows)
+constexpr uint32_t R_VEC = 131072;  // two buffers of rq[64] rk[64] beta[64] gamma[64] as loaded
+constexpr uint32_t R_SCR = R_VEC + 2048;
 // scratch floats: per chunk parity p, at S_V + 384 p, the per-token vectors beta, gamma,
-// e^gamma rk, e^{gamma_C - gamma} rk, e^gamma rq dk^-1/2 and the scalar e^{gamma_C}
+// -e^gamma rk, e^{gamma_C - gamma} rk, e^gamma rq dk^-1/2 and the scalar e^{gamma_C}
 constexpr int S_V = 0, S_F = 768, S_NW = 832, S_PART = 960, S_RSTD = 1216, S_END = 1280;
 constexpr int V_B = 0, V_G = 64, V_EK = 128, V_EF = 192, V_EQ = 256, V_EC = 320;
 constexpr uint32_t R_BAR = R_SCR + S_END * 4;
@@ -72,11 +73,14 @@ __device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 
 __device__ __forceinline__ float bf_at(const unsigned char* base, int idx) {
     return __uint_as_float((uint32_t)(*reinterpret_cast<const uint16_t*>(base + 2 * idx)) << 16);
 }
+__device__ __forceinline__ uint32_t bf2_bits(float a, float b) {
+    const __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&t);
+}
 // a pair of values rounded to bf16 (nearest, ties to even) with one packed
 // conversion; the packed bits in *bits
 __device__ __forceinline__ void round2_bf16(float& a, float& b, uint32_t* bits = nullptr) {
-    const __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
-    const uint32_t u = *reinterpret_cast<const uint32_t*>(&t);
+    const uint32_t u = bf2_bits(a, b);
     a = bf_lo(u);
     b = bf_hi(u);
     if (bits) *bits = u;
@@ -88,13 +92,42 @@ __device__ __forceinline__ float tf32_rn(float x) {
     const float t = __fmul_rn(x, 8193.0f);
     return __fsub_rn(t, __fsub_rn(t, x));
 }
-__device__ __forceinline__ float4 tf32_rn4(float4 v) {
-    return make_float4(tf32_rn(v.x), tf32_rn(v.y), tf32_rn(v.z), tf32_rn(v.w));
+// packed fp32 pairs (one instruction for two lanes of arithmetic); a - b as fma(b, -1, a)
+__device__ __forceinline__ float2 f2_sub(float2 a, float2 b) { return __ffma2_rn(b, make_float2(-1.f, -1.f), a); }
+__device__ __forceinline__ float2 tf32_rn2(float2 x) {  // tf32_rn of both lanes
+    const float2 t = __fmul2_rn(x, make_float2(8193.0f, 8193.0f));
+    return f2_sub(t, f2_sub(t, x));
 }
 
-// named barriers: 1 = state warpgroups (256 threads; warps 1-7 may only arrive
-// while warp 0 waits), 2 / 3 = output warpgroup
-// 0 / 1 (128 threads each), 4 = both output warpgroups (256)
+// 32 fp32 values as bf16 pairs hi + lo (hi = bf16(x), lo = bf16(x - hi); the
+// difference is exact, so hi + lo is within 2^-17 of x relative), packed for a
+// kind::f16 A operand: column j of each half holds elements 2j, 2j + 1.  The
+// 32 columns at taddr: hi pairs in the first 16, lo pairs in the next 16.
+__device__ __forceinline__ void store_split32(uint32_t taddr, const float (&x)[32]) {
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {  // 8 pairs at a time
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float a = x[16 * hf + 2 * j], c = x[16 * hf + 2 * j + 1];
+            const uint32_t u = bf2_bits(a, c);
+            hi[j] = u;
+            const float2 r = f2_sub(make_float2(a, c), make_float2(bf_lo(u), bf_hi(u)));
+            lo[j] = bf2_bits(r.x, r.y);
+        }
+        umma::tmem_st8(taddr + 8 * hf, hi);
+        umma::tmem_st8(taddr + 16 + 8 * hf, lo);
+    }
+}
+// tensor-memory column of the hi (or lo) pairs of k-step kk (16 elements) of a
+// split operand stored by store_split32 in 32-column blocks
+__host__ __device__ constexpr uint32_t split_col(int kk, bool lo) {
+    return (uint32_t)(32 * (kk >> 1) + 8 * (kk & 1) + (lo ? 16 : 0));
+}
+
+// named barriers: 1 and 5 = state warpgroups (256 threads; warps 1-7 may only
+// arrive while warp 0 waits), 2 / 3 = output warpgroup 0 / 1 (128 threads
+// each), 4 = both output warpgroups (256)
 __device__ __forceinline__ void nb_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 __device__ __forceinline__ bool nb_any(bool pred, int id, int n) {
     uint32_t r;
@@ -115,8 +148,8 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 
 __global__ void __launch_bounds__(NT, 1)
     prefill_seq_kernel(const MixParams p, const CkptList ck, const PrefillWs ws,
-                       const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_z,
-                       const __grid_constant__ CUtensorMap tm_out) {
+                       const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_v,
+                       const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_out) {
     extern __shared__ unsigned char raw[];
     const uint32_t raw_addr = smem_u32(raw);
     unsigned char* sm = raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -126,14 +159,14 @@ __global__ void __launch_bounds__(NT, 1)
     float* sNW = scr + S_NW;
     float* sPart = scr + S_PART;
     float* sRstd = scr + S_RSTD;
-    const float* vec = reinterpret_cast<const float*>(sm + R_VEC);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + R_BAR);
     uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + R_BAR + 96);
-    // copies issued (qk, v, tp) and copies waited for (qk, v, tp), for the drain at exit
+    // input copies issued per barrier (q/k buffer 0, 1, v, T/P), for the drain at exit
     int* n_cp = reinterpret_cast<int*>(sm + R_BAR + 100);
-    const uint32_t bar_qk = smem_u32(&bars[0]), bar_v = smem_u32(&bars[1]), bar_z = smem_u32(&bars[2]),
-                   bar_tp = smem_u32(&bars[3]), bar_mma = smem_u32(&bars[4]), bar_ordy = smem_u32(&bars[5]),
-                   bar_ofree = smem_u32(&bars[6]), bar_bdone = smem_u32(&bars[7]), bar_staged = smem_u32(&bars[8]);
+    const uint32_t bar_qk0 = smem_u32(&bars[0]), bar_v = smem_u32(&bars[2]), bar_z = smem_u32(&bars[3]),
+                   bar_tp = smem_u32(&bars[4]), bar_mma = smem_u32(&bars[5]), bar_ordy = smem_u32(&bars[6]),
+                   bar_ofree = smem_u32(&bars[7]), bar_staged = smem_u32(&bars[8]), bar_o1 = smem_u32(&bars[9]);
+    auto bar_qk = [&](int cc) { return bar_qk0 + 8u * (uint32_t)(cc & 1); };
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int wg = warp >> 2, q4 = warp & 3;
@@ -146,13 +179,14 @@ __global__ void __launch_bounds__(NT, 1)
     const int NC = ws.nc;
 
     if (tid == 0) {
-        for (int i = 0; i < 6; ++i) mbar_init(smem_u32(&bars[i]), 1);
+        for (int i = 0; i < 7; ++i) mbar_init(smem_u32(&bars[i]), 1);
+        mbar_init(bar_o1, 1);
         mbar_init(bar_ofree, NT - NMAIN);
-        mbar_init(bar_bdone, 1);
         mbar_init(bar_staged, NT - NMAIN);
-        for (int i = 0; i < 6; ++i) n_cp[i] = 0;
+        for (int i = 0; i < 4; ++i) n_cp[i] = 0;
         fence_mbar_init();
-        prefetch_tmap(&tm_qkv);
+        prefetch_tmap(&tm_qk);
+        prefetch_tmap(&tm_v);
         prefetch_tmap(&tm_z);
         prefetch_tmap(&tm_out);
     }
@@ -167,55 +201,53 @@ __global__ void __launch_bounds__(NT, 1)
     umma::fence_after_sync();
     const uint32_t tmem = *tslot;
 
-    // initial state, transposed: lane dv, column dk (warpgroup wg: dk 32 wg .. 32 wg + 31)
+    // initial state, transposed: lane dv, column dk (warpgroup wg: dk 32 wg .. 32 wg + 31);
+    // its bf16 hi / lo operand in the same 32 columns of the operand region
     {
         const int c0 = 32 * wg;
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = p.S_in ? __ldcs(p.S_in + ((size_t)bh * D + c0 + j) * D + dv) : 0.f;
         umma::tmem_st32(tmem + lane_base + C_MS + c0, v);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = tf32_rn(v[j]);
-        umma::tmem_st32(tmem + lane_base + C_OP + c0, v);
+        store_split32(tmem + lane_base + C_OP + c0, v);
         umma::tmem_wait_st();
     }
 
     const int v_ch = 2 * p.Hk * D + h * D;
-    // Each input region is reloaded only after every reader of the previous chunk's copy is done
-    // (and that copy was waited for), so one copy per barrier is in flight at a time.
-    auto issue_qk = [&](int cc) {
-        atomicAdd(&n_cp[0], 1);
-        mbar_arrive_expect_tx(bar_qk, 2u * C * D * 2u + 1024u);
-        tma_load_3d(sb + R_QS, &tm_qkv, kh * D, cc * C, b, bar_qk);
-        tma_load_3d(sb + R_KS, &tm_qkv, p.Hk * D + kh * D, cc * C, b, bar_qk);
-        bulk_load(sb + R_VEC, ws.nrm + (((size_t)b * p.Hk + kh) * NC + cc) * 128, 512, bar_qk);
-        bulk_load(sb + R_VEC + 512, ws.gate + (((size_t)b * p.Hv + h) * NC + cc) * 128, 512, bar_qk);
+    // Every input region is reloaded only after all readers of its previous copy are done and
+    // that copy was seen complete by the issuing thread, so one copy per barrier is in flight.
+    auto issue_qk = [&](int cc) {  // into buffer cc & 1
+        const uint32_t dst = sb + R_QK + QK_BYTES * (uint32_t)(cc & 1), bar = bar_qk(cc);
+        atomicAdd(&n_cp[cc & 1], 1);
+        mbar_arrive_expect_tx(bar, 4u * 8192u + 1024u);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            tma_load_3d(dst + 16384u * j, &tm_qk, p.Hk * D + kh * D + 64 * j, cc * C, b, bar);  // k rows
+            tma_load_3d(dst + 16384u * j + 8192u, &tm_qk, kh * D + 64 * j, cc * C, b, bar);     // q rows
+        }
+        const uint32_t vdst = sb + R_VEC + 1024u * (uint32_t)(cc & 1);
+        bulk_load(vdst, ws.nrm + (((size_t)b * p.Hk + kh) * NC + cc) * 128, 512, bar);
+        bulk_load(vdst + 512, ws.gate + (((size_t)b * p.Hv + h) * NC + cc) * 128, 512, bar);
     };
     auto issue_v = [&](int cc) {
-        atomicAdd(&n_cp[1], 1);
+        atomicAdd(&n_cp[2], 1);
         mbar_arrive_expect_tx(bar_v, (uint32_t)C * D * 2u);
-        tma_load_3d(sb + R_VS, &tm_qkv, v_ch, cc * C, b, bar_v);
+        tma_load_3d(sb + R_VS, &tm_v, v_ch, cc * C, b, bar_v);
     };
     auto issue_z = [&](int cc) {
         mbar_arrive_expect_tx(bar_z, (uint32_t)C * D * 2u);
         tma_load_3d(sb + R_ZS, &tm_z, h * D, cc * C, b, bar_z);
     };
     auto issue_tp = [&](int cc) {
-        atomicAdd(&n_cp[2], 1);
+        atomicAdd(&n_cp[3], 1);
         mbar_arrive_expect_tx(bar_tp, 2u * C * C * 4u);
         bulk_load(sb + R_TP, ws.tp + (((size_t)b * p.Hv + h) * NC + cc) * (2 * C * C), 2u * C * C * 4u, bar_tp);
     };
-    // a chunk with a checkpoint strictly inside keeps its k rows until the state path's step 5a
-    auto sub_in = [&](int cc) {
-        for (int i = 0; i < ck.n; ++i)
-            if (ck.off[i] > cc * C && ck.off[i] - cc * C < C) return true;
-        return false;
-    };
-    // copies waited for (uniform in the waiting group); z copies issued
-    int n_z = 0;
-    int w_qk = 0, w_v = 0, w_z = 0, w_tp = 0, w_st = 0;
+    // z copies issued / waited for (output group)
+    int n_z = 0, w_z = 0;
     if (tid == 0) {
         issue_qk(0);
+        if (NC > 1) issue_qk(1);
         issue_v(0);
         issue_tp(0);
     }
@@ -226,22 +258,18 @@ __global__ void __launch_bounds__(NT, 1)
     umma::fence_before_sync();
     __syncthreads();
 
-    // Input copies: thread 0 issues every chunk's first ones and, for a chunk with a checkpoint
-    // strictly inside, the next q/k rows after step 5a; the output group's first thread issues
-    // the rest once the readers are done: v and T/P of chunk c + 1 when MMA-d of chunk c
-    // completes (o_ready: Z and MMA-c of chunk c are then done too), q/k rows of chunk c + 2
-    // when the output group has staged chunk c + 1.
+    // Input copies after the first ones: the output group's first thread issues v and T/P of
+    // chunk c + 1 and the q/k rows of chunk c + 2 (into the buffer of chunk c) when MMA-d / MMA-e
+    // of chunk c complete (o_ready: Z, step 5a and every MMA reading those regions are done).
     bool failed = false;
     if (main_grp) {
         // ======================= state path (warpgroups 0-1) =======================
         const uint32_t idesc_c = umma::idesc_tf32(128, 64, 0, 0);
-        const uint32_t idesc_e = umma::idesc_tf32(128, 128, 0, 1);
+        const uint32_t idesc_b = umma::idesc_bf16(128, 64, 0, 0);
+        const uint32_t idesc_e = umma::idesc_bf16(128, 128, 0, 1);
         // B-operand descriptors at k-step 0 (the operand regions never move)
-        const uint32_t idesc_b = umma::idesc_tf32(128, 128, 0, 0);
-        const uint64_t d_kq = umma::desc_kmajor0(sb + R_KQ), d_t = umma::desc_kmajor0(sb + R_TP),
-                       d_p = umma::desc_kmajor0(sb + R_TP + C * C * 4), d_km = umma::desc_mnmajor0(sb + R_KM, C);
+        const uint64_t d_t = umma::desc_kmajor0(sb + R_TP), d_p = umma::desc_kmajor0(sb + R_TP + C * C * 4);
         uint32_t mma_phase = 0;
-        int n_ofree = 0;  // o_free phases waited (warp 0)
         bool mma_pending = false;
         int ck_i = 0;
         // A bounded wait that runs out marks this thread bad; the threads agree on it once per
@@ -255,10 +283,8 @@ __global__ void __launch_bounds__(NT, 1)
             bad |= !ok;
             if (ok) mma_pending = false;
         };
-        auto wait_copy = [&](uint32_t bar, int& count) {
-            const bool ok = mbar_wait_bounded(bar, (uint32_t)count & 1u, GDN_DEVERR_TMA_TIMEOUT);
-            bad |= !ok;
-            count += ok;
+        auto wait_phase = [&](uint32_t bar, int phase) {
+            bad |= !mbar_wait_bounded(bar, (uint32_t)phase & 1u, GDN_DEVERR_TMA_TIMEOUT);
         };
         // the tensor-memory stores of all 256 threads before warp 0 issues the next MMA; the
         // other warps only arrive (they next wait for that MMA, so none can run a phase ahead)
@@ -272,47 +298,63 @@ __global__ void __launch_bounds__(NT, 1)
         for (int c = 0; c < NC; ++c) {
             const int t0 = c * C;
             float* sv = scr + S_V + 384 * (c & 1);
-            // ---------------- 1. operands of the chunk (staged by the output warps) ----------------
-            wait_copy(bar_staged, w_st);
-            // checkpoints strictly inside this chunk keep the k rows (and rk) until step 5
-            const bool has_sub = ck_i < ck.n && ck.off[ck_i] > t0 && ck.off[ck_i] - t0 < C;
+            const uint32_t r_qk = R_QK + QK_BYTES * (uint32_t)(c & 1);
             // ---------------- 2. MMA-b (after the output warps released O of the last chunk) ----------------
-            // (warp 0 issues every MMA: elect.sync picks lane 0, which also issues the copies)
+            // (warp 0 issues every MMA: elect.sync picks lane 0)
             if (warp == 0) {
-                if (c > 0) {
-                    bad |= !mbar_wait_bounded(bar_ofree, (uint32_t)n_ofree & 1u, GDN_DEVERR_MMA_TIMEOUT);
-                    ++n_ofree;
-                }
+                wait_phase(bar_qk(c), c >> 1);
+                if (c > 0) bad |= !mbar_wait_bounded(bar_ofree, (uint32_t)(c - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
                 __syncwarp();
                 umma::fence_after_sync();
+                // Y^T (k rows) first, committed for the state path; then O1^T (q rows, for the
+                // output warps), committed to o1_done, which MMA-e (it overwrites the state
+                // operand columns) waits for; o_ready covers it too
+                const uint64_t d_k = umma::desc_kmajor0(sb + r_qk), d_q = umma::desc_kmajor0(sb + r_qk + 8192);
 #pragma unroll
-                for (int kk = 0; kk < D / 8; ++kk)
-                    umma::mma_tf32_ta_elect(tmem + C_YO, tmem + C_OP + kk * 8,
-                                            umma::desc_add(d_kq, umma::kmajor_kstep(kk, 128)), idesc_b, kk > 0);
+                for (int kk = 0; kk < D / 16; ++kk)
+                    umma::mma_bf16_ta_elect(tmem + C_YO, tmem + C_OP + split_col(kk, false),
+                                            umma::desc_add(d_k, umma::kmajor_kstep(kk, 128)), idesc_b, kk > 0);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    umma::mma_bf16_ta_elect(tmem + C_YO, tmem + C_OP + split_col(kk, true),
+                                            umma::desc_add(d_k, umma::kmajor_kstep(kk, 128)), idesc_b, 1u);
                 umma::mma_commit_elect(bar_mma);
-                umma::mma_commit_elect(bar_bdone);  // [K;Q] may be restaged for the next chunk
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    umma::mma_bf16_ta_elect(tmem + C_YO + 64, tmem + C_OP + split_col(kk, false),
+                                            umma::desc_add(d_q, umma::kmajor_kstep(kk, 128)), idesc_b, kk > 0);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    umma::mma_bf16_ta_elect(tmem + C_YO + 64, tmem + C_OP + split_col(kk, true),
+                                            umma::desc_add(d_q, umma::kmajor_kstep(kk, 128)), idesc_b, 1u);
+                umma::mma_commit_elect(bar_o1);
                 mma_pending = true;
             }
             mma_wait();
-            wait_copy(bar_v, w_v);
-            // ---------------- 3. Z^T = beta (V - e^gamma Y)^T (warpgroup wg: tokens 32 wg ..) ----------------
+            wait_phase(bar_staged, c);  // the chunk's vectors (staged by the output warps)
+            wait_phase(bar_v, c);
+            // ---------------- 3. Z^T = beta (V - e^gamma rk Y)^T (warpgroup wg: tokens 32 wg ..) ----------------
             {
                 float y[32];
                 umma::tmem_ld32(tmem + lane_base + C_YO + 32 * wg, y);
                 umma::tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
+                for (int j = 0; j < 32; j += 2) {
                     const int t = 32 * wg + j;
-                    const float vv = bf_at(sm + R_VS, t * D + dv);
-                    y[j] = tf32_rn(sv[V_B + t] * (vv - sv[V_EK + t] * y[j]));
+                    const float2 vv = make_float2(bf_at(sm + R_VS, t * D + dv), bf_at(sm + R_VS, (t + 1) * D + dv));
+                    const float2 nek = *reinterpret_cast<const float2*>(sv + V_EK + t);  // -e^gamma rk
+                    const float2 be = *reinterpret_cast<const float2*>(sv + V_B + t);
+                    const float2 r = tf32_rn2(__fmul2_rn(be, __ffma2_rn(nek, make_float2(y[j], y[j + 1]), vv)));
+                    y[j] = r.x;
+                    y[j + 1] = r.y;
                 }
                 umma::tmem_st32(tmem + lane_base + C_Z + 32 * wg, y);
                 umma::tmem_wait_st();
             }
             stores_to_warp0();
-            // ---------------- 4. MMA-c: v_new^T = Z^T T^T; next chunk's v copy ----------------
+            // ---------------- 4. MMA-c: v_new^T = Z^T T^T ----------------
             if (warp == 0) {
-                wait_copy(bar_tp, w_tp);
+                wait_phase(bar_tp, c);
                 __syncwarp();
                 umma::fence_after_sync();
 #pragma unroll
@@ -327,6 +369,7 @@ __global__ void __launch_bounds__(NT, 1)
             // S_s = e^{gamma_{s-1}} S + sum_{t<s} e^{gamma_{s-1}-gamma_t} k_t^T v_new_t (deltanet.py:375-388)
             while (ck_i < ck.n && ck.off[ck_i] > t0 && ck.off[ck_i] - t0 < C) {
                 const int s_off = ck.off[ck_i] - t0;
+                const float* vec = reinterpret_cast<const float*>(sm + R_VEC + 1024u * (uint32_t)(c & 1));
                 if (tid < C) sF[tid] = tid < s_off ? expf(sv[V_G + s_off - 1] - sv[V_G + tid]) : 0.f;
                 nb_sync(1, NMAIN);
                 const float es = expf(sv[V_G + s_off - 1]);
@@ -346,13 +389,16 @@ __global__ void __launch_bounds__(NT, 1)
                         umma::tmem_wait_ld();
 #pragma unroll
                         for (int j = 0; j < 32; ++j) wv[j] *= sF[32 * th + j] * vec[64 + 32 * th + j];  // decay, rk
+                        // k row t = 32 th + j, key columns cb + 8 j8 .. + 7: one 16-byte unit of the
+                        // swizzled rows (kmajor_off16 with t % 8 = j % 8 known at compile time)
+                        const unsigned char* kb = sm + r_qk + 16384 * wg + 4096 * th;
+                        const uint32_t hx0 = 64u * hb, hx1 = 64u - 64u * hb;
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
-                            const int t = 32 * th + j;
-                            const uint4* krow = reinterpret_cast<const uint4*>(sm + R_KS + t * D * 2 + cb * 2);
+                            const unsigned char* rowp = kb + (j >> 3) * 1024 + (j & 7) * 128 + ((j & 4) ? hx1 : hx0);
 #pragma unroll
-                            for (int j8 = 0; j8 < 4; ++j8) {
-                                const uint4 k8 = krow[j8];
+                            for (int j8 = 0; j8 < 4; ++j8) {  // 8 key columns per 16-byte swizzle unit
+                                const uint4 k8 = *reinterpret_cast<const uint4*>(rowp + ((j8 ^ (j & 3)) << 4));
                                 const uint32_t kw[4] = {k8.x, k8.y, k8.z, k8.w};
 #pragma unroll
                                 for (int e = 0; e < 4; ++e) {
@@ -368,43 +414,72 @@ __global__ void __launch_bounds__(NT, 1)
                 nb_sync(1, NMAIN);
                 ++ck_i;
             }
-            if (tid == 0 && has_sub && c + 1 < NC) {
-                fence_proxy_async_smem();
-                issue_qk(c + 1);
-            }
-            // ---------------- 5b. v_new^T (tf32) and its e^{gamma_C - gamma} scaled copy (tokens 32 wg ..) ----------------
+            // ---------------- 5b. (e^{gamma_C - gamma} rk v_new)^T as bf16 hi / lo ----------------
             {
-                float v[32], w[32];
-                umma::tmem_ld32(tmem + lane_base + C_V + 32 * wg, v);
+                float w[32];
+                umma::tmem_ld32(tmem + lane_base + C_V + 32 * wg, w);
                 umma::tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int t = 32 * wg + j;
-                    w[j] = tf32_rn(v[j] * sv[V_EF + t]);
-                    v[j] = tf32_rn(v[j]);
+                for (int j = 0; j < 32; j += 2) {
+                    const float2 r = __fmul2_rn(make_float2(w[j], w[j + 1]),
+                                                *reinterpret_cast<const float2*>(sv + V_EF + 32 * wg + j));
+                    w[j] = r.x;
+                    w[j + 1] = r.y;
                 }
-                umma::tmem_st32(tmem + lane_base + C_V + 32 * wg, v);
-                umma::tmem_st32(tmem + lane_base + C_Z + 32 * wg, w);
+                store_split32(tmem + lane_base + C_Z + 32 * wg, w);
                 umma::tmem_wait_st();
             }
             stores_to_warp0();
-            // ---------------- 6. MMA-d (D^T = v_new^T P^T), MMA-e (dS^T) ----------------
+            // ---------------- 6a. MMA-e: dS^T, into the operand columns (the state path waits for it) ----------------
+            if (warp == 0) {
+                wait_phase(bar_o1, c);
+                __syncwarp();
+                umma::fence_after_sync();
+                const uint64_t d_km = umma::desc_mnmajor16_0(sb + r_qk, 16384);
+#pragma unroll
+                for (int kk = 0; kk < C / 16; ++kk)
+                    umma::mma_bf16_ta_elect(tmem + C_OP, tmem + C_Z + split_col(kk, false),
+                                            umma::desc_add(d_km, umma::mnmajor16_kstep(kk)), idesc_e, kk > 0);
+#pragma unroll
+                for (int kk = 0; kk < C / 16; ++kk)
+                    umma::mma_bf16_ta_elect(tmem + C_OP, tmem + C_Z + split_col(kk, true),
+                                            umma::desc_add(d_km, umma::mnmajor16_kstep(kk)), idesc_e, 1u);
+                umma::mma_commit_elect(bar_mma);
+                mma_pending = true;
+            }
+            // ---------------- 5c. v_new^T (tf32) for MMA-d while MMA-e runs ----------------
+            {
+                float v[32];
+                umma::tmem_ld32(tmem + lane_base + C_V + 32 * wg, v);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const float2 r = tf32_rn2(make_float2(v[j], v[j + 1]));
+                    v[j] = r.x;
+                    v[j + 1] = r.y;
+                }
+                umma::tmem_st32(tmem + lane_base + C_V + 32 * wg, v);
+                umma::tmem_wait_st();
+            }
+            // (a second barrier id: warps 1-7 reach this one without waiting on an MMA first)
+            umma::fence_before_sync();
+            if (warp == 0)
+                nb_sync(5, NMAIN);
+            else
+                nb_arrive(5, NMAIN);
+            // ---------------- 6b. MMA-d: D^T = v_new^T P^T (for the output warps) ----------------
             if (warp == 0) {
                 umma::fence_after_sync();
 #pragma unroll
                 for (int kk = 0; kk < C / 8; ++kk)
                     umma::mma_tf32_ta_elect(tmem + C_YO, tmem + C_V + kk * 8,
                                             umma::desc_add(d_p, umma::kmajor_kstep(kk, C)), idesc_c, kk > 0);
-#pragma unroll
-                for (int kk = 0; kk < C / 8; ++kk)
-                    umma::mma_tf32_ta_elect(tmem + C_OP, tmem + C_Z + kk * 8,
-                                            umma::desc_add(d_km, umma::mnmajor_kstep(kk)), idesc_e, kk > 0);
-                umma::mma_commit_elect(bar_mma);
                 umma::mma_commit_elect(bar_ordy);  // O of this chunk is complete for the output warps
-                mma_pending = true;
             }
             mma_wait();
             // ---------------- 7. state update (key columns 64 wg ..), checkpoints, final state ----------------
+            // each thread reads dS^T from, and writes the new bf16 hi / lo operand into, the same
+            // 32 columns of its own lane
             {
                 const float ec = sv[V_EC];
                 const bool last = c == NC - 1;
@@ -415,11 +490,14 @@ __global__ void __launch_bounds__(NT, 1)
                     umma::tmem_ld32(tmem + lane_base + C_OP + c0, d);
                     umma::tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) m[j] = fmaf(m[j], ec, d[j]);
+                    for (int j = 0; j < 32; j += 2) {
+                        const float2 r = __ffma2_rn(make_float2(m[j], m[j + 1]), make_float2(ec, ec),
+                                                    make_float2(d[j], d[j + 1]));
+                        m[j] = r.x;
+                        m[j + 1] = r.y;
+                    }
                     umma::tmem_st32(tmem + lane_base + C_MS + c0, m);
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) d[j] = tf32_rn(m[j]);
-                    umma::tmem_st32(tmem + lane_base + C_OP + c0, d);
+                    store_split32(tmem + lane_base + C_OP + c0, m);
                     for (int w = ck_i; w < ck.n && ck.off[w] - t0 == C; ++w) {
                         float* dst = p.S_ckpt + ((size_t)ck.slot[w] * p.B * p.Hv + bh) * (size_t)(D * D);
 #pragma unroll
@@ -440,96 +518,39 @@ __global__ void __launch_bounds__(NT, 1)
             }
             umma::fence_after_sync();
         }
-        if (tid == 0) {
-            n_cp[4] = w_v;
-            n_cp[5] = w_tp;
-            // an MMA in flight finishes (bounded) before the CTA exits
-            if (failed && mma_pending) mbar_wait_bounded(bar_mma, (mma_phase - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
-        }
+        if (tid == 0 && failed && mma_pending)  // an MMA in flight finishes (bounded) before the CTA exits
+            mbar_wait_bounded(bar_mma, (mma_phase - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
     } else {
-        // ======================= output rows and operand staging (warpgroups 2-3) =======================
+        // ======================= per-token vectors and output rows (warpgroups 2-3) =======================
         const int owg = wg - 2, tw = 32 * owg;  // this warpgroup's tokens tw .. tw + 31
         const int otid = tid - NMAIN;
         const float nw = sNW[dv];
-        // chunk cc's per-token vectors from the loaded rows (rq, rk, beta, gamma): the norm
-        // factors ride on the vectors, so the operand rows stay the exact bf16 values
+        // chunk cc's per-token vectors from its loaded rq, rk, beta, gamma: the norm factors
+        // ride on the vectors, so the operand rows stay the exact bf16 values
         auto stage_vectors = [&](int cc) {
+            const float* vec = reinterpret_cast<const float*>(sm + R_VEC + 1024u * (uint32_t)(cc & 1));
             float* sv = scr + S_V + 384 * (cc & 1);
             if (otid < C) {
                 const float gC = vec[192 + C - 1], gt = vec[192 + otid], rk = vec[64 + otid];
                 const float eg = expf(gt);
                 sv[V_B + otid] = vec[128 + otid];
                 sv[V_G + otid] = gt;
-                sv[V_EK + otid] = eg * rk;
+                sv[V_EK + otid] = -(eg * rk);
                 sv[V_EF + otid] = expf(gC - gt) * rk;
                 sv[V_EQ + otid] = eg * (vec[otid] * p.q_scale);
                 if (otid == 0) sv[V_EC] = expf(gC);
             }
         };
-        // [K;Q] rows of the loaded chunk as tf32 operands (bf16 values are exact in tf32); with
-        // km, the K rows also go to the K MN-major operand
-        auto stage_rows = [&](bool kq, bool km) {
-            uint2 raws[16];
-#pragma unroll
-            for (int u = 0; u < 16; ++u) {  // every shared operand first (no load behind a store)
-                const int idx = otid + u * (NT - NMAIN), r = idx >> 5, c4 = (idx & 31) * 4, t = r & 63;
-                if (u < 8 || kq) raws[u] = *reinterpret_cast<const uint2*>(sm + (u < 8 ? R_KS : R_QS) + t * D * 2 + c4 * 2);
-            }
-#pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                if (!(u < 8 || kq)) continue;
-                const int idx = otid + u * (NT - NMAIN), r = idx >> 5, c4 = (idx & 31) * 4;
-                const uint2 raw2 = raws[u];
-                const uint4 f = make_uint4(raw2.x << 16, raw2.x & 0xFFFF0000u, raw2.y << 16, raw2.y & 0xFFFF0000u);
-                if (u < 8 && km) *reinterpret_cast<uint4*>(sm + R_KM + umma::mnmajor_off(r, c4, C)) = f;
-                if (kq) *reinterpret_cast<uint4*>(sm + R_KQ + umma::kmajor_off(r, c4, 128)) = f;
-            }
-            fence_proxy_async_smem();
-        };
-        int n_bdone = 0;
-        // the first chunk's operands
-        {
-            const bool ok = mbar_wait_bounded(bar_qk, (uint32_t)w_qk & 1u, GDN_DEVERR_TMA_TIMEOUT);
-            w_qk += ok;
-            if (!nb_any(!ok, 4, NT - NMAIN)) {
-                stage_vectors(0);
-                stage_rows(true, true);
-                mbar_arrive(bar_staged);
-                nb_sync(4, NT - NMAIN);  // every output thread has read the rows of chunk 0
-                if (tid == NMAIN && NC > 1 && !sub_in(0)) {
-                    fence_proxy_async_smem();
-                    issue_qk(1);
-                }
-            } else {
-                failed = true;
-            }
-        }
+        bool bad = false;
+        bad |= !mbar_wait_bounded(bar_qk(0), 0u, GDN_DEVERR_TMA_TIMEOUT);
+        stage_vectors(0);
+        mbar_arrive(bar_staged);
         for (int c = 0; c < NC && !failed; ++c) {
             const int t0 = c * C;
             const float* sv = scr + S_V + 384 * (c & 1);
-            if (c + 1 < NC) {
-                // [K;Q] of the next chunk once MMA-b of this one has read the operand region
-                const bool bd = mbar_wait_bounded(bar_bdone, (uint32_t)n_bdone & 1u, GDN_DEVERR_MMA_TIMEOUT);
-                ++n_bdone;
-                bool lq = false;
-                if (bd) {
-                    lq = mbar_wait_bounded(bar_qk, (uint32_t)w_qk & 1u, GDN_DEVERR_TMA_TIMEOUT);
-                    w_qk += lq;
-                }
-                if (nb_any(!lq, 4, NT - NMAIN)) {
-                    failed = true;
-                    break;
-                }
-                stage_vectors(c + 1);
-                stage_rows(true, false);
-            }
-            const bool rdy = mbar_wait_bounded(bar_ordy, (uint32_t)c & 1u, GDN_DEVERR_MMA_TIMEOUT);
-            if (nb_any(!rdy, 4, NT - NMAIN)) {
-                failed = true;
-                break;
-            }
+            bad |= !mbar_wait_bounded(bar_ordy, (uint32_t)c & 1u, GDN_DEVERR_MMA_TIMEOUT);
             umma::fence_after_sync();
-            // O[t][dv] = e^{gamma_t} O1 + D
+            // O[t][dv] = e^{gamma_t} rq dk^-1/2 O1 + D
             float o[32];
             {
                 float o1[32], dd[32];
@@ -542,12 +563,29 @@ __global__ void __launch_bounds__(NT, 1)
             umma::fence_before_sync();
             mbar_arrive(bar_ofree);  // these tensor-memory columns may be overwritten now
             if (c + 1 < NC) {
-                // K MN-major of the next chunk: MMA-e of this one (before o_ready) has read it
-                stage_rows(false, true);
+                // the next chunk's vectors: after o_ready of this chunk the state path is done with
+                // the previous chunk's (same parity), and it waits for these only in this chunk's
+                // successor, so the staged phases never run two ahead of it
+                bad |= !mbar_wait_bounded(bar_qk(c + 1), (uint32_t)((c + 1) >> 1) & 1u, GDN_DEVERR_TMA_TIMEOUT);
+                stage_vectors(c + 1);
                 mbar_arrive(bar_staged);
-                if (tid == NMAIN) {  // MMA-c and MMA-d of chunk c are complete, Z has read v
-                    issue_v(c + 1);
-                    issue_tp(c + 1);
+            }
+            if (tid == NMAIN && !bad) {
+                // MMA-c, MMA-d and MMA-e of chunk c are complete; the previous copy into each
+                // region must also have been seen complete here before the next one is issued
+                if (c + 1 < NC) {
+                    const bool ok = mbar_wait_bounded(bar_v, (uint32_t)c & 1u, GDN_DEVERR_TMA_TIMEOUT) &&
+                                    mbar_wait_bounded(bar_tp, (uint32_t)c & 1u, GDN_DEVERR_TMA_TIMEOUT);
+                    bad |= !ok;
+                    if (ok) {
+                        issue_v(c + 1);
+                        issue_tp(c + 1);
+                    }
+                }
+                if (c + 2 < NC) {
+                    const bool ok = mbar_wait_bounded(bar_qk(c), (uint32_t)(c >> 1) & 1u, GDN_DEVERR_TMA_TIMEOUT);
+                    bad |= !ok;
+                    if (ok) issue_qk(c + 2);
                 }
             }
 #pragma unroll
@@ -576,7 +614,8 @@ __global__ void __launch_bounds__(NT, 1)
                 sRstd[t] = rsqrtf(ss / (float)D + p.eps);
             }
             const bool zok = mbar_wait_bounded(bar_z, (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
-            ++w_z;
+            w_z += zok;
+            bad |= !zok;
             nb_sync(2 + owg, 128);
             // the rows are assembled in the z tile's place ([64 tokens][128] bf16) and leave by one
             // tensor store, so every z value is read before the tile is overwritten
@@ -584,66 +623,57 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
                 y[j] = o[j] * sRstd[tw + j];
-                zv[j] = zok ? bf_at(sm + R_ZS, (tw + j) * D + dv) : 0.f;
+                zv[j] = bf_at(sm + R_ZS, (tw + j) * D + dv);
             }
             nb_sync(4, NT - NMAIN);
-            if (tid == NMAIN && c + 2 < NC && !sub_in(c + 1)) {  // every output thread has staged chunk c + 1
-                fence_proxy_async_smem();
-                issue_qk(c + 2);
-            }
             uint16_t* tile = reinterpret_cast<uint16_t*>(sm + R_ZS) + tw * D + dv;
-            if (zok) {
 #pragma unroll
-                for (int j = 0; j < 32; j += 2) round2_bf16(y[j], y[j + 1]);
+            for (int j = 0; j < 32; j += 2) round2_bf16(y[j], y[j + 1]);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) y[j] *= nw;
+            for (int j = 0; j < 32; ++j) y[j] *= nw;
 #pragma unroll
-                for (int j = 0; j < 32; j += 2) round2_bf16(y[j], y[j + 1]);
+            for (int j = 0; j < 32; j += 2) round2_bf16(y[j], y[j + 1]);
 #pragma unroll
-                for (int j = 0; j < 32; j += 2) {
-                    const float z0 = zv[j], z1 = zv[j + 1];
-                    float a0 = y[j] * __fdividef(z0, 1.0f + __expf(-z0));
-                    float a1 = y[j + 1] * __fdividef(z1, 1.0f + __expf(-z1));
-                    uint32_t bits;
-                    round2_bf16(a0, a1, &bits);
-                    tile[j * D] = (uint16_t)(bits & 0xFFFFu);
-                    tile[(j + 1) * D] = (uint16_t)(bits >> 16);
-                }
+            for (int j = 0; j < 32; j += 2) {
+                const float z0 = zv[j], z1 = zv[j + 1];
+                float a0 = y[j] * __fdividef(z0, 1.0f + __expf(-z0));
+                float a1 = y[j + 1] * __fdividef(z1, 1.0f + __expf(-z1));
+                uint32_t bits;
+                round2_bf16(a0, a1, &bits);
+                tile[j * D] = (uint16_t)(bits & 0xFFFFu);
+                tile[(j + 1) * D] = (uint16_t)(bits >> 16);
             }
             fence_proxy_async_smem();
-            nb_sync(4, NT - NMAIN);
+            // the group agrees on a wait that ran out (any thread) once per chunk, before the store
+            if (nb_any(bad, 4, NT - NMAIN)) {
+                failed = true;
+                break;
+            }
             if (tid == NMAIN) {
-                if (zok) {
-                    // rows past the sequence end fall outside the tensor map and are not written
-                    tma_store_3d(&tm_out, sb + R_ZS, h * D, t0, b);
-                    bulk_commit_group();
+                // rows past the sequence end fall outside the tensor map and are not written
+                tma_store_3d(&tm_out, sb + R_ZS, h * D, t0, b);
+                bulk_commit_group();
+                if (c + 1 < NC) {
                     bulk_wait_group_read0();  // the tile is read: the next z rows may land there
-                }
-                if (c + 1 < NC && zok) {
                     issue_z(c + 1);
                     ++n_z;
                 }
             }
-            if (nb_any(!zok, 4, NT - NMAIN)) {
-                failed = true;
-                break;
-            }
         }
-        if (failed && tid == NMAIN)
-            for (; w_z < n_z; ++w_z) mbar_wait_bounded(bar_z, (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
         if (tid == NMAIN) {
+            if (failed)
+                for (; w_z < n_z; ++w_z) mbar_wait_bounded(bar_z, (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
             bulk_wait_group0();  // output rows written before the CTA exits
-            n_cp[3] = w_qk;
         }
     }
     umma::fence_before_sync();
     __syncthreads();
     if (tid == 0) {
-        // input copies still in flight (a wait ran out) land before the CTA exits (bounded)
-        const uint32_t bar_cp[3] = {bar_qk, bar_v, bar_tp};
-        for (int i = 0; i < 3; ++i)
-            for (int k = n_cp[3 + i]; k < n_cp[i]; ++k)
-                mbar_wait_bounded(bar_cp[i], (uint32_t)k & 1u, GDN_DEVERR_TMA_TIMEOUT);
+        // the last input copy into each region lands before the CTA exits (bounded; every
+        // earlier copy on the same barrier was seen complete before the next was issued)
+        const uint32_t bar_cp[4] = {bar_qk0, bar_qk0 + 8u, bar_v, bar_tp};
+        for (int i = 0; i < 4; ++i)
+            if (n_cp[i] > 0) mbar_wait_bounded(bar_cp[i], (uint32_t)(n_cp[i] - 1) & 1u, GDN_DEVERR_TMA_TIMEOUT);
     }
     if (warp == 0) umma::tmem_dealloc(tmem, T_COLS);
 }
@@ -652,8 +682,10 @@ __global__ void __launch_bounds__(NT, 1)
 
 cudaError_t launch_prefill_seq(const MixParams& p, const CkptList& ck, const PrefillWs& ws, cudaStream_t s) {
     const uint64_t conv_dim = 2ull * p.Hk * 128 + (uint64_t)p.Hv * 128;
-    CUtensorMap tm_qkv, tm_z, tm_out;
-    if (!encode_tmap_3d_bf16(&tm_qkv, ws.qkv, conv_dim, (uint64_t)ws.tp_len, (uint64_t)p.B, conv_dim * 2,
+    CUtensorMap tm_qk, tm_v, tm_z, tm_out;
+    if (!encode_tmap_3d_bf16(&tm_qk, ws.qkv, conv_dim, (uint64_t)ws.tp_len, (uint64_t)p.B, conv_dim * 2,
+                             conv_dim * 2 * (uint64_t)ws.tp_len, 64, pseq::C, true) ||
+        !encode_tmap_3d_bf16(&tm_v, ws.qkv, conv_dim, (uint64_t)ws.tp_len, (uint64_t)p.B, conv_dim * 2,
                              conv_dim * 2 * (uint64_t)ws.tp_len, 128, pseq::C) ||
         !encode_tmap_3d_bf16(&tm_z, p.z, (uint64_t)p.Hv * 128, (uint64_t)p.T, (uint64_t)p.B, (uint64_t)p.zs_t * 2,
                              (uint64_t)p.zs_b * 2, 128, pseq::C) ||
@@ -671,7 +703,7 @@ cudaError_t launch_prefill_seq(const MixParams& p, const CkptList& ck, const Pre
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
-    pseq::prefill_seq_kernel<<<p.B * p.Hv, pseq::NT, pseq::SMEM_BYTES, s>>>(p, ck, ws, tm_qkv, tm_z, tm_out);
+    pseq::prefill_seq_kernel<<<p.B * p.Hv, pseq::NT, pseq::SMEM_BYTES, s>>>(p, ck, ws, tm_qk, tm_v, tm_z, tm_out);
     return cudaGetLastError();
 }
 
