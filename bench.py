@@ -513,7 +513,7 @@ def run_prefill(torch, dist, m, local, dev, world, barrier, B=8, T=8192):
             "roofline": {"bound": "tensor", "achieved": ach, "peak": tflops, "unit": "TFLOP/s",
                          "frac": ach / tflops, "peak_source": src, "flops_per_launch": fl,
                          "min_bytes_per_launch": prefill_min_bytes(B, T, hk, hv, d),
-                         "kernel": "gdn::pseq::prefill_seq_kernel (tcgen05 tf32, state in tensor memory, 1 CTA per (batch, head)) after gdn::pprep::prefill_prep_kernel"}}
+                         "kernel": "gdn::pseq::prefill_seq_kernel (tcgen05 bf16 hi+lo and tf32, state in tensor memory, 1 CTA per (batch, head)) after gdn::pprep::prefill_prep_kernel"}}
 
 
 def run_rollback(torch, dist, m, local, dev, world, barrier, steps=1024):
