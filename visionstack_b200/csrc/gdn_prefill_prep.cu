@@ -80,27 +80,30 @@ __device__ __forceinline__ void round2(float& a, float& b) {
 // Column j of the inverse of the unit lower triangular 32x32 block I + A
 // (A strictly lower triangular, row stride A_STRIDE) by forward substitution:
 // X[i][j] = [i == j] - sum_{k<i} A[i][k] X[k][j] (X[k][j] = 0 for k < j).
+// Four partial sums (k mod 4) on packed fp32 pairs; x starts at zero and A is
+// zero on and above its diagonal, so the products past k = i - 1 add exact zeros.
 __device__ __forceinline__ void tri_inverse_block32(const float* A, int j, float (&x)[32]) {
 #pragma unroll
+    for (int i = 0; i < 32; ++i) x[i] = 0.f;
+#pragma unroll
     for (int i = 0; i < 32; ++i) {
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int k = 0; k < i; k += 4) {
             const float4 a = *reinterpret_cast<const float4*>(A + i * A_STRIDE + k);
-            s0 = fmaf(a.x, x[k], s0);
-            if (k + 1 < i) s1 = fmaf(a.y, x[k + 1], s1);
-            if (k + 2 < i) s2 = fmaf(a.z, x[k + 2], s2);
-            if (k + 3 < i) s3 = fmaf(a.w, x[k + 3], s3);
+            s01 = __ffma2_rn(make_float2(a.x, a.y), make_float2(x[k], x[k + 1]), s01);
+            s23 = __ffma2_rn(make_float2(a.z, a.w), make_float2(x[k + 2], x[k + 3]), s23);
         }
-        x[i] = (i == j ? 1.f : 0.f) - ((s0 + s1) + (s2 + s3));
+        x[i] = (i == j ? 1.f : 0.f) - ((s01.x + s01.y) + (s23.x + s23.y));
     }
 }
 
-// out[i][jb..jb+7] (+)= sign * sum_k L[i][k] R[k][jb..jb+7] over 32 k, row stride A_STRIDE.
+// out[i][jb..jb+7] (+)= sign * sum_k L[i][k] R[k][jb..jb+7] over 32 k, row stride A_STRIDE
+// (packed fp32 pairs).
 __device__ __forceinline__ void block_row8(const float* L, const float* R, int i, int jb, float* out, float sign) {
-    float acc[8];
+    float2 acc[4];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    for (int e = 0; e < 4; ++e) acc[e] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < 32; k += 4) {
         const float4 a = *reinterpret_cast<const float4*>(L + i * A_STRIDE + k);
@@ -109,20 +112,17 @@ __device__ __forceinline__ void block_row8(const float* L, const float* R, int i
         for (int kk = 0; kk < 4; ++kk) {
             const float4 r0 = *reinterpret_cast<const float4*>(R + (k + kk) * A_STRIDE + jb);
             const float4 r1 = *reinterpret_cast<const float4*>(R + (k + kk) * A_STRIDE + jb + 4);
-            acc[0] = fmaf(av[kk], r0.x, acc[0]);
-            acc[1] = fmaf(av[kk], r0.y, acc[1]);
-            acc[2] = fmaf(av[kk], r0.z, acc[2]);
-            acc[3] = fmaf(av[kk], r0.w, acc[3]);
-            acc[4] = fmaf(av[kk], r1.x, acc[4]);
-            acc[5] = fmaf(av[kk], r1.y, acc[5]);
-            acc[6] = fmaf(av[kk], r1.z, acc[6]);
-            acc[7] = fmaf(av[kk], r1.w, acc[7]);
+            const float2 a2 = make_float2(av[kk], av[kk]);
+            acc[0] = __ffma2_rn(a2, make_float2(r0.x, r0.y), acc[0]);
+            acc[1] = __ffma2_rn(a2, make_float2(r0.z, r0.w), acc[1]);
+            acc[2] = __ffma2_rn(a2, make_float2(r1.x, r1.y), acc[2]);
+            acc[3] = __ffma2_rn(a2, make_float2(r1.z, r1.w), acc[3]);
         }
     }
     *reinterpret_cast<float4*>(out + i * A_STRIDE + jb) =
-        make_float4(sign * acc[0], sign * acc[1], sign * acc[2], sign * acc[3]);
+        make_float4(sign * acc[0].x, sign * acc[0].y, sign * acc[1].x, sign * acc[1].y);
     *reinterpret_cast<float4*>(out + i * A_STRIDE + jb + 4) =
-        make_float4(sign * acc[4], sign * acc[5], sign * acc[6], sign * acc[7]);
+        make_float4(sign * acc[2].x, sign * acc[2].y, sign * acc[3].x, sign * acc[3].y);
 }
 
 __global__ void __launch_bounds__(NT, 3)
@@ -293,41 +293,33 @@ __global__ void __launch_bounds__(NT, 3)
     }
     __syncthreads();
 
-    // ---- [K;Q] tf32 operand (rows 0..63 K, 64..127 Q) over the staging area ----
+    // ---- [k;q] as a bf16 K-major operand (rows 0..63 k, 64..127 q: the exact conv outputs;
+    //      the norm factors are applied to G and P0 afterwards) over the staging area ----
     if (tid == 0) bulk_wait_group_read0();  // the conv-output stores have read the staging rows
-    uint2 kq_raw[16];
+    uint4 kq_raw[8];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) {
-        const int idx = tid + u * NT, r = idx >> 5, c4 = (idx & 31) * 4;
+    for (int u = 0; u < 8; ++u) {
+        const int idx = tid + u * NT, r = idx >> 4, c8 = (idx & 15) * 8;
         const int g = r < C ? 1 : 0, t = r & 63;
-        kq_raw[u] = *reinterpret_cast<const uint2*>(sm + g * GROUP_BYTES + (t + HIST) * D * 2 + c4 * 2);
+        kq_raw[u] = *reinterpret_cast<const uint4*>(sm + g * GROUP_BYTES + (t + HIST) * D * 2 + c8 * 2);
     }
     __syncthreads();
 #pragma unroll
-    for (int u = 0; u < 16; ++u) {
-        const int idx = tid + u * NT, r = idx >> 5, c4 = (idx & 31) * 4;
-        const int t = r & 63;
-        const uint2 v = kq_raw[u];
-        float4 f = make_float4(bf_lo(v.x), bf_hi(v.x), bf_lo(v.y), bf_hi(v.y));
-        if (r < C) {
-            const float s = sRK[t];
-            f = make_float4(f.x * s, f.y * s, f.z * s, f.w * s);
-        } else {
-            const float s = sRQ[t];
-            f = make_float4((f.x * s) * p.q_scale, (f.y * s) * p.q_scale, (f.z * s) * p.q_scale,
-                            (f.w * s) * p.q_scale);
-        }
-        *reinterpret_cast<float4*>(sm + umma::kmajor_off(r, c4, 128)) = umma::tf32_rna4(f);
+    for (int u = 0; u < 8; ++u) {
+        const int idx = tid + u * NT, r = idx >> 4, c8 = (idx & 15) * 8;
+        *reinterpret_cast<uint4*>(sm + umma::kmajor_off16(r, c8, 128)) = kq_raw[u];
     }
     fence_proxy_async_smem();
     umma::fence_before_sync();
     __syncthreads();
     if (tid == 0) {
         umma::fence_after_sync();
-        const uint32_t sb = smem_u32(sm);
-        const uint32_t idesc = umma::idesc_tf32(128, 64, 0, 0);
-        for (int kk = 0; kk < D / 8; ++kk)
-            umma::mma_tf32(tmem, umma::desc_kmajor(sb, 128, kk), umma::desc_kmajor(sb, 128, kk), idesc, kk > 0);
+        const uint64_t d0 = umma::desc_kmajor0(smem_u32(sm));
+        const uint32_t idesc = umma::idesc_bf16(128, 64, 0, 0);
+        for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t d = umma::desc_add(d0, umma::kmajor_kstep(kk, 128));
+            umma::mma_bf16(tmem, d, d, idesc, kk > 0);  // [G; P0] = [k; q] k^T (raw rows)
+        }
         umma::mma_commit(bar_mma);
     }
 
@@ -372,7 +364,7 @@ __global__ void __launch_bounds__(NT, 3)
     for (int i = tid; i < rep * C; i += NT) {
         const int r = i / C, t = i % C;
         sEG[i] = expf(sG[i]);
-        sENG[i] = expf(-sG[i]);
+        sENG[i] = expf(-sG[i]) * sRK[t];  // the column's norm factor rides on e^{-gamma_j}
         float* gate = ws.gate + (((size_t)b * p.Hv + kh * rep + r) * NC + c) * 128;
         gate[t] = sB[r * 64 + t];
         gate[64 + t] = sG[r * 64 + t];
@@ -403,58 +395,64 @@ __global__ void __launch_bounds__(NT, 3)
             const float* gr = sG + r * 64;
             const float gt = gr[t];
             // decay e^{gamma_t - gamma_j}: as e^{gamma_t} e^{-gamma_j} when neither factor can
-            // leave the normal range (gamma >= -80 over the chunk), else one exp per pair
+            // leave the normal range (gamma >= -80 over the chunk), else one exp per pair; the
+            // column's norm factor rk_j rides on it (G and P0 are products of the raw rows)
             const bool split = gr[C - 1] >= -80.f;
             const float egt = sEG[r * 64 + t];
-            const float bt = sB[r * 64 + t];
+            // row factor: beta_t rk_t for A, rq_t dk^-1/2 for P (q * rq * dk^-1/2), folded into
+            // the decay while the tensor-memory load is in flight
+            const float rowf = g_rows ? sB[r * 64 + t] * sRK[t] : sRQ[t] * p.q_scale;
             float* arow = reinterpret_cast<float*>(sm + r * A_BYTES) + t * A_STRIDE;
             unsigned char* img = sm + rep * A_BYTES + r * IMG_BYTES;
-#pragma unroll
+#pragma unroll 1
             for (int hf = 0; hf < 2; ++hf) {
                 float v[32], dec[32];
                 umma::tmem_ld32(tmem + lane_base + 32 * hf, v);
                 if (split) {
                     const float4* e4 = reinterpret_cast<const float4*>(sENG + r * 64 + 32 * hf);
+                    const float2 eg2 = make_float2(egt * rowf, egt * rowf);
 #pragma unroll
                     for (int q = 0; q < 8; ++q) {
                         const float4 e = e4[q];
-                        dec[4 * q] = egt * e.x;
-                        dec[4 * q + 1] = egt * e.y;
-                        dec[4 * q + 2] = egt * e.z;
-                        dec[4 * q + 3] = egt * e.w;
+                        const float2 d01 = __fmul2_rn(eg2, make_float2(e.x, e.y));
+                        const float2 d23 = __fmul2_rn(eg2, make_float2(e.z, e.w));
+                        dec[4 * q] = d01.x;
+                        dec[4 * q + 1] = d01.y;
+                        dec[4 * q + 2] = d23.x;
+                        dec[4 * q + 3] = d23.y;
                     }
                 } else {
                     const float4* g4 = reinterpret_cast<const float4*>(gr + 32 * hf);
+                    const float4* k4 = reinterpret_cast<const float4*>(sRK + 32 * hf);
 #pragma unroll
                     for (int q = 0; q < 8; ++q) {
-                        const float4 e = g4[q];
-                        dec[4 * q] = __expf(gt - e.x);
-                        dec[4 * q + 1] = __expf(gt - e.y);
-                        dec[4 * q + 2] = __expf(gt - e.z);
-                        dec[4 * q + 3] = __expf(gt - e.w);
+                        const float4 e = g4[q], rk = k4[q];
+                        dec[4 * q] = __expf(gt - e.x) * (rowf * rk.x);
+                        dec[4 * q + 1] = __expf(gt - e.y) * (rowf * rk.y);
+                        dec[4 * q + 2] = __expf(gt - e.z) * (rowf * rk.z);
+                        dec[4 * q + 3] = __expf(gt - e.w) * (rowf * rk.w);
                     }
                 }
                 umma::tmem_wait_ld();
-                if (g_rows) {
 #pragma unroll
-                    for (int jj = 0; jj < 32; jj += 4) {
-                        const int j = 32 * hf + jj;
+                for (int jj = 0; jj < 32; jj += 4) {
+                    const int j = 32 * hf + jj;
+                    const float2 p01 = __fmul2_rn(make_float2(v[jj], v[jj + 1]), make_float2(dec[jj], dec[jj + 1]));
+                    const float2 p23 =
+                        __fmul2_rn(make_float2(v[jj + 2], v[jj + 3]), make_float2(dec[jj + 2], dec[jj + 3]));
+                    if (g_rows) {
                         float4 a;
-                        a.x = j + 0 < t ? (bt * v[jj + 0]) * dec[jj + 0] : 0.f;
-                        a.y = j + 1 < t ? (bt * v[jj + 1]) * dec[jj + 1] : 0.f;
-                        a.z = j + 2 < t ? (bt * v[jj + 2]) * dec[jj + 2] : 0.f;
-                        a.w = j + 3 < t ? (bt * v[jj + 3]) * dec[jj + 3] : 0.f;
+                        a.x = j + 0 < t ? p01.x : 0.f;
+                        a.y = j + 1 < t ? p01.y : 0.f;
+                        a.z = j + 2 < t ? p23.x : 0.f;
+                        a.w = j + 3 < t ? p23.y : 0.f;
                         *reinterpret_cast<float4*>(arow + j) = a;
-                    }
-                } else {
-#pragma unroll
-                    for (int jj = 0; jj < 32; jj += 4) {
-                        const int j = 32 * hf + jj;
+                    } else {
                         float4 a;
-                        a.x = j + 0 <= t ? umma::tf32_rna(v[jj + 0] * dec[jj + 0]) : 0.f;
-                        a.y = j + 1 <= t ? umma::tf32_rna(v[jj + 1] * dec[jj + 1]) : 0.f;
-                        a.z = j + 2 <= t ? umma::tf32_rna(v[jj + 2] * dec[jj + 2]) : 0.f;
-                        a.w = j + 3 <= t ? umma::tf32_rna(v[jj + 3] * dec[jj + 3]) : 0.f;
+                        a.x = j + 0 <= t ? umma::tf32_rna(p01.x) : 0.f;
+                        a.y = j + 1 <= t ? umma::tf32_rna(p01.y) : 0.f;
+                        a.z = j + 2 <= t ? umma::tf32_rna(p23.x) : 0.f;
+                        a.w = j + 3 <= t ? umma::tf32_rna(p23.y) : 0.f;
                         *reinterpret_cast<float4*>(img + umma::kmajor_off(t, j, C)) = a;
                     }
                 }
