@@ -5,10 +5,11 @@
 // state S[d][d] (one contiguous 64 KB block at d = 128), the raw projections
 // of its q/k/v channels and z for every token, its conv-state and
 // conv-weight rows - arrive in the group's shared-memory stage through bulk
-// asynchronous copies (cp.async.bulk, completion on one mbarrier).  As soon as
-// the group has moved the state into registers and run the conv, it releases
-// the stage and issues the copies of its next tile, so that copy overlaps the
-// rest of the computation.  The two groups interleave, keeping two state
+// asynchronous copies (cp.async.bulk; the state and the small inputs complete
+// on two mbarriers).  As soon as the group has moved the state into registers
+// it issues the copy of its next tile's state, and after the conv the copies
+// of the next tile's inputs, so those copies overlap the rest of the
+// computation.  The two groups interleave, keeping two state
 // tiles in flight per SM while the SMs do the conv / norm / delta-rule /
 // gated-norm work.  The new state leaves from registers with streaming
 // 128-bit stores (in place when state_out == state_in).
@@ -57,7 +58,7 @@ struct GroupLayout {
     static constexpr int OFF_RED = OFF_O + D * 4;                // [2][RG][D]
     static constexpr int OFF_GATE = OFF_RED + 2 * RG * D * 4;    // [2][TMAX]
     static constexpr int OFF_BAR = (OFF_GATE + 2 * TMAX * 4 + 7) / 8 * 8;
-    static constexpr int BYTES = (OFF_BAR + 8 + 127) / 128 * 128;
+    static constexpr int BYTES = (OFF_BAR + 16 + 127) / 128 * 128;  // two mbarriers: inputs, state
 };
 
 // Pool slot of column `col` of row b's slot table; -1 (and the error bit) when
@@ -110,7 +111,7 @@ __global__ void __launch_bounds__(NT, 1)
     float* so = reinterpret_cast<float*>(gbase + GL::OFF_O);
     float* red = reinterpret_cast<float*>(gbase + GL::OFF_RED);
     float* sgate = reinterpret_cast<float*>(gbase + GL::OFF_GATE);
-    const uint32_t bar = smem_u32(gbase + GL::OFF_BAR);
+    const uint32_t bar = smem_u32(gbase + GL::OFF_BAR), bar_s = bar + 8u;
 
     const int cg = tid % CG, rg = tid / CG;
     const int rep = p.Hv / p.Hk;
@@ -123,25 +124,32 @@ __global__ void __launch_bounds__(NT, 1)
 
     if (tid == 0) {
         mbar_init(bar, 1);
+        mbar_init(bar_s, 1);
         fence_mbar_init();
     }
     __syncthreads();
 
-    // thread 0 of the group issues every copy of one tile into the group's stage
+    // Thread 0 of the group issues the copies of one tile into the group's stage: the state
+    // (on bar_s: it refills as soon as the state is in registers) and the small inputs (on bar:
+    // they refill after the conv).
+    auto start_slot = [&](int b) -> size_t {  // pool slot of the starting state (slot mode)
+        if (!p.slot_table) return 0;
+        const int s0 = row_slot(p, b, 0);
+        return s0 < 0 ? 0 : (size_t)s0;
+    };
+    auto issue_state = [&](int tile) {
+        const size_t slot0 = start_slot(tile / p.Hv);
+        mbar_arrive_expect_tx(bar_s, (uint32_t)GL::S_BYTES);
+        bulk_load(smem_u32(gbase + GL::OFF_S), p.S_in + (slot0 * p.B * p.Hv + tile) * D * D, GL::S_BYTES, bar_s);
+    };
     auto issue = [&](int tile) {
         const int b = tile / p.Hv, h = tile - (tile / p.Hv) * p.Hv, kh = h / rep;
         const uint32_t mrow = D * sizeof(TA);
         const int c0 = kh * D, c1 = p.Hk * D + kh * D, c2 = 2 * p.Hk * D + h * D;
-        size_t slot0 = 0;  // pool slot of the starting state (slot mode)
-        if (p.slot_table) {
-            const int s0 = row_slot(p, b, 0);
-            slot0 = s0 < 0 ? 0 : (size_t)s0;
-        }
-        uint32_t bytes = (has_S ? GL::S_BYTES : 0) + 4u * T * mrow + 3u * D * KC * sizeof(TA);
+        const size_t slot0 = start_slot(b);
+        uint32_t bytes = 4u * T * mrow + 3u * D * KC * sizeof(TA);
         if (has_cs) bytes += 3u * D * LC * sizeof(TA);
         mbar_arrive_expect_tx(bar, bytes);
-        if (has_S)
-            bulk_load(smem_u32(gbase + GL::OFF_S), p.S_in + (slot0 * p.B * p.Hv + tile) * D * D, GL::S_BYTES, bar);
         for (int t = 0; t < T; ++t) {
             const TA* row = gmixed + (size_t)b * p.ms_b + (size_t)t * p.ms_t;
             bulk_load(smem_u32(gbase + GL::OFF_MQ + t * mrow), row + c0, mrow, bar);
@@ -164,7 +172,10 @@ __global__ void __launch_bounds__(NT, 1)
     };
 
     const int worker = blockIdx.x * NG + grp, nworkers = gridDim.x * NG;
-    if (tid == 0 && worker < num_tiles) issue(worker);
+    if (tid == 0 && worker < num_tiles) {
+        if (has_S) issue_state(worker);
+        issue(worker);
+    }
 
     // gate inputs of the next tile are loaded one tile ahead into registers
     float na = 0.f, nb = 0.f;
@@ -195,7 +206,8 @@ __global__ void __launch_bounds__(NT, 1)
             sgate[TMAX + tid] = expf(-expf(p.A_log[h]) * softplus_f(cur_a + p.dt_bias[h]));
         }
 
-        const bool ok = mbar_wait_bounded(bar, k & 1u, GDN_DEVERR_TMA_TIMEOUT);
+        const bool ok = (!has_S || mbar_wait_bounded(bar_s, k & 1u, GDN_DEVERR_TMA_TIMEOUT)) &&
+                        mbar_wait_bounded(bar, k & 1u, GDN_DEVERR_TMA_TIMEOUT);
         if (group_any(!ok, bar_id)) {
             failed = true;
             break;
@@ -207,6 +219,13 @@ __global__ void __launch_bounds__(NT, 1)
         for (int r = 0; r < RPT; ++r)
             S[r] = has_S ? *reinterpret_cast<const float4*>(sS + (rg * RPT + r) * D + cg * 4)
                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (has_S) {
+            group_sync(bar_id);  // the state is in registers: its region takes the next tile's state
+            if (tid == 0 && tile + nworkers < num_tiles) {
+                fence_proxy_async_smem();
+                issue_state(tile + nworkers);
+            }
+        }
 
         const bool own_qk = (h % rep) == 0;
         const int cbeg = own_qk ? 0 : 2 * D;
@@ -296,15 +315,19 @@ __global__ void __launch_bounds__(NT, 1)
                 qr[r4] = (q4.x * rq) * p.q_scale; qr[r4 + 1] = (q4.y * rq) * p.q_scale;
                 qr[r4 + 2] = (q4.z * rq) * p.q_scale; qr[r4 + 3] = (q4.w * rq) * p.q_scale;
             }
-            float4 pk = make_float4(0.f, 0.f, 0.f, 0.f), pq = pk;
+            // packed fp32 pairs: the same fused multiply-adds, two lanes per instruction
+            float2 pk01 = make_float2(0.f, 0.f), pk23 = pk01, pq01 = pk01, pq23 = pk01;
 #pragma unroll
             for (int r = 0; r < RPT; ++r) {
-                const float kv = kr[r], qv = qr[r];
-                pk.x = fmaf(kv, S[r].x, pk.x); pk.y = fmaf(kv, S[r].y, pk.y);
-                pk.z = fmaf(kv, S[r].z, pk.z); pk.w = fmaf(kv, S[r].w, pk.w);
-                pq.x = fmaf(qv, S[r].x, pq.x); pq.y = fmaf(qv, S[r].y, pq.y);
-                pq.z = fmaf(qv, S[r].z, pq.z); pq.w = fmaf(qv, S[r].w, pq.w);
+                const float2 kv = make_float2(kr[r], kr[r]), qv = make_float2(qr[r], qr[r]);
+                const float2 s01 = make_float2(S[r].x, S[r].y), s23 = make_float2(S[r].z, S[r].w);
+                pk01 = __ffma2_rn(kv, s01, pk01);
+                pk23 = __ffma2_rn(kv, s23, pk23);
+                pq01 = __ffma2_rn(qv, s01, pq01);
+                pq23 = __ffma2_rn(qv, s23, pq23);
             }
+            const float4 pk = make_float4(pk01.x, pk01.y, pk23.x, pk23.y);
+            const float4 pq = make_float4(pq01.x, pq01.y, pq23.x, pq23.y);
             reinterpret_cast<float4*>(red + rg * D)[cg] = pk;
             reinterpret_cast<float4*>(red + (RG + rg) * D)[cg] = pq;
             group_sync(bar_id);
@@ -321,13 +344,14 @@ __global__ void __launch_bounds__(NT, 1)
 
             {
                 const float4 u4 = reinterpret_cast<const float4*>(su)[cg];
+                const float2 u01 = make_float2(u4.x, u4.y), u23 = make_float2(u4.z, u4.w);
+                const float2 al = make_float2(alpha, alpha);
 #pragma unroll
                 for (int r = 0; r < RPT; ++r) {
-                    const float kv = kr[r];
-                    S[r].x = fmaf(kv, u4.x, alpha * S[r].x);
-                    S[r].y = fmaf(kv, u4.y, alpha * S[r].y);
-                    S[r].z = fmaf(kv, u4.z, alpha * S[r].z);
-                    S[r].w = fmaf(kv, u4.w, alpha * S[r].w);
+                    const float2 kv = make_float2(kr[r], kr[r]);
+                    const float2 s01 = __ffma2_rn(kv, u01, __fmul2_rn(al, make_float2(S[r].x, S[r].y)));
+                    const float2 s23 = __ffma2_rn(kv, u23, __fmul2_rn(al, make_float2(S[r].z, S[r].w)));
+                    S[r] = make_float4(s01.x, s01.y, s23.x, s23.y);
                 }
             }
             while (ck_i < ck.n && ck.off[ck_i] == t + 1) {
@@ -369,7 +393,8 @@ __global__ void __launch_bounds__(NT, 1)
     }
 
     if (failed && tid == 0) {
-        // the copy this group waited for may still land: wait for it (bounded) before exiting
+        // the copies this group waited for may still land: wait for them (bounded) before exiting
+        if (has_S) mbar_wait_bounded(bar_s, k & 1u, GDN_DEVERR_TMA_TIMEOUT);
         mbar_wait_bounded(bar, k & 1u, GDN_DEVERR_TMA_TIMEOUT);
     }
 }

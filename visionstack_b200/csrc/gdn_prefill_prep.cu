@@ -14,12 +14,14 @@
 //      activation dtype), written to the workspace in bf16 - exactly the
 //      values the reference feeds to the delta rule;
 //   3. L2-norm factors rq = (|q|^2 + 1e-6)^-1/2, rk likewise (config.py:114-115);
-//   4. [K;Q] (normalised, q times dk^-1/2, rounded to tf32) in swizzled shared
-//      memory and one tcgen05 MMA: G = K K^T, P0 = Q K^T;
+//   4. the raw [k;q] rows as a bf16 operand in swizzled shared memory and one
+//      tcgen05 MMA (kind::f16; bf16 products are exact): G = k k^T, P0 = q k^T;
 //   5. per value head h of the key head: beta = sigmoid(b) rounded,
 //      g = -exp(A_log) softplus(a + dt_bias), gamma = cumsum(g)
-//      (deltanet.py:516-517, 278-281); A = tril(beta_i G_ij e^{gamma_i-gamma_j}, -1),
-//      P = P0 o e^{gamma_i-gamma_j} (j <= i), T = (I + A)^-1 by forward
+//      (deltanet.py:516-517, 278-281); with the normalised rows K = k rk and
+//      Q = q rq dk^-1/2 applied as row / column factors,
+//      A = tril(beta_i K_i.K_j e^{gamma_i-gamma_j}, -1),
+//      P = Q_i.K_j e^{gamma_i-gamma_j} (j <= i), T = (I + A)^-1 by forward
 //      substitution in fp32 (the reference's triangular solve,
 //      deltanet.py:93-162, restated);
 //   6. T and P, rounded to tf32, are written as ready-made K-major 128-byte
