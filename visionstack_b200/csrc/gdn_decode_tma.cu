@@ -307,13 +307,16 @@ __global__ void __launch_bounds__(NT, 1)
             const float beta = sgate[t], alpha = sgate[TMAX + t];
 
             float kr[RPT], qr[RPT];
+            const float2 rk2 = make_float2(rk, rk), rq2 = make_float2(rq, rq), qs2 = make_float2(p.q_scale, p.q_scale);
 #pragma unroll
             for (int r4 = 0; r4 < RPT; r4 += 4) {
                 const float4 k4 = *reinterpret_cast<const float4*>(ckk + rg * RPT + r4);
                 const float4 q4 = *reinterpret_cast<const float4*>(cq + rg * RPT + r4);
-                kr[r4] = k4.x * rk; kr[r4 + 1] = k4.y * rk; kr[r4 + 2] = k4.z * rk; kr[r4 + 3] = k4.w * rk;
-                qr[r4] = (q4.x * rq) * p.q_scale; qr[r4 + 1] = (q4.y * rq) * p.q_scale;
-                qr[r4 + 2] = (q4.z * rq) * p.q_scale; qr[r4 + 3] = (q4.w * rq) * p.q_scale;
+                const float2 k01 = __fmul2_rn(make_float2(k4.x, k4.y), rk2), k23 = __fmul2_rn(make_float2(k4.z, k4.w), rk2);
+                const float2 q01 = __fmul2_rn(__fmul2_rn(make_float2(q4.x, q4.y), rq2), qs2);
+                const float2 q23 = __fmul2_rn(__fmul2_rn(make_float2(q4.z, q4.w), rq2), qs2);
+                kr[r4] = k01.x; kr[r4 + 1] = k01.y; kr[r4 + 2] = k23.x; kr[r4 + 3] = k23.y;
+                qr[r4] = q01.x; qr[r4 + 1] = q01.y; qr[r4 + 2] = q23.x; qr[r4 + 3] = q23.y;
             }
             // packed fp32 pairs: the same fused multiply-adds, two lanes per instruction
             float2 pk01 = make_float2(0.f, 0.f), pk23 = pk01, pq01 = pk01, pq23 = pk01;
