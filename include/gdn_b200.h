@@ -60,6 +60,7 @@ extern "C" {
 #define GDN_DEVERR_TMA_TIMEOUT 0x1u
 #define GDN_DEVERR_MMA_TIMEOUT 0x2u
 #define GDN_DEVERR_BAD_SLOT 0x4u   /* slot-table entry or accepted count out of range */
+#define GDN_DEVERR_HANDOFF_TIMEOUT 0x8u  /* chunked prefill: a chain's state hand-off never arrived */
 
 /* Size of the library's fixed device scratch used by gdn_mixer_prefill_noalloc
  * (64 MiB per device: the two-kernel prefill's workspace for about 1.9k
@@ -227,7 +228,10 @@ int32_t gdn_mixer_prefill(const gdn_mixer_args* args, void* stream);
  * arguments: 0 when the call takes a path without workspace, a negative
  * GDN_ERR_* code when the arguments are invalid.  At batch 8 x 8192 tokens,
  * 16 / 32 heads of 128 this is about 2.2 GB (the conv outputs in bf16 plus a
- * 32 KB pair of 64x64 tf32 matrices per chunk and value head).
+ * 32 KB pair of 64x64 tf32 matrices per chunk and value head).  When there
+ * are more (batch, value head) chains than the current device has SMs it adds
+ * one state-sized hand-off slot per SM, so ask with the device current that
+ * will run the call.
  */
 int64_t gdn_prefill_workspace_bytes(const gdn_mixer_args* args);
 

@@ -267,6 +267,22 @@ def test_tensor_core_prefill_vs_oracle(B, T, with_state, offsets, fused):
     assert _lib.device_error() == 0
 
 
+def test_two_kernel_prefill_chains_split_across_ctas():
+    """More (batch, value head) chains than SMs: the sequential kernel runs one CTA per SM,
+    cuts the chains' chunks into equal runs and hands the state from one CTA to the next
+    (chain heads, tails and whole chains; checkpoints on both sides of a hand-off)."""
+    from visionstack_b200 import _lib
+    shape = W.LayerShape(256, 2, 4, 128, 128)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    B, T = sms // shape.num_v_heads + 3, 200  # B * 4 chains > SMs; 4 chunks per chain
+    offs = (1, 37, 64, 100, 128, 199, 200)
+    m, params = make_layer(shape, "bf16")
+    d = mixer_inputs(shape, B, T, "bf16", seed=77, with_state=True)
+    check(shape, "bf16", run_ours(m, shape, d, "bf16", False, offs),
+          run_oracle(shape, params, d, "bf16", chunk=True, offsets=offs), offs, "split chains")
+    assert _lib.device_error() == 0
+
+
 @pytest.mark.parametrize("rep", [1, 4])
 def test_two_kernel_prefill_gqa_groupings(rep):
     """Key heads shared by 1 or 4 value heads (the preparation pass handles

@@ -74,6 +74,38 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     }
 }
 
+// Invalidate an mbarrier (before it is initialised again for reuse).
+__device__ __forceinline__ void mbar_inval(uint32_t bar) {
+    asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// A flag in global memory that another CTA of the same grid sets: wait (bounded) until it is
+// non-zero, with acquire semantics at GPU scope; false (and GDN_DEVERR_HANDOFF_TIMEOUT) after
+// the limit.
+__device__ __forceinline__ bool wait_flag_bounded(const int* flag) {
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        if (v != 0) return true;
+        if ((it & 63u) == 0u) {
+            const uint64_t now = global_timer_ns();
+            if (it == 0u) {
+                t0 = now;
+            } else if (now - t0 > GDN_WAIT_LIMIT_NS) {
+                atomicOr(&g_device_error, GDN_DEVERR_HANDOFF_TIMEOUT);
+                return false;
+            }
+        }
+        __nanosleep(64);
+    }
+}
+// Set a flag with release semantics at GPU scope (after this thread's writes and, through a
+// prior block barrier and fences, its block's).
+__device__ __forceinline__ void release_flag(int* flag) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(1) : "memory");
+}
+
 // One bulk copy global -> shared of `bytes` (multiple of 16, both addresses
 // 16-byte aligned), completing `bytes` of transaction count on `bar`.
 __device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes, uint32_t bar) {

@@ -242,6 +242,17 @@ int32_t gdn_device_error(uint32_t* flags_out, int32_t clear) {
     return ok();
 }
 
+// Hand-off slots of the sequential prefill kernel on the current device (prefill_ws_layout).
+static int handoff_slots(const gdn_mixer_args* args) {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    return gdn::prefill_handoff_slots(args->batch * args->num_v_heads, sms);
+}
+
 int64_t gdn_prefill_workspace_bytes(const gdn_mixer_args* args) {
     gdn::CkptList ck;
     gdn::MixParams p;
@@ -250,10 +261,10 @@ int64_t gdn_prefill_workspace_bytes(const gdn_mixer_args* args) {
     if ((args->flags & GDN_FLAG_CUDA_CORE_PREFILL) || !gdn::prefill_prep_supported(p, args->head_k_dim,
                                                                                  args->act_dtype))
         return 0;
-    size_t off[4];
+    size_t off[6];
     ok();
     return (int64_t)gdn::prefill_ws_layout(args->batch, args->seq_len, args->num_k_heads, args->num_v_heads,
-                                           args->head_k_dim, off);
+                                           args->head_k_dim, handoff_slots(args), off);
 }
 
 int32_t gdn_mixer_prefill_ws(const gdn_mixer_args* args, void* workspace, int64_t workspace_bytes, void* stream) {
@@ -264,9 +275,10 @@ int32_t gdn_mixer_prefill_ws(const gdn_mixer_args* args, void* workspace, int64_
     if ((args->flags & GDN_FLAG_CUDA_CORE_PREFILL) || !gdn::prefill_prep_supported(p, args->head_k_dim,
                                                                                  args->act_dtype))
         return gdn_mixer_prefill(args, stream);  // needs no workspace
-    size_t off[4];
+    size_t off[6];
+    const int n_hs = handoff_slots(args);
     const size_t need = gdn::prefill_ws_layout(args->batch, args->seq_len, args->num_k_heads, args->num_v_heads,
-                                               args->head_k_dim, off);
+                                               args->head_k_dim, n_hs, off);
     if (!workspace || workspace_bytes < 0 || (size_t)workspace_bytes < need)
         return fail(GDN_ERR_INVALID_ARG, "workspace of %lld bytes needed (got %lld)", (long long)need,
                     (long long)workspace_bytes);
@@ -277,6 +289,9 @@ int32_t gdn_mixer_prefill_ws(const gdn_mixer_args* args, void* workspace, int64_
     ws.nrm = reinterpret_cast<float*>(base + off[1]);
     ws.gate = reinterpret_cast<float*>(base + off[2]);
     ws.tp = reinterpret_cast<float*>(base + off[3]);
+    ws.hs = reinterpret_cast<float*>(base + off[4]);
+    ws.hflag = reinterpret_cast<int*>(base + off[5]);
+    ws.n_hs = n_hs;
     ws.nc = (args->seq_len + 63) / 64;
     ws.tp_len = ws.nc * 64;
     cudaError_t e = gdn::launch_prefill_prep(p, ws, static_cast<cudaStream_t>(stream));

@@ -149,7 +149,8 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 __global__ void __launch_bounds__(NT, 1)
     prefill_seq_kernel(const MixParams p, const CkptList ck, const PrefillWs ws,
                        const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_v,
-                       const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_out) {
+                       const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_out,
+                       const int split) {
     extern __shared__ unsigned char raw[];
     const uint32_t raw_addr = smem_u32(raw);
     unsigned char* sm = raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -173,41 +174,106 @@ __global__ void __launch_bounds__(NT, 1)
     const bool main_grp = tid < NMAIN;
     const int dv = 32 * q4 + lane;  // this thread's tensor-memory lane
     const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
-    const int bh = blockIdx.x;
-    const int b = bh / p.Hv, h = bh - (bh / p.Hv) * p.Hv;
-    const int rep = p.Hv / p.Hk, kh = h / rep;
-    const int NC = ws.nc;
+    const int NCg = ws.nc;  // chunks of a chain
+    const int chains = p.B * p.Hv;
 
+    if (warp == 0) {
+        umma::tmem_alloc(smem_u32(tslot), T_COLS);
+        umma::tmem_relinquish();
+    }
     if (tid == 0) {
-        for (int i = 0; i < 7; ++i) mbar_init(smem_u32(&bars[i]), 1);
-        mbar_init(bar_o1, 1);
-        mbar_init(bar_ofree, NT - NMAIN);
-        mbar_init(bar_staged, NT - NMAIN);
-        for (int i = 0; i < 4; ++i) n_cp[i] = 0;
-        fence_mbar_init();
         prefetch_tmap(&tm_qk);
         prefetch_tmap(&tm_v);
         prefetch_tmap(&tm_z);
         prefetch_tmap(&tm_out);
     }
-    if (warp == 0) {
-        umma::tmem_alloc(smem_u32(tslot), T_COLS);
-        umma::tmem_relinquish();
-    }
-    write_conv_windows<TA, D, D, NT>(p, ck, b, h, kh, rep);
     if (tid < D) sNW[tid] = Act<TA>::ldg(static_cast<const TA*>(p.normw) + tid);
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
     const uint32_t tmem = *tslot;
 
+    // Split mode (more chains than CTAs): the chains' chunks laid end to end are cut into
+    // gridDim.x equal runs of at least one chain each.  A run holds at most a chain's last
+    // chunks (its tail), whole chains, and a chain's first chunks (its head); the CTA does the
+    // head first and the tail last, so the head of a chain (at the previous CTA's start) is done
+    // long before its tail begins.  The state crosses in hand-off slot k of the workspace
+    // (between CTAs k and k + 1), released by a flag.  Otherwise one CTA takes one chain.
+    long long lo = 0, hi = 0;
+    int first = blockIdx.x, last = blockIdx.x;
+    if (split) {
+        const long long total = (long long)chains * NCg;
+        const long long L = (total + gridDim.x - 1) / gridDim.x;
+        lo = (long long)blockIdx.x * L;
+        hi = lo + L < total ? lo + L : total;
+        first = (int)(lo / NCg);
+        last = (int)((hi - 1) / NCg);
+    }
+    auto piece_of = [&](int j, int& cs, int& ce) {
+        if (!split) {
+            cs = 0;
+            ce = NCg;
+            return;
+        }
+        const long long a0 = (long long)j * NCg;
+        cs = (int)((lo > a0 ? lo : a0) - a0);
+        ce = (int)((hi < a0 + NCg ? hi : a0 + NCg) - a0);
+    };
+    int cs_first, ce_first, cs_last, ce_last;
+    piece_of(first, cs_first, ce_first);
+    piece_of(last, cs_last, ce_last);
+    const bool has_head = split && hi > lo && ce_last < NCg;  // the run ends inside chain `last`
+    const bool has_tail = split && hi > lo && cs_first > 0 && !(has_head && first == last);
+    const int npieces = split ? (hi > lo ? last - first + 1 : 0) : 1;
+    bool cta_failed = false;
+    for (int pi = 0; pi < npieces && !cta_failed; ++pi) {
+    // time order: the head piece, the whole chains, the tail piece
+    int chain = first;
+    if (split) {
+        const int k = pi - (has_head ? 1 : 0);  // index among the other pieces
+        const int n_rest = npieces - (has_head ? 1 : 0);
+        if (has_head && pi == 0) chain = last;
+        else if (has_tail) chain = k < n_rest - 1 ? first + 1 + k : first;
+        else chain = first + k;
+    }
+    int c_base, c_end;
+    piece_of(chain, c_base, c_end);
+    const int NC = c_end - c_base;                              // chunks of this piece
+    const int in_slot = c_base > 0 ? (int)blockIdx.x - 1 : -1;  // state from the hand-off
+    const int out_slot = c_end < NCg ? (int)blockIdx.x : -1;    // state to the hand-off
+    const int bh = chain;
+    const int b = bh / p.Hv, h = bh - (bh / p.Hv) * p.Hv;
+    const int rep = p.Hv / p.Hk, kh = h / rep;
+
+    if (tid == 0) {
+        if (pi > 0)
+            for (int i = 0; i < 10; ++i) mbar_inval(smem_u32(&bars[i]));
+        for (int i = 0; i < 7; ++i) mbar_init(smem_u32(&bars[i]), 1);
+        mbar_init(bar_o1, 1);
+        mbar_init(bar_ofree, NT - NMAIN);
+        mbar_init(bar_staged, NT - NMAIN);
+        for (int i = 0; i < 4; ++i) n_cp[i] = 0;
+        fence_mbar_init();
+    }
+    if (c_base == 0) write_conv_windows<TA, D, D, NT>(p, ck, b, h, kh, rep);
+    bool hand_ok = true;
+    if (in_slot >= 0 && tid == 0) hand_ok = wait_flag_bounded(ws.hflag + in_slot);
+    umma::fence_before_sync();
+    if (__syncthreads_or(!hand_ok)) {
+        cta_failed = true;
+        break;
+    }
+    umma::fence_after_sync();
+
     // initial state, transposed: lane dv, column dk (warpgroup wg: dk 32 wg .. 32 wg + 31);
     // its bf16 hi / lo operand in the same 32 columns of the operand region
     {
         const int c0 = 32 * wg;
+        const float* src = in_slot >= 0 ? ws.hs + (size_t)in_slot * D * D
+                                         : (p.S_in ? p.S_in + (size_t)bh * D * D : nullptr);
         float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = p.S_in ? __ldcs(p.S_in + ((size_t)bh * D + c0 + j) * D + dv) : 0.f;
+        for (int j = 0; j < 32; ++j) v[j] = src ? __ldcg(src + (size_t)(c0 + j) * D + dv) : 0.f;
         umma::tmem_st32(tmem + lane_base + C_MS + c0, v);
         store_split32(tmem + lane_base + C_OP + c0, v);
         umma::tmem_wait_st();
@@ -222,26 +288,27 @@ __global__ void __launch_bounds__(NT, 1)
         mbar_arrive_expect_tx(bar, 4u * 8192u + 1024u);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-            tma_load_3d(dst + 16384u * j, &tm_qk, p.Hk * D + kh * D + 64 * j, cc * C, b, bar);  // k rows
-            tma_load_3d(dst + 16384u * j + 8192u, &tm_qk, kh * D + 64 * j, cc * C, b, bar);     // q rows
+            tma_load_3d(dst + 16384u * j, &tm_qk, p.Hk * D + kh * D + 64 * j, (c_base + cc) * C, b, bar);  // k
+            tma_load_3d(dst + 16384u * j + 8192u, &tm_qk, kh * D + 64 * j, (c_base + cc) * C, b, bar);     // q
         }
         const uint32_t vdst = sb + R_VEC + 1024u * (uint32_t)(cc & 1);
-        bulk_load(vdst, ws.nrm + (((size_t)b * p.Hk + kh) * NC + cc) * 128, 512, bar);
-        bulk_load(vdst + 512, ws.gate + (((size_t)b * p.Hv + h) * NC + cc) * 128, 512, bar);
+        bulk_load(vdst, ws.nrm + (((size_t)b * p.Hk + kh) * NCg + c_base + cc) * 128, 512, bar);
+        bulk_load(vdst + 512, ws.gate + (((size_t)b * p.Hv + h) * NCg + c_base + cc) * 128, 512, bar);
     };
     auto issue_v = [&](int cc) {
         atomicAdd(&n_cp[2], 1);
         mbar_arrive_expect_tx(bar_v, (uint32_t)C * D * 2u);
-        tma_load_3d(sb + R_VS, &tm_v, v_ch, cc * C, b, bar_v);
+        tma_load_3d(sb + R_VS, &tm_v, v_ch, (c_base + cc) * C, b, bar_v);
     };
     auto issue_z = [&](int cc) {
         mbar_arrive_expect_tx(bar_z, (uint32_t)C * D * 2u);
-        tma_load_3d(sb + R_ZS, &tm_z, h * D, cc * C, b, bar_z);
+        tma_load_3d(sb + R_ZS, &tm_z, h * D, (c_base + cc) * C, b, bar_z);
     };
     auto issue_tp = [&](int cc) {
         atomicAdd(&n_cp[3], 1);
         mbar_arrive_expect_tx(bar_tp, 2u * C * C * 4u);
-        bulk_load(sb + R_TP, ws.tp + (((size_t)b * p.Hv + h) * NC + cc) * (2 * C * C), 2u * C * C * 4u, bar_tp);
+        bulk_load(sb + R_TP, ws.tp + (((size_t)b * p.Hv + h) * NCg + c_base + cc) * (2 * C * C), 2u * C * C * 4u,
+                  bar_tp);
     };
     // z copies issued / waited for (output group)
     int n_z = 0, w_z = 0;
@@ -271,7 +338,8 @@ __global__ void __launch_bounds__(NT, 1)
         const uint64_t d_t = umma::desc_kmajor0(sb + R_TP), d_p = umma::desc_kmajor0(sb + R_TP + C * C * 4);
         uint32_t mma_phase = 0;
         bool mma_pending = false;
-        int ck_i = 0;
+        int ck_i = 0;  // first checkpoint past the piece's start (earlier ones belong to the head)
+        while (ck_i < ck.n && ck.off[ck_i] <= c_base * C) ++ck_i;
         // A bounded wait that runs out marks this thread bad; the threads agree on it once per
         // chunk (the closing barrier) and leave together.  Until then a bad thread keeps going
         // on stale data: every address it touches is fixed by the chunk index, never by data.
@@ -296,7 +364,7 @@ __global__ void __launch_bounds__(NT, 1)
                 nb_arrive(1, NMAIN);
         };
         for (int c = 0; c < NC; ++c) {
-            const int t0 = c * C;
+            const int t0 = (c_base + c) * C;
             float* sv = scr + S_V + 384 * (c & 1);
             const uint32_t r_qk = R_QK + QK_BYTES * (uint32_t)(c & 1);
             // ---------------- 2. MMA-b (after the output warps released O of the last chunk) ----------------
@@ -483,6 +551,9 @@ __global__ void __launch_bounds__(NT, 1)
             {
                 const float ec = sv[V_EC];
                 const bool last = c == NC - 1;
+                float* const s_end = !last ? nullptr
+                                     : out_slot >= 0 ? ws.hs + (size_t)out_slot * D * D
+                                                     : (p.S_out ? p.S_out + (size_t)bh * D * D : nullptr);
 #pragma unroll 1
                 for (int c0 = 64 * wg; c0 < 64 * wg + 64; c0 += 32) {
                     float m[32], d[32];
@@ -503,12 +574,13 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
                         for (int j = 0; j < 32; ++j) __stcs(dst + (size_t)(c0 + j) * D + dv, m[j]);
                     }
-                    if (last && p.S_out) {
+                    if (s_end) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) __stcs(p.S_out + ((size_t)bh * D + c0 + j) * D + dv, m[j]);
+                        for (int j = 0; j < 32; ++j) __stcg(s_end + (size_t)(c0 + j) * D + dv, m[j]);
                     }
                 }
                 umma::tmem_wait_st();
+                if (last && out_slot >= 0) __threadfence();  // the hand-off state before its flag
             }
             while (ck_i < ck.n && ck.off[ck_i] - t0 == C) ++ck_i;
             umma::fence_before_sync();
@@ -517,6 +589,7 @@ __global__ void __launch_bounds__(NT, 1)
                 break;
             }
             umma::fence_after_sync();
+            if (c == NC - 1 && out_slot >= 0 && tid == 0) release_flag(ws.hflag + out_slot);  // state written
         }
         if (tid == 0 && failed && mma_pending)  // an MMA in flight finishes (bounded) before the CTA exits
             mbar_wait_bounded(bar_mma, (mma_phase - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
@@ -546,7 +619,7 @@ __global__ void __launch_bounds__(NT, 1)
         stage_vectors(0);
         mbar_arrive(bar_staged);
         for (int c = 0; c < NC && !failed; ++c) {
-            const int t0 = c * C;
+            const int t0 = (c_base + c) * C;
             const float* sv = scr + S_V + 384 * (c & 1);
             bad |= !mbar_wait_bounded(bar_ordy, (uint32_t)c & 1u, GDN_DEVERR_MMA_TIMEOUT);
             umma::fence_after_sync();
@@ -667,14 +740,18 @@ __global__ void __launch_bounds__(NT, 1)
         }
     }
     umma::fence_before_sync();
-    __syncthreads();
+    cta_failed = __syncthreads_or(failed);
     if (tid == 0) {
-        // the last input copy into each region lands before the CTA exits (bounded; every
+        // the last input copy into each region lands before the piece ends (bounded; every
         // earlier copy on the same barrier was seen complete before the next was issued)
         const uint32_t bar_cp[4] = {bar_qk0, bar_qk0 + 8u, bar_v, bar_tp};
         for (int i = 0; i < 4; ++i)
             if (n_cp[i] > 0) mbar_wait_bounded(bar_cp[i], (uint32_t)(n_cp[i] - 1) & 1u, GDN_DEVERR_TMA_TIMEOUT);
     }
+    __syncthreads();
+    }  // pieces
+    umma::fence_before_sync();
+    __syncthreads();
     if (warp == 0) umma::tmem_dealloc(tmem, T_COLS);
 }
 
@@ -703,7 +780,21 @@ cudaError_t launch_prefill_seq(const MixParams& p, const CkptList& ck, const Pre
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
-    pseq::prefill_seq_kernel<<<p.B * p.Hv, pseq::NT, pseq::SMEM_BYTES, s>>>(p, ck, ws, tm_qk, tm_v, tm_z, tm_out);
+    const int chains = p.B * p.Hv;
+    if (ws.n_hs > 1 && chains > ws.n_hs) {
+        // split mode: one CTA per SM, all resident at once (a cooperative launch guarantees it),
+        // the chains cut into equal runs with state hand-offs between neighbouring CTAs
+        e = cudaMemsetAsync(ws.hflag, 0, (size_t)ws.n_hs * sizeof(int), s);
+        if (e != cudaSuccess) return e;
+        int split = 1;
+        void* kargs[] = {const_cast<MixParams*>(&p), const_cast<CkptList*>(&ck), const_cast<PrefillWs*>(&ws),
+                         &tm_qk, &tm_v, &tm_z, &tm_out, &split};
+        e = cudaLaunchCooperativeKernel((const void*)pseq::prefill_seq_kernel, dim3(ws.n_hs), dim3(pseq::NT), kargs,
+                                        pseq::SMEM_BYTES, s);
+        if (e == cudaSuccess) return cudaSuccess;
+        (void)cudaGetLastError();  // not launchable as one resident wave here: one CTA per chain
+    }
+    pseq::prefill_seq_kernel<<<chains, pseq::NT, pseq::SMEM_BYTES, s>>>(p, ck, ws, tm_qk, tm_v, tm_z, tm_out, 0);
     return cudaGetLastError();
 }
 
