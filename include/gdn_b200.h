@@ -213,6 +213,18 @@ int32_t gdn_device_error(uint32_t* flags_out, int32_t clear);
 int32_t gdn_selftest_umma(int32_t mode, const float* A, const float* B, float* D, void* stream);
 
 /*
+ * Failure-detection self-test: one thread runs one of the kernels' bounded
+ * waits on something that never arrives, so that the wait gives up after
+ * its limit (1 s) and the kernel returns.  kind 0 waits on an mbarrier with
+ * no arrival (sets GDN_DEVERR_TMA_TIMEOUT); kind 1 waits on the device int
+ * flag[0] (the chunked prefill's state hand-off wait; sets
+ * GDN_DEVERR_HANDOFF_TIMEOUT unless flag[0] is already non-zero).  flag[1]
+ * receives 1 when the wait succeeded and 2 when it gave up; the context
+ * stays usable.  No counterpart in the reference.
+ */
+int32_t gdn_selftest_expired_wait(int32_t kind, int32_t* flag, void* stream);
+
+/*
  * Chunked token mixer for any seq_len >= 1 (prefill).  Replaces
  * deltanet.py:479-561 on the _chunk_gated_delta_rule branch
  * (deltanet.py:266-407): the WY/UT intra-chunk solve and the sequential

@@ -36,10 +36,13 @@ EXPORTED_SYMBOLS = (
     "gdn_accept_slots",
     "gdn_device_error",
     "gdn_selftest_umma",
+    "gdn_selftest_expired_wait",
 )
 GDN_FLAG_REGISTER_KERNEL = 1
 GDN_FLAG_CUDA_CORE_PREFILL = 2
+GDN_DEVERR_TMA_TIMEOUT = 0x1
 GDN_DEVERR_BAD_SLOT = 0x4
+GDN_DEVERR_HANDOFF_TIMEOUT = 0x8
 GDN_STATIC_SCRATCH_BYTES = 64 << 20
 
 _c_void_p = ctypes.c_void_p
@@ -112,6 +115,8 @@ def load() -> ctypes.CDLL:
                                           _c_void_p, _c_void_p, _i32, _c_void_p]
         lib.gdn_selftest_umma.restype = _i32
         lib.gdn_selftest_umma.argtypes = [_i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p]
+        lib.gdn_selftest_expired_wait.restype = _i32
+        lib.gdn_selftest_expired_wait.argtypes = [_i32, _c_void_p, _c_void_p]
         lib.gdn_prefill_workspace_bytes.restype = _i64
         lib.gdn_prefill_workspace_bytes.argtypes = [ctypes.POINTER(MixerArgs)]
         lib.gdn_mixer_prefill_ws.restype = _i32

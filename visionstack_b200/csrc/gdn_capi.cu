@@ -300,6 +300,14 @@ int32_t gdn_mixer_prefill_ws(const gdn_mixer_args* args, void* workspace, int64_
     return cuda_status(e, "gdn_mixer_prefill_ws sequential launch");
 }
 
+int32_t gdn_selftest_expired_wait(int32_t kind, int32_t* flag, void* stream) {
+    if (kind < 0 || kind > 1) return fail(GDN_ERR_INVALID_ARG, "kind %d not in 0..1", kind);
+    if (!flag) return fail(GDN_ERR_INVALID_ARG, "flag is NULL");
+    if (reinterpret_cast<uintptr_t>(flag) % 4) return fail(GDN_ERR_ALIGNMENT, "misaligned flag");
+    return cuda_status(gdn::launch_expired_wait_selftest(kind, flag, static_cast<cudaStream_t>(stream)),
+                       "gdn_selftest_expired_wait launch");
+}
+
 int32_t gdn_selftest_umma(int32_t mode, const float* A, const float* B, float* D, void* stream) {
     if (mode < 0 || mode > 8) return fail(GDN_ERR_INVALID_ARG, "mode %d not in 0..8", mode);
     if (!A || !B || !D) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");

@@ -67,6 +67,7 @@ cudaError_t launch_accept_slots(const int* accepted, int* table, int B, int n_sl
 unsigned int slots_device_error(bool clear);
 cudaError_t launch_umma_selftest(int mode, const float* A, const float* B, float* D, cudaStream_t s);
 unsigned int umma_device_error(bool clear);
+cudaError_t launch_expired_wait_selftest(int kind, int* flag, cudaStream_t s);
 cudaError_t launch_prefill_tc(const MixParams& p, const CkptList& ck, int d, int dtype, cudaStream_t s,
                               bool* supported);
 unsigned int prefill_tc_device_error(bool clear);

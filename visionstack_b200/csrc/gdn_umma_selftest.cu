@@ -169,7 +169,32 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const f
     if (warp == 0) umma::tmem_dealloc(tbase, 256);
 }
 
+// One thread runs one of the kernels' bounded waits on something that never arrives:
+// kind 0 an mbarrier with no arrival (GDN_DEVERR_TMA_TIMEOUT after the limit), kind 1 the
+// global flag flag[0] (GDN_DEVERR_HANDOFF_TIMEOUT unless flag[0] is already non-zero).
+// flag[1] receives 1 when the wait succeeded, 2 when it gave up.
+__global__ void __launch_bounds__(32, 1) expired_wait_kernel(int kind, int* flag) {
+    __shared__ alignas(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    bool ok;
+    if (kind == 0) {
+        const uint32_t b = smem_u32(&bar);
+        mbar_init(b, 1);
+        fence_mbar_init();
+        ok = mbar_wait_bounded(b, 0, GDN_DEVERR_TMA_TIMEOUT);
+        mbar_inval(b);
+    } else {
+        ok = wait_flag_bounded(flag);
+    }
+    flag[1] = ok ? 1 : 2;
+}
+
 }  // namespace
+
+cudaError_t launch_expired_wait_selftest(int kind, int* flag, cudaStream_t s) {
+    expired_wait_kernel<<<1, 32, 0, s>>>(kind, flag);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_umma_selftest(int mode, const float* A, const float* B, float* D, cudaStream_t s) {
     const int bytes = 2 * 128 * 128 * 4 + 64 + 1024;
