@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--prefill-batch", type=int, default=8)
     ap.add_argument("--prefill-seq", type=int, default=8192)
     ap.add_argument("--no-rollback", action="store_true", help="skip the secondary rollback measurement")
+    ap.add_argument("--stack", action="store_true",
+                    help="also time the 48-layer hybrid stack (B32: prefill 4096, decode 256; 1 GPU)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-s", type=float, default=12.0, help="seconds of CPU work for the CPU baseline")
     return ap.parse_args()
@@ -463,6 +465,13 @@ def run_ours(args, rank: int, world: int) -> None:
     if not args.no_rollback:
         rollback = run_rollback(torch, dist, m, local, dev, world, barrier)
 
+    stack = None
+    if args.stack and world == 1:
+        try:
+            stack = run_stack(torch, dev)
+        except Exception as e:  # the stack is a secondary measurement: never lose the line to it
+            stack = {"error": f"{type(e).__name__}: {e}"[:300]}
+
     if rank != 0:
         return
     hbm, tflops, src = measured_peaks()
@@ -488,6 +497,8 @@ def run_ours(args, rank: int, world: int) -> None:
         line["prefill"] = prefill
     if rollback is not None:
         line["rollback"] = rollback
+    if stack is not None:
+        line["stack"] = stack
     if world == 1 and not args.no_cpu_baseline:
         rate, n, el = cpu_decode_rate(args.cpu_sample_s)
         line["cpu_baseline"] = {"value": rate, "unit": "steps/s", "cores": cpu_cores(), "kind": "port",
@@ -534,6 +545,91 @@ def run_prefill(torch, dist, m, local, dev, world, barrier, B=8, T=8192):
                          "frac": ach / tflops, "peak_source": src, "flops_per_launch": fl,
                          "min_bytes_per_launch": prefill_min_bytes(B, T, hk, hv, d),
                          "kernel": "gdn::pseq::prefill_seq_kernel (tcgen05 bf16 hi+lo and tf32, state in tensor memory, 1 CTA per (batch, head)) after gdn::pprep::prefill_prep_kernel"}}
+
+
+def run_stack(torch, dev):
+    """The 48-layer hybrid stack (36 Gated DeltaNet layers on the CUDA token mixer, 12 gated
+    attention layers and all MLPs on library kernels), random bf16 weights, B32: a 4096-token
+    prefill into a hybrid cache, then 256 decode steps of random token ids.  Eager PyTorch around
+    the mixer (no CUDA graph); the KV cache is preallocated."""
+    from visionstack_b200 import Qwen3_5HybridCache, Qwen3_5TextConfig
+    from visionstack_b200.stack import Qwen3_5TextModel
+    cfg = Qwen3_5TextConfig(**W.STACK_48)
+    R = W.STACK_48_RUN
+    B, P, D = R["batch"], R["prefill"], R["decode"]
+    with torch.device("meta"):
+        model = Qwen3_5TextModel(cfg)
+    model = model.to_empty(device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(R["seed"])
+    bf = torch.bfloat16
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if name.endswith("A_log"):
+                p.data = torch.empty(p.shape, device=dev).uniform_(-1.0, 1.0, generator=g)
+            elif name.endswith("dt_bias"):
+                p.data = torch.zeros(p.shape, device=dev)
+            elif name.endswith("linear_attn.norm.weight"):
+                p.data = torch.ones(p.shape, device=dev, dtype=bf)
+            elif name.endswith("norm.weight") or name.endswith("layernorm.weight"):
+                p.data = torch.zeros(p.shape, device=dev, dtype=bf)
+            else:
+                t = torch.randn(p.shape, generator=g, device=dev, dtype=bf)
+                if p.dim() == 2 and not name.endswith("embed_tokens.weight"):
+                    t.mul_(p.shape[1] ** -0.5)
+                elif name.endswith("conv1d.weight"):
+                    t.mul_(0.5)
+                p.data = t
+    ids = torch.randint(0, cfg.vocab_size, (B, P + D), generator=g, device=dev)
+
+    def run(n_pre, n_dec):
+        cache = Qwen3_5HybridCache()
+        cache.kv_capacity = n_pre + n_dec
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        torch.cuda.synchronize(dev)
+        ev[0].record()
+        model(input_ids=ids[:, :n_pre], past_key_values=cache, use_cache=True)
+        ev[1].record()
+        for i in range(n_dec):
+            model(input_ids=ids[:, n_pre + i:n_pre + i + 1], past_key_values=cache, use_cache=True)
+        ev[2].record()
+        torch.cuda.synchronize(dev)
+        return ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+
+    with torch.inference_mode():
+        run(256, 4)
+        run(P, 8)
+        t_pre, t_dec = run(P, D)
+    peak_mem = torch.cuda.max_memory_allocated(dev)
+    nl = sum(1 for t in cfg.layer_types if t == "linear_attention")
+    na = cfg.num_hidden_layers - nl
+    params = sum(p.numel() for n, p in model.named_parameters() if not n.endswith("embed_tokens.weight"))
+    wbytes = sum(p.numel() * p.element_size() for n, p in model.named_parameters()
+                 if not n.endswith("embed_tokens.weight"))
+    hv, dk = cfg.linear_num_value_heads, cfg.linear_key_head_dim
+    conv_dim = 2 * cfg.linear_num_key_heads * dk + hv * cfg.linear_value_head_dim
+    state_rw = nl * (2 * B * hv * dk * dk * 4 + 2 * B * conv_dim * 3 * 2)
+    kv_read = na * B * 2 * (P + D // 2) * cfg.num_key_value_heads * cfg.head_dim * 2
+    dec_bytes = wbytes + state_rw + kv_read
+    ms_dec = t_dec / D
+    hbm, tflops, src = measured_peaks()
+    attn_fl = na * B * cfg.num_attention_heads * (P * P / 2) * cfg.head_dim * 4
+    pre_fl = 2.0 * params * B * P + attn_fl + nl * prefill_flops(B, P, hv, dk)
+    del model
+    torch.cuda.empty_cache()
+    return {"workload": f"48-layer hybrid stack (36 Gated DeltaNet + 12 gated attention, hidden 2048, MLP 12288, "
+                        f"vocab 151936), random bf16 weights, B{B}: prefill {P} tokens then {D} decode steps",
+            "prefill_tokens_per_s": B * P / (t_pre * 1e-3), "prefill_ms": t_pre,
+            "decode_steps_per_s": 1000.0 / ms_dec, "decode_tokens_per_s": B * 1000.0 / ms_dec,
+            "decode_ms_per_step": ms_dec, "peak_memory_gb": peak_mem / 1e9,
+            "prefill_roofline": {"bound": "tensor", "achieved": pre_fl / (t_pre * 1e-3) / 1e12, "peak": tflops,
+                                 "unit": "TFLOP/s", "frac": pre_fl / (t_pre * 1e-3) / 1e12 / tflops,
+                                 "flops": pre_fl, "peak_source": src},
+            "decode_roofline": {"bound": "hbm", "achieved": dec_bytes / (ms_dec * 1e-3) / 1e9, "peak": hbm,
+                                "unit": "GB/s", "frac": dec_bytes / (ms_dec * 1e-3) / 1e9 / hbm,
+                                "bytes_per_step": dec_bytes, "peak_source": src},
+            "path": "visionstack_b200.stack.Qwen3_5TextModel, eager; DeltaNet layers on gdn_mixer_prefill_ws / "
+                    "gdn_mixer_decode, attention on torch SDPA, GEMMs on cuBLAS"}
 
 
 def run_rollback(torch, dist, m, local, dev, world, barrier, steps=1024):

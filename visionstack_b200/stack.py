@@ -1,0 +1,297 @@
+"""The hybrid decoder stack around the token mixer: a harness for the 48-layer workload.
+
+Mirrors ShadowBoxer/models/qwen35/text.py (class names, parameter names, forward contracts and
+cache side effects) so a reference state dict loads unchanged: every `linear_attention` layer is
+this package's `Qwen3_5GatedDeltaNet` (the CUDA token mixer); the full-attention layers, the MLPs
+and the norms are plain PyTorch with library kernels (cuBLAS GEMMs, SDPA attention).
+
+One change of mechanism, not of result: the reference appends every step's keys and values to the
+cache with `torch.cat` (text.py:170-178), copying the whole history per step.  Given a
+`kv_capacity` on the cache, `Qwen3_5Attention` writes them into a per-layer buffer of that
+capacity instead and stores views of the filled part under the same dict keys, so the cached
+tensors hold the same values.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from .cache import Qwen3_5HybridCache
+from .config import Qwen3_5TextConfig, _linear
+from .deltanet import Qwen3_5GatedDeltaNet
+
+
+class Qwen3_5RMSNorm(nn.Module):
+    """RMSNorm with a zero-centred weight, x / rms(x) * (1 + w), in fp32 (config.py:118-127)."""
+
+    def __init__(self, dim: int, eps: float = 1e-6):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.zeros(dim))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        inv = torch.rsqrt(xf.square().mean(-1, keepdim=True) + self.eps)
+        return (xf * inv * (1.0 + self.weight.float())).to(x.dtype)
+
+
+def _act(x: torch.Tensor, name: str) -> torch.Tensor:
+    """The MLP activation by config name (config.py:99-106; unknown names fall back to SiLU)."""
+    if name == "gelu_pytorch_tanh":
+        return F.gelu(x, approximate="tanh")
+    if name == "gelu":
+        return F.gelu(x)
+    return F.silu(x)
+
+
+def _rotate_half(x: torch.Tensor) -> torch.Tensor:
+    h = x.shape[-1] // 2
+    return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
+
+
+class Qwen3_5TextRotaryEmbedding(nn.Module):
+    """Partial multimodal rotary embedding (text.py:25-73).
+
+    `rotary = head_dim * partial_rotary_factor` channels rotate with inverse frequencies
+    base^(-2i/rotary).  Positions come as [3, B, T] (temporal, height, width); frequency i takes
+    the height position when i = 1 (mod 3) and i < 3 * mrope_section[1], the width position when
+    i = 2 (mod 3) and i < 3 * mrope_section[2], the temporal position otherwise.  For text all
+    three are equal.  cos / sin are [B, T, rotary] in the activation dtype.
+    """
+
+    def __init__(self, config: Qwen3_5TextConfig):
+        super().__init__()
+        rp = config.rope_parameters or {}
+        self.base = float(rp.get("rope_theta", 10000000.0))
+        head_dim = getattr(config, "head_dim", config.hidden_size // config.num_attention_heads)
+        self.dim = int(head_dim * float(rp.get("partial_rotary_factor", 0.25)))
+        self.mrope_section = list(rp.get("mrope_section", [11, 11, 10]))
+        self._inv: Dict[torch.device, torch.Tensor] = {}
+
+    def inv_freq(self, device: torch.device) -> torch.Tensor:
+        t = self._inv.get(device)
+        if t is None:  # computed on the host, then moved (as text.py:41-48 does)
+            ex = torch.arange(0, self.dim, 2, dtype=torch.float32) / self.dim
+            t = (1.0 / (self.base ** ex)).to(device)
+            self._inv[device] = t
+        return t
+
+    def _select(self, f: torch.Tensor) -> torch.Tensor:
+        # f [3, B, T, dim/2] -> [B, T, dim/2] with the sections' interleaved picks
+        out = f[0].clone()
+        n = f.shape[-1]
+        for axis in (1, 2):
+            idx = torch.arange(axis, min(n, 3 * self.mrope_section[axis]), 3, device=f.device)
+            out[..., idx] = f[axis][..., idx]
+        return torch.cat((out, out), dim=-1)
+
+    @torch.no_grad()
+    def forward(self, x: torch.Tensor, position_ids: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        pos = position_ids.expand(3, -1, -1).float()
+        f = pos[..., None] * self.inv_freq(x.device)
+        return self._select(f.cos()).to(x.dtype), self._select(f.sin()).to(x.dtype)
+
+
+def _apply_rotary_pos_emb_partial(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor,
+                                  sin: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Rotate the first `rotary` channels of q and k ([B, H, T, hd]); the rest pass (text.py:76-86)."""
+    c, s = cos.unsqueeze(1), sin.unsqueeze(1)
+    r = c.shape[-1]
+
+    def rot(x: torch.Tensor) -> torch.Tensor:
+        xr = x[..., :r]
+        return torch.cat([xr * c + _rotate_half(xr) * s, x[..., r:]], dim=-1)
+
+    return rot(q), rot(k)
+
+
+class Qwen3_5Attention(nn.Module):
+    """Gated grouped-query attention (text.py:89-212): q_proj yields a query and a gate per head;
+    q / k RMS-normalised per head, partial rotary, SDPA, output times sigmoid(gate), o_proj."""
+
+    def __init__(self, config: Qwen3_5TextConfig, layer_idx: int):
+        super().__init__()
+        self.layer_idx = layer_idx
+        self.head_dim = getattr(config, "head_dim", config.hidden_size // config.num_attention_heads)
+        self.num_heads = config.num_attention_heads
+        self.num_kv_heads = config.num_key_value_heads
+        self.num_key_value_groups = self.num_heads // self.num_kv_heads
+        self.scaling = self.head_dim ** -0.5
+        hd, bias = self.head_dim, config.attention_bias
+        self.q_proj = nn.Linear(config.hidden_size, self.num_heads * hd * 2, bias=bias)
+        self.k_proj = nn.Linear(config.hidden_size, self.num_kv_heads * hd, bias=bias)
+        self.v_proj = nn.Linear(config.hidden_size, self.num_kv_heads * hd, bias=bias)
+        self.o_proj = nn.Linear(self.num_heads * hd, config.hidden_size, bias=bias)
+        self.q_norm = Qwen3_5RMSNorm(hd, eps=config.rms_norm_eps)
+        self.k_norm = Qwen3_5RMSNorm(hd, eps=config.rms_norm_eps)
+
+    def _store_kv(self, cache: Qwen3_5HybridCache, k: torch.Tensor, v: torch.Tensor):
+        """Append k, v ([B, kvh, T, hd]) to this layer's cache entry; returns the full history."""
+        l = self.layer_idx
+        pk, pv = cache.key_cache.get(l), cache.value_cache.get(l)
+        has_past = pk is not None and pv is not None
+        cap = int(getattr(cache, "kv_capacity", 0) or 0)
+        if cap:
+            bufs = cache.__dict__.setdefault("_kv_buffers", {})
+            prev = pk.shape[2] if has_past else 0
+            need = prev + k.shape[2]
+            buf = bufs.get(l)
+            ours = buf is not None and has_past and pk.data_ptr() == buf[0].data_ptr() and \
+                pv.data_ptr() == buf[1].data_ptr()
+            if buf is None or not (ours or not has_past) or buf[0].shape[2] < need or \
+                    buf[0].shape[:2] != k.shape[:2] or buf[0].dtype != k.dtype:
+                size = max(cap, need)
+                buf = (k.new_empty(k.shape[0], k.shape[1], size, k.shape[3]),
+                       v.new_empty(v.shape[0], v.shape[1], size, v.shape[3]))
+                if has_past:
+                    buf[0][:, :, :prev].copy_(pk)
+                    buf[1][:, :, :prev].copy_(pv)
+                bufs[l] = buf
+            buf[0][:, :, prev:need].copy_(k)
+            buf[1][:, :, prev:need].copy_(v)
+            k, v = buf[0][:, :, :need], buf[1][:, :, :need]
+        elif has_past:
+            k, v = torch.cat([pk, k], dim=2), torch.cat([pv, v], dim=2)
+        cache.key_cache[l] = k
+        cache.value_cache[l] = v
+        return k, v, has_past
+
+    def forward(self, hidden_states: torch.Tensor, position_embeddings: Tuple[torch.Tensor, torch.Tensor],
+                attention_mask: Optional[torch.Tensor] = None,
+                cache: Optional[Qwen3_5HybridCache] = None) -> torch.Tensor:
+        B, T = hidden_states.shape[:2]
+        hd = self.head_dim
+        qg = _linear(self.q_proj, hidden_states).view(B, T, self.num_heads, 2 * hd)
+        q, gate = qg[..., :hd], qg[..., hd:].reshape(B, T, self.num_heads * hd)
+        q = self.q_norm(q).transpose(1, 2)
+        k = self.k_norm(_linear(self.k_proj, hidden_states).view(B, T, self.num_kv_heads, hd)).transpose(1, 2)
+        v = _linear(self.v_proj, hidden_states).view(B, T, self.num_kv_heads, hd).transpose(1, 2)
+        q, k = _apply_rotary_pos_emb_partial(q, k, *position_embeddings)
+        has_past = False
+        if cache is not None:
+            k, v, has_past = self._store_kv(cache, k, v)
+        gqa = self.num_key_value_groups > 1
+        kv_len = k.shape[2]
+        if attention_mask is not None and attention_mask.ndim == 4:
+            o = F.scaled_dot_product_attention(q, k, v, attn_mask=attention_mask, is_causal=False,
+                                               scale=self.scaling, enable_gqa=gqa)
+        elif has_past and T > 1:
+            causal = torch.ones((T, kv_len), dtype=torch.bool, device=q.device).tril(diagonal=kv_len - T)
+            o = F.scaled_dot_product_attention(q, k, v, attn_mask=causal[None, None], is_causal=False,
+                                               scale=self.scaling, enable_gqa=gqa)
+        else:
+            o = F.scaled_dot_product_attention(q, k, v, is_causal=(T > 1 and not has_past), scale=self.scaling,
+                                               enable_gqa=gqa)
+        o = o.transpose(1, 2).reshape(B, T, -1).contiguous() * torch.sigmoid(gate)
+        return _linear(self.o_proj, o)
+
+
+class Qwen3_5MLP(nn.Module):
+    """Gated MLP down(act(gate(x)) * up(x)) (text.py:215-230)."""
+
+    def __init__(self, config: Qwen3_5TextConfig, intermediate_size: int):
+        super().__init__()
+        self.gate_proj = nn.Linear(config.hidden_size, intermediate_size, bias=False)
+        self.up_proj = nn.Linear(config.hidden_size, intermediate_size, bias=False)
+        self.down_proj = nn.Linear(intermediate_size, config.hidden_size, bias=False)
+        self.act_name = config.hidden_act
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return _linear(self.down_proj, _act(_linear(self.gate_proj, x), self.act_name) * _linear(self.up_proj, x))
+
+
+class Qwen3_5DecoderLayer(nn.Module):
+    """Pre-norm residual block: token mixer (DeltaNet or attention by `layer_types`), then the MLP
+    (text.py:233-276)."""
+
+    def __init__(self, config: Qwen3_5TextConfig, layer_idx: int):
+        super().__init__()
+        self.block_type = config.layer_types[layer_idx]
+        if self.block_type == "linear_attention":
+            self.linear_attn = Qwen3_5GatedDeltaNet(config, layer_idx)
+        elif self.block_type == "full_attention":
+            self.self_attn = Qwen3_5Attention(config, layer_idx)
+        self.mlp = Qwen3_5MLP(config, config.intermediate_size)
+        self.input_layernorm = Qwen3_5RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self.post_attention_layernorm = Qwen3_5RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+
+    def forward(self, hidden_states: torch.Tensor, position_embeddings: Tuple[torch.Tensor, torch.Tensor],
+                linear_mask: Optional[torch.Tensor] = None, full_attn_mask: Optional[torch.Tensor] = None,
+                cache: Optional[Qwen3_5HybridCache] = None) -> torch.Tensor:
+        h = self.input_layernorm(hidden_states)
+        if self.block_type == "linear_attention":
+            h = self.linear_attn(h, attention_mask=linear_mask, cache=cache)
+        else:
+            h = self.self_attn(h, position_embeddings=position_embeddings, attention_mask=full_attn_mask, cache=cache)
+        hidden_states = hidden_states + h
+        return hidden_states + self.mlp(self.post_attention_layernorm(hidden_states))
+
+
+@dataclass
+class Qwen3_5ModelOutput:
+    """Output record with the reference's field names (config.py:146-151)."""
+    last_hidden_state: torch.Tensor
+    pooler_output: Optional[torch.Tensor] = None
+    rope_deltas: Optional[torch.Tensor] = None
+    past_key_values: Optional[Qwen3_5HybridCache] = None
+
+
+class Qwen3_5TextModel(nn.Module):
+    """Embedding, decoder layers, final norm (text.py:341-456), with the same position, mask and
+    cache handling."""
+
+    def __init__(self, config: Qwen3_5TextConfig):
+        super().__init__()
+        self.config = config
+        pad = config.pad_token_id
+        pad_idx = int(pad) if pad is not None and 0 <= int(pad) < int(config.vocab_size) else None
+        self.embed_tokens = nn.Embedding(config.vocab_size, config.hidden_size, pad_idx)
+        self.layers = nn.ModuleList([Qwen3_5DecoderLayer(config, i) for i in range(config.num_hidden_layers)])
+        self.norm = Qwen3_5RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self.rotary_emb = Qwen3_5TextRotaryEmbedding(config)
+
+    def forward(self, input_ids: Optional[torch.LongTensor] = None, attention_mask: Optional[torch.Tensor] = None,
+                position_ids: Optional[torch.LongTensor] = None, inputs_embeds: Optional[torch.Tensor] = None,
+                past_key_values: Optional[Qwen3_5HybridCache] = None, use_cache: bool = False,
+                **kwargs) -> Qwen3_5ModelOutput:
+        if (input_ids is None) ^ (inputs_embeds is not None):
+            raise ValueError("Specify exactly one of input_ids or inputs_embeds.")
+        if inputs_embeds is None:
+            inputs_embeds = self.embed_tokens(input_ids)
+        cache = past_key_values if past_key_values is not None else (Qwen3_5HybridCache() if use_cache else None)
+        past = cache.past_seen_tokens if cache is not None else 0
+        B, T, _ = inputs_embeds.shape
+        dev = inputs_embeds.device
+        if cache is not None and cache.record_checkpoints:
+            cache.resolve_active_checkpoints(past, T)
+
+        if position_ids is None:
+            pos = torch.arange(past, past + T, device=dev).view(1, 1, -1)
+            if cache is not None and cache.rope_deltas is not None and past > 0:
+                pos = pos + cache.rope_deltas.to(device=dev).unsqueeze(0)
+            position_ids = pos.expand(3, B, -1)
+        elif position_ids.ndim == 2:
+            position_ids = position_ids[None].expand(3, B, -1)
+        elif position_ids.ndim == 3 and position_ids.shape[0] == 4:
+            position_ids = position_ids[1:]
+
+        linear_mask = full_mask = None
+        if attention_mask is not None and attention_mask.ndim == 2 and not attention_mask.bool().all():
+            linear_mask = attention_mask[:, -T:].bool()
+            total = past + T
+            causal = torch.ones((T, total), dtype=torch.bool, device=dev).tril(diagonal=past)
+            m2 = attention_mask.bool()
+            m2 = m2[:, :total] if m2.shape[1] >= total else F.pad(m2, (total - m2.shape[1], 0), value=True)
+            full_mask = causal[None, None] & m2[:, None, None, :]
+
+        h = inputs_embeds
+        pe = self.rotary_emb(h, position_ids)
+        for layer in self.layers:
+            h = layer(h, position_embeddings=pe, linear_mask=linear_mask, full_attn_mask=full_mask, cache=cache)
+        if cache is not None:
+            cache.past_seen_tokens = past + T
+        return Qwen3_5ModelOutput(last_hidden_state=self.norm(h), past_key_values=cache)

@@ -157,3 +157,72 @@ def make_gate_inputs(rng: np.random.Generator, B: int, T: int, H: int):
 
 def with_batch(wl: Workload, batch: int) -> Workload:
     return replace(wl, batch=batch)
+
+
+# ---------------------------------------------------------------------------
+# The hybrid decoder stack (ShadowBoxer/models/qwen35/text.py): every 4th layer
+# full attention, the rest Gated DeltaNet.
+# ---------------------------------------------------------------------------
+
+# The 48-layer workload: hidden 2048, 16 query / 2 KV heads of 256, the DeltaNet heads of the
+# decode / prefill workloads, vocab 151936; the MLP width is the reference config's default
+# (12288), as the workload leaves it open.  B32, prefill 4096 tokens then 256 decode steps.
+STACK_48 = dict(vocab_size=151936, hidden_size=2048, intermediate_size=12288, num_hidden_layers=48,
+                num_attention_heads=16, num_key_value_heads=2, head_dim=256, linear_num_key_heads=16,
+                linear_num_value_heads=32, linear_key_head_dim=128, linear_value_head_dim=128,
+                linear_conv_kernel_dim=4, rms_norm_eps=1e-6)
+STACK_48_RUN = dict(batch=32, prefill=4096, decode=256, seed=4)
+
+# A 4-layer stack (3 DeltaNet + 1 attention) small enough for the reference on the host.
+STACK_TINY = dict(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=4,
+                  num_attention_heads=4, num_key_value_heads=2, head_dim=64, linear_num_key_heads=2,
+                  linear_num_value_heads=4, linear_key_head_dim=64, linear_value_head_dim=64,
+                  linear_conv_kernel_dim=4, rms_norm_eps=1e-6)
+
+
+def make_stack_params(shapes: Dict[str, tuple], seed: int, dtype: str) -> Dict[str, np.ndarray]:
+    """Seeded arrays for every entry of a stack's state dict, given its names and shapes.
+
+    Each tensor draws from its own generator keyed by (seed, crc32 of its name), so the values do
+    not depend on the order a model lists its parameters in.  Linear weights ~ N(0, 1/fan_in),
+    embeddings ~ N(0, 1), zero-centred RMSNorm weights ~ N(0, 0.1^2), the gated norm's weight
+    1 + N(0, 0.1^2), conv weights xavier-uniform, ``A_log`` ~ U(-1, 1) and ``dt_bias`` ~
+    N(0, 0.1^2) (these two stay float32, as the reference loader keeps them).
+    """
+    import zlib
+    out: Dict[str, np.ndarray] = {}
+    for name in sorted(shapes):
+        shp = tuple(int(s) for s in shapes[name])
+        rng = np.random.default_rng([int(seed), zlib.crc32(name.encode())])
+        if name.endswith("A_log"):
+            out[name] = rng.uniform(-1.0, 1.0, size=shp).astype(np.float32)
+            continue
+        if name.endswith("dt_bias"):
+            out[name] = (0.1 * rng.standard_normal(shp)).astype(np.float32)
+            continue
+        if name.endswith("linear_attn.norm.weight"):
+            v = 1.0 + 0.1 * rng.standard_normal(shp)
+        elif name.endswith("norm.weight") or name.endswith("layernorm.weight"):
+            v = 0.1 * rng.standard_normal(shp)
+        elif name.endswith("conv1d.weight"):
+            v = _xavier(rng, shp, shp[2], shp[0] * shp[2])
+        elif name.endswith("embed_tokens.weight"):
+            v = rng.standard_normal(shp)
+        elif len(shp) == 2:
+            v = rng.standard_normal(shp) / np.sqrt(shp[1])
+        else:
+            v = 0.02 * rng.standard_normal(shp)
+        out[name] = cast(np.asarray(v, dtype=np.float32), dtype)
+    return out
+
+
+def make_stack_calls(cfg: Dict, seed: int = 4):
+    """Token ids and the call sequence of the small stack fixture: a 70-token prefill with a
+    cache, three 1-token decode steps, one 4-token step, and separately a 40-token call without a
+    cache under a 2-D attention mask with a hole (row 1, positions 10..12)."""
+    rng = np.random.default_rng(seed)
+    ids = rng.integers(0, cfg["vocab_size"], size=(2, 77), dtype=np.int64)
+    spans = [(0, 70), (70, 71), (71, 72), (72, 73), (73, 77)]
+    mask = np.ones((2, 40), dtype=np.int64)
+    mask[1, 10:13] = 0
+    return ids, spans, mask
