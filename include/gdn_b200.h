@@ -225,6 +225,25 @@ int32_t gdn_selftest_umma(int32_t mode, const float* A, const float* B, float* D
 int32_t gdn_selftest_expired_wait(int32_t kind, int32_t* flag, void* stream);
 
 /*
+ * Decode attention of the hybrid stack's full-attention layers: one query
+ * token per row against a fixed-capacity KV buffer, grouped-query
+ * (text.py:160-212 with q_len 1; SDPA with enable_gqa).  q and out are
+ * [batch][kv_heads * groups][head_dim] bf16 (query head h reads KV head
+ * h / groups); k_cache and v_cache are [batch][kv_heads][capacity][head_dim]
+ * bf16; keys 0..*pos attend (pos is read on the device, so a captured launch
+ * serves every step; *pos >= capacity is clamped to the buffer).
+ * out = softmax(scale q K^T) V in fp32, rounded to bf16.  groups in
+ * {1, 2, 4, 8}, head_dim in {64, 128, 256}; pointers 16-byte aligned;
+ * workspace of gdn_attn_decode_workspace_bytes (scratch).  No counterpart in
+ * the reference's C code (the reference calls torch SDPA).
+ */
+int64_t gdn_attn_decode_workspace_bytes(int32_t batch, int32_t kv_heads, int32_t groups, int32_t head_dim,
+                                        int32_t capacity);
+int32_t gdn_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, void* out,
+                        int32_t batch, int32_t kv_heads, int32_t groups, int32_t head_dim, int32_t capacity,
+                        float scale, void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * Chunked token mixer for any seq_len >= 1 (prefill).  Replaces
  * deltanet.py:479-561 on the _chunk_gated_delta_rule branch
  * (deltanet.py:266-407): the WY/UT intra-chunk solve and the sequential

@@ -159,3 +159,17 @@ def test_layer_refuses_cpu_tensors():
                                                linear_key_head_dim=32, linear_value_head_dim=32), 0)
     with pytest.raises(RuntimeError, match="CUDA"):
         m(torch.zeros(1, 3, 64))
+
+
+def test_attn_decode_validation():
+    lib = _lib.load()
+    assert lib.gdn_attn_decode_workspace_bytes(32, 2, 8, 256, 4352) > 0
+    assert lib.gdn_attn_decode_workspace_bytes(32, 2, 3, 256, 4352) == -1  # groups not in {1, 2, 4, 8}
+    assert lib.gdn_attn_decode_workspace_bytes(32, 2, 8, 96, 4352) == -1   # head_dim
+    n = lib.gdn_attn_decode_workspace_bytes(2, 2, 8, 256, 64)
+    p = 0x100000
+    # NULL pointer, misaligned pointer, short workspace: rejected on the host, nothing launches
+    assert lib.gdn_attn_decode(0, p, p, p, p, 2, 2, 8, 256, 64, 0.0625, p, n, None) == -1
+    assert lib.gdn_attn_decode(p + 2, p, p, p, p, 2, 2, 8, 256, 64, 0.0625, p, n, None) < 0
+    assert lib.gdn_attn_decode(p, p, p, p, p, 2, 2, 8, 256, 64, 0.0625, p, n - 16, None) == -1
+    assert lib.gdn_last_error_string()

@@ -17,7 +17,7 @@ import torch
 
 from visionstack_b200 import Qwen3_5HybridCache, Qwen3_5TextConfig
 from visionstack_b200 import workloads as W
-from visionstack_b200.stack import Qwen3_5TextModel
+from visionstack_b200.stack import Qwen3_5TextModel, StackDecodeGraph
 
 pytestmark = pytest.mark.gpu
 
@@ -67,3 +67,37 @@ def test_stack_matches_reference(dtype, kv_capacity):
         assert np.abs(S - Sr).max() <= 2e-3 * np.abs(Sr).max() * (1 if dtype == "f32" else 20), "state of layer 0"
         o = model(input_ids=ids_t[:, :40], attention_mask=torch.from_numpy(mask).cuda())
         close(o.last_hidden_state, ref["h_mask"], dtype, "masked call")
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_decode_graph_matches_eager_decode(dtype):
+    """Decode steps replayed from one CUDA graph (static KV buffers, positions on the device, conv
+    state copied back) against the eager decode path, after the same prefill."""
+    model = build(dtype)
+    ids, _, _ = W.make_stack_calls(W.STACK_TINY)
+    ids_t = torch.from_numpy(ids).cuda()
+    P, N = 70, ids.shape[1]
+    tol = {"f32": (1e-4, 1e-5), "bf16": (0.07, 0.004)}[dtype]
+    with torch.inference_mode():
+        caches = []
+        for _ in range(2):
+            c = Qwen3_5HybridCache()
+            c.kv_capacity = 96
+            model(input_ids=ids_t[:, :P], past_key_values=c, use_cache=True)
+            caches.append(c)
+        ce, cg = caches
+        dg = StackDecodeGraph(model, cg, ids_t)
+        for p in range(P, N):
+            he = model(input_ids=ids_t[:, p:p + 1], past_key_values=ce, use_cache=True).last_hidden_state
+            hg = dg.step().clone()
+            d = (he.float() - hg.float()).abs()
+            assert d.max() <= tol[0] and d.mean() <= tol[1], f"step {p}: max {d.max():.3e} mean {d.mean():.3e}"
+        dg.finish()
+        torch.cuda.synchronize()
+    assert cg.past_seen_tokens == ce.past_seen_tokens == N
+    for l in (0, 1, 2):
+        assert torch.equal(cg.conv_states[l], ce.conv_states[l]) or dtype == "bf16"
+        d = (cg.recurrent_states[l] - ce.recurrent_states[l]).abs().max().item()
+        assert d <= 1e-3 * ce.recurrent_states[l].abs().max().item() * (1 if dtype == "f32" else 20)
+    assert cg.key_cache[3].shape == ce.key_cache[3].shape
+    assert (cg.key_cache[3].float() - ce.key_cache[3].float()).abs().max().item() <= tol[0]

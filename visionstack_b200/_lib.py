@@ -37,6 +37,8 @@ EXPORTED_SYMBOLS = (
     "gdn_device_error",
     "gdn_selftest_umma",
     "gdn_selftest_expired_wait",
+    "gdn_attn_decode_workspace_bytes",
+    "gdn_attn_decode",
 )
 GDN_FLAG_REGISTER_KERNEL = 1
 GDN_FLAG_CUDA_CORE_PREFILL = 2
@@ -117,6 +119,11 @@ def load() -> ctypes.CDLL:
         lib.gdn_selftest_umma.argtypes = [_i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p]
         lib.gdn_selftest_expired_wait.restype = _i32
         lib.gdn_selftest_expired_wait.argtypes = [_i32, _c_void_p, _c_void_p]
+        lib.gdn_attn_decode_workspace_bytes.restype = _i64
+        lib.gdn_attn_decode_workspace_bytes.argtypes = [_i32, _i32, _i32, _i32, _i32]
+        lib.gdn_attn_decode.restype = _i32
+        lib.gdn_attn_decode.argtypes = [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32,
+                                        _i32, _i32, ctypes.c_float, _c_void_p, _i64, _c_void_p]
         lib.gdn_prefill_workspace_bytes.restype = _i64
         lib.gdn_prefill_workspace_bytes.argtypes = [ctypes.POINTER(MixerArgs)]
         lib.gdn_mixer_prefill_ws.restype = _i32

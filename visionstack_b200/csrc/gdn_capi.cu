@@ -300,6 +300,75 @@ int32_t gdn_mixer_prefill_ws(const gdn_mixer_args* args, void* workspace, int64_
     return cuda_status(e, "gdn_mixer_prefill_ws sequential launch");
 }
 
+namespace {
+// Key ranges of the decode attention: about four CTAs per SM of a 148-SM part, each range a
+// multiple of 32 keys; a function of the shapes only, so the workspace size is too.
+void attn_split(int32_t batch, int32_t kv_heads, int32_t capacity, int* splits, int* span) {
+    const int kb = 32;
+    const int pairs = std::max(1, batch * kv_heads);
+    int S = std::max(1, (4 * 148 + pairs - 1) / pairs);
+    S = std::min(S, (capacity + kb - 1) / kb);
+    int sp = (capacity + S - 1) / S;
+    sp = (sp + kb - 1) / kb * kb;
+    *span = sp;
+    *splits = (capacity + sp - 1) / sp;
+}
+int64_t attn_ws_bytes(int32_t batch, int32_t kv_heads, int32_t groups, int32_t head_dim, int32_t capacity,
+                      int64_t* off_ml) {
+    int S, sp;
+    attn_split(batch, kv_heads, capacity, &S, &sp);
+    const int64_t po = (int64_t)batch * kv_heads * S * groups * head_dim * 4;
+    *off_ml = (po + 255) / 256 * 256;
+    return *off_ml + (int64_t)batch * kv_heads * S * groups * 2 * 4;
+}
+bool attn_shape_ok(int32_t batch, int32_t kv_heads, int32_t groups, int32_t head_dim, int32_t capacity) {
+    return batch > 0 && kv_heads > 0 && capacity > 0 && (groups == 1 || groups == 2 || groups == 4 || groups == 8) &&
+           (head_dim == 64 || head_dim == 128 || head_dim == 256) &&
+           (int64_t)batch * kv_heads * capacity * head_dim < (int64_t)1 << 40;
+}
+}  // namespace
+
+int64_t gdn_attn_decode_workspace_bytes(int32_t batch, int32_t kv_heads, int32_t groups, int32_t head_dim,
+                                        int32_t capacity) {
+    if (!attn_shape_ok(batch, kv_heads, groups, head_dim, capacity))
+        return fail(GDN_ERR_INVALID_ARG, "unsupported decode-attention shape");
+    int64_t off;
+    return attn_ws_bytes(batch, kv_heads, groups, head_dim, capacity, &off);
+}
+
+int32_t gdn_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int64_t* pos, void* out,
+                        int32_t batch, int32_t kv_heads, int32_t groups, int32_t head_dim, int32_t capacity,
+                        float scale, void* workspace, int64_t workspace_bytes, void* stream) {
+    if (!q || !k_cache || !v_cache || !pos || !out || !workspace)
+        return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
+    if (!attn_shape_ok(batch, kv_heads, groups, head_dim, capacity))
+        return fail(GDN_ERR_INVALID_ARG, "unsupported decode-attention shape");
+    const void* ptrs[] = {q, k_cache, v_cache, out, workspace};
+    for (const void* p : ptrs)
+        if (!aligned16(p)) return fail(GDN_ERR_ALIGNMENT, "pointers must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(pos) % 8) return fail(GDN_ERR_ALIGNMENT, "misaligned pos");
+    int64_t off_ml;
+    const int64_t need = attn_ws_bytes(batch, kv_heads, groups, head_dim, capacity, &off_ml);
+    if (workspace_bytes < need) return fail(GDN_ERR_INVALID_ARG, "workspace too small (%lld < %lld)",
+                                            (long long)workspace_bytes, (long long)need);
+    gdn::AttnDecodeArgs a{};
+    a.q = q;
+    a.k = k_cache;
+    a.v = v_cache;
+    a.out = out;
+    a.pos = reinterpret_cast<const long long*>(pos);
+    a.batch = batch;
+    a.kv_heads = kv_heads;
+    a.groups = groups;
+    a.head_dim = head_dim;
+    a.capacity = capacity;
+    attn_split(batch, kv_heads, capacity, &a.splits, &a.span);
+    a.qscale = scale * 1.4426950408889634f;
+    a.part_o = static_cast<float*>(workspace);
+    a.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + off_ml);
+    return cuda_status(gdn::launch_attn_decode(a, static_cast<cudaStream_t>(stream)), "gdn_attn_decode launch");
+}
+
 int32_t gdn_selftest_expired_wait(int32_t kind, int32_t* flag, void* stream) {
     if (kind < 0 || kind > 1) return fail(GDN_ERR_INVALID_ARG, "kind %d not in 0..1", kind);
     if (!flag) return fail(GDN_ERR_INVALID_ARG, "flag is NULL");

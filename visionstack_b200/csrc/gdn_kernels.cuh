@@ -68,6 +68,20 @@ unsigned int slots_device_error(bool clear);
 cudaError_t launch_umma_selftest(int mode, const float* A, const float* B, float* D, cudaStream_t s);
 unsigned int umma_device_error(bool clear);
 cudaError_t launch_expired_wait_selftest(int kind, int* flag, cudaStream_t s);
+// single-token grouped-query attention over a fixed-capacity KV buffer (stack_attn_decode.cu)
+struct AttnDecodeArgs {
+    const void* q;  // [batch][kv_heads * groups][head_dim] bf16
+    const void* k;  // [batch][kv_heads][capacity][head_dim] bf16
+    const void* v;
+    void* out;              // like q
+    const long long* pos;   // device: index of the last valid key
+    int batch, kv_heads, groups, head_dim, capacity;
+    int splits, span;       // key ranges of span keys (a multiple of 32)
+    float qscale;           // softmax scale * log2(e)
+    float* part_o;          // [batch][kv_heads][splits][groups][head_dim]
+    float* part_ml;         // [batch][kv_heads][splits][groups][2]
+};
+cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st);
 cudaError_t launch_prefill_tc(const MixParams& p, const CkptList& ck, int d, int dtype, cudaStream_t s,
                               bool* supported);
 unsigned int prefill_tc_device_error(bool clear);

@@ -34,9 +34,9 @@ class Qwen3_5RMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.zeros(dim))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        xf = x.float()
-        inv = torch.rsqrt(xf.square().mean(-1, keepdim=True) + self.eps)
-        return (xf * inv * (1.0 + self.weight.float())).to(x.dtype)
+        # one fused normalisation kernel in fp32 (same math, one pass) instead of six elementwise ones
+        w = 1.0 + self.weight.float()
+        return F.rms_norm(x.float(), (x.shape[-1],), weight=w, eps=self.eps).to(x.dtype)
 
 
 def _act(x: torch.Tensor, name: str) -> torch.Tensor:
@@ -109,6 +109,33 @@ def _apply_rotary_pos_emb_partial(q: torch.Tensor, k: torch.Tensor, cos: torch.T
     return rot(q), rot(k)
 
 
+def _decode_attention(q: torch.Tensor, kb: torch.Tensor, vb: torch.Tensor, pos: torch.Tensor,
+                      scale: float) -> torch.Tensor:
+    """One query token per row against fixed-capacity KV buffers on the CUDA decode-attention
+    kernel (gdn_attn_decode): q [B, H, 1, hd], kb / vb [B, KVH, cap, hd] (bf16, contiguous), keys
+    0..pos[0] (int64 on the device).  Returns [B, H, 1, hd]."""
+    from . import _lib
+    B, H, _, hd = q.shape
+    kvh, cap = kb.shape[1], kb.shape[2]
+    lib = _lib.load()
+    n = int(lib.gdn_attn_decode_workspace_bytes(B, kvh, H // kvh, hd, cap))
+    if n < 0:
+        _lib.check("gdn_attn_decode_workspace_bytes", n)
+    ws = torch.empty(n, dtype=torch.uint8, device=q.device)
+    q = q.contiguous()
+    out = torch.empty_like(q)
+    _lib.check("gdn_attn_decode", lib.gdn_attn_decode(
+        q.data_ptr(), kb.data_ptr(), vb.data_ptr(), pos.data_ptr(), out.data_ptr(), B, kvh, H // kvh, hd, cap,
+        float(scale), ws.data_ptr(), n, torch.cuda.current_stream(q.device).cuda_stream))
+    return out
+
+
+def _kernel_decode_ok(q: torch.Tensor, kb: torch.Tensor) -> bool:
+    g = q.shape[1] // kb.shape[1]
+    return (q.is_cuda and q.dtype == torch.bfloat16 and kb.dtype == torch.bfloat16 and kb.is_contiguous() and
+            q.shape[-1] in (64, 128, 256) and g in (1, 2, 4, 8) and q.shape[1] == g * kb.shape[1])
+
+
 class Qwen3_5Attention(nn.Module):
     """Gated grouped-query attention (text.py:89-212): q_proj yields a query and a gate per head;
     q / k RMS-normalised per head, partial rotary, SDPA, output times sigmoid(gate), o_proj."""
@@ -145,8 +172,9 @@ class Qwen3_5Attention(nn.Module):
             if buf is None or not (ours or not has_past) or buf[0].shape[2] < need or \
                     buf[0].shape[:2] != k.shape[:2] or buf[0].dtype != k.dtype:
                 size = max(cap, need)
-                buf = (k.new_empty(k.shape[0], k.shape[1], size, k.shape[3]),
-                       v.new_empty(v.shape[0], v.shape[1], size, v.shape[3]))
+                # zeroed: the static decode path masks the unwritten tail, whose scores must be finite
+                buf = (k.new_zeros(k.shape[0], k.shape[1], size, k.shape[3]),
+                       v.new_zeros(v.shape[0], v.shape[1], size, v.shape[3]))
                 if has_past:
                     buf[0][:, :, :prev].copy_(pk)
                     buf[1][:, :, :prev].copy_(pv)
@@ -160,6 +188,27 @@ class Qwen3_5Attention(nn.Module):
         cache.value_cache[l] = v
         return k, v, has_past
 
+    def _static_decode(self, cache: Qwen3_5HybridCache, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                       pos: torch.Tensor, attention_mask: Optional[torch.Tensor]) -> torch.Tensor:
+        """One decode token against this layer's fixed-capacity KV buffers with the position on
+        the device (CUDA-graph capturable): k, v written at `pos`, attention over the keys 0..pos
+        (the decode-attention kernel for bf16; otherwise SDPA over the whole buffer with the
+        positions past `pos` masked out)."""
+        if q.shape[2] != 1 or attention_mask is not None:
+            raise ValueError("the static decode path takes one token and no attention mask")
+        kb, vb = cache._kv_buffers[self.layer_idx]
+        kb.index_copy_(2, pos, k)
+        vb.index_copy_(2, pos, v)
+        if _kernel_decode_ok(q, kb) and vb.is_contiguous():
+            return _decode_attention(q, kb, vb, pos, self.scaling)
+        cap = kb.shape[2]
+        valid = (torch.arange(cap, device=q.device) <= pos).view(1, 1, 1, cap)
+        B, hd = q.shape[0], self.head_dim
+        G = self.num_key_value_groups
+        o = F.scaled_dot_product_attention(q.reshape(B, self.num_kv_heads, G, hd), kb, vb, attn_mask=valid,
+                                           scale=self.scaling)
+        return o.reshape(B, self.num_heads, 1, hd)
+
     def forward(self, hidden_states: torch.Tensor, position_embeddings: Tuple[torch.Tensor, torch.Tensor],
                 attention_mask: Optional[torch.Tensor] = None,
                 cache: Optional[Qwen3_5HybridCache] = None) -> torch.Tensor:
@@ -171,12 +220,30 @@ class Qwen3_5Attention(nn.Module):
         k = self.k_norm(_linear(self.k_proj, hidden_states).view(B, T, self.num_kv_heads, hd)).transpose(1, 2)
         v = _linear(self.v_proj, hidden_states).view(B, T, self.num_kv_heads, hd).transpose(1, 2)
         q, k = _apply_rotary_pos_emb_partial(q, k, *position_embeddings)
+        static_pos = getattr(cache, "static_pos", None) if cache is not None else None
+        if static_pos is not None:
+            o = self._static_decode(cache, q, k, v, static_pos, attention_mask)
+            o = o.transpose(1, 2).reshape(B, T, -1).contiguous() * torch.sigmoid(gate)
+            return _linear(self.o_proj, o)
         has_past = False
         if cache is not None:
             k, v, has_past = self._store_kv(cache, k, v)
         gqa = self.num_key_value_groups > 1
         kv_len = k.shape[2]
-        if attention_mask is not None and attention_mask.ndim == 4:
+        bufs = getattr(cache, "_kv_buffers", {}) if cache is not None else {}
+        buf = bufs.get(self.layer_idx)
+        if attention_mask is None and has_past and T == 1 and buf is not None and \
+                k.data_ptr() == buf[0].data_ptr() and v.data_ptr() == buf[1].data_ptr() and \
+                _kernel_decode_ok(q, buf[0]) and buf[1].is_contiguous():
+            pos = torch.tensor([kv_len - 1], dtype=torch.long, device=q.device)
+            o = _decode_attention(q, buf[0], buf[1], pos, self.scaling)
+        elif attention_mask is None and has_past and T == 1 and gqa:
+            # one query per head: the query heads of one KV head become that head's queries
+            # (the grouping of the GQA head expansion, h -> h // groups), so no K / V expansion
+            G = self.num_key_value_groups
+            o = F.scaled_dot_product_attention(q.reshape(B, self.num_kv_heads, G, hd), k, v, scale=self.scaling)
+            o = o.reshape(B, self.num_heads, 1, hd)
+        elif attention_mask is not None and attention_mask.ndim == 4:
             o = F.scaled_dot_product_attention(q, k, v, attn_mask=attention_mask, is_causal=False,
                                                scale=self.scaling, enable_gqa=gqa)
         elif has_past and T > 1:
@@ -295,3 +362,75 @@ class Qwen3_5TextModel(nn.Module):
         if cache is not None:
             cache.past_seen_tokens = past + T
         return Qwen3_5ModelOutput(last_hidden_state=self.norm(h), past_key_values=cache)
+
+
+class StackDecodeGraph:
+    """Single-token decode steps of a `Qwen3_5TextModel` replayed from one CUDA graph.
+
+    Built after a prefill into `cache` with `cache.kv_capacity` >= the final length.  The token of
+    step i is column `cache.past_seen_tokens` of `ids` ([B, N] int64 on the device), its position
+    that same column: both are read on the device, so the graph is position independent.  The
+    attention layers switch to their static-KV path (write at the position, attend over the keys
+    up to it); every DeltaNet layer's recurrent state is updated in place and its new conv state
+    is copied back into the buffer the next step reads.  The first step runs eagerly (it also
+    warms the libraries up), the graph is captured after it.  `step()` returns the step's final
+    hidden state [B, 1, hidden] (a buffer the next step overwrites).
+    """
+
+    def __init__(self, model: Qwen3_5TextModel, cache: Qwen3_5HybridCache, ids: torch.Tensor):
+        self.model, self.cache, self.ids = model, cache, ids
+        dev = ids.device
+        self.pos = torch.full((1,), int(cache.past_seen_tokens), dtype=torch.long, device=dev)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.out: Optional[torch.Tensor] = None
+        self._lin = [i for i, t in enumerate(model.config.layer_types) if t == "linear_attention"]
+        bufs = getattr(cache, "_kv_buffers", {})
+        for i, t in enumerate(model.config.layer_types):
+            if t == "full_attention" and (i not in bufs or cache.key_cache.get(i) is None or
+                                          cache.key_cache[i].data_ptr() != bufs[i][0].data_ptr()):
+                raise ValueError("prefill the cache with kv_capacity set before building the decode graph")
+        self._conv = {l: cache.conv_states[l] for l in self._lin}
+        self.capacity = min(bufs[i][0].shape[2] for i in bufs) if bufs else 1 << 30
+
+    def _one(self) -> torch.Tensor:
+        B = self.ids.shape[0]
+        tok = self.ids.gather(1, self.pos.view(1, 1).expand(B, 1))
+        pid = self.pos.view(1, 1, 1).expand(3, B, 1)
+        self.cache.static_pos = self.pos
+        try:
+            h = self.model(input_ids=tok, position_ids=pid, past_key_values=self.cache, use_cache=True)
+        finally:
+            self.cache.static_pos = None
+        for l in self._lin:
+            self._conv[l].copy_(self.cache.conv_states[l])
+            self.cache.conv_states[l] = self._conv[l]
+        self.pos.add_(1)
+        return h.last_hidden_state
+
+    def step(self) -> torch.Tensor:
+        seen = int(self.cache.past_seen_tokens)
+        if seen >= self.capacity:
+            raise ValueError("the KV buffers are full")
+        if self.graph is None:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):  # the eager step doubles as the libraries' warm-up
+                first = self._one()
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):  # recorded, not run: the output buffer fills on replay
+                self.out = self._one()
+            self.cache.past_seen_tokens = seen + 1
+            return first
+        self.graph.replay()
+        self.cache.past_seen_tokens = seen + 1
+        return self.out
+
+    def finish(self) -> None:
+        """Leave the cache as the eager path would: key / value entries trimmed to the tokens seen."""
+        n = int(self.cache.past_seen_tokens)
+        for i, (kb, vb) in getattr(self.cache, "_kv_buffers", {}).items():
+            self.cache.key_cache[i] = kb[:, :, :n]
+            self.cache.value_cache[i] = vb[:, :, :n]
+        self.graph = None
