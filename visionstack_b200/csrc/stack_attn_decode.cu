@@ -4,15 +4,17 @@
 // so one captured launch serves every step.
 //
 // Split-KV in two kernels.  attn_split_kernel: one CTA per (key range, KV head, batch row); each
-// warp walks blocks of 32 keys, a lane scoring one key against the G queries of the KV head
-// (its key row read once, the queries from shared memory), an online softmax per query in the
-// log2 domain, then the 32 keys' value rows accumulated with a lane holding HD/32 dims of all G
-// outputs.  The warps' partial (max, sum, output) merge in shared memory into one partial per
-// CTA.  attn_combine_kernel merges the key ranges and writes bf16.  HBM-bound: every key and
-// value row is read once.
+// warp walks blocks of 32 keys: the block's key rows arrive in the warp's shared-memory stage by
+// asynchronous 16-byte copies (one latency per block), a lane scores one key against the G
+// queries of the KV head (the queries from shared memory, packed fp32x2 arithmetic), the value
+// rows follow into the same stage while the online softmax per query runs (log2 domain), and a
+// lane accumulates HD/32 dims of all G outputs over the block's value rows.  The warps' partial
+// (max, sum, output) merge in shared memory into one partial per CTA.  attn_combine_kernel merges
+// the key ranges and writes bf16.  HBM-bound: every key and value row is read once.
 #include <cuda_bf16.h>
 #include <math_constants.h>
 
+#include "gdn_async.cuh"  // smem_u32
 #include "gdn_kernels.cuh"
 
 namespace gdn {
@@ -71,26 +73,56 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-// shared memory of attn_split_kernel, in floats
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Row r of a warp's stage holds HD bf16 as HD/8 chunks of 16 bytes; chunk c sits at position
+// c ^ (r mod HD/8), so a lane per row (the scores) and a row per warp (the values) both read
+// without bank conflicts.
+template <int HD>
+__device__ __forceinline__ uint32_t stage_off(int r, int byte_in_row) {
+    constexpr int CH = HD / 8;
+    const int c = byte_in_row >> 4;
+    return (uint32_t)(r * HD * 2 + ((c ^ (r & (CH - 1))) << 4) + (byte_in_row & 15));
+}
+
+// rows blk .. blk+nk-1 of one head's [cap][HD] buffer into the warp's stage (asynchronous)
+template <int HD>
+__device__ __forceinline__ void stage_rows(uint32_t stage, const __nv_bfloat16* head, int blk, int nk, int lane) {
+    constexpr int CH = HD / 8;
+    for (int idx = lane; idx < nk * CH; idx += 32) {
+        const int r = idx / CH, c = idx % CH;
+        cp_async16(stage + stage_off<HD>(r, c * 16), head + (size_t)(blk + r) * HD + c * 8);
+    }
+    cp_async_commit();
+}
+
+// shared memory of attn_split_kernel, in bytes
 template <int HD, int G>
 struct Smem {
-    static constexpr int Q = 0;                  // [G][HD] query * scale * log2(e)
-    static constexpr int P = Q + G * HD;         // [NW][KB][G] probabilities of a warp's block
-    static constexpr int ML = P + NW * KB * G;   // [NW][G][2] warp max / sum
-    static constexpr int ACC = ML + NW * G * 2;  // [NW][G][HD] warp outputs
-    static constexpr int FLOATS = ACC + NW * G * HD;
+    static constexpr int GP = (G + 1) / 2;                  // query pairs
+    static constexpr int STAGE = 0;                         // [NW][KB][HD] bf16 (then [NW][G][HD] f32)
+    static constexpr int Q = STAGE + NW * KB * HD * 2;      // [GP][HD] float2: (q_2p[d], q_2p+1[d]) * scale * log2 e
+    static constexpr int P = Q + GP * HD * 8;               // [NW][KB][G] f32 probabilities of a warp's block
+    static constexpr int ML = P + NW * KB * G * 4;          // [NW][G][2] f32 warp max / sum
+    static constexpr int BYTES = ML + NW * G * 2 * 4;
+    static_assert(NW * G * HD * 4 <= NW * KB * HD * 2, "the merge area must fit in the stages");
 };
 
 template <int HD, int G>
-__global__ void __launch_bounds__(NT, 2) attn_split_kernel(const __nv_bfloat16* __restrict__ q,
+__global__ void __launch_bounds__(NT, 1) attn_split_kernel(const __nv_bfloat16* __restrict__ q,
                                                            const __nv_bfloat16* __restrict__ kbuf,
                                                            const __nv_bfloat16* __restrict__ vbuf,
                                                            const long long* __restrict__ pos, int cap, int span,
                                                            float qscale, float* __restrict__ part_o,
                                                            float* __restrict__ part_ml) {
     using SM = Smem<HD, G>;
-    constexpr int DL = HD / 32;  // dims per lane
-    extern __shared__ float sm[];
+    constexpr int GP = SM::GP;
+    constexpr int DL = HD / 32;  // value dims per lane
+    extern __shared__ __align__(16) unsigned char smem[];
     const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int S = gridDim.x, KVH = gridDim.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -108,53 +140,64 @@ __global__ void __launch_bounds__(NT, 2) attn_split_kernel(const __nv_bfloat16* 
         }
         return;
     }
-    for (int i = threadIdx.x; i < G * HD; i += NT)
-        sm[SM::Q + i] = __bfloat162float(q[head * G * HD + i]) * qscale;
+    float2* sq = reinterpret_cast<float2*>(smem + SM::Q);
+    for (int i = threadIdx.x; i < GP * HD; i += NT) {
+        const int pq = i / HD, d = i % HD;
+        const float a = __bfloat162float(q[(head * G + 2 * pq) * HD + d]) * qscale;
+        const float c = 2 * pq + 1 < G ? __bfloat162float(q[(head * G + 2 * pq + 1) * HD + d]) * qscale : 0.f;
+        sq[i] = make_float2(a, c);
+    }
     __syncthreads();
 
     const __nv_bfloat16* kh = kbuf + head * (size_t)cap * HD;
     const __nv_bfloat16* vh = vbuf + head * (size_t)cap * HD;
-    float m[G], l[G], acc[G][DL];
+    const uint32_t stage = smem_u32(smem + SM::STAGE + warp * KB * HD * 2);
+    const unsigned char* stage_p = smem + SM::STAGE + warp * KB * HD * 2;
+    float* sp = reinterpret_cast<float*>(smem + SM::P) + warp * KB * G;
+    float m[G], l[G];
+    float2 acc[G][DL / 2];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         m[g] = -CUDART_INF_F;
         l[g] = 0.f;
 #pragma unroll
-        for (int i = 0; i < DL; ++i) acc[g][i] = 0.f;
+        for (int i = 0; i < DL / 2; ++i) acc[g][i] = make_float2(0.f, 0.f);
     }
-    float* sp = sm + SM::P + warp * KB * G;
     for (int blk = k0 + warp * KB; blk < k1; blk += NW * KB) {
-        // scores of key blk + lane (log2 domain), -inf past the valid keys
-        const int kk = blk + lane;
+        const int nk = min(KB, k1 - blk);
+        stage_rows<HD>(stage, kh, blk, nk, lane);
+        cp_async_wait_all();
+        __syncwarp();
+        // scores of key blk + lane against every query (log2 domain), -inf past the valid keys
         float sc[G];
+        if (lane < nk) {
+            float2 s2[GP];
 #pragma unroll
-        for (int g = 0; g < G; ++g) sc[g] = 0.f;
-        if (kk < k1) {
-            const uint4* kr = reinterpret_cast<const uint4*>(kh + (size_t)kk * HD);
-#pragma unroll 4
+            for (int pq = 0; pq < GP; ++pq) s2[pq] = make_float2(0.f, 0.f);
+#pragma unroll 2
             for (int c = 0; c < HD / 8; ++c) {
+                const uint4 raw = *reinterpret_cast<const uint4*>(stage_p + stage_off<HD>(lane, c * 16));
                 float kf[8];
-                unpack_row<8>(__ldg(kr + c), kf);
+                unpack_row<8>(raw, kf);
 #pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const float4 qa = *reinterpret_cast<const float4*>(sm + SM::Q + g * HD + c * 8);
-                    const float4 qb = *reinterpret_cast<const float4*>(sm + SM::Q + g * HD + c * 8 + 4);
-                    float t = sc[g];
-                    t = fmaf(qa.x, kf[0], t);
-                    t = fmaf(qa.y, kf[1], t);
-                    t = fmaf(qa.z, kf[2], t);
-                    t = fmaf(qa.w, kf[3], t);
-                    t = fmaf(qb.x, kf[4], t);
-                    t = fmaf(qb.y, kf[5], t);
-                    t = fmaf(qb.z, kf[6], t);
-                    t = fmaf(qb.w, kf[7], t);
-                    sc[g] = t;
+                for (int pq = 0; pq < GP; ++pq) {
+#pragma unroll
+                    for (int d2 = 0; d2 < 4; ++d2) {
+                        const float4 qq = *reinterpret_cast<const float4*>(sq + pq * HD + c * 8 + 2 * d2);
+                        s2[pq] = __ffma2_rn(make_float2(qq.x, qq.y), make_float2(kf[2 * d2], kf[2 * d2]), s2[pq]);
+                        s2[pq] = __ffma2_rn(make_float2(qq.z, qq.w), make_float2(kf[2 * d2 + 1], kf[2 * d2 + 1]),
+                                            s2[pq]);
+                    }
                 }
             }
+#pragma unroll
+            for (int g = 0; g < G; ++g) sc[g] = (g & 1) ? s2[g >> 1].y : s2[g >> 1].x;
         } else {
 #pragma unroll
             for (int g = 0; g < G; ++g) sc[g] = -CUDART_INF_F;
         }
+        __syncwarp();  // every lane is done with the key rows: the stage takes the value rows
+        stage_rows<HD>(stage, vh, blk, nk, lane);
         // online softmax per query over this block (lane 0's key is always valid)
 #pragma unroll
         for (int g = 0; g < G; ++g) {
@@ -164,56 +207,62 @@ __global__ void __launch_bounds__(NT, 2) attn_split_kernel(const __nv_bfloat16* 
             l[g] = l[g] * corr + warp_sum(p);
             m[g] = mn;
 #pragma unroll
-            for (int i = 0; i < DL; ++i) acc[g][i] *= corr;
+            for (int i = 0; i < DL / 2; ++i) acc[g][i] = __fmul2_rn(acc[g][i], make_float2(corr, corr));
             sp[lane * G + g] = p;
         }
+        cp_async_wait_all();
         __syncwarp();
-        const int nk = min(KB, k1 - blk);
         for (int j = 0; j < nk; ++j) {
             float vf[DL];
-            unpack_row<DL>(__ldg(reinterpret_cast<const typename Row<HD>::T*>(vh + (size_t)(blk + j) * HD) + lane),
+            unpack_row<DL>(*reinterpret_cast<const typename Row<HD>::T*>(stage_p + stage_off<HD>(j, lane * DL * 2)),
                            vf);
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 const float p = sp[j * G + g];
 #pragma unroll
-                for (int i = 0; i < DL; ++i) acc[g][i] = fmaf(p, vf[i], acc[g][i]);
+                for (int i = 0; i < DL / 2; ++i)
+                    acc[g][i] = __ffma2_rn(make_float2(p, p), make_float2(vf[2 * i], vf[2 * i + 1]), acc[g][i]);
             }
         }
-        __syncwarp();
+        __syncwarp();  // the stage and the probabilities are rewritten by the next block
     }
 
-    // merge the warps: common max per query, then the scaled sums
+    // merge the warps (the merge area reuses the stages): common max per query, then the scaled sums
+    float* sml = reinterpret_cast<float*>(smem + SM::ML);
+    float* sacc = reinterpret_cast<float*>(smem + SM::STAGE);
     if (lane == 0) {
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            sm[SM::ML + (warp * G + g) * 2] = m[g];
-            sm[SM::ML + (warp * G + g) * 2 + 1] = l[g];
+            sml[(warp * G + g) * 2] = m[g];
+            sml[(warp * G + g) * 2 + 1] = l[g];
         }
     }
     __syncthreads();
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         float M = -CUDART_INF_F;
-        for (int w = 0; w < NW; ++w) M = fmaxf(M, sm[SM::ML + (w * G + g) * 2]);
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, sml[(w * G + g) * 2]);
         const float f = m[g] == -CUDART_INF_F ? 0.f : exp2f(m[g] - M);
 #pragma unroll
-        for (int i = 0; i < DL; ++i) sm[SM::ACC + (warp * G + g) * HD + lane * DL + i] = acc[g][i] * f;
+        for (int i = 0; i < DL / 2; ++i) {
+            sacc[(warp * G + g) * HD + lane * DL + 2 * i] = acc[g][i].x * f;
+            sacc[(warp * G + g) * HD + lane * DL + 2 * i + 1] = acc[g][i].y * f;
+        }
     }
     __syncthreads();
     for (int e = threadIdx.x; e < G * HD; e += NT) {
         float t = 0.f;
-        for (int w = 0; w < NW; ++w) t += sm[SM::ACC + w * G * HD + e];
+        for (int w = 0; w < NW; ++w) t += sacc[w * G * HD + e];
         po[e] = t;
     }
     if (threadIdx.x < G) {
         const int g = threadIdx.x;
         float M = -CUDART_INF_F;
-        for (int w = 0; w < NW; ++w) M = fmaxf(M, sm[SM::ML + (w * G + g) * 2]);
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, sml[(w * G + g) * 2]);
         float L = 0.f;
         for (int w = 0; w < NW; ++w) {
-            const float mw = sm[SM::ML + (w * G + g) * 2];
-            if (mw != -CUDART_INF_F) L += sm[SM::ML + (w * G + g) * 2 + 1] * exp2f(mw - M);
+            const float mw = sml[(w * G + g) * 2];
+            if (mw != -CUDART_INF_F) L += sml[(w * G + g) * 2 + 1] * exp2f(mw - M);
         }
         pml[2 * g] = M;
         pml[2 * g + 1] = L;
@@ -247,7 +296,7 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(const float* __restric
 
 template <int HD, int G>
 cudaError_t launch_t(const AttnDecodeArgs& a, cudaStream_t st) {
-    const int bytes = Smem<HD, G>::FLOATS * 4;
+    const int bytes = Smem<HD, G>::BYTES;
     cudaError_t e = cudaFuncSetAttribute(attn_split_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return e;
     attn_split_kernel<HD, G><<<dim3(a.splits, a.kv_heads, a.batch), NT, bytes, st>>>(
