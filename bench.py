@@ -61,8 +61,9 @@ def parse():
     ap.add_argument("--prefill-batch", type=int, default=8)
     ap.add_argument("--prefill-seq", type=int, default=8192)
     ap.add_argument("--no-rollback", action="store_true", help="skip the secondary rollback measurement")
-    ap.add_argument("--stack", action="store_true",
-                    help="also time the 48-layer hybrid stack (B32: prefill 4096, decode 256; 1 GPU)")
+    ap.add_argument("--no-stack", action="store_true",
+                    help="skip the secondary 48-layer hybrid stack measurement (B32: prefill 4096, decode 256; "
+                         "run at 1 GPU only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-s", type=float, default=12.0, help="seconds of CPU work for the CPU baseline")
     return ap.parse_args()
@@ -466,7 +467,7 @@ def run_ours(args, rank: int, world: int) -> None:
         rollback = run_rollback(torch, dist, m, local, dev, world, barrier)
 
     stack = None
-    if args.stack and world == 1:
+    if not args.no_stack and world == 1:
         try:
             stack = run_stack(torch, dev)
         except Exception as e:  # the stack is a secondary measurement: never lose the line to it
