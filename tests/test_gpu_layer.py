@@ -197,3 +197,39 @@ def test_functional_delta_rule_checkpoints():
     o, s = _chunk_gated_delta_rule(cu(d["c_q"][:, :3]), cu(d["c_k"][:, :3]), cu(d["c_v"][:, :3]),
                                    cu(d["c_g"][:, :3]), cu(d["c_b"][:, :3]), output_final_state=True)
     assert max_abs(o, d["e_out"]) < 1e-5 and rel_max(s, d["e_state"]) < 1e-5
+
+
+def test_fused_input_projection():
+    """The four input projections run as one GEMM over a fused weight whose row ranges the
+    parameters become: the state dict keeps its names, shapes and values, loading a state dict
+    afterwards updates the fused weight, and the layer output matches the four separate GEMMs."""
+    shape = W.SHAPE_SMALL
+    m, _ = make_layer(shape, "bf16")
+    sd_before = {k: v.clone() for k, v in m.state_dict().items()}
+    g = torch.Generator(device="cuda")
+    g.manual_seed(21)
+    x = torch.randn(2, 70, shape.hidden_size, generator=g, device="cuda").to(torch.bfloat16)
+    with torch.no_grad():
+        fused = m.project(x)
+        f = m._in_proj_fused
+        assert f is not None and m.in_proj_z.weight.data_ptr() == f[shape.conv_dim].data_ptr()
+        sd_after = m.state_dict()
+        assert list(sd_after) == list(sd_before)
+        for k in sd_before:
+            assert sd_after[k].shape == sd_before[k].shape and torch.equal(sd_after[k], sd_before[k]), k
+        m.fuse_in_proj = False
+        sep = m.project(x)
+        for a, b in zip(fused, sep):
+            assert a.shape == b.shape
+            assert (a.float() - b.float()).abs().max().item() <= 0.02 * b.float().abs().max().item() + 1e-2
+        y_sep = m(x)
+        m.fuse_in_proj = True
+        y_fused = m(x)
+        assert_bf16_close(y_fused, y_sep, "layer output, fused vs separate projections", scale=2.0)
+        # loading a state dict after the fusion writes through to the fused weight
+        sd2 = {k: (v * 0.5 if k == "in_proj_b.weight" else v) for k, v in sd_before.items()}
+        m.load_state_dict(sd2)
+        assert m.project(x)[2].data_ptr() != 0
+        assert torch.equal(m._in_proj_fused[shape.conv_dim + shape.value_dim:
+                                            shape.conv_dim + shape.value_dim + shape.num_v_heads],
+                           sd2["in_proj_b.weight"])

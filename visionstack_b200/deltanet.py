@@ -218,6 +218,8 @@ class Qwen3_5GatedDeltaNet(nn.Module):
         self.in_proj_b = nn.Linear(self.hidden_size, self.num_v_heads, bias=False)
         self.in_proj_a = nn.Linear(self.hidden_size, self.num_v_heads, bias=False)
         self.inplace_state = True
+        self.fuse_in_proj = True
+        self._in_proj_fused: Optional[torch.Tensor] = None
 
     # -- helpers -----------------------------------------------------------
     def _act_dtype(self, x: torch.Tensor) -> torch.dtype:
@@ -229,11 +231,53 @@ class Qwen3_5GatedDeltaNet(nn.Module):
     def _param_as(self, p: torch.Tensor, dt: torch.dtype) -> torch.Tensor:
         return p if p.dtype == dt else p.to(dt)
 
+    def _fused_in_proj_weight(self) -> Optional[torch.Tensor]:
+        """The four input-projection weights as row ranges of one [conv_dim + Hv*dv + 2 Hv, H]
+        tensor, or None where one GEMM cannot serve them (fp8 or mixed dtypes / devices, or a row
+        length that would leave the outputs' rows off 16-byte boundaries, which the kernels'
+        bulk copies need).  On first use the parameters are re-pointed at their row ranges of the
+        fused weight (the state dict keeps its names, shapes and values; loading into it writes
+        the fused weight); after anything replaces a parameter's storage (``.to``, assignment)
+        the next call fuses again."""
+        ws = [self.in_proj_qkv.weight, self.in_proj_z.weight, self.in_proj_b.weight, self.in_proj_a.weight]
+        if not self.fuse_in_proj or any(w.dtype in _FP8_DTYPES for w in ws) or \
+                len({(w.dtype, w.device) for w in ws}) != 1 or ws[0].device.type != "cuda":
+            return None
+        n = sum(w.shape[0] for w in ws)
+        if (n * ws[0].element_size()) % 16:
+            return None
+        f = self._in_proj_fused
+        if f is not None and f.dtype == ws[0].dtype and f.device == ws[0].device and f.shape[0] == n:
+            off, ok = 0, True
+            for w in ws:
+                ok = ok and w.data_ptr() == f[off].data_ptr() and w.is_contiguous()
+                off += w.shape[0]
+            if ok:
+                return f
+        with torch.no_grad():
+            f = torch.cat([w.detach() for w in ws], 0).contiguous()
+            off = 0
+            for w in ws:
+                w.data = f[off:off + w.shape[0]]
+                off += w.shape[0]
+        self._in_proj_fused = f
+        return f
+
     def project(self, hidden_states: torch.Tensor):
-        """The four input projections (library GEMMs): mixed_qkv [B,T,conv_dim],
-        z [B,T,Hv*dv], b, a [B,T,Hv]."""
-        return (_linear(self.in_proj_qkv, hidden_states), _linear(self.in_proj_z, hidden_states),
-                _linear(self.in_proj_b, hidden_states), _linear(self.in_proj_a, hidden_states))
+        """The four input projections (library GEMMs; the reference's _linear dtype rule):
+        mixed_qkv [B,T,conv_dim], z [B,T,Hv*dv], b, a [B,T,Hv].  On a GPU they run as one GEMM
+        over the fused weight; the outputs are then column ranges of one [B,T,N] tensor (last
+        dimension contiguous, rows 16-byte aligned), which the token mixer reads in place."""
+        f = self._fused_in_proj_weight()
+        if f is None:
+            return (_linear(self.in_proj_qkv, hidden_states), _linear(self.in_proj_z, hidden_states),
+                    _linear(self.in_proj_b, hidden_states), _linear(self.in_proj_a, hidden_states))
+        x = hidden_states if hidden_states.dtype == f.dtype else hidden_states.to(f.dtype)
+        y = F.linear(x, f)
+        c0 = self.conv_dim
+        c1 = c0 + self.value_dim
+        c2 = c1 + self.num_v_heads
+        return y[..., :c0], y[..., c0:c1], y[..., c1:c2], y[..., c2:]
 
     def mixer(self, mixed_qkv: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: torch.Tensor,
               conv_state: Optional[torch.Tensor] = None, rec_state: Optional[torch.Tensor] = None,
