@@ -100,18 +100,42 @@ __device__ __forceinline__ void stage_rows(uint32_t stage, const __nv_bfloat16* 
     cp_async_commit();
 }
 
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t* r) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+// d[16x8] += a[16x16] b[16x8], bf16 in, fp32 accumulate (warp-wide)
+__device__ __forceinline__ void mma16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 // shared memory of attn_split_kernel, in bytes
 template <int HD, int G>
 struct Smem {
-    static constexpr int GP = (G + 1) / 2;                  // query pairs
-    static constexpr int STAGE = 0;                         // [NW][KB][HD] bf16 (then [NW][G][HD] f32)
-    static constexpr int Q = STAGE + NW * KB * HD * 2;      // [GP][HD] float2: (q_2p[d], q_2p+1[d]) * scale * log2 e
-    static constexpr int P = Q + GP * HD * 8;               // [NW][KB][G] f32 probabilities of a warp's block
-    static constexpr int ML = P + NW * KB * G * 4;          // [NW][G][2] f32 warp max / sum
-    static constexpr int BYTES = ML + NW * G * 2 * 4;
+    static constexpr int STAGE = 0;                     // [NW][KB][HD] bf16 (then [NW][G][HD] f32)
+    static constexpr int PT = STAGE + NW * KB * HD * 2;  // [NW][8][KB] bf16: a warp's probabilities, query-major
+    static constexpr int ML = PT + NW * 8 * KB * 2;      // [NW][8][2] f32 warp max / sum
+    static constexpr int BYTES = ML + NW * 8 * 2 * 4;
     static_assert(NW * G * HD * 4 <= NW * KB * HD * 2, "the merge area must fit in the stages");
 };
 
+// Per warp and block of 32 keys, on the tensor cores (mma.sync m16n8k16, bf16 in, fp32 out):
+// scores S[32 keys][8 queries] = K_blk Q^T (two 16-key tiles x HD/16 steps, K from the stage by
+// ldmatrix, Q fragments held in registers; queries past G are zero), then
+// O^T[HD][8] += V_blk^T P^T (HD/16 dim tiles x two 16-key steps, V transposed by ldmatrix.trans,
+// P rounded to bf16 as the flash form of attention does).  Lane (g = lane / 4, t = lane % 4)
+// holds scores of keys {g, g+8} (+16) for queries {2t, 2t+1} and outputs of dims {g, g+8} (+16i)
+// for the same two queries, so the softmax state of a query lives in the lanes with its t.
 template <int HD, int G>
 __global__ void __launch_bounds__(NT, 1) attn_split_kernel(const __nv_bfloat16* __restrict__ q,
                                                            const __nv_bfloat16* __restrict__ kbuf,
@@ -120,12 +144,12 @@ __global__ void __launch_bounds__(NT, 1) attn_split_kernel(const __nv_bfloat16* 
                                                            float qscale, float* __restrict__ part_o,
                                                            float* __restrict__ part_ml) {
     using SM = Smem<HD, G>;
-    constexpr int GP = SM::GP;
-    constexpr int DL = HD / 32;  // value dims per lane
+    constexpr int KS = HD / 16;  // 16-dim steps of the scores, 16-dim tiles of the outputs
     extern __shared__ __align__(16) unsigned char smem[];
     const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int S = gridDim.x, KVH = gridDim.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, tq = lane & 3;
     const long long last = pos[0];
     const int n_valid = last < 0 ? 0 : (int)min((long long)cap, last + 1);
     const int k0 = s * span, k1 = min(k0 + span, n_valid);
@@ -140,88 +164,108 @@ __global__ void __launch_bounds__(NT, 1) attn_split_kernel(const __nv_bfloat16* 
         }
         return;
     }
-    float2* sq = reinterpret_cast<float2*>(smem + SM::Q);
-    for (int i = threadIdx.x; i < GP * HD; i += NT) {
-        const int pq = i / HD, d = i % HD;
-        const float a = __bfloat162float(q[(head * G + 2 * pq) * HD + d]) * qscale;
-        const float c = 2 * pq + 1 < G ? __bfloat162float(q[(head * G + 2 * pq + 1) * HD + d]) * qscale : 0.f;
-        sq[i] = make_float2(a, c);
+    // Q fragments (B operand, k = dim, n = query): query gq, dims 16ks + 2tq + {0,1} and + 8
+    uint32_t qf[KS][2];
+    {
+        const __nv_bfloat16* qrow = q + (head * G + gq) * HD;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            qf[ks][0] = gq < G ? __ldg(reinterpret_cast<const unsigned int*>(qrow + ks * 16 + 2 * tq)) : 0u;
+            qf[ks][1] = gq < G ? __ldg(reinterpret_cast<const unsigned int*>(qrow + ks * 16 + 2 * tq + 8)) : 0u;
+        }
     }
-    __syncthreads();
 
     const __nv_bfloat16* kh = kbuf + head * (size_t)cap * HD;
     const __nv_bfloat16* vh = vbuf + head * (size_t)cap * HD;
     const uint32_t stage = smem_u32(smem + SM::STAGE + warp * KB * HD * 2);
-    const unsigned char* stage_p = smem + SM::STAGE + warp * KB * HD * 2;
-    float* sp = reinterpret_cast<float*>(smem + SM::P) + warp * KB * G;
-    float m[G], l[G];
-    float2 acc[G][DL / 2];
+    unsigned char* stage_p = smem + SM::STAGE + warp * KB * HD * 2;
+    __nv_bfloat16* spt = reinterpret_cast<__nv_bfloat16*>(smem + SM::PT) + warp * 8 * KB;
+    const uint32_t spt_a = smem_u32(spt);
+    float m[2] = {-CUDART_INF_F, -CUDART_INF_F}, l[2] = {0.f, 0.f};
+    float acc[KS][4];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        m[g] = -CUDART_INF_F;
-        l[g] = 0.f;
-#pragma unroll
-        for (int i = 0; i < DL / 2; ++i) acc[g][i] = make_float2(0.f, 0.f);
-    }
+    for (int i = 0; i < KS; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+
     for (int blk = k0 + warp * KB; blk < k1; blk += NW * KB) {
         const int nk = min(KB, k1 - blk);
         stage_rows<HD>(stage, kh, blk, nk, lane);
         cp_async_wait_all();
         __syncwarp();
-        // scores of key blk + lane against every query (log2 domain), -inf past the valid keys
-        float sc[G];
-        if (lane < nk) {
-            float2 s2[GP];
+        // scores: c[mt] = S[keys 16mt + gq (+8)][queries 2tq, 2tq+1]
+        float c[2][4];
 #pragma unroll
-            for (int pq = 0; pq < GP; ++pq) s2[pq] = make_float2(0.f, 0.f);
-#pragma unroll 2
-            for (int c = 0; c < HD / 8; ++c) {
-                const uint4 raw = *reinterpret_cast<const uint4*>(stage_p + stage_off<HD>(lane, c * 16));
-                float kf[8];
-                unpack_row<8>(raw, kf);
+        for (int mt = 0; mt < 2; ++mt) {
+            c[mt][0] = c[mt][1] = c[mt][2] = c[mt][3] = 0.f;
 #pragma unroll
-                for (int pq = 0; pq < GP; ++pq) {
-#pragma unroll
-                    for (int d2 = 0; d2 < 4; ++d2) {
-                        const float4 qq = *reinterpret_cast<const float4*>(sq + pq * HD + c * 8 + 2 * d2);
-                        s2[pq] = __ffma2_rn(make_float2(qq.x, qq.y), make_float2(kf[2 * d2], kf[2 * d2]), s2[pq]);
-                        s2[pq] = __ffma2_rn(make_float2(qq.z, qq.w), make_float2(kf[2 * d2 + 1], kf[2 * d2 + 1]),
-                                            s2[pq]);
-                    }
-                }
+            for (int ks = 0; ks < KS; ++ks) {
+                uint32_t a[4];
+                ldsm_x4(stage + stage_off<HD>(mt * 16 + (lane & 15), (ks * 2 + (lane >> 4)) * 16), a);
+                mma16816(c[mt], a, qf[ks][0], qf[ks][1]);
             }
-#pragma unroll
-            for (int g = 0; g < G; ++g) sc[g] = (g & 1) ? s2[g >> 1].y : s2[g >> 1].x;
-        } else {
-#pragma unroll
-            for (int g = 0; g < G; ++g) sc[g] = -CUDART_INF_F;
         }
         __syncwarp();  // every lane is done with the key rows: the stage takes the value rows
         stage_rows<HD>(stage, vh, blk, nk, lane);
-        // online softmax per query over this block (lane 0's key is always valid)
+        // online softmax (log2 domain) for queries 2tq + jj over the block's valid keys
+        float corr[2];
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const float mn = fmaxf(m[g], warp_max(sc[g]));
-            const float corr = exp2f(m[g] - mn);
-            const float p = exp2f(sc[g] - mn);
-            l[g] = l[g] * corr + warp_sum(p);
-            m[g] = mn;
+        for (int jj = 0; jj < 2; ++jj) {
+            float sv[4];
 #pragma unroll
-            for (int i = 0; i < DL / 2; ++i) acc[g][i] = __fmul2_rn(acc[g][i], make_float2(corr, corr));
-            sp[lane * G + g] = p;
+            for (int e = 0; e < 4; ++e) {
+                const int key = (e >> 1) * 16 + gq + (e & 1) * 8;
+                sv[e] = key < nk ? c[e >> 1][(e & 1) * 2 + jj] * qscale : -CUDART_INF_F;
+            }
+            float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float mn = fmaxf(m[jj], mx);
+            corr[jj] = exp2f(m[jj] - mn);
+            float sum = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float p = exp2f(sv[e] - mn);
+                sum += p;
+                const int key = (e >> 1) * 16 + gq + (e & 1) * 8;
+                spt[(2 * tq + jj) * KB + key] = __float2bfloat16_rn(p);
+            }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+            l[jj] = l[jj] * corr[jj] + sum;
+            m[jj] = mn;
+        }
+#pragma unroll
+        for (int i = 0; i < KS; ++i) {
+            acc[i][0] *= corr[0];
+            acc[i][1] *= corr[1];
+            acc[i][2] *= corr[0];
+            acc[i][3] *= corr[1];
         }
         cp_async_wait_all();
+        if (nk < KB) {  // rows past the valid keys: zero (their probabilities are 0; 0 x stale data)
+            for (int idx = lane; idx < (KB - nk) * (HD / 8); idx += 32) {
+                const int r = nk + idx / (HD / 8), cc = idx % (HD / 8);
+                *reinterpret_cast<uint4*>(stage_p + stage_off<HD>(r, cc * 16)) = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
         __syncwarp();
-        for (int j = 0; j < nk; ++j) {
-            float vf[DL];
-            unpack_row<DL>(*reinterpret_cast<const typename Row<HD>::T*>(stage_p + stage_off<HD>(j, lane * DL * 2)),
-                           vf);
+        // P^T fragments (B operand, k = key, n = query): query gq, keys 16kk + 2tq + {0,1} and + 8
+        uint32_t pb[2][2];
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float p = sp[j * G + g];
+        for (int kk = 0; kk < 2; ++kk) {
+            asm volatile("ld.shared.b32 %0, [%1];" : "=r"(pb[kk][0]) : "r"(spt_a + (gq * KB + kk * 16 + 2 * tq) * 2));
+            asm volatile("ld.shared.b32 %0, [%1];" : "=r"(pb[kk][1]) : "r"(spt_a + (gq * KB + kk * 16 + 2 * tq + 8) * 2));
+        }
+        // outputs: acc[dt] = O[dims 16dt + gq (+8)][queries 2tq, 2tq+1]
 #pragma unroll
-                for (int i = 0; i < DL / 2; ++i)
-                    acc[g][i] = __ffma2_rn(make_float2(p, p), make_float2(vf[2 * i], vf[2 * i + 1]), acc[g][i]);
+        for (int dt = 0; dt < KS; ++dt) {
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) {
+                uint32_t a[4];
+                ldsm_x4_trans(stage + stage_off<HD>(kk * 16 + ((lane >> 4) << 3) + (lane & 7),
+                                                    (dt * 2 + ((lane >> 3) & 1)) * 16), a);
+                mma16816(acc[dt], a, pb[kk][0], pb[kk][1]);
             }
         }
         __syncwarp();  // the stage and the probabilities are rewritten by the next block
@@ -230,23 +274,25 @@ __global__ void __launch_bounds__(NT, 1) attn_split_kernel(const __nv_bfloat16* 
     // merge the warps (the merge area reuses the stages): common max per query, then the scaled sums
     float* sml = reinterpret_cast<float*>(smem + SM::ML);
     float* sacc = reinterpret_cast<float*>(smem + SM::STAGE);
-    if (lane == 0) {
+    if (gq == 0) {
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-            sml[(warp * G + g) * 2] = m[g];
-            sml[(warp * G + g) * 2 + 1] = l[g];
+        for (int jj = 0; jj < 2; ++jj) {
+            sml[(warp * 8 + 2 * tq + jj) * 2] = m[jj];
+            sml[(warp * 8 + 2 * tq + jj) * 2 + 1] = l[jj];
         }
     }
     __syncthreads();
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
+    for (int jj = 0; jj < 2; ++jj) {
+        const int n = 2 * tq + jj;
+        if (n >= G) continue;
         float M = -CUDART_INF_F;
-        for (int w = 0; w < NW; ++w) M = fmaxf(M, sml[(w * G + g) * 2]);
-        const float f = m[g] == -CUDART_INF_F ? 0.f : exp2f(m[g] - M);
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, sml[(w * 8 + n) * 2]);
+        const float f = m[jj] == -CUDART_INF_F ? 0.f : exp2f(m[jj] - M);
 #pragma unroll
-        for (int i = 0; i < DL / 2; ++i) {
-            sacc[(warp * G + g) * HD + lane * DL + 2 * i] = acc[g][i].x * f;
-            sacc[(warp * G + g) * HD + lane * DL + 2 * i + 1] = acc[g][i].y * f;
+        for (int dt = 0; dt < KS; ++dt) {
+            sacc[(warp * G + n) * HD + dt * 16 + gq] = acc[dt][jj] * f;
+            sacc[(warp * G + n) * HD + dt * 16 + gq + 8] = acc[dt][2 + jj] * f;
         }
     }
     __syncthreads();
@@ -256,16 +302,16 @@ __global__ void __launch_bounds__(NT, 1) attn_split_kernel(const __nv_bfloat16* 
         po[e] = t;
     }
     if (threadIdx.x < G) {
-        const int g = threadIdx.x;
+        const int n = threadIdx.x;
         float M = -CUDART_INF_F;
-        for (int w = 0; w < NW; ++w) M = fmaxf(M, sml[(w * G + g) * 2]);
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, sml[(w * 8 + n) * 2]);
         float L = 0.f;
         for (int w = 0; w < NW; ++w) {
-            const float mw = sml[(w * G + g) * 2];
-            if (mw != -CUDART_INF_F) L += sml[(w * G + g) * 2 + 1] * exp2f(mw - M);
+            const float mw = sml[(w * 8 + n) * 2];
+            if (mw != -CUDART_INF_F) L += sml[(w * 8 + n) * 2 + 1] * exp2f(mw - M);
         }
-        pml[2 * g] = M;
-        pml[2 * g + 1] = L;
+        pml[2 * n] = M;
+        pml[2 * n + 1] = L;
     }
 }
 
