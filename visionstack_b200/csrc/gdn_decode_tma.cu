@@ -208,23 +208,23 @@ __global__ void __launch_bounds__(NT, 1)
 
         const bool ok = (!has_S || mbar_wait_bounded(bar_s, k & 1u, GDN_DEVERR_TMA_TIMEOUT)) &&
                         mbar_wait_bounded(bar, k & 1u, GDN_DEVERR_TMA_TIMEOUT);
-        if (group_any(!ok, bar_id)) {
-            failed = true;
-            break;
-        }
 
         // ---- consume the stage: state to registers, conv windows, conv of every token, z ----
+        // The state is read before the group agrees on the waits (a thread whose wait gave up
+        // reads stale, in-bounds data that is then discarded), so one barrier both agrees on
+        // failure and releases the state region for the next tile's state.
         float4 S[RPT];  // rows rg*RPT .. +RPT-1, columns cg*4 .. cg*4+3
 #pragma unroll
         for (int r = 0; r < RPT; ++r)
             S[r] = has_S ? *reinterpret_cast<const float4*>(sS + (rg * RPT + r) * D + cg * 4)
                          : make_float4(0.f, 0.f, 0.f, 0.f);
-        if (has_S) {
-            group_sync(bar_id);  // the state is in registers: its region takes the next tile's state
-            if (tid == 0 && tile + nworkers < num_tiles) {
-                fence_proxy_async_smem();
-                issue_state(tile + nworkers);
-            }
+        if (group_any(!ok, bar_id)) {
+            failed = true;
+            break;
+        }
+        if (has_S && tid == 0 && tile + nworkers < num_tiles) {
+            fence_proxy_async_smem();
+            issue_state(tile + nworkers);
         }
 
         const bool own_qk = (h % rep) == 0;
@@ -385,7 +385,9 @@ __global__ void __launch_bounds__(NT, 1)
                 const float y = Act<TA>::round(Act<TA>::ldg(normw + j) * Act<TA>::round(o * rstd));
                 Act<TA>::st(out + j, y * silu_f(zbuf[t * D + j]));
             }
-            group_sync(bar_id);  // su / so / red are rewritten by the next token or tile
+            // su / so / red are rewritten by the next token; after the last token the next
+            // tile's first two barriers come before any thread writes them (or the gates)
+            if (t + 1 < T) group_sync(bar_id);
         }
 
         if (p.S_out) {
