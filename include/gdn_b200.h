@@ -286,8 +286,8 @@ int32_t gdn_mixer_prefill_ws(const gdn_mixer_args* args, void* workspace, int64_
 
 /*
  * gdn_mixer_prefill_ws with the workspace taken from a fixed scratch array
- * of this library (GDN_STATIC_SCRATCH_BYTES per device, address looked up
- * once per device with cudaGetSymbolAddress): the call allocates no device
+ * of this library (GDN_STATIC_SCRATCH_BYTES per device, its address looked up
+ * with cudaGetSymbolAddress on every call): the call allocates no device
  * memory, for callers that have no device allocator of their own (a C or FFI
  * host without PyTorch, which would otherwise need a cudaMalloc / cudaFree
  * pair - each synchronising the device - around every call).  Calls that need
@@ -295,9 +295,14 @@ int32_t gdn_mixer_prefill_ws(const gdn_mixer_args* args, void* workspace, int64_
  * are rejected with GDN_ERR_INVALID_ARG.  Every call on a device shares the
  * one scratch array: calls that can run at the same time on a device
  * (different streams, or host threads without ordering between them) race
- * on it and must be serialised by the caller.  Nothing in the scratch needs
- * to be zero or survives a call.  No counterpart in the reference (its
- * PyTorch path takes its temporaries from torch's allocator).
+ * on it and must be serialised by the caller.  The call clears what must
+ * start at zero (the state hand-off flags, by an asynchronous memset on the
+ * call's stream); the rest is written before it is read.  The array occupies
+ * GDN_STATIC_SCRATCH_BYTES on every device where the library's module is
+ * loaded (at library load with CUDA_MODULE_LOADING=EAGER, at its first kernel
+ * launch with the default lazy loading), until the process exits, whether or
+ * not this entry is called.  No counterpart in the reference (its PyTorch
+ * path takes its temporaries from torch's allocator).
  */
 int32_t gdn_mixer_prefill_noalloc(const gdn_mixer_args* args, void* stream);
 
@@ -334,6 +339,31 @@ int32_t gdn_delta_rule(int32_t batch, int32_t seq_len, int32_t num_heads, int32_
 int32_t gdn_causal_conv1d(int32_t batch, int32_t channels, int32_t seq_len, int32_t kernel,
                           int32_t dtype, const void* x, const void* weight, const void* state_in,
                           void* out, void* state_out, int32_t apply_silu, void* stream);
+
+/*
+ * Unit lower triangular solve, the functional boundary of
+ * _solve_unit_lower_triangular (deltanet.py:112-162) and, with rhs NULL,
+ * _invert_unit_lower_triangular_block (deltanet.py:93-109):
+ *   out[i] = (I + tril(ut[i], -1))^-1 rhs[i]       for i < batch
+ * ut [batch, n, n] (its diagonal and upper triangle are ignored), rhs and out
+ * [batch, n, m], float32, contiguous; rhs NULL means the identity (m == n).
+ * fp32 forward substitution; same result as the reference's block-doubling
+ * products up to float rounding.  out must not overlap ut or rhs.
+ */
+int32_t gdn_solve_unit_lower_triangular(const float* ut, const float* rhs, float* out, int64_t batch,
+                                        int32_t n, int32_t m, void* stream);
+
+/*
+ * Gated RMSNorm over the last dimension, the math of
+ * Qwen3_5RMSNormGated.forward (config.py:136-143):
+ *   out = ((weight * round(x * rsqrt(mean(x^2) + eps))) * SiLU(gate)) rounded
+ * to x's dtype, where round() is to x's dtype and the weight product is
+ * rounded to bf16 when x and weight are both bf16 (torch's type promotion).
+ * x, gate, out [rows, dim] contiguous (out in x's dtype), weight [dim].
+ */
+int32_t gdn_rms_norm_gated(const void* x, const void* gate, const void* weight, void* out, int64_t rows,
+                           int32_t dim, float eps, int32_t x_dtype, int32_t gate_dtype,
+                           int32_t weight_dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -8,3 +8,11 @@ if REPO not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+def pytest_terminal_summary(terminalreporter):
+    from tests.helpers import PARITY_REPORT
+    if PARITY_REPORT:
+        terminalreporter.section("parity at the workloads' full sizes")
+        for line in PARITY_REPORT:
+            terminalreporter.write_line(line)

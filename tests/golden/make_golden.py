@@ -1,9 +1,9 @@
 """Generate the golden fixtures by running the reference implementation.
 
-Run in a container that has the reference checkout (read-only) at
-``/root/reference``:
+Run where a checkout of the reference is available (read-only), given by
+``--ref`` or the ``VISIONSTACK_REF`` environment variable:
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <reference checkout>
 
 The reference is plain PyTorch, so it runs here on CPU.  Inputs come from
 ``numpy.random.default_rng`` seeds (``visionstack_b200.workloads``) so the
@@ -48,8 +48,11 @@ def digest(*arrays: np.ndarray) -> str:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("VISIONSTACK_REF"),
+                    help="checkout of the reference (or set VISIONSTACK_REF)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give --ref <reference checkout> or set VISIONSTACK_REF")
     sys.path.insert(0, os.path.join(args.ref, "ShadowBoxer"))
     import torch
 

@@ -1,7 +1,7 @@
 """Generate ``stack_tiny_f32.npz`` / ``stack_tiny_bf16.npz`` by running the reference's text
 stack (ShadowBoxer/models/qwen35/text.py, ``Qwen3_5TextModel``) on the host.
 
-    python tests/golden/make_stack_golden.py [--ref /root/reference]
+    python tests/golden/make_stack_golden.py --ref <reference checkout>
 
 The 4-layer stack of ``visionstack_b200.workloads.STACK_TINY`` (three Gated DeltaNet layers and
 one gated attention layer) gets the seeded parameters of ``make_stack_params`` and runs the calls
@@ -28,8 +28,11 @@ from visionstack_b200 import workloads as W  # noqa: E402
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("VISIONSTACK_REF"),
+                    help="checkout of the reference (or set VISIONSTACK_REF)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give --ref <reference checkout> or set VISIONSTACK_REF")
     sys.path.insert(0, os.path.join(args.ref, "ShadowBoxer"))
     import torch
 

@@ -144,6 +144,27 @@ def test_functional_validation():
                               None) == -1
     assert lib.gdn_causal_conv1d(1, 8, 4, 6, 0, 16, 16, None, 16, None, 1, None) == -2
     assert lib.gdn_causal_conv1d(1, 8, 4, 4, 1, 17, 16, None, 16, None, 1, None) == -3
+    # triangular solve: sizes, the identity needs m == n, alignment, out overlapping ut
+    p = 0x100000
+    assert lib.gdn_solve_unit_lower_triangular(p, p + 0x10000, p + 0x20000, 0, 64, 8, None) == -1
+    assert lib.gdn_solve_unit_lower_triangular(p, None, p + 0x20000, 2, 64, 8, None) == -1
+    assert lib.gdn_solve_unit_lower_triangular(p + 2, None, p + 0x20000, 2, 64, 64, None) == -3
+    assert lib.gdn_solve_unit_lower_triangular(p, None, p + 64, 2, 64, 64, None) == -1
+    assert b"overlap" in lib.gdn_last_error_string()
+    # gated norm: dtype codes, NULL pointers, misaligned bf16 rows
+    assert lib.gdn_rms_norm_gated(p, p, p, p, 4, 128, 1e-6, 7, 1, 1, None) == -2
+    assert lib.gdn_rms_norm_gated(p, None, p, p, 4, 128, 1e-6, 1, 1, 1, None) == -1
+    assert lib.gdn_rms_norm_gated(p + 1, p, p, p, 4, 128, 1e-6, 1, 1, 1, None) == -3
+    assert lib.gdn_rms_norm_gated(p, p, p, p, 0, 128, 1e-6, 1, 1, 1, None) == -1
+
+
+def test_functional_names_of_the_reference_module_are_exported():
+    import visionstack_b200.deltanet as D
+    for name in ("_causal_conv1d_fn", "_chunk_gated_delta_rule", "_recurrent_gated_delta_rule",
+                 "_solve_unit_lower_triangular", "_invert_unit_lower_triangular_block"):
+        assert name in D.__all__ and callable(getattr(D, name))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        D._solve_unit_lower_triangular(torch.eye(4), torch.ones(4, 2))
 
 
 def test_state_dict_matches_reference_layout():

@@ -1,9 +1,13 @@
-"""gdn_mixer_prefill_noalloc: the two-kernel chunked prefill with its scratch
-in the library's fixed device array (no allocation in the call).  Compared,
-bit for bit, with gdn_mixer_prefill_ws (workspace from torch's allocator) on
-two calls in a row with different inputs; oversize calls are rejected.  This
-file is collected last so that it also runs after every other test has used
-the library on the same device."""
+"""gdn_mixer_prefill_noalloc: the chunked prefill with its scratch in the
+library's fixed device array (no allocation in the call), for C / FFI callers
+that have no device allocator.  Compared, bit for bit, with
+gdn_mixer_prefill_ws (workspace from torch's allocator) on two calls in a row
+with different inputs, once with fewer (batch, head) chains than SMs and once
+with more (160 chains: the sequential pass then cuts the chains into runs with
+state hand-offs through flags in the shared scratch, which every call must
+clear again); oversize calls are rejected.  This file is collected last so
+that it also runs after every other test has used the library on the same
+device."""
 from __future__ import annotations
 
 import ctypes
@@ -46,17 +50,19 @@ def test_noalloc_rejects_calls_larger_than_the_static_scratch():
 
 
 @pytest.mark.gpu
-def test_noalloc_matches_workspace_entry_on_two_calls_in_a_row():
+@pytest.mark.parametrize("B,T", [(1, 700), (5, 256)])
+def test_noalloc_matches_workspace_entry_on_two_calls_in_a_row(B, T):
     from tests.helpers import assert_bit_exact
     from tests.test_gpu_mixer import make_layer, mixer_inputs
     shape = W.SHAPE_QWEN
     m, _ = make_layer(shape, "bf16", seed=21)
-    B, T = 1, 700
     dev = torch.device("cuda")
+    if B * shape.num_v_heads > 148:
+        assert torch.cuda.get_device_properties(dev).multi_processor_count < B * shape.num_v_heads
     lib = _lib.load()
     t = lambda a: torch.from_numpy(a).to(dev).to(torch.bfloat16)  # noqa: E731
     for call in range(2):
-        d = mixer_inputs(shape, B, T, "bf16", seed=200 + call, with_state=True)
+        d = mixer_inputs(shape, B, T, "bf16", seed=200 + 10 * B + call, with_state=True)
         ins = (t(d["mixed"]), t(d["z"]), t(d["b"]), t(d["a"]))
         cs_in, S_in = t(d["conv_state"]), torch.from_numpy(d["rec_state"]).to(dev)
         results = []

@@ -11,7 +11,9 @@ from .deltanet import (
     _causal_conv1d_fn,
     _chunk_gated_delta_rule,
     _extract_conv_state_at_offset,
+    _invert_unit_lower_triangular_block,
     _recurrent_gated_delta_rule,
+    _solve_unit_lower_triangular,
 )
 from .slots import StateSlots
 
@@ -24,5 +26,7 @@ __all__ = [
     "_causal_conv1d_fn",
     "_chunk_gated_delta_rule",
     "_extract_conv_state_at_offset",
+    "_invert_unit_lower_triangular_block",
     "_recurrent_gated_delta_rule",
+    "_solve_unit_lower_triangular",
 ]

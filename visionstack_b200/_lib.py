@@ -39,6 +39,8 @@ EXPORTED_SYMBOLS = (
     "gdn_selftest_expired_wait",
     "gdn_attn_decode_workspace_bytes",
     "gdn_attn_decode",
+    "gdn_solve_unit_lower_triangular",
+    "gdn_rms_norm_gated",
 )
 GDN_FLAG_REGISTER_KERNEL = 1
 GDN_FLAG_CUDA_CORE_PREFILL = 2
@@ -134,6 +136,11 @@ def load() -> ctypes.CDLL:
         lib.gdn_mixer_verify_slots.argtypes = [ctypes.POINTER(MixerArgs), _c_void_p, _i32, _c_void_p]
         lib.gdn_accept_slots.restype = _i32
         lib.gdn_accept_slots.argtypes = [_c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p]
+        lib.gdn_solve_unit_lower_triangular.restype = _i32
+        lib.gdn_solve_unit_lower_triangular.argtypes = [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _c_void_p]
+        lib.gdn_rms_norm_gated.restype = _i32
+        lib.gdn_rms_norm_gated.argtypes = [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i32, ctypes.c_float,
+                                           _i32, _i32, _i32, _c_void_p]
         lib.gdn_device_error.restype = _i32
         lib.gdn_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32), _i32]
         _lib = lib

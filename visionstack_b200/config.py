@@ -4,8 +4,9 @@
 text config (ShadowBoxer/models/qwen35/config.py:184-254) so that a config
 built for the reference constructs this layer unchanged; only the DeltaNet
 fields are read here.  ``Qwen3_5RMSNormGated`` keeps the parameter name
-``weight`` of config.py:130-134 for state-dict compatibility; its math runs
-inside the CUDA kernels (epilogue of the token mixer).
+``weight`` of config.py:130-134 for state-dict compatibility; inside the
+layer its math runs in the token-mixer kernels' epilogue, and its
+``forward(hidden_states, gate)`` runs the stand-alone ``gdn_rms_norm_gated``.
 """
 from __future__ import annotations
 
@@ -86,13 +87,42 @@ def _linear(layer: nn.Linear, x: torch.Tensor) -> torch.Tensor:
 
 
 class Qwen3_5RMSNormGated(nn.Module):
-    """Holds the gated-norm weight; the normalisation itself is fused into
-    the token-mixer kernels (the reference math is config.py:136-143)."""
+    """Gated RMSNorm over the last dimension (config.py:130-143).  Inside the
+    DeltaNet layer the normalisation is fused into the token-mixer kernels;
+    ``forward`` is the stand-alone form for other callers and runs
+    ``gdn_rms_norm_gated`` (CUDA tensors only, no CPU path)."""
 
     def __init__(self, hidden_size: int, eps: float = 1e-6):
         super().__init__()
         self.weight = nn.Parameter(torch.ones(hidden_size))
         self.variance_epsilon = eps
+
+    def forward(self, hidden_states: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+        from . import _lib
+        codes = {torch.float32: _lib.GDN_DTYPE_F32, torch.bfloat16: _lib.GDN_DTYPE_BF16}
+        for t in (hidden_states, gate, self.weight):
+            if not t.is_cuda:
+                raise RuntimeError("Qwen3_5RMSNormGated needs CUDA tensors (there is no CPU path)")
+            if t.dtype not in codes:
+                raise TypeError(f"unsupported dtype {t.dtype} (float32 or bfloat16)")
+        dim = hidden_states.shape[-1]
+        if gate.shape != hidden_states.shape or self.weight.shape != (dim,):
+            raise ValueError(f"shapes {tuple(hidden_states.shape)}, gate {tuple(gate.shape)}, "
+                             f"weight {tuple(self.weight.shape)} do not match")
+        x = hidden_states.contiguous()
+        gt = gate.contiguous()
+        w = self.weight.detach().contiguous()
+        out = torch.empty_like(x)
+        rows = x.numel() // max(1, dim)
+        if rows == 0:
+            return out
+        lib = _lib.load()
+        with torch.cuda.device(x.device):
+            _lib.check("gdn_rms_norm_gated", lib.gdn_rms_norm_gated(
+                x.data_ptr(), gt.data_ptr(), w.data_ptr(), out.data_ptr(), rows, dim,
+                float(self.variance_epsilon), codes[x.dtype], codes[gt.dtype], codes[w.dtype],
+                torch.cuda.current_stream(x.device).cuda_stream))
+        return out
 
 
 def q_scale(head_k_dim: int) -> float:

@@ -473,6 +473,43 @@ int32_t gdn_causal_conv1d(int32_t batch, int32_t channels, int32_t seq_len, int3
     return cuda_status(e, "gdn_causal_conv1d launch");
 }
 
+int32_t gdn_solve_unit_lower_triangular(const float* ut, const float* rhs, float* out, int64_t batch, int32_t n,
+                                        int32_t m, void* stream) {
+    if (batch < 1 || n < 1 || m < 1) return fail(GDN_ERR_INVALID_ARG, "batch, n and m must be >= 1");
+    if (batch > 0x7FFFFFFFll) return fail(GDN_ERR_INVALID_ARG, "batch %lld too large", (long long)batch);
+    if (n > 4096 || m > (1 << 20)) return fail(GDN_ERR_INVALID_ARG, "n %d or m %d too large", n, m);
+    if (!ut || !out) return fail(GDN_ERR_INVALID_ARG, "ut and out are required");
+    if (!rhs && m != n) return fail(GDN_ERR_INVALID_ARG, "the inverse (rhs NULL) needs m == n");
+    const void* ptrs[] = {ut, rhs, out};
+    for (const void* ptr : ptrs)
+        if (ptr && !aligned_elem(ptr, GDN_DTYPE_F32)) return fail(GDN_ERR_ALIGNMENT, "misaligned pointer");
+    const int64_t n_out = batch * (int64_t)n * m, n_u = batch * (int64_t)n * n;
+    auto overlaps = [](const float* a, int64_t na, const float* b, int64_t nb) {
+        return a && b && a < b + nb && b < a + na;
+    };
+    if (overlaps(out, n_out, ut, n_u) || overlaps(out, n_out, rhs, n_out))
+        return fail(GDN_ERR_INVALID_ARG, "out must not overlap ut or rhs");
+    const cudaError_t e = gdn::launch_trisolve(ut, rhs, out, batch, n, m, static_cast<cudaStream_t>(stream));
+    return cuda_status(e, "gdn_solve_unit_lower_triangular launch");
+}
+
+int32_t gdn_rms_norm_gated(const void* x, const void* gate, const void* weight, void* out, int64_t rows, int32_t dim,
+                           float eps, int32_t x_dtype, int32_t gate_dtype, int32_t weight_dtype, void* stream) {
+    if (rows < 1 || dim < 1) return fail(GDN_ERR_INVALID_ARG, "rows and dim must be >= 1");
+    if (rows > ((int64_t)1 << 33)) return fail(GDN_ERR_INVALID_ARG, "too many rows");
+    const int32_t dts[] = {x_dtype, gate_dtype, weight_dtype};
+    for (int32_t d : dts)
+        if (d != GDN_DTYPE_F32 && d != GDN_DTYPE_BF16) return fail(GDN_ERR_UNSUPPORTED, "dtype %d", d);
+    if (!x || !gate || !weight || !out) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
+    if (!aligned_elem(x, x_dtype) || !aligned_elem(out, x_dtype) || !aligned_elem(gate, gate_dtype) ||
+        !aligned_elem(weight, weight_dtype))
+        return fail(GDN_ERR_ALIGNMENT, "misaligned pointer");
+    if (!(eps >= 0.f)) return fail(GDN_ERR_INVALID_ARG, "eps must be >= 0");
+    const cudaError_t e = gdn::launch_rms_norm_gated(x, gate, weight, out, rows, dim, eps, x_dtype, gate_dtype,
+                                                     weight_dtype, static_cast<cudaStream_t>(stream));
+    return cuda_status(e, "gdn_rms_norm_gated launch");
+}
+
 int32_t gdn_mixer_prefill_noalloc(const gdn_mixer_args* args, void* stream) {
     const int64_t need = gdn_prefill_workspace_bytes(args);
     if (need < 0) return (int32_t)need;  // invalid arguments, message already set

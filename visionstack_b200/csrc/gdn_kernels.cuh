@@ -97,5 +97,10 @@ cudaError_t launch_prefill(const MixParams& p, const CkptList& ck, int d, int dt
                            cudaStream_t s, bool* supported);
 cudaError_t launch_conv1d(int B, int C, int T, int K, int dtype, const void* x, const void* w,
                           const void* state_in, void* out, void* state_out, int silu, cudaStream_t s);
+// functional boundary (gdn_functional.cu): unit lower triangular solve and the gated RMSNorm
+cudaError_t launch_trisolve(const float* ut, const float* rhs, float* out, long long batch, int n, int m,
+                            cudaStream_t s);
+cudaError_t launch_rms_norm_gated(const void* x, const void* gate, const void* w, void* out, long long rows, int dim,
+                                  float eps, int x_dtype, int gate_dtype, int w_dtype, cudaStream_t s);
 
 }  // namespace gdn

@@ -116,6 +116,50 @@ def _causal_conv1d_fn(hidden_states: torch.Tensor, weight: torch.Tensor, bias: O
     return res
 
 
+def _solve_unit_lower_triangular(ut_system: torch.Tensor, rhs: torch.Tensor) -> torch.Tensor:
+    """(I + tril(ut_system, -1))^-1 @ rhs over the last two dimensions, signature of
+    deltanet.py:112-114; runs ``gdn_solve_unit_lower_triangular`` (fp32 forward
+    substitution; the batch dimensions broadcast as in the reference's matmul)."""
+    dev = _require_cuda(ut_system, rhs)
+    n = ut_system.shape[-1]
+    if ut_system.shape[-2] != n or rhs.shape[-2] != n:
+        raise ValueError(f"shapes {tuple(ut_system.shape)} and {tuple(rhs.shape)} do not form an n x n system")
+    m = rhs.shape[-1]
+    batch = torch.broadcast_shapes(ut_system.shape[:-2], rhs.shape[:-2])
+    u = ut_system.to(torch.float32).expand(*batch, n, n).contiguous()
+    r = rhs.to(torch.float32).expand(*batch, n, m).contiguous()
+    out = torch.empty((*batch, n, m), dtype=torch.float32, device=dev)
+    nb = max(1, int(torch.Size(batch).numel()))
+    if out.numel() == 0:
+        return out.to(torch.result_type(ut_system, rhs))
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check("gdn_solve_unit_lower_triangular",
+                   lib.gdn_solve_unit_lower_triangular(u.data_ptr(), r.data_ptr(), out.data_ptr(), nb, n, m,
+                                                       _stream(dev)))
+    return out.to(torch.result_type(ut_system, rhs))
+
+
+def _invert_unit_lower_triangular_block(u_blk: torch.Tensor) -> torch.Tensor:
+    """(I + tril(u_blk, -1))^-1 over the last two dimensions, signature of
+    deltanet.py:93; ``gdn_solve_unit_lower_triangular`` with the identity as
+    right-hand side."""
+    dev = _require_cuda(u_blk)
+    n = u_blk.shape[-1]
+    if u_blk.shape[-2] != n:
+        raise ValueError(f"shape {tuple(u_blk.shape)} is not square")
+    u = u_blk.to(torch.float32).contiguous()
+    out = torch.empty_like(u)
+    nb = max(1, int(torch.Size(u.shape[:-2]).numel()))
+    if out.numel() == 0:
+        return out.to(u_blk.dtype)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check("gdn_solve_unit_lower_triangular",
+                   lib.gdn_solve_unit_lower_triangular(u.data_ptr(), None, out.data_ptr(), nb, n, n, _stream(dev)))
+    return out.to(u_blk.dtype)
+
+
 def _delta_rule(query, key, value, g, beta, initial_state, output_final_state, use_qk_l2norm,
                 checkpoint_positions, checkpoint_states_out, past_seen_tokens, chunked: bool):
     dt = query.dtype if query.dtype in _DTYPES else torch.float32
@@ -543,5 +587,7 @@ __all__ = [
     "_causal_conv1d_fn",
     "_recurrent_gated_delta_rule",
     "_chunk_gated_delta_rule",
+    "_solve_unit_lower_triangular",
+    "_invert_unit_lower_triangular_block",
     "Qwen3_5GatedDeltaNet",
 ]
