@@ -50,11 +50,14 @@ extern "C" {
 #define GDN_DTYPE_BF16 1
 
 /* gdn_mixer_args.flags: run the register-tile token-by-token kernel even
- * where the bulk-copy pipelined one applies, and the CUDA-core chunked kernel
- * even where the tensor-core one applies (same results up to float rounding;
- * for testing and comparison). */
+ * where the bulk-copy pipelined one applies, the CUDA-core chunked kernel even
+ * where the tensor-core one applies, and (gdn_mixer_prefill_ws) the two-kernel
+ * chunked form with its preparation pass through the workspace instead of the
+ * single fused kernel (same results up to float rounding; for testing and
+ * comparison). */
 #define GDN_FLAG_REGISTER_KERNEL 1
 #define GDN_FLAG_CUDA_CORE_PREFILL 2
+#define GDN_FLAG_TWO_KERNEL_PREFILL 4
 
 /* Bits of the device error word (gdn_device_error). */
 #define GDN_DEVERR_TMA_TIMEOUT 0x1u
@@ -257,26 +260,34 @@ int32_t gdn_mixer_prefill(const gdn_mixer_args* args, void* stream);
 /*
  * Device workspace, in bytes, that gdn_mixer_prefill_ws needs for these
  * arguments: 0 when the call takes a path without workspace, a negative
- * GDN_ERR_* code when the arguments are invalid.  At batch 8 x 8192 tokens,
- * 16 / 32 heads of 128 this is about 2.2 GB (the conv outputs in bf16 plus a
- * 32 KB pair of 64x64 tf32 matrices per chunk and value head).  When there
- * are more (batch, value head) chains than the current device has SMs it adds
- * one state-sized hand-off slot per SM, so ask with the device current that
- * will run the call.
+ * GDN_ERR_* code when the arguments are invalid.  The default (fused) form
+ * needs workspace only when there are more (batch, value head) chains than
+ * the current device has SMs: one state-sized hand-off slot (64 KB) and flag
+ * per SM, about 9.7 MB on a 148-SM B200, whatever the sequence length.  With
+ * GDN_FLAG_TWO_KERNEL_PREFILL it is the two-kernel form's workspace (about
+ * 2.2 GB at batch 8 x 8192 tokens, 16 / 32 heads of 128: the conv outputs in
+ * bf16 plus a 32 KB pair of 64x64 tf32 matrices per chunk and value head,
+ * plus the hand-off slots).  Ask with the device current that will run the
+ * call.
  */
 int64_t gdn_prefill_workspace_bytes(const gdn_mixer_args* args);
 
 /*
- * Chunked token mixer in two kernels (prefill), same arguments, results and
- * cache semantics as gdn_mixer_prefill.  A fully parallel preparation kernel
- * (one CTA per batch row, key head and chunk of 64 tokens) computes what does
- * not depend on the recurrent state - conv + SiLU, L2-norm factors, gates,
- * and each chunk's (I + A)^-1 and masked Q K^T (deltanet.py:266-343) - into
- * `workspace`; the sequential kernel (one CTA per batch row and value head)
- * then carries the state through the chunks (deltanet.py:345-389) with every
- * state product on the tensor cores.  `workspace` (device, 16-byte aligned,
- * at least gdn_prefill_workspace_bytes, not overlapping any other argument)
- * is scratch: nothing in it needs to be initialised or survives the call.
+ * Chunked token mixer (prefill) with a caller workspace, same arguments,
+ * results and cache semantics as gdn_mixer_prefill.  By default one fused
+ * kernel (one CTA per batch row and value head, or one cooperative wave of
+ * one CTA per SM when there are more chains than SMs) carries the state
+ * through the chunks (deltanet.py:345-389) with every state product on the
+ * tensor cores, while a producer warpgroup pair in the same CTA computes, two
+ * chunks ahead, what does not depend on the state - conv + SiLU, L2-norm
+ * factors, gates, and each chunk's (I + A)^-1 and masked Q K^T
+ * (deltanet.py:266-343) - in shared memory.  With GDN_FLAG_TWO_KERNEL_PREFILL
+ * a fully parallel preparation kernel (one CTA per batch row, key head and
+ * chunk of 64 tokens) writes that part to `workspace` first and a sequential
+ * kernel reads it back.  `workspace` (device, 16-byte aligned, at least
+ * gdn_prefill_workspace_bytes, not overlapping any other argument; may be
+ * NULL when that is 0) is scratch: the call clears what must start at zero
+ * and nothing in it survives the call.
  * Shapes the two-kernel form does not cover (activations other than bf16,
  * head dims other than 128, conv_kernel != 4, num_v_heads / num_k_heads not
  * in {1, 2, 4}, misaligned inputs) or GDN_FLAG_CUDA_CORE_PREFILL run

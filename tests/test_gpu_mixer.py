@@ -46,7 +46,8 @@ def mixer_inputs(shape: W.LayerShape, B: int, T: int, dtype: str, seed: int, wit
     return d
 
 
-def run_ours(m, shape, d, dtype, token_by_token, offsets=(), register_kernel=False, fused_prefill=False):
+def run_ours(m, shape, d, dtype, token_by_token, offsets=(), register_kernel=False, fused_prefill=False,
+             two_kernel_prefill=False):
     dev = torch.device("cuda")
     t = lambda a: torch.from_numpy(a).to(dev).to(TDT[dtype])  # noqa: E731
     B, T = d["mixed"].shape[:2]
@@ -62,7 +63,8 @@ def run_ours(m, shape, d, dtype, token_by_token, offsets=(), register_kernel=Fal
     out = m.mixer(t(d["mixed"]), t(d["z"]), t(d["b"]), t(d["a"]), conv_state=cs, rec_state=rs,
                   conv_state_out=cs_out, rec_state_out=rs_out, checkpoint_offsets=offsets,
                   state_checkpoints=st_ck, conv_checkpoints=cv_ck, token_by_token=token_by_token,
-                  register_kernel=register_kernel, fused_prefill=fused_prefill)
+                  register_kernel=register_kernel, fused_prefill=fused_prefill,
+                  two_kernel_prefill=two_kernel_prefill)
     torch.cuda.synchronize()
     return out, cs_out, rs_out, st_ck, cv_ck
 
@@ -246,28 +248,35 @@ def test_mixer_plan_matches_mixer():
     assert torch.equal(o1, o2) and torch.equal(S1, S2) and torch.equal(cs1, cs2)
 
 
-@pytest.mark.parametrize("fused", [False, True])
+PREFILL_FORMS = {"default": {}, "two_kernel": {"two_kernel_prefill": True}, "single_kernel": {"fused_prefill": True}}
+
+
+@pytest.mark.parametrize("form", list(PREFILL_FORMS))
 @pytest.mark.parametrize("B,T,with_state,offsets", [
     (2, 200, True, (1, 37, 64, 100, 128, 199, 200)),
     (1, 64, False, (64,)),
     (3, 7, True, (3, 7)),
     (1, 513, False, (256, 500, 513)),
+    (2, 130, True, (65, 66, 67, 129)),
 ])
-def test_tensor_core_prefill_vs_oracle(B, T, with_state, offsets, fused):
+def test_tensor_core_prefill_vs_oracle(B, T, with_state, offsets, form):
     """The tcgen05 chunked kernels (bf16, head dim 128) against the oracle, with
     sub-chunk and chunk-boundary checkpoints, ragged last chunks and T < 64:
-    the two-kernel form (parallel preparation + sequential pass, the default)
-    and the single fused kernel."""
+    the default single kernel with its in-kernel preparation two chunks ahead,
+    the two-kernel form (parallel preparation pass through a workspace, then
+    the sequential pass) and the older single kernel that prepares each chunk
+    on the state's critical path."""
     from visionstack_b200 import _lib
     shape = W.LayerShape(256, 2, 4, 128, 128)
     m, params = make_layer(shape, "bf16")
     d = mixer_inputs(shape, B, T, "bf16", seed=40 + T, with_state=with_state)
-    check(shape, "bf16", run_ours(m, shape, d, "bf16", False, offsets, fused_prefill=fused),
-          run_oracle(shape, params, d, "bf16", chunk=True, offsets=offsets), offsets, f"tc T{T}")
+    check(shape, "bf16", run_ours(m, shape, d, "bf16", False, offsets, **PREFILL_FORMS[form]),
+          run_oracle(shape, params, d, "bf16", chunk=True, offsets=offsets), offsets, f"tc T{T} {form}")
     assert _lib.device_error() == 0
 
 
-def test_two_kernel_prefill_chains_split_across_ctas():
+@pytest.mark.parametrize("form", ["default", "two_kernel"])
+def test_prefill_chains_split_across_ctas(form):
     """More (batch, value head) chains than SMs: the sequential kernel runs one CTA per SM,
     cuts the chains' chunks into equal runs and hands the state from one CTA to the next
     (chain heads, tails and whole chains; checkpoints on both sides of a hand-off)."""
@@ -278,13 +287,14 @@ def test_two_kernel_prefill_chains_split_across_ctas():
     offs = (1, 37, 64, 100, 128, 199, 200)
     m, params = make_layer(shape, "bf16")
     d = mixer_inputs(shape, B, T, "bf16", seed=77, with_state=True)
-    check(shape, "bf16", run_ours(m, shape, d, "bf16", False, offs),
-          run_oracle(shape, params, d, "bf16", chunk=True, offsets=offs), offs, "split chains")
+    check(shape, "bf16", run_ours(m, shape, d, "bf16", False, offs, **PREFILL_FORMS[form]),
+          run_oracle(shape, params, d, "bf16", chunk=True, offsets=offs), offs, f"split chains {form}")
     assert _lib.device_error() == 0
 
 
+@pytest.mark.parametrize("form", ["default", "two_kernel"])
 @pytest.mark.parametrize("rep", [1, 4])
-def test_two_kernel_prefill_gqa_groupings(rep):
+def test_prefill_gqa_groupings(rep, form):
     """Key heads shared by 1 or 4 value heads (the preparation pass handles
     every value head of a key head in one CTA)."""
     from visionstack_b200 import _lib
@@ -292,8 +302,8 @@ def test_two_kernel_prefill_gqa_groupings(rep):
     m, params = make_layer(shape, "bf16")
     d = mixer_inputs(shape, 2, 150, "bf16", seed=60 + rep, with_state=True)
     offs = (10, 64, 150)
-    check(shape, "bf16", run_ours(m, shape, d, "bf16", False, offs),
-          run_oracle(shape, params, d, "bf16", chunk=True, offsets=offs), offs, f"rep{rep}")
+    check(shape, "bf16", run_ours(m, shape, d, "bf16", False, offs, **PREFILL_FORMS[form]),
+          run_oracle(shape, params, d, "bf16", chunk=True, offsets=offs), offs, f"rep{rep} {form}")
     assert _lib.device_error() == 0
 
 
@@ -305,15 +315,15 @@ def test_tensor_core_prefill_matches_cuda_core_kernel():
     t = lambda a: torch.from_numpy(a).to(dev).to(torch.bfloat16)  # noqa: E731
     S0 = torch.from_numpy(d["rec_state"]).to(dev)
     outs = []
-    for kw in ({}, {"fused_prefill": True}, {"cuda_core_prefill": True}):
+    for kw in ({}, {"fused_prefill": True}, {"cuda_core_prefill": True}, {"two_kernel_prefill": True}):
         S = torch.empty_like(S0)
         o = m.mixer(t(d["mixed"]), t(d["z"]), t(d["b"]), t(d["a"]), conv_state=t(d["conv_state"]), rec_state=S0,
                     rec_state_out=S, token_by_token=False, **kw)
         outs.append((o, S))
     torch.cuda.synchronize()
-    for i, name in ((1, "fused"), (2, "cuda-core")):
-        assert_bf16_close(outs[0][0], outs[i][0], f"two-kernel vs {name} out", scale=2.0)
-        assert_state_close(outs[0][1], outs[i][1], f"two-kernel vs {name} state", scale=2.0)
+    for i, name in ((1, "single-kernel"), (2, "cuda-core"), (3, "two-kernel")):
+        assert_bf16_close(outs[0][0], outs[i][0], f"default vs {name} out", scale=2.0)
+        assert_state_close(outs[0][1], outs[i][1], f"default vs {name} state", scale=2.0)
 
 
 def test_prefill_plan_matches_mixer():

@@ -37,12 +37,17 @@ def _fake_args(B: int, T: int):
 
 def test_noalloc_rejects_calls_larger_than_the_static_scratch():
     lib = _lib.load()
+    # the default (fused) prefill needs at most one hand-off state per SM, at any length
+    assert 0 <= lib.gdn_prefill_workspace_bytes(ctypes.byref(_fake_args(8, 8192))) <= 148 * (64 << 10) + 4096
+    # the two-kernel form keeps every chunk's preparation in the workspace: far beyond the scratch
     big = _fake_args(8, 8192)
+    big.flags = _lib.GDN_FLAG_TWO_KERNEL_PREFILL
     need = lib.gdn_prefill_workspace_bytes(ctypes.byref(big))
     assert need > _lib.GDN_STATIC_SCRATCH_BYTES
     assert lib.gdn_mixer_prefill_noalloc(ctypes.byref(big), None) == -1
     assert b"static scratch" in lib.gdn_last_error_string()
     small = _fake_args(1, 512)
+    small.flags = _lib.GDN_FLAG_TWO_KERNEL_PREFILL
     assert 0 < lib.gdn_prefill_workspace_bytes(ctypes.byref(small)) <= _lib.GDN_STATIC_SCRATCH_BYTES
     bad = _fake_args(1, 512)
     bad.batch = 0
@@ -50,8 +55,9 @@ def test_noalloc_rejects_calls_larger_than_the_static_scratch():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("flags", [0, _lib.GDN_FLAG_TWO_KERNEL_PREFILL], ids=["fused", "two_kernel"])
 @pytest.mark.parametrize("B,T", [(1, 700), (5, 256)])
-def test_noalloc_matches_workspace_entry_on_two_calls_in_a_row(B, T):
+def test_noalloc_matches_workspace_entry_on_two_calls_in_a_row(B, T, flags):
     from tests.helpers import assert_bit_exact
     from tests.test_gpu_mixer import make_layer, mixer_inputs
     shape = W.SHAPE_QWEN
@@ -70,14 +76,17 @@ def test_noalloc_matches_workspace_entry_on_two_calls_in_a_row(B, T):
             out = torch.full((B, T, shape.value_dim), float("nan"), dtype=torch.bfloat16, device=dev)
             S = torch.full_like(S_in, float("nan"))
             cs = torch.zeros_like(cs_in)
-            args, out, keep = m._mixer_args(*ins, cs_in, S_in, cs, S, out, 0)
+            args, out, keep = m._mixer_args(*ins, cs_in, S_in, cs, S, out, flags)
             nbytes = lib.gdn_prefill_workspace_bytes(ctypes.byref(args))
-            assert 0 < nbytes <= _lib.GDN_STATIC_SCRATCH_BYTES
+            assert 0 <= nbytes <= _lib.GDN_STATIC_SCRATCH_BYTES
+            if B * shape.num_v_heads > 148:  # state hand-offs between CTAs: their flags live in the scratch
+                assert nbytes > 0
             stream = torch.cuda.current_stream(dev).cuda_stream
             if entry == "ws":
-                ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+                ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
                 _lib.check("gdn_mixer_prefill_ws",
-                           lib.gdn_mixer_prefill_ws(ctypes.byref(args), ws.data_ptr(), nbytes, stream))
+                           lib.gdn_mixer_prefill_ws(ctypes.byref(args), ws.data_ptr() if nbytes else None, nbytes,
+                                                    stream))
             else:
                 _lib.check("gdn_mixer_prefill_noalloc", lib.gdn_mixer_prefill_noalloc(ctypes.byref(args), stream))
             torch.cuda.synchronize()

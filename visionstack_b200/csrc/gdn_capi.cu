@@ -80,7 +80,7 @@ int32_t validate_mixer(const gdn_mixer_args* a, gdn::MixParams* p, gdn::CkptList
     if (a->act_dtype != GDN_DTYPE_F32 && a->act_dtype != GDN_DTYPE_BF16)
         return fail(GDN_ERR_UNSUPPORTED, "act_dtype %d", a->act_dtype);
     if (!(a->norm_eps >= 0.0f)) return fail(GDN_ERR_INVALID_ARG, "norm_eps must be >= 0");
-    if (a->flags & ~(GDN_FLAG_REGISTER_KERNEL | GDN_FLAG_CUDA_CORE_PREFILL))
+    if (a->flags & ~(GDN_FLAG_REGISTER_KERNEL | GDN_FLAG_CUDA_CORE_PREFILL | GDN_FLAG_TWO_KERNEL_PREFILL))
         return fail(GDN_ERR_INVALID_ARG, "unknown flags 0x%x", a->flags);
     if (!a->mixed_qkv || !a->z || !a->a || !a->b || !a->conv_weight || !a->A_log || !a->dt_bias ||
         !a->norm_weight || !a->out)
@@ -232,7 +232,8 @@ int32_t gdn_device_error(uint32_t* flags_out, int32_t clear) {
     const unsigned int words[] = {gdn::decode_tma_device_error(clear != 0), gdn::umma_device_error(clear != 0),
                                   gdn::prefill_tc_device_error(clear != 0), gdn::slots_device_error(clear != 0),
                                   gdn::prefill_prep_device_error(clear != 0),
-                                  gdn::prefill_seq_device_error(clear != 0)};
+                                  gdn::prefill_seq_device_error(clear != 0),
+                                  gdn::prefill_fused_device_error(clear != 0)};
     uint32_t all = 0;
     for (unsigned int w : words) {
         if (w == 0xFFFFFFFFu) return fail(GDN_ERR_CUDA, "could not read the device error word");
@@ -261,10 +262,15 @@ int64_t gdn_prefill_workspace_bytes(const gdn_mixer_args* args) {
     if ((args->flags & GDN_FLAG_CUDA_CORE_PREFILL) || !gdn::prefill_prep_supported(p, args->head_k_dim,
                                                                                  args->act_dtype))
         return 0;
-    size_t off[6];
     ok();
-    return (int64_t)gdn::prefill_ws_layout(args->batch, args->seq_len, args->num_k_heads, args->num_v_heads,
-                                           args->head_k_dim, handoff_slots(args), off);
+    if (args->flags & GDN_FLAG_TWO_KERNEL_PREFILL) {
+        size_t off[6];
+        return (int64_t)gdn::prefill_ws_layout(args->batch, args->seq_len, args->num_k_heads, args->num_v_heads,
+                                               args->head_k_dim, handoff_slots(args), off);
+    }
+    const int n_hs = handoff_slots(args);
+    size_t off[2];
+    return n_hs > 0 ? (int64_t)gdn::prefill_fused_ws_layout(n_hs, off) : 0;
 }
 
 int32_t gdn_mixer_prefill_ws(const gdn_mixer_args* args, void* workspace, int64_t workspace_bytes, void* stream) {
@@ -275,6 +281,24 @@ int32_t gdn_mixer_prefill_ws(const gdn_mixer_args* args, void* workspace, int64_
     if ((args->flags & GDN_FLAG_CUDA_CORE_PREFILL) || !gdn::prefill_prep_supported(p, args->head_k_dim,
                                                                                  args->act_dtype))
         return gdn_mixer_prefill(args, stream);  // needs no workspace
+    if (!(args->flags & GDN_FLAG_TWO_KERNEL_PREFILL)) {
+        // the fused kernel: workspace only for the state hand-offs of split mode
+        const int n_hs = handoff_slots(args);
+        size_t off[2];
+        const size_t need = n_hs > 0 ? gdn::prefill_fused_ws_layout(n_hs, off) : 0;
+        if (need > 0) {
+            if (!workspace || workspace_bytes < 0 || (size_t)workspace_bytes < need)
+                return fail(GDN_ERR_INVALID_ARG, "workspace of %lld bytes needed (got %lld)", (long long)need,
+                            (long long)workspace_bytes);
+            if (!aligned16(workspace)) return fail(GDN_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
+        }
+        unsigned char* base = static_cast<unsigned char*>(workspace);
+        float* hs = need > 0 ? reinterpret_cast<float*>(base + off[0]) : nullptr;
+        int* hflag = need > 0 ? reinterpret_cast<int*>(base + off[1]) : nullptr;
+        const cudaError_t e =
+            gdn::launch_prefill_fused(p, ck, hs, hflag, need > 0 ? n_hs : 0, static_cast<cudaStream_t>(stream));
+        return cuda_status(e, "gdn_mixer_prefill_ws fused launch");
+    }
     size_t off[6];
     const int n_hs = handoff_slots(args);
     const size_t need = gdn::prefill_ws_layout(args->batch, args->seq_len, args->num_k_heads, args->num_v_heads,

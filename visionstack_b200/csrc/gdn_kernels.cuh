@@ -91,6 +91,11 @@ cudaError_t launch_prefill_prep(const MixParams& p, const PrefillWs& ws, cudaStr
 unsigned int prefill_prep_device_error(bool clear);
 cudaError_t launch_prefill_seq(const MixParams& p, const CkptList& ck, const PrefillWs& ws, cudaStream_t s);
 unsigned int prefill_seq_device_error(bool clear);
+// single fused chunked prefill (gdn_prefill_fused.cu): workspace = n_hs hand-off states + flags
+size_t prefill_fused_ws_layout(int n_hs, size_t off[2]);
+cudaError_t launch_prefill_fused(const MixParams& p, const CkptList& ck, float* hs, int* hflag, int n_hs,
+                                 cudaStream_t s);
+unsigned int prefill_fused_device_error(bool clear);
 // address of the fixed prefill scratch on the current device (looked up once per device)
 cudaError_t static_prefill_scratch(void** addr);
 cudaError_t launch_prefill(const MixParams& p, const CkptList& ck, int d, int dtype, bool mixer,

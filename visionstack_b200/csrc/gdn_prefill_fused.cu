@@ -91,7 +91,7 @@ constexpr int B_RAWQK = 0,   // 3: raw q/k rows of buffer i landed
     B_KQ = 11,               // 3: conv'd [k;q] rows and vectors of buffer i ready (1 arrival)
     B_VR = 14,               // 2: conv'd v rows ready (1 arrival)
     B_TPR = 16,              // 2: T / P images ready (1 arrival)
-    B_GPFREE = 18;           // [G; P0] copied out of tensor memory (1 arrival)
+    B_GPFREE = 18;           // [G; P0] copied out of tensor memory (256 arrivals)
 
 using TA = __nv_bfloat16;
 
@@ -181,3 +181,934 @@ __device__ __forceinline__ uint32_t conv_silu_pair(__nv_bfloat162 x0, __nv_bfloa
     return bf2_bits(__fdividef(ca, 1.0f + __expf(-ca)), __fdividef(cb, 1.0f + __expf(-cb)));
 }
 __device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
+
+struct FusedMaps {
+    CUtensorMap qk;    // raw mixed rows, box 64 channels x 64 tokens, 128-byte swizzle
+    CUtensorMap v;     // raw mixed rows, box 128 channels x 64 tokens
+    CUtensorMap hist;  // raw mixed rows, box 64 channels x 4 tokens
+    CUtensorMap z;     // z rows, box 128 x 64
+    CUtensorMap out;   // output rows, box 128 x 64
+};
+
+__global__ void __launch_bounds__(NT, 1)
+    prefill_fused_kernel(const MixParams p, const CkptList ck, float* __restrict__ hs, int* __restrict__ hflag,
+                         const __grid_constant__ FusedMaps maps, const int split) {
+    extern __shared__ unsigned char raw[];
+    const uint32_t raw_addr = smem_u32(raw);
+    unsigned char* sm = raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+    const uint32_t sb = smem_u32(sm);
+    float* scr = reinterpret_cast<float*>(sm + R_SCR);
+    float* sNW = scr + S_NW;
+    float* sPart = scr + S_PART;
+    float* sRstd = scr + S_RSTD;
+    float* sF = scr + S_F;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + R_BAR);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + R_BAR + NBAR * 8);
+    auto bar = [&](int i) { return smem_u32(&bars[i]); };
+    auto vecs = [&](int cc) { return reinterpret_cast<float*>(sm + R_VEC) + VEC_FLOATS * (cc % NQK); };
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int wg = warp >> 2, q4 = warp & 3;
+    const bool main_grp = tid < NMAIN;
+    const int dv = 32 * q4 + lane;  // this thread's tensor-memory lane
+    const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
+    const int NCg = (p.T + C - 1) / C;  // chunks of a chain
+    const int chains = p.B * p.Hv;
+    const int conv_dim = 2 * p.Hk * D + p.Hv * D;
+
+    if (warp == 0) {
+        umma::tmem_alloc(smem_u32(tslot), T_COLS);
+        umma::tmem_relinquish();
+    }
+    if (tid == 0) {
+        prefetch_tmap(&maps.qk);
+        prefetch_tmap(&maps.v);
+        prefetch_tmap(&maps.hist);
+        prefetch_tmap(&maps.z);
+        prefetch_tmap(&maps.out);
+    }
+    if (tid < D) sNW[tid] = Act<TA>::ldg(static_cast<const TA*>(p.normw) + tid);
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = *tslot;
+
+    // Split mode (more chains than CTAs): the chains' chunks laid end to end are cut into
+    // gridDim.x equal runs.  A run holds at most a chain's last chunks (its tail), whole chains
+    // and a chain's first chunks (its head); the CTA does the head first and the tail last, so
+    // the head of a chain (at the previous CTA's start) is done long before its tail begins.
+    // The state crosses in hand-off slot k (between CTAs k and k + 1), released by a flag.
+    long long lo = 0, hi = 0;
+    int first = blockIdx.x, last = blockIdx.x;
+    if (split) {
+        const long long total = (long long)chains * NCg;
+        const long long L = (total + gridDim.x - 1) / gridDim.x;
+        lo = (long long)blockIdx.x * L;
+        hi = lo + L < total ? lo + L : total;
+        first = (int)(lo / NCg);
+        last = (int)((hi - 1) / NCg);
+    }
+    auto piece_of = [&](int j, int& cs, int& ce) {
+        if (!split) {
+            cs = 0;
+            ce = NCg;
+            return;
+        }
+        const long long a0 = (long long)j * NCg;
+        cs = (int)((lo > a0 ? lo : a0) - a0);
+        ce = (int)((hi < a0 + NCg ? hi : a0 + NCg) - a0);
+    };
+    int cs_first, ce_first, cs_last, ce_last;
+    piece_of(first, cs_first, ce_first);
+    piece_of(last, cs_last, ce_last);
+    const bool has_head = split && hi > lo && ce_last < NCg;
+    const bool has_tail = split && hi > lo && cs_first > 0 && !(has_head && first == last);
+    const int npieces = split ? (hi > lo ? last - first + 1 : 0) : 1;
+    bool cta_failed = false;
+    for (int pi = 0; pi < npieces && !cta_failed; ++pi) {
+    int chain = first;
+    if (split) {
+        const int k = pi - (has_head ? 1 : 0);
+        const int n_rest = npieces - (has_head ? 1 : 0);
+        if (has_head && pi == 0) chain = last;
+        else if (has_tail) chain = k < n_rest - 1 ? first + 1 + k : first;
+        else chain = first + k;
+    }
+    int c_base, c_end;
+    piece_of(chain, c_base, c_end);
+    const int NC = c_end - c_base;
+    const int in_slot = c_base > 0 ? (int)blockIdx.x - 1 : -1;
+    const int out_slot = c_end < NCg ? (int)blockIdx.x : -1;
+    const int bh = chain;
+    const int b = bh / p.Hv, h = bh - (bh / p.Hv) * p.Hv;
+    const int rep = p.Hv / p.Hk, kh = h / rep;
+
+    if (tid == 0) {
+        if (pi > 0)
+            for (int i = 0; i < NBAR; ++i) mbar_inval(bar(i));
+        // every producer / output thread arrives on o_free and gp_free; one thread on the others
+        for (int i = 0; i < NBAR; ++i) mbar_init(bar(i), (i == B_OFREE || i == B_GPFREE) ? NT - NMAIN : 1);
+        fence_mbar_init();
+    }
+    if (c_base == 0) write_conv_windows<TA, D, D, NT>(p, ck, b, h, kh, rep);
+    bool hand_ok = true;
+    if (in_slot >= 0 && tid == 0) hand_ok = wait_flag_bounded(hflag + in_slot);
+    umma::fence_before_sync();
+    if (__syncthreads_or(!hand_ok)) {
+        cta_failed = true;
+        break;
+    }
+    umma::fence_after_sync();
+
+    // initial state, transposed: lane dv, column dk (warpgroup wg: dk 32 wg .. 32 wg + 31) in the
+    // fp32 master, and its bf16 hi / lo operand in the same 32 columns of the operand region
+    if (main_grp) {
+        const int c0 = 32 * wg;
+        const float* src = in_slot >= 0 ? hs + (size_t)in_slot * D * D
+                                         : (p.S_in ? p.S_in + (size_t)bh * D * D : nullptr);
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = src ? __ldcg(src + (size_t)(c0 + j) * D + dv) : 0.f;
+        umma::tmem_st32(tmem + lane_base + C_MS + c0, v);
+        store_split32(tmem + lane_base + C_OP + c0, v);
+        umma::tmem_wait_st();
+    }
+    const int v_ch = 2 * p.Hk * D + h * D;  // first v channel of this value head
+    // input copies of chunk cc of the piece: raw [k;q] rows + their history into buffer cc % 3,
+    // raw v rows + history into buffer cc % 2, z rows into the z tile
+    auto issue_qk = [&](int cc) {
+        const int t0 = (c_base + cc) * C;
+        const uint32_t dst = sb + R_QK + QK_BYTES * (uint32_t)(cc % NQK), hb = sb + R_HQK + 4 * HATOM * (cc % NQK);
+        const uint32_t br = bar(B_RAWQK + cc % NQK);
+        mbar_arrive_expect_tx(br, QK_BYTES + 4 * HATOM);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            tma_load_3d(dst + 16384u * j, &maps.qk, p.Hk * D + kh * D + 64 * j, t0, b, br);          // k
+            tma_load_3d(dst + 16384u * j + 8192u, &maps.qk, kh * D + 64 * j, t0, b, br);             // q
+            tma_load_3d(hb + HATOM * j, &maps.hist, kh * D + 64 * j, t0 - (int)HROWS, b, br);        // q history
+            tma_load_3d(hb + HATOM * (2 + j), &maps.hist, p.Hk * D + kh * D + 64 * j, t0 - (int)HROWS, b, br);
+        }
+    };
+    auto issue_v = [&](int cc) {
+        const int t0 = (c_base + cc) * C;
+        const uint32_t br = bar(B_RAWV + cc % NVB), hb = sb + R_HV + 2 * HATOM * (cc % NVB);
+        mbar_arrive_expect_tx(br, V_BYTES + 2 * HATOM);
+        tma_load_3d(sb + R_V + V_BYTES * (uint32_t)(cc % NVB), &maps.v, v_ch, t0, b, br);
+        tma_load_3d(hb, &maps.hist, v_ch, t0 - (int)HROWS, b, br);
+        tma_load_3d(hb + HATOM, &maps.hist, v_ch + 64, t0 - (int)HROWS, b, br);
+    };
+    auto issue_z = [&](int cc) {
+        mbar_arrive_expect_tx(bar(B_Z), (uint32_t)C * D * 2u);
+        tma_load_3d(sb + R_Z, &maps.z, h * D, (c_base + cc) * C, b, bar(B_Z));
+    };
+    if (tid == NMAIN) {
+        issue_qk(0);
+        if (NC > 1) issue_qk(1);
+        if (NC > 2) issue_qk(2);
+        issue_v(0);
+        if (NC > 1) issue_v(1);
+        issue_z(0);
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    bool failed = false;
+    if (main_grp) {
+        // ======================= state path (warpgroups 0-1) =======================
+        const uint32_t idesc_c = umma::idesc_tf32(128, 64, 0, 0);
+        const uint32_t idesc_b = umma::idesc_bf16(128, 64, 0, 0);
+        const uint32_t idesc_e = umma::idesc_bf16(128, 128, 0, 1);
+        uint32_t mma_phase = 0;
+        bool mma_pending = false;
+        int ck_i = 0;  // first checkpoint past the piece's start (earlier ones belong to the head)
+        while (ck_i < ck.n && ck.off[ck_i] <= c_base * C) ++ck_i;
+        // A bounded wait that runs out marks this thread bad; the threads agree on it once per
+        // chunk and leave together.  Until then a bad thread keeps going on stale data: every
+        // address it touches is fixed by the chunk index, never by data.
+        bool bad = false;
+        auto mma_wait = [&]() {
+            const bool ok = mbar_wait_bounded(bar(B_MMA), mma_phase & 1u, GDN_DEVERR_MMA_TIMEOUT);
+            ++mma_phase;
+            umma::fence_after_sync();
+            bad |= !ok;
+            if (ok) mma_pending = false;
+        };
+        auto wait_phase = [&](uint32_t br, int phase) {
+            bad |= !mbar_wait_bounded(br, (uint32_t)phase & 1u, GDN_DEVERR_TMA_TIMEOUT);
+        };
+        auto stores_to_warp0 = [&]() {
+            umma::fence_before_sync();
+            if (warp == 0)
+                nb_sync(1, NMAIN);
+            else
+                nb_arrive(1, NMAIN);
+        };
+        for (int c = 0; c < NC; ++c) {
+            const int t0 = (c_base + c) * C;
+            const float* sv = vecs(c);
+            const uint32_t r_qk = R_QK + QK_BYTES * (uint32_t)(c % NQK);
+            const uint32_t r_tp = R_TP + TP_BYTES * (uint32_t)(c % NTP);
+            const unsigned char* vrows = sm + R_V + V_BYTES * (uint32_t)(c % NVB);
+            // ---------------- MMA-b (after the output warps released O of the last chunk) ----------------
+            if (warp == 0) {
+                wait_phase(bar(B_KQ + c % NQK), c / NQK);
+                if (c > 0) bad |= !mbar_wait_bounded(bar(B_OFREE), (uint32_t)(c - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
+                __syncwarp();
+                umma::fence_after_sync();
+                const uint64_t d_k = umma::desc_kmajor0(sb + r_qk), d_q = umma::desc_kmajor0(sb + r_qk + 8192);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    umma::mma_bf16_ta_elect(tmem + C_YO, tmem + C_OP + split_col(kk, false),
+                                            umma::desc_add(d_k, umma::kmajor_kstep(kk, 128)), idesc_b, kk > 0);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    umma::mma_bf16_ta_elect(tmem + C_YO, tmem + C_OP + split_col(kk, true),
+                                            umma::desc_add(d_k, umma::kmajor_kstep(kk, 128)), idesc_b, 1u);
+                umma::mma_commit_elect(bar(B_MMA));
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    umma::mma_bf16_ta_elect(tmem + C_YO + 64, tmem + C_OP + split_col(kk, false),
+                                            umma::desc_add(d_q, umma::kmajor_kstep(kk, 128)), idesc_b, kk > 0);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    umma::mma_bf16_ta_elect(tmem + C_YO + 64, tmem + C_OP + split_col(kk, true),
+                                            umma::desc_add(d_q, umma::kmajor_kstep(kk, 128)), idesc_b, 1u);
+                umma::mma_commit_elect(bar(B_O1));
+                mma_pending = true;
+            }
+            mma_wait();
+            wait_phase(bar(B_KQ + c % NQK), c / NQK);  // the chunk's vectors (every reader acquires them)
+            wait_phase(bar(B_VR + c % NVB), c / NVB);  // the chunk's conv'd v rows
+            const float ec = sv[V_EC];
+            // ---------------- Z^T = beta (V - e^gamma rk Y)^T (warpgroup wg: tokens 32 wg ..) ----------------
+            {
+                float y[32];
+                umma::tmem_ld32(tmem + lane_base + C_YO + 32 * wg, y);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const int t = 32 * wg + j;
+                    const float2 vv = make_float2(bf_at(vrows, t * D + dv), bf_at(vrows, (t + 1) * D + dv));
+                    const float2 nek = *reinterpret_cast<const float2*>(sv + V_EK + t);
+                    const float2 be = *reinterpret_cast<const float2*>(sv + V_B + t);
+                    const float2 r = tf32_rn2(__fmul2_rn(be, __ffma2_rn(nek, make_float2(y[j], y[j + 1]), vv)));
+                    y[j] = r.x;
+                    y[j + 1] = r.y;
+                }
+                umma::tmem_st32(tmem + lane_base + C_Z + 32 * wg, y);
+                umma::tmem_wait_st();
+            }
+            stores_to_warp0();
+            // ---------------- MMA-c: v_new^T = Z^T T^T (after the producer returned columns 448-511) ----------------
+            if (warp == 0) {
+                wait_phase(bar(B_TPR + c % NTP), c / NTP);
+                const int gp = c + 1 < NC ? c + 1 : (c == 0 ? 0 : -1);
+                if (gp >= 0) bad |= !mbar_wait_bounded(bar(B_GPFREE), (uint32_t)gp & 1u, GDN_DEVERR_MMA_TIMEOUT);
+                __syncwarp();
+                umma::fence_after_sync();
+                const uint64_t d_t = umma::desc_kmajor0(sb + r_tp);
+#pragma unroll
+                for (int kk = 0; kk < C / 8; ++kk)
+                    umma::mma_tf32_ta_elect(tmem + C_V, tmem + C_Z + kk * 8,
+                                            umma::desc_add(d_t, umma::kmajor_kstep(kk, C)), idesc_c, kk > 0);
+                umma::mma_commit_elect(bar(B_MMA));
+                mma_pending = true;
+            }
+            mma_wait();
+            // ---------------- sub-chunk checkpoints (fp32 v_new, bf16 k rows, state before the update) ----------------
+            // S_s = e^{gamma_{s-1}} S + sum_{t<s} e^{gamma_{s-1}-gamma_t} k_t^T v_new_t (deltanet.py:375-388)
+            while (ck_i < ck.n && ck.off[ck_i] > t0 && ck.off[ck_i] - t0 < C) {
+                const int s_off = ck.off[ck_i] - t0;
+                if (tid < C) sF[tid] = tid < s_off ? expf(sv[V_G + s_off - 1] - sv[V_G + tid]) : 0.f;
+                nb_sync(1, NMAIN);
+                const float es = expf(sv[V_G + s_off - 1]);
+                float* dst = p.S_ckpt + ((size_t)ck.slot[ck_i] * p.B * p.Hv + bh) * (size_t)(D * D);
+#pragma unroll 1
+                for (int hb = 0; hb < 2; ++hb) {  // 32 key columns at a time
+                    const int cb = 64 * wg + 32 * hb;
+                    float m[32];
+                    umma::tmem_ld32(tmem + lane_base + C_MS + cb, m);
+                    umma::tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) m[j] *= es;
+#pragma unroll 1
+                    for (int th = 0; th < 2; ++th) {  // 32 tokens at a time
+                        float wv[32];
+                        umma::tmem_ld32(tmem + lane_base + C_V + 32 * th, wv);
+                        umma::tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) wv[j] *= sF[32 * th + j] * sv[V_RK + 32 * th + j];
+                        // k row t = 32 th + j, key columns cb + 8 j8 .. + 7: one 16-byte unit of the
+                        // swizzled rows
+                        const unsigned char* kb = sm + r_qk + 16384 * wg + 4096 * th;
+                        const uint32_t hx0 = 64u * hb, hx1 = 64u - 64u * hb;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const unsigned char* rowp = kb + (j >> 3) * 1024 + (j & 7) * 128 + ((j & 4) ? hx1 : hx0);
+#pragma unroll
+                            for (int j8 = 0; j8 < 4; ++j8) {
+                                const uint4 k8 = *reinterpret_cast<const uint4*>(rowp + ((j8 ^ (j & 3)) << 4));
+                                const uint32_t kw[4] = {k8.x, k8.y, k8.z, k8.w};
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    m[8 * j8 + 2 * e] = fmaf(wv[j], bf_lo(kw[e]), m[8 * j8 + 2 * e]);
+                                    m[8 * j8 + 2 * e + 1] = fmaf(wv[j], bf_hi(kw[e]), m[8 * j8 + 2 * e + 1]);
+                                }
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) __stcs(dst + (size_t)(cb + j) * D + dv, m[j]);
+                }
+                nb_sync(1, NMAIN);
+                ++ck_i;
+            }
+            // ---------------- (e^{gamma_C - gamma} rk v_new)^T as bf16 hi / lo ----------------
+            {
+                float w[32];
+                umma::tmem_ld32(tmem + lane_base + C_V + 32 * wg, w);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const float2 r = __fmul2_rn(make_float2(w[j], w[j + 1]),
+                                                *reinterpret_cast<const float2*>(sv + V_EF + 32 * wg + j));
+                    w[j] = r.x;
+                    w[j + 1] = r.y;
+                }
+                store_split32(tmem + lane_base + C_Z + 32 * wg, w);
+                umma::tmem_wait_st();
+            }
+            stores_to_warp0();
+            // ---------------- MMA-e: dS^T into the operand columns (the state path waits for it) ----------------
+            if (warp == 0) {
+                wait_phase(bar(B_O1), c);
+                __syncwarp();
+                umma::fence_after_sync();
+                const uint64_t d_km = umma::desc_mnmajor16_0(sb + r_qk, 16384);
+#pragma unroll
+                for (int kk = 0; kk < C / 16; ++kk)
+                    umma::mma_bf16_ta_elect(tmem + C_OP, tmem + C_Z + split_col(kk, false),
+                                            umma::desc_add(d_km, umma::mnmajor16_kstep(kk)), idesc_e, kk > 0);
+#pragma unroll
+                for (int kk = 0; kk < C / 16; ++kk)
+                    umma::mma_bf16_ta_elect(tmem + C_OP, tmem + C_Z + split_col(kk, true),
+                                            umma::desc_add(d_km, umma::mnmajor16_kstep(kk)), idesc_e, 1u);
+                umma::mma_commit_elect(bar(B_MMA));
+                mma_pending = true;
+            }
+            // ---------------- v_new^T (tf32) for MMA-d while MMA-e runs ----------------
+            {
+                float v[32];
+                umma::tmem_ld32(tmem + lane_base + C_V + 32 * wg, v);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const float2 r = tf32_rn2(make_float2(v[j], v[j + 1]));
+                    v[j] = r.x;
+                    v[j + 1] = r.y;
+                }
+                umma::tmem_st32(tmem + lane_base + C_V + 32 * wg, v);
+                umma::tmem_wait_st();
+            }
+            umma::fence_before_sync();
+            if (warp == 0)
+                nb_sync(5, NMAIN);
+            else
+                nb_arrive(5, NMAIN);
+            // ---------------- MMA-d: (P v_new)^T for the output warps ----------------
+            if (warp == 0) {
+                umma::fence_after_sync();
+                const uint64_t d_p = umma::desc_kmajor0(sb + r_tp + 16384);
+#pragma unroll
+                for (int kk = 0; kk < C / 8; ++kk)
+                    umma::mma_tf32_ta_elect(tmem + C_YO, tmem + C_V + kk * 8,
+                                            umma::desc_add(d_p, umma::kmajor_kstep(kk, C)), idesc_c, kk > 0);
+                umma::mma_commit_elect(bar(B_ORDY));
+            }
+            mma_wait();
+            // ---------------- state update (key columns 64 wg ..), checkpoints, final state ----------------
+            {
+                const bool lastc = c == NC - 1;
+                float* const s_end = !lastc ? nullptr
+                                     : out_slot >= 0 ? hs + (size_t)out_slot * D * D
+                                                     : (p.S_out ? p.S_out + (size_t)bh * D * D : nullptr);
+#pragma unroll 1
+                for (int c0 = 64 * wg; c0 < 64 * wg + 64; c0 += 32) {
+                    float m[32], d[32];
+                    umma::tmem_ld32(tmem + lane_base + C_MS + c0, m);
+                    umma::tmem_ld32(tmem + lane_base + C_OP + c0, d);
+                    umma::tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        const float2 r = __ffma2_rn(make_float2(m[j], m[j + 1]), make_float2(ec, ec),
+                                                    make_float2(d[j], d[j + 1]));
+                        m[j] = r.x;
+                        m[j + 1] = r.y;
+                    }
+                    umma::tmem_st32(tmem + lane_base + C_MS + c0, m);
+                    store_split32(tmem + lane_base + C_OP + c0, m);
+                    for (int w = ck_i; w < ck.n && ck.off[w] - t0 == C; ++w) {
+                        float* dst = p.S_ckpt + ((size_t)ck.slot[w] * p.B * p.Hv + bh) * (size_t)(D * D);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) __stcs(dst + (size_t)(c0 + j) * D + dv, m[j]);
+                    }
+                    if (s_end) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) __stcg(s_end + (size_t)(c0 + j) * D + dv, m[j]);
+                    }
+                }
+                umma::tmem_wait_st();
+                if (lastc && out_slot >= 0) __threadfence();  // the hand-off state before its flag
+            }
+            while (ck_i < ck.n && ck.off[ck_i] - t0 == C) ++ck_i;
+            umma::fence_before_sync();
+            if (nb_any(bad, 1, NMAIN)) {
+                failed = true;
+                break;
+            }
+            umma::fence_after_sync();
+            if (c == NC - 1 && out_slot >= 0 && tid == 0) release_flag(hflag + out_slot);  // state written
+        }
+        if (tid == 0 && failed && mma_pending)  // an MMA in flight finishes (bounded) before the CTA exits
+            mbar_wait_bounded(bar(B_MMA), (mma_phase - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
+    } else {
+        // ================ producer and output rows (warpgroups 2-3, 256 threads) ================
+        const int ptid = tid - NMAIN;
+        const int owg = wg - 2, tw = 32 * owg;  // output tokens / [G; P0] columns tw .. tw + 31
+        const float nw = sNW[dv];
+        const TA* convw = static_cast<const TA*>(p.convw);
+        const TA* cs_in = static_cast<const TA*>(p.cs_in);
+        // this thread's q / k channel pair (conv of 32 tokens) and v channel pair (16 tokens)
+        const int hf = ptid >> 7, pp = ptid & 127;
+        const bool isk = pp >= 64;
+        const int qch = 2 * (pp & 63), qatom = qch >> 6, qchl = qch & 63;
+        const int gqk = (isk ? p.Hk * D : 0) + kh * D + qch;
+        const int qt = ptid >> 6, vch = 2 * (ptid & 63);
+        const int gv = v_ch + vch;
+        __nv_bfloat162 wqk[4], wvv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            wqk[j] = __halves2bfloat162(convw[(size_t)gqk * 4 + j], convw[(size_t)(gqk + 1) * 4 + j]);
+            wvv[j] = __halves2bfloat162(convw[(size_t)gv * 4 + j], convw[(size_t)(gv + 1) * 4 + j]);
+        }
+        // raw history pair of channels (gc, gc + 1) at token tk < 0 of the chain: the conv state
+        auto cs_pair = [&](int gc, int tk) -> uint32_t {
+            if (!cs_in) return 0u;
+            const TA* s = cs_in + ((size_t)b * conv_dim + gc) * 3 + (3 + tk);
+            __nv_bfloat162 r = __halves2bfloat162(s[0], s[3]);
+            return *reinterpret_cast<uint32_t*>(&r);
+        };
+        bool bad = false;
+        int n_rqk[NQK] = {0, 0, 0}, n_rv[NVB] = {0, 0}, n_z = 0, w_z = 0;  // copies issued (thread 0)
+        if (ptid == 0) {
+            for (int i = 0; i < NQK && i < NC; ++i) n_rqk[i] = 1;
+            for (int i = 0; i < NVB && i < NC; ++i) n_rv[i] = 1;
+            n_z = 1;
+        }
+        bool gp_pending = false;
+        int n_gp = 0;  // [G; P0] MMAs issued in this piece (thread 0)
+
+        // --- conv + SiLU in place of the q / k rows of chunk cq and the v rows of chunk cv, norm
+        //     factors, gates and per-token vectors of chunk cq; signals kq_ready(cq), v_ready(cv)
+        auto prep = [&](int cq, int cv) {
+            const int t0q = (c_base + cq) * C, t0v = (c_base + cv) * C;
+            if (cq >= 0) bad |= !mbar_wait_bounded(bar(B_RAWQK + cq % NQK), (uint32_t)(cq / NQK) & 1u,
+                                                   GDN_DEVERR_TMA_TIMEOUT);
+            if (cv >= 0) bad |= !mbar_wait_bounded(bar(B_RAWV + cv % NVB), (uint32_t)(cv / NVB) & 1u,
+                                                   GDN_DEVERR_TMA_TIMEOUT);
+            float raw_a = 0.f, raw_b = 0.f;
+            if (cq >= 0 && ptid < C && t0q + ptid < p.T) {
+                const size_t ai = (size_t)b * p.as_b + (size_t)(t0q + ptid) * p.as_t + h;
+                raw_a = Act<TA>::ld(static_cast<const TA*>(p.a) + ai);
+                raw_b = Act<TA>::ld(static_cast<const TA*>(p.b) + ai);
+            }
+            unsigned char* qkb = sm + R_QK + QK_BYTES * (uint32_t)(cq % NQK) + qatom * 16384 + (isk ? 0 : 8192);
+            unsigned char* vb = sm + R_V + V_BYTES * (uint32_t)(cv % NVB);
+            // phase 1: the raw values of the three tokens before this thread's first token
+            uint32_t q1 = 0u, q2 = 0u, q3 = 0u, v1 = 0u, v2 = 0u, v3 = 0u;
+            if (cq >= 0) {
+                if (hf == 1) {
+                    q3 = *reinterpret_cast<const uint32_t*>(qkb + sw128(29, qchl));
+                    q2 = *reinterpret_cast<const uint32_t*>(qkb + sw128(30, qchl));
+                    q1 = *reinterpret_cast<const uint32_t*>(qkb + sw128(31, qchl));
+                } else if (t0q > 0) {
+                    const unsigned char* hb = sm + R_HQK + 4 * HATOM * (cq % NQK) + HATOM * ((isk ? 2 : 0) + qatom);
+                    q3 = *reinterpret_cast<const uint32_t*>(hb + 1 * 128 + qchl * 2);
+                    q2 = *reinterpret_cast<const uint32_t*>(hb + 2 * 128 + qchl * 2);
+                    q1 = *reinterpret_cast<const uint32_t*>(hb + 3 * 128 + qchl * 2);
+                } else {
+                    q3 = cs_pair(gqk, -3);
+                    q2 = cs_pair(gqk, -2);
+                    q1 = cs_pair(gqk, -1);
+                }
+            }
+            if (cv >= 0) {
+                if (qt > 0) {
+                    v3 = *reinterpret_cast<const uint32_t*>(vb + (16 * qt - 3) * 256 + vch * 2);
+                    v2 = *reinterpret_cast<const uint32_t*>(vb + (16 * qt - 2) * 256 + vch * 2);
+                    v1 = *reinterpret_cast<const uint32_t*>(vb + (16 * qt - 1) * 256 + vch * 2);
+                } else if (t0v > 0) {
+                    const unsigned char* hb = sm + R_HV + 2 * HATOM * (cv % NVB) + HATOM * (vch >> 6);
+                    v3 = *reinterpret_cast<const uint32_t*>(hb + 1 * 128 + (vch & 63) * 2);
+                    v2 = *reinterpret_cast<const uint32_t*>(hb + 2 * 128 + (vch & 63) * 2);
+                    v1 = *reinterpret_cast<const uint32_t*>(hb + 3 * 128 + (vch & 63) * 2);
+                } else {
+                    v3 = cs_pair(gv, -3);
+                    v2 = cs_pair(gv, -2);
+                    v1 = cs_pair(gv, -1);
+                }
+            }
+            nb_sync(4, NT - NMAIN);
+            // phase 2: conv + SiLU in place; outputs of tokens past the sequence end are zero
+            if (cq >= 0) {
+                __nv_bfloat162 x1 = as_bf2(q1), x2 = as_bf2(q2), x3 = as_bf2(q3);
+                float sq[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int t = 32 * hf + j;
+                    uint32_t* cell = reinterpret_cast<uint32_t*>(qkb + sw128(t, qchl));
+                    const __nv_bfloat162 x0 = as_bf2(*cell);
+                    const uint32_t o = t0q + t < p.T ? conv_silu_pair(x0, x1, x2, x3, wqk) : 0u;
+                    *cell = o;
+                    x3 = x2;
+                    x2 = x1;
+                    x1 = x0;
+                    const float a0 = bf_lo(o), a1 = bf_hi(o);
+                    sq[j] = fmaf(a0, a0, a1 * a1);
+                }
+                // per-token sums over this warp's 64 channels: halving exchange that leaves token
+                // 32 hf + lane in this lane
+#pragma unroll
+                for (int st = 0; st < 5; ++st) {
+                    const int s = 16 >> st, half = 16 >> st;
+                    const bool up = (lane & s) != 0;
+#pragma unroll
+                    for (int k = 0; k < half; ++k) {
+                        const float send = up ? sq[k] : sq[k + half];
+                        const float keep = up ? sq[k + half] : sq[k];
+                        sq[k] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+                    }
+                }
+                sPart[(isk ? 128 : 0) + qatom * 64 + 32 * hf + lane] = sq[0];
+            }
+            if (cv >= 0) {
+                __nv_bfloat162 x1 = as_bf2(v1), x2 = as_bf2(v2), x3 = as_bf2(v3);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int t = 16 * qt + j;
+                    uint32_t* cell = reinterpret_cast<uint32_t*>(vb + t * 256 + vch * 2);
+                    const __nv_bfloat162 x0 = as_bf2(*cell);
+                    *cell = t0v + t < p.T ? conv_silu_pair(x0, x1, x2, x3, wvv) : 0u;
+                    x3 = x2;
+                    x2 = x1;
+                    x1 = x0;
+                }
+            }
+            fence_proxy_async_smem();  // the conv outputs are read by the tensor cores next
+            nb_sync(4, NT - NMAIN);
+            if (cv >= 0 && ptid == 0) mbar_arrive(bar(B_VR + cv % NVB));
+            if (cq < 0) return;
+            float* vv = vecs(cq);
+            if (ptid < C) {
+                const int t = ptid;
+                const bool valid = t0q + t < p.T;
+                vv[V_RQ + t] = rsqrtf((sPart[t] + sPart[64 + t]) + 1e-6f);
+                vv[V_RK + t] = rsqrtf((sPart[128 + t] + sPart[192 + t]) + 1e-6f);
+                vv[V_B + t] = valid ? Act<TA>::round(sigmoid_f(raw_b)) : 0.f;
+                vv[V_G + t] = valid ? -expf(p.A_log[h]) * softplus_f(raw_a + p.dt_bias[h]) : 0.f;
+                nb_sync(6, C);
+                if (t == 0) {  // sequential cumsum over the chunk (the reference's torch.cumsum)
+                    float acc = 0.f;
+#pragma unroll 8
+                    for (int i = 0; i < C; ++i) {
+                        acc += vv[V_G + i];
+                        vv[V_G + i] = acc;
+                    }
+                }
+                nb_sync(6, C);
+                const float gt = vv[V_G + t], gC = vv[V_G + C - 1], rk = vv[V_RK + t];
+                const float eg = expf(gt);
+                vv[V_EG + t] = eg;
+                vv[V_EK + t] = -(eg * rk);
+                vv[V_EF + t] = expf(gC - gt) * rk;
+                vv[V_EQ + t] = eg * (vv[V_RQ + t] * p.q_scale);
+                vv[V_ENG + t] = expf(-gt) * rk;
+                if (t == 0) vv[V_EC] = expf(gC);
+            }
+            nb_sync(4, NT - NMAIN);
+            if (ptid == 0) mbar_arrive(bar(B_KQ + cq % NQK));
+        };
+        // --- [G; P0] = [k; q] k^T of chunk cc (raw conv outputs, exact bf16 products) into the
+        //     borrowed tensor-memory columns; issued by thread 0
+        auto issue_gp = [&](int cc) {
+            if (ptid != 0) return;
+            umma::fence_after_sync();
+            const uint64_t d = umma::desc_kmajor0(sb + R_QK + QK_BYTES * (uint32_t)(cc % NQK));
+            const uint32_t idesc = umma::idesc_bf16(128, 64, 0, 0);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                const uint64_t dk = umma::desc_add(d, umma::kmajor_kstep(kk, 128));
+                umma::mma_bf16(tmem + C_V, dk, dk, idesc, kk > 0);
+            }
+            umma::mma_commit(bar(B_GP));
+            gp_pending = true;
+            ++n_gp;
+        };
+        // --- wait for [G; P0] of chunk cc, copy this thread's row segment out of tensor memory
+        //     (lane dv: rows 0-63 = G, 64-127 = P0; columns tw .. tw + 31), give the columns back,
+        //     and write A (lower triangle, fp32) and P (tf32, masked) of the chunk
+        auto build_ap = [&](int cc) {
+            const bool ok = mbar_wait_bounded(bar(B_GP), (uint32_t)cc & 1u, GDN_DEVERR_MMA_TIMEOUT);
+            bad |= !ok;
+            if (ok && ptid == 0) gp_pending = false;
+            umma::fence_after_sync();
+            float g[32];
+            umma::tmem_ld32(tmem + lane_base + C_V + tw, g);
+            umma::tmem_wait_ld();
+            umma::fence_before_sync();
+            mbar_arrive(bar(B_GPFREE));
+            const float* vv = vecs(cc);
+            const bool g_row = dv < C;
+            const int t = dv & (C - 1);
+            const float gt = vv[V_G + t];
+            // decay e^{gamma_t - gamma_j}: as e^{gamma_t} e^{-gamma_j} when neither factor leaves
+            // the normal range (gamma >= -80 over the chunk), else one exp per pair; the column
+            // norm factor rk_j rides on it, the row factor is beta_t rk_t (A) or rq_t dk^-1/2 (P)
+            const bool factored = vv[V_G + C - 1] >= -80.f;
+            const float rowf = g_row ? vv[V_B + t] * vv[V_RK + t] : vv[V_RQ + t] * p.q_scale;
+            const float erow = vv[V_EG + t] * rowf;
+            unsigned char* dst = sm + R_TP + TP_BYTES * (uint32_t)(cc % NTP) + (g_row ? 0u : 16384u);
+#pragma unroll
+            for (int jj = 0; jj < 32; jj += 4) {
+                const int j = tw + jj;
+                float val[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float dec = factored ? erow * vv[V_ENG + j + e]
+                                               : __expf(gt - vv[V_G + j + e]) * (rowf * vv[V_RK + j + e]);
+                    const float x = g[jj + e] * dec;
+                    val[e] = g_row ? (j + e < t ? x : 0.f) : (j + e <= t ? umma::tf32_rna(x) : 0.f);
+                }
+                *reinterpret_cast<float4*>(dst + img_off(t, j)) = make_float4(val[0], val[1], val[2], val[3]);
+            }
+        };
+        // --- T = (I + A)^-1 of chunk cc in place over A (K-major operand image layout):
+        //     T11, T22 by forward substitution (one warp per 32 x 32 block, lane = column),
+        //     X = A21 T11 parked in the zero upper-right block, T21 = -T22 X over A21; then every
+        //     element rounded to tf32 (nearest), zero above the diagonal; signals tp_ready(cc)
+        auto build_t = [&](int cc) {
+            unsigned char* Tb = sm + R_TP + TP_BYTES * (uint32_t)(cc % NTP);
+            nb_sync(4, NT - NMAIN);
+            const int pw = ptid >> 5;
+            if (pw < 2) {
+                const int o = 32 * pw;
+                float x[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) x[i] = 0.f;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int k = 0; k < i; k += 4) {
+                        const float4 a = *reinterpret_cast<const float4*>(Tb + img_off(o + i, o + k));
+                        s01 = __ffma2_rn(make_float2(a.x, a.y), make_float2(x[k], x[k + 1]), s01);
+                        s23 = __ffma2_rn(make_float2(a.z, a.w), make_float2(x[k + 2], x[k + 3]), s23);
+                    }
+                    x[i] = (i == lane ? 1.f : 0.f) - ((s01.x + s01.y) + (s23.x + s23.y));
+                }
+#pragma unroll
+                for (int i = 0; i < 32; ++i) *reinterpret_cast<float*>(Tb + img_off(o + i, o + lane)) = x[i];
+            }
+            nb_sync(4, NT - NMAIN);
+            const int bi = ptid >> 3, jb = (ptid & 7) * 4;
+            {  // X[bi][jb..] = A21[bi][:] T11[:][jb..]  (T11[k][j] = 0 for k < j)
+                float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
+                for (int k = jb; k < 32; k += 4) {
+                    const float4 a = *reinterpret_cast<const float4*>(Tb + img_off(32 + bi, k));
+                    const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const float4 r = *reinterpret_cast<const float4*>(Tb + img_off(k + kk, jb));
+                        a01 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.x, r.y), a01);
+                        a23 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.z, r.w), a23);
+                    }
+                }
+                // the upper-right block is read by nobody in this phase
+                *reinterpret_cast<float4*>(Tb + img_off(bi, 32 + jb)) = make_float4(a01.x, a01.y, a23.x, a23.y);
+            }
+            nb_sync(4, NT - NMAIN);
+            {  // T21[bi][jb..] = -T22[bi][:] X[:][jb..]  (T22[i][k] = 0 for k > i)
+                float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
+                for (int k = 0; k <= bi; k += 4) {
+                    const float4 a = *reinterpret_cast<const float4*>(Tb + img_off(32 + bi, 32 + k));
+                    const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const float4 r = *reinterpret_cast<const float4*>(Tb + img_off(k + kk, 32 + jb));
+                        a01 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.x, r.y), a01);
+                        a23 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.z, r.w), a23);
+                    }
+                }
+                // A21 was last read in the previous phase
+                *reinterpret_cast<float4*>(Tb + img_off(32 + bi, jb)) =
+                    make_float4(-a01.x, -a01.y, -a23.x, -a23.y);
+            }
+            nb_sync(4, NT - NMAIN);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int idx = ptid + (NT - NMAIN) * e, i = idx >> 4, j = (idx & 15) * 4;
+                float4* cell = reinterpret_cast<float4*>(Tb + img_off(i, j));
+                const float4 v = *cell;
+                *cell = make_float4(j + 0 <= i ? umma::tf32_rna(v.x) : 0.f, j + 1 <= i ? umma::tf32_rna(v.y) : 0.f,
+                                    j + 2 <= i ? umma::tf32_rna(v.z) : 0.f, j + 3 <= i ? umma::tf32_rna(v.w) : 0.f);
+            }
+            fence_proxy_async_smem();  // T and P are read by the tensor cores next
+            nb_sync(4, NT - NMAIN);
+            if (ptid == 0) mbar_arrive(bar(B_TPR + cc % NTP));
+        };
+
+        // ---- prologue: chunks 0 and 1 convolved, their T / P images built ----
+        prep(0, 0);
+        if (NC > 1) prep(1, -1);
+        issue_gp(0);
+        build_ap(0);
+        build_t(0);
+        if (NC > 1) {
+            issue_gp(1);
+            build_ap(1);
+            build_t(1);
+        }
+        if (nb_any(bad, 4, NT - NMAIN)) failed = true;
+        for (int c = 0; c < NC && !failed; ++c) {
+            const int t0 = (c_base + c) * C;
+            // a. conv of the q / k rows of chunk c + 2 and the v rows of chunk c + 1
+            const int cq = c + 2 < NC ? c + 2 : -1, cv = c + 1 < NC ? c + 1 : -1;
+            if (cq >= 0 || cv >= 0) prep(cq, cv);
+            // b. O of chunk c out of tensor memory; [G; P0], A and P of chunk c + 2
+            bad |= !mbar_wait_bounded(bar(B_ORDY), (uint32_t)c & 1u, GDN_DEVERR_MMA_TIMEOUT);
+            umma::fence_after_sync();
+            if (cq >= 0) issue_gp(cq);
+            const float* sv = vecs(c);
+            float o[32];
+            {  // O[t][dv] = e^{gamma_t} rq dk^-1/2 O1 + P v_new
+                float o1[32], dd[32];
+                umma::tmem_ld32(tmem + lane_base + C_YO + 64 + tw, o1);
+                umma::tmem_ld32(tmem + lane_base + C_YO + tw, dd);
+                umma::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) o[j] = fmaf(sv[V_EQ + tw + j], o1[j], dd[j]);
+            }
+            umma::fence_before_sync();
+            mbar_arrive(bar(B_OFREE));  // these tensor-memory columns may be overwritten now
+            if (cq >= 0) build_ap(cq);
+            // the raw rows of chunks c + 3 (q / k) and c + 2 (v) into the buffers chunk c used
+            // (every MMA and checkpoint read of them is complete: o_ready of chunk c)
+            if (ptid == 0 && !bad) {
+                if (c + 3 < NC) {
+                    issue_qk(c + 3);
+                    ++n_rqk[(c + 3) % NQK];
+                }
+                if (c + 2 < NC) {
+                    issue_v(c + 2);
+                    ++n_rv[(c + 2) % NVB];
+                }
+            }
+            // c. output rows of chunk c through the gated RMSNorm (config.py:136-143)
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) round2_bf16(o[j], o[j + 1]);
+            float sq[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sq[j] = o[j] * o[j];
+#pragma unroll
+            for (int st = 0; st < 5; ++st) {
+                const int s = 16 >> st, half = 16 >> st;
+                const bool up = (lane & s) != 0;
+#pragma unroll
+                for (int k = 0; k < half; ++k) {
+                    const float send = up ? sq[k] : sq[k + half];
+                    const float keep = up ? sq[k + half] : sq[k];
+                    sq[k] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+                }
+            }
+            sPart[q4 * C + tw + lane] = sq[0];
+            nb_sync(2 + owg, 128);
+            if (q4 == 0) {
+                const int t = tw + lane;
+                const float ss = (sPart[t] + sPart[C + t]) + (sPart[2 * C + t] + sPart[3 * C + t]);
+                sRstd[t] = rsqrtf(ss / (float)D + p.eps);
+            }
+            const bool zok = mbar_wait_bounded(bar(B_Z), (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            w_z += zok;
+            bad |= !zok;
+            nb_sync(2 + owg, 128);
+            // the rows are assembled in the z tile's place ([64 tokens][128] bf16) and leave by one
+            // tensor store, so every z value is read before the tile is overwritten
+            float y[32], zv[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                y[j] = o[j] * sRstd[tw + j];
+                zv[j] = bf_at(sm + R_Z, (tw + j) * D + dv);
+            }
+            nb_sync(4, NT - NMAIN);
+            uint16_t* tile = reinterpret_cast<uint16_t*>(sm + R_Z) + tw * D + dv;
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) round2_bf16(y[j], y[j + 1]);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) y[j] *= nw;
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) round2_bf16(y[j], y[j + 1]);
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+                const float z0 = zv[j], z1 = zv[j + 1];
+                float a0 = y[j] * __fdividef(z0, 1.0f + __expf(-z0));
+                float a1 = y[j + 1] * __fdividef(z1, 1.0f + __expf(-z1));
+                uint32_t bits;
+                round2_bf16(a0, a1, &bits);
+                tile[j * D] = (uint16_t)(bits & 0xFFFFu);
+                tile[(j + 1) * D] = (uint16_t)(bits >> 16);
+            }
+            fence_proxy_async_smem();
+            // the group agrees on a wait that ran out (any thread) once per chunk, before the store
+            if (nb_any(bad, 4, NT - NMAIN)) {
+                failed = true;
+                break;
+            }
+            if (ptid == 0) {
+                // rows past the sequence end fall outside the tensor map and are not written
+                tma_store_3d(&maps.out, sb + R_Z, h * D, t0, b);
+                bulk_commit_group();
+                if (c + 1 < NC) {
+                    bulk_wait_group_read0();  // the tile is read: the next z rows may land there
+                    issue_z(c + 1);
+                    ++n_z;
+                }
+            }
+            // d. T of chunk c + 2
+            if (cq >= 0) build_t(cq);
+        }
+        if (ptid == 0) {
+            if (failed)
+                for (; w_z < n_z; ++w_z) mbar_wait_bounded(bar(B_Z), (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            bulk_wait_group0();  // output rows written before the piece ends
+            // the last copy into each buffer lands before the piece ends (bounded; every earlier one
+            // on the same barrier was waited for before the next was issued)
+            for (int i = 0; i < NQK; ++i)
+                if (n_rqk[i] > 0)
+                    mbar_wait_bounded(bar(B_RAWQK + i), (uint32_t)(n_rqk[i] - 1) & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            for (int i = 0; i < NVB; ++i)
+                if (n_rv[i] > 0)
+                    mbar_wait_bounded(bar(B_RAWV + i), (uint32_t)(n_rv[i] - 1) & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            if (gp_pending) mbar_wait_bounded(bar(B_GP), (uint32_t)(n_gp - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
+        }
+    }
+    umma::fence_before_sync();
+    cta_failed = __syncthreads_or(failed);
+    }  // pieces
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) umma::tmem_dealloc(tmem, T_COLS);
+}
+
+}  // namespace pfused
+
+size_t prefill_fused_ws_layout(int n_hs, size_t off[2]) {
+    off[0] = 0;
+    off[1] = ((size_t)n_hs * 128 * 128 * 4 + 1023) & ~(size_t)1023;
+    return (off[1] + (size_t)n_hs * 4 + 1023) & ~(size_t)1023;
+}
+
+cudaError_t launch_prefill_fused(const MixParams& p, const CkptList& ck, float* hs, int* hflag, int n_hs,
+                                 cudaStream_t s) {
+    const uint64_t conv_dim = 2ull * p.Hk * 128 + (uint64_t)p.Hv * 128;
+    pfused::FusedMaps maps;
+    const uint64_t T = (uint64_t)p.T, B = (uint64_t)p.B;
+    if (!encode_tmap_3d_bf16(&maps.qk, p.mixed, conv_dim, T, B, (uint64_t)p.ms_t * 2, (uint64_t)p.ms_b * 2, 64,
+                             pfused::C, true) ||
+        !encode_tmap_3d_bf16(&maps.v, p.mixed, conv_dim, T, B, (uint64_t)p.ms_t * 2, (uint64_t)p.ms_b * 2, 128,
+                             pfused::C) ||
+        !encode_tmap_3d_bf16(&maps.hist, p.mixed, conv_dim, T, B, (uint64_t)p.ms_t * 2, (uint64_t)p.ms_b * 2, 64,
+                             pfused::HROWS) ||
+        !encode_tmap_3d_bf16(&maps.z, p.z, (uint64_t)p.Hv * 128, T, B, (uint64_t)p.zs_t * 2, (uint64_t)p.zs_b * 2,
+                             128, pfused::C) ||
+        !encode_tmap_3d_bf16(&maps.out, p.out, (uint64_t)p.Hv * 128, T, B, (uint64_t)p.Hv * 128 * 2,
+                             (uint64_t)p.Hv * 128 * 2 * T, 128, pfused::C))
+        return cudaErrorInvalidValue;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        e = cudaFuncSetAttribute(pfused::prefill_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)pfused::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    const int chains = p.B * p.Hv;
+    if (n_hs > 1 && chains > n_hs) {
+        // split mode: one CTA per SM, all resident at once (a cooperative launch guarantees it),
+        // the chains cut into equal runs with state hand-offs between neighbouring CTAs; the
+        // hand-off flags start at zero on every call
+        e = cudaMemsetAsync(hflag, 0, (size_t)n_hs * sizeof(int), s);
+        if (e != cudaSuccess) return e;
+        int split = 1;
+        void* kargs[] = {const_cast<MixParams*>(&p), const_cast<CkptList*>(&ck), &hs, &hflag, &maps, &split};
+        e = cudaLaunchCooperativeKernel((const void*)pfused::prefill_fused_kernel, dim3(n_hs), dim3(pfused::NT),
+                                        kargs, pfused::SMEM_BYTES, s);
+        if (e == cudaSuccess) return cudaSuccess;
+        (void)cudaGetLastError();  // not launchable as one resident wave here: one CTA per chain
+    }
+    pfused::prefill_fused_kernel<<<chains, pfused::NT, pfused::SMEM_BYTES, s>>>(p, ck, hs, hflag, maps, 0);
+    return cudaGetLastError();
+}
+
+unsigned int prefill_fused_device_error(bool clear) {
+    unsigned int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+    if (clear && v) {
+        const unsigned int zero = 0;
+        cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+    }
+    return v;
+}
+
+}  // namespace gdn
