@@ -29,11 +29,9 @@ numpy oracle) on the host cores, on the same decode workload.
 from __future__ import annotations
 
 import argparse
-import glob
 import json
 import math
 import os
-import re
 import statistics
 import sys
 import threading
@@ -47,6 +45,7 @@ sys.path.insert(0, REPO)
 from visionstack_b200 import workloads as W  # noqa: E402
 
 FALLBACK_HBM_GBS = 6650.0
+DECODE_RUN_STEPS = 512  # the decode workload: 512 single-token steps per bench step
 FALLBACK_BF16_TFLOPS = 1590.0
 
 
@@ -123,16 +122,11 @@ def measured_peaks():
         return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
 
 
-def profiled_traffic(kernel_key: str):
-    """dram bytes per launch recorded from an ncu capture (profiles/*.md line
-    ``traffic_bytes_per_launch[<key>]: <int>``), or None."""
-    pat = re.compile(r"traffic_bytes_per_launch\[" + re.escape(kernel_key) + r"\]:\s*([0-9]+)")
-    for path in sorted(glob.glob(os.path.join(REPO, "profiles", "*.md"))):
-        with open(path) as f:
-            m = pat.search(f.read())
-        if m:
-            return int(m.group(1))
-    return None
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the decode kernel at
+# B64 x 32 heads, recorded from one ncu capture of this kernel (the capture command and its
+# summary are in the profiles folder).  A recorded constant, not measured by this run: ncu
+# cannot run inside a timed benchmark.
+DECODE_B64_TRAFFIC_RECORDED = 218625024
 
 
 # ----------------------------------------------------------------------------
@@ -260,7 +254,8 @@ def run_reference(args, rank: int, world: int) -> None:
 
 
 def decode_config(n: int):
-    return {"workload": "decode step: B64 per GPU, hidden 2048, 16 k-heads / 32 v-heads, d128, conv 4",
+    return {"workload": "decode: B64 per GPU, hidden 2048, 16 k-heads / 32 v-heads, d128, conv 4; one bench step "
+                        f"= {DECODE_RUN_STEPS} single-token steps (one kernel launch each), states updated in place",
             "global_batch": 64 * n, "seq_len": 1,
             "parallelism": f"value-head sharding x{n}, batch {64 * n} (64 per GPU)" if n > 1 else "single GPU",
             "l2": "inputs larger than L2: 4 rotating 134 MB state slots"}
@@ -334,19 +329,22 @@ def run_ours(args, rank: int, world: int) -> None:
         m.mixer(mixed[j], z[j], bb[j], aa[j], conv_state=cin, rec_state=states[slot], conv_state_out=cout,
                 rec_state_out=states[slot], out=out, token_by_token=True)
 
+    # One bench step = the decode workload's run of RUN single-token steps (RUN kernel launches,
+    # captured once into a CUDA graph); W untimed replays, then K timed ones.
     K, Wm = args.steps, max(3, args.warmup)
+    RUN = DECODE_RUN_STEPS
     stream = torch.cuda.Stream(device=dev)
-    # untimed warm-up (eager), then capture the K timed steps into one CUDA graph
     with torch.cuda.stream(stream):
-        for i in range(Wm):
+        for i in range(4):
             step(i)
     torch.cuda.synchronize(dev)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        for i in range(K):
-            step(Wm + i)
+        for i in range(RUN):
+            step(i)
     torch.cuda.synchronize(dev)
-    graph.replay()  # one untimed replay: graph upload / first-launch costs
+    for _ in range(Wm):
+        graph.replay()
     torch.cuda.synchronize(dev)
 
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -355,7 +353,8 @@ def run_ours(args, rank: int, world: int) -> None:
     with sampler:
         with torch.cuda.stream(stream):
             ev0.record(stream)
-            graph.replay()
+            for _ in range(K):
+                graph.replay()
             ev1.record(stream)
         torch.cuda.synchronize(dev)
     barrier()
@@ -364,7 +363,8 @@ def run_ours(args, rank: int, world: int) -> None:
     if world > 1:
         dist.all_reduce(t_local, op=dist.ReduceOp.MAX)
     ms_total = float(t_local.item())
-    ms_step = ms_total / K
+    ms_run = ms_total / K            # one bench step: RUN decode launches
+    ms_step = ms_run / RUN           # one decode step
     del graph
 
     # end to end through the public API: every step copies its projection
@@ -478,15 +478,19 @@ def run_ours(args, rank: int, world: int) -> None:
     hbm, tflops, src = measured_peaks()
     bytes_launch = decode_bytes(B, hk, hv, d, 4)
     achieved = bytes_launch / (ms_step * 1e-3) / 1e9
-    traffic = profiled_traffic("decode_b64") if world == 1 else None
+    traffic = DECODE_B64_TRAFFIC_RECORDED if world == 1 else None
     line = {
         "metric": "DeltaNet decode steps/s (B64, 16/32 heads, d128, bf16, fp32 state)",
         "value": world * 1000.0 / ms_step, "unit": "steps/s", "n_gpus": world, "steps": K, "warmup": Wm,
-        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": ms_run, "ms_per_decode_step": ms_step, "decode_steps_per_bench_step": RUN,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (seeded torch.randn on device)", "config": decode_config(world),
-        "gpu_launches": K,
+        "gpu_launches": K * RUN,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "traffic": traffic, "peak_source": src, "bytes_per_launch": bytes_launch,
+                     "traffic": traffic,
+                     "traffic_source": "recorded constant from one ncu capture of this kernel at B64 (not "
+                                       "measured by this run)" if traffic else None,
+                     "peak_source": src, "bytes_per_launch": bytes_launch,
                      "kernel": "gdn::dtma::decode_tma_kernel<128,1,bf16> (2 groups x 256 threads, 1 CTA/SM)"},
         "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "Qwen3_5GatedDeltaNet.mixer_plan -> gdn_mixer_decode in CUDA graphs of 32 steps; every "

@@ -300,9 +300,10 @@ __global__ void __launch_bounds__(NT, 1)
     }
     umma::fence_after_sync();
 
-    // initial state, transposed: lane dv, column dk (warpgroup wg: dk 32 wg .. 32 wg + 31) in the
-    // fp32 master, and its bf16 hi / lo operand in the same 32 columns of the operand region
-    if (main_grp) {
+    // initial state, transposed: lane dv, column dk (warpgroup wg of all four: dk 32 wg ..
+    // 32 wg + 31) in the fp32 master, and its bf16 hi / lo operand in the same 32 columns of
+    // the operand region
+    {
         const int c0 = 32 * wg;
         const float* src = in_slot >= 0 ? hs + (size_t)in_slot * D * D
                                          : (p.S_in ? p.S_in + (size_t)bh * D * D : nullptr);
