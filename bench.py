@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--no-stack", action="store_true",
                     help="skip the secondary 48-layer hybrid stack measurement (B32: prefill 4096, decode 256; "
                          "run at 1 GPU only)")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the head-sharded layer measurement (projections, mixer, out_proj, all-reduce)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-s", type=float, default=12.0, help="seconds of CPU work for the CPU baseline")
     return ap.parse_args()
@@ -197,9 +199,16 @@ class ClockSampler:
 # CPU side: oracle timings (CPU baseline and the reference arm)
 # ----------------------------------------------------------------------------
 
-def cpu_decode_rate(sample_s: float):
+def cpu_decode_rate(sample_s: float, threads: int):
     """Time the oracle's decode step (numpy restatement of the reference,
-    deltanet.py:165-233 + conv + gated norm) at the full decode batch."""
+    deltanet.py:165-233 + conv + gated norm) at the full decode batch (B64), the
+    rows split into ``threads`` slices run concurrently on host threads (numpy
+    releases the GIL inside its array operations; BLAS held to one thread per
+    slice).  Returns (steps/s, steps, seconds, threads used)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from threadpoolctl import threadpool_limits
+
     from oracle import gdn_oracle as O
 
     wl = W.WORKLOADS["decode"]
@@ -211,18 +220,82 @@ def cpu_decode_rate(sample_s: float):
     mixed, z, a, b = f(B, 1, s.conv_dim, sc=0.7), f(B, 1, s.num_v_heads, s.head_v_dim), f(B, 1, s.num_v_heads), \
         f(B, 1, s.num_v_heads)
     st = W.make_decode_states(wl)
-    conv, rec = st["conv"], st["recurrent"]
-    O.mixer_forward(s, mixed, z, a, b, p["conv1d.weight"], p["A_log"], p["dt_bias"], p["norm.weight"], "bf16",
-                    conv, rec, chunk=False)  # warm-up
-    n, t0 = 0, time.perf_counter()
-    while True:
-        _, conv, rec, _, _ = O.mixer_forward(s, mixed, z, a, b, p["conv1d.weight"], p["A_log"], p["dt_bias"],
-                                             p["norm.weight"], "bf16", conv, rec, chunk=False)
-        n += 1
+    P = max(1, min(threads, B))
+    cut = [B * i // P for i in range(P + 1)]
+    conv = [st["conv"][cut[k]:cut[k + 1]].copy() for k in range(P)]
+    rec = [st["recurrent"][cut[k]:cut[k + 1]].copy() for k in range(P)]
+
+    def work(k):
+        r0, r1 = cut[k], cut[k + 1]
+        _, conv[k], rec[k], _, _ = O.mixer_forward(s, mixed[r0:r1], z[r0:r1], a[r0:r1], b[r0:r1], p["conv1d.weight"],
+                                                   p["A_log"], p["dt_bias"], p["norm.weight"], "bf16", conv[k],
+                                                   rec[k], chunk=False)
+
+    with threadpool_limits(limits=1, user_api="blas"), ThreadPoolExecutor(P) as ex:
+        list(ex.map(work, range(P)))  # warm-up
+        n, t0 = 0, time.perf_counter()
+        while True:
+            list(ex.map(work, range(P)))
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= sample_s or n >= 400:
+                break
+    return n / el, n, el, P
+
+
+def cpu_prefill_rate(threads: int, rows: int = 8, T: int = 1024):
+    """The oracle's chunked prefill (deltanet.py:236-407 + conv + gated norm) on ``rows`` batch rows
+    of the prefill workload's layout (16 / 32 heads, d 128, bf16), T tokens each, one row per host
+    thread.  The chunked algorithm's cost is linear in the tokens, so tokens/s of this sample is
+    the rate at the full batch 8 x 8192.  Returns (tokens/s, seconds, threads used)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from threadpoolctl import threadpool_limits
+
+    from oracle import gdn_oracle as O
+
+    s = W.SHAPE_QWEN
+    p = W.make_layer_params(s, 1, "bf16")
+    P = max(1, min(threads, rows))
+    rng = np.random.default_rng(3)
+    f = lambda *sh, sc=1.0: W.cast(sc * rng.standard_normal(sh).astype(np.float32), "bf16")  # noqa: E731
+    ins = [(f(1, T, s.conv_dim, sc=0.7), f(1, T, s.num_v_heads, s.head_v_dim), f(1, T, s.num_v_heads),
+            f(1, T, s.num_v_heads)) for _ in range(rows)]
+
+    def work(k):
+        mixed, z, a, b = ins[k]
+        O.mixer_forward(s, mixed, z, a, b, p["conv1d.weight"], p["A_log"], p["dt_bias"], p["norm.weight"], "bf16")
+
+    blas = max(1, threads // P)
+    with threadpool_limits(limits=blas, user_api="blas"), ThreadPoolExecutor(P) as ex:
+        t0 = time.perf_counter()
+        list(ex.map(work, range(rows)))
         el = time.perf_counter() - t0
-        if el >= sample_s or n >= 200:
-            break
-    return n / el, n, el
+    return rows * T / el, el, P * blas
+
+
+def cpu_layer_cpu_plumbing():
+    """The reference's CPU-runnable case: one fp32 layer, batch 1 x 256 tokens, hidden 1024,
+    8 / 8 heads of 128, through the oracle's layer forward (projections, conv, chunked delta rule,
+    gated norm, out_proj, hybrid-cache side effects), then a 16-token decode continuation.
+    Returns (prefill ms, decode ms per token)."""
+    from oracle import gdn_oracle as O
+
+    wl = W.WORKLOADS["cpu_plumbing"]
+    p = W.make_layer_params(wl.shape, wl.w_seed, "f32")
+    x = W.make_hidden(wl)
+    cache = O.OracleCache()
+    t0 = time.perf_counter()
+    O.deltanet_layer_forward(p, wl.shape, x, "f32", cache=cache)
+    t_pre = time.perf_counter() - t0
+    cache.past_seen_tokens = wl.seq_len
+    xs = [W.make_hidden(wl, seq_len=1, seed_offset=i + 1) for i in range(16)]
+    t0 = time.perf_counter()
+    for xd in xs:
+        O.deltanet_layer_forward(p, wl.shape, xd, "f32", cache=cache)
+        cache.past_seen_tokens += 1
+    t_dec = (time.perf_counter() - t0) / 16
+    return t_pre * 1e3, t_dec * 1e3
 
 
 def cpu_cores() -> int:
@@ -232,22 +305,42 @@ def cpu_cores() -> int:
         return os.cpu_count() or 1
 
 
+def cpu_baselines(args, full: bool):
+    """The CPU restatement of the reference path (the numpy oracle) timed on this host's cores:
+    the decode workload (B64), and with ``full`` also the prefill workload's per-token rate and
+    the reference's CPU-runnable layer case."""
+    threads = cpu_cores()
+    rate, n, el, P = cpu_decode_rate(args.cpu_sample_s, threads)
+    out = {"value": rate, "unit": "steps/s", "cores": P, "kind": "port",
+           "sample": f"{n} decode steps of the numpy oracle at B64 x 32 heads ({el:.1f} s), the 64 rows split "
+                     f"over {P} host threads (BLAS one thread each)"}
+    if full:
+        tps, pel, pc = cpu_prefill_rate(threads)
+        out["prefill"] = {"value": tps, "unit": "tokens/s", "cores": pc, "kind": "port",
+                          "sample": f"the numpy oracle's chunked prefill on 8 rows x 1024 tokens of the prefill "
+                                    f"layout ({pel:.1f} s), one row per host thread; the cost is linear in the "
+                                    f"tokens, so this is the rate at 8 x 8192"}
+        pre_ms, dec_ms = cpu_layer_cpu_plumbing()
+        out["cpu_plumbing_layer"] = {"prefill_ms": pre_ms, "decode_ms_per_token": dec_ms, "cores": 1,
+                                     "kind": "port",
+                                     "sample": "one fp32 layer, B1 x 256 tokens, hidden 1024, 8 / 8 heads of 128, "
+                                               "then 16 decode tokens (numpy, BLAS on the host cores)"}
+    return out
+
+
 def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
-    rates = []
-    for _ in range(max(1, args.steps if args.steps < 3 else 3)):
-        r, n, el = cpu_decode_rate(max(3.0, args.cpu_sample_s / 3))
-        rates.append(r)
-    rate = statistics.median(rates)
+    base = cpu_baselines(args, full=True)
+    rate = base["value"]
     line = {
         "metric": "DeltaNet decode steps/s (B64, 16/32 heads, d128, bf16, fp32 state)",
         "value": rate, "unit": "steps/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 / rate, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": DECODE_RUN_STEPS * 1000.0 / rate, "ms_per_decode_step": 1000.0 / rate,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (seeded numpy)", "impl": "reference",
         "config": decode_config(args.gpus),
-        "cpu_baseline": {"value": rate, "unit": "steps/s", "cores": cpu_cores(), "kind": "port",
-                         "sample": f"numpy oracle decode step at B64 x 32 heads, median of {len(rates)} samples"},
+        "cpu_baseline": base,
         "e2e": {"value": rate, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -466,6 +559,10 @@ def run_ours(args, rank: int, world: int) -> None:
     if not args.no_rollback:
         rollback = run_rollback(torch, dist, m, local, dev, world, barrier)
 
+    sharded = None
+    if not args.no_sharded:
+        sharded = run_sharded_layer(torch, dist, m, local, rank, world, dev, barrier)
+
     stack = None
     if not args.no_stack and world == 1:
         try:
@@ -502,12 +599,15 @@ def run_ours(args, rank: int, world: int) -> None:
         line["prefill"] = prefill
     if rollback is not None:
         line["rollback"] = rollback
+    if sharded is not None:
+        line["sharded_layer"] = sharded
     if stack is not None:
         line["stack"] = stack
     if world == 1 and not args.no_cpu_baseline:
-        rate, n, el = cpu_decode_rate(args.cpu_sample_s)
-        line["cpu_baseline"] = {"value": rate, "unit": "steps/s", "cores": cpu_cores(), "kind": "port",
-                                "sample": f"{n} decode steps of the numpy oracle at B64 x 32 heads ({el:.1f} s)"}
+        base = cpu_baselines(args, full=prefill is not None)
+        if prefill is not None and "prefill" in base:
+            prefill["cpu_baseline"] = base.pop("prefill")
+        line["cpu_baseline"] = base
     print(json.dumps(line), flush=True)
 
 
@@ -644,6 +744,243 @@ def run_stack(torch, dev):
             "path": "visionstack_b200.stack.Qwen3_5TextModel (prefill eager, decode from one CUDA graph); "
                     "DeltaNet layers on gdn_mixer_prefill_ws / gdn_mixer_decode, decode attention on "
                     "gdn_attn_decode, prefill attention on torch SDPA, GEMMs on cuBLAS"}
+
+
+
+# ----------------------------------------------------------------------------
+# the head-sharded layer: input projections, token mixer, out_proj, all-reduce
+# ----------------------------------------------------------------------------
+
+def _allreduce_busbw(nbytes: int, ms: float, world: int) -> float:
+    """NCCL-convention bus bandwidth of an all-reduce: bytes * 2 (N - 1) / N / time."""
+    return nbytes * 2.0 * (world - 1) / world / (ms * 1e-3) / 1e9 if world > 1 and ms > 0 else 0.0
+
+
+def _ev_time(torch, fn, reps: int, stream=None) -> float:
+    """Mean ms of ``fn`` over ``reps`` calls, CUDA events on the current stream."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def _max_over_ranks(torch, dist, world, dev, *vals):
+    t = torch.tensor(list(vals), device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
+
+
+def sharded_decode(torch, dist, m, local, dev, world, barrier, Bg: int, steps: int = 256, graph_steps: int = 32):
+    """One decode step of the value-head-sharded layer at global batch Bg: this rank's fused input
+    projection, the token mixer on its heads (state in place), its out_proj column slice, and the
+    all-reduce (NCCL, bf16 sum) of the [Bg, 1, hidden] partial outputs.  Steps replay from CUDA
+    graphs of ``graph_steps`` steps; state slots rotate so the states never sit in L2."""
+    import torch.nn.functional as F
+    hv, d, H = local.num_v_heads, local.head_k_dim, W.SHAPE_QWEN.hidden_size
+    state_bytes = Bg * hv * d * d * 4
+    nslot = max(2, -(-300_000_000 // state_bytes))
+    nslot += nslot % 2
+    NIN = 16
+    g = torch.Generator(device=dev)
+    g.manual_seed(2)
+    with torch.no_grad():
+        xs = torch.randn(NIN, Bg, 1, H, generator=g, device=dev).to(torch.bfloat16)
+        states = [0.02 * torch.randn(Bg, hv, d, d, generator=g, device=dev) for _ in range(nslot)]
+        convs = [[torch.zeros(Bg, local.conv_dim, 3, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+                 for _ in range(nslot)]
+        core = torch.empty(Bg, 1, local.value_dim, dtype=torch.bfloat16, device=dev)
+        y = torch.empty(Bg, 1, H, dtype=torch.bfloat16, device=dev)
+    w_out = m.out_proj.weight
+    plan = m.mixer_plan(Bg, 1, torch.bfloat16, dev, token_by_token=True)
+
+    def step(i, reduce=True):
+        slot = i % nslot
+        mixed, z, bb, aa = m.project(xs[i % NIN])
+        plan(mixed, z, bb, aa, convs[slot][(i // nslot) % 2], states[slot], convs[slot][(i // nslot + 1) % 2],
+             states[slot], core)
+        torch.matmul(core, w_out.t(), out=y)
+        if reduce and world > 1:
+            dist.all_reduce(y, op=dist.ReduceOp.SUM)
+
+    stream = torch.cuda.Stream(device=dev)
+    with torch.no_grad(), torch.cuda.stream(stream):
+        for i in range(4):
+            step(i)
+    torch.cuda.synchronize(dev)
+    graphs = {}
+    try:
+        for reduce in (True, False):
+            gr = torch.cuda.CUDAGraph()
+            with torch.no_grad(), torch.cuda.graph(gr, stream=stream):
+                for i in range(graph_steps):
+                    step(i, reduce)
+            graphs[reduce] = gr
+        mode = "CUDA graphs"
+    except Exception as e:  # a capture the library refuses: time the eager loop instead
+        graphs = {}
+        mode = f"eager ({type(e).__name__})"
+    torch.cuda.synchronize(dev)
+    reps = max(1, steps // graph_steps)
+
+    def run(reduce):
+        if graphs:
+            graphs[reduce].replay()
+        else:
+            with torch.no_grad():
+                for i in range(graph_steps):
+                    step(i, reduce)
+
+    with torch.cuda.stream(stream):
+        run(True)
+        run(False)
+        barrier()
+        ms_full = _ev_time(torch, lambda: run(True), reps) / graph_steps
+        barrier()
+        ms_local = _ev_time(torch, lambda: run(False), reps) / graph_steps
+        barrier()
+        # the all-reduce of one step's partial outputs, alone
+        ms_ar = _ev_time(torch, lambda: dist.all_reduce(y, op=dist.ReduceOp.SUM), 64) if world > 1 else 0.0
+        barrier()
+    graphs.clear()
+    ms_full, ms_local, ms_ar = _max_over_ranks(torch, dist, world, dev, ms_full, ms_local, ms_ar)
+    ar_bytes = Bg * H * 2
+    w_bytes = sum(p.numel() * p.element_size() for n, p in m.named_parameters())
+    hbm_bytes = w_bytes + decode_bytes(Bg, local.num_k_heads, hv, d, 4) + 2 * Bg * H * 2
+    hbm, _, src = measured_peaks()
+    return {"global_batch": Bg, "ms_per_step": ms_full, "steps_per_s": 1000.0 / ms_full,
+            "ms_per_step_without_allreduce": ms_local, "allreduce_ms_alone": ms_ar,
+            "allreduce_bytes": ar_bytes, "allreduce_busbw_gbs": _allreduce_busbw(ar_bytes, ms_ar, world),
+            "roofline": {"bound": "hbm", "bytes_per_gpu_per_step": hbm_bytes,
+                         "achieved": hbm_bytes / (ms_full * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": hbm_bytes / (ms_full * 1e-3) / 1e9 / hbm, "peak_source": src},
+            "timing": mode}
+
+
+def sharded_prefill(torch, dist, m, local, dev, world, barrier, Bg: int, T: int, slabs: int = 4, reps: int = 3):
+    """Prefill of the value-head-sharded layer at global batch Bg x T tokens, the sequence cut into
+    ``slabs`` T-slabs: per slab this rank's input projection, the token mixer on its heads (states
+    handed from slab to slab), its out_proj partial, and that slab's all-reduce issued
+    asynchronously, so NCCL's stream reduces slab i while slab i + 1 computes."""
+    H = W.SHAPE_QWEN.hidden_size
+    hv, d = local.num_v_heads, local.head_k_dim
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    with torch.no_grad():
+        x = torch.randn(Bg, T, H, generator=g, device=dev).to(torch.bfloat16)
+        S = torch.empty(Bg, hv, d, d, device=dev)
+        cs = [torch.empty(Bg, local.conv_dim, 3, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    bounds = [T * i // slabs for i in range(slabs + 1)]
+    with torch.no_grad():
+        # per slab: a contiguous gated-norm output and a contiguous partial output (NCCL reduces
+        # whole tensors; the slabs' reductions stay in flight while the next slab computes)
+        core = torch.empty(Bg, bounds[1], local.value_dim, dtype=torch.bfloat16, device=dev)
+        ys = [torch.empty(Bg, bounds[i + 1] - bounds[i], H, dtype=torch.bfloat16, device=dev) for i in range(slabs)]
+    w_out = m.out_proj.weight
+
+    def once(reduce=True):
+        works = []
+        with torch.no_grad():
+            for i in range(slabs):
+                t0, t1 = bounds[i], bounds[i + 1]
+                mixed, z, bb, aa = m.project(x[:, t0:t1])
+                c = core.view(-1)[:Bg * (t1 - t0) * local.value_dim].view(Bg, t1 - t0, local.value_dim)
+                m.mixer(mixed, z, bb, aa, conv_state=cs[(i + 1) % 2] if i else None, rec_state=S if i else None,
+                        conv_state_out=cs[i % 2], rec_state_out=S, out=c, token_by_token=False)
+                torch.matmul(c, w_out.t(), out=ys[i])
+                if reduce and world > 1:
+                    works.append(dist.all_reduce(ys[i], op=dist.ReduceOp.SUM, async_op=True))
+        for w in works:
+            w.wait()
+
+    once()
+    once(False)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms_full = _ev_time(torch, once, reps)
+    barrier()
+    ms_local = _ev_time(torch, lambda: once(False), reps)
+    barrier()
+    ms_ar = _ev_time(torch, lambda: [dist.all_reduce(t, op=dist.ReduceOp.SUM) for t in ys], reps) \
+        if world > 1 else 0.0
+    barrier()
+    ms_full, ms_local, ms_ar = _max_over_ranks(torch, dist, world, dev, ms_full, ms_local, ms_ar)
+    _, tflops, src = measured_peaks()
+    gemm_fl = 2.0 * Bg * T * H * (local.conv_dim + local.value_dim + 2 * hv) + 2.0 * Bg * T * local.value_dim * H
+    fl = gemm_fl + prefill_flops(Bg, T, hv, d)
+    ar_bytes = Bg * T * H * 2
+    return {"global_batch": Bg, "seq_len": T, "slabs": slabs, "ms_per_call": ms_full,
+            "tokens_per_s": Bg * T / (ms_full * 1e-3), "ms_per_call_without_allreduce": ms_local,
+            "allreduce_ms_alone": ms_ar, "allreduce_bytes": ar_bytes,
+            "allreduce_busbw_gbs": _allreduce_busbw(ar_bytes, ms_ar, world),
+            "allreduce_exposed_ms": max(0.0, ms_full - ms_local),
+            "roofline": {"bound": "tensor", "flops_per_gpu": fl, "achieved": fl / (ms_full * 1e-3) / 1e12,
+                         "peak": tflops, "unit": "TFLOP/s", "frac": fl / (ms_full * 1e-3) / 1e12 / tflops,
+                         "peak_source": src}}
+
+
+def sharded_parity(torch, dist, m, local, rank, world, dev):
+    """Rank 0's all-reduced output of one sharded prefill (B2 x 300) and one decode step against the
+    unsharded layer (all heads, the same weights) on the same GPU: max abs difference."""
+    import torch.nn.functional as F
+    H = W.SHAPE_QWEN.hidden_size
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    x = torch.randn(2, 300, H, generator=g, device=dev).to(torch.bfloat16)
+    xd = torch.randn(2, 1, H, generator=g, device=dev).to(torch.bfloat16)
+
+    def layer_out(layer, lc, reduce):
+        with torch.no_grad():
+            S = torch.empty(2, lc.num_v_heads, lc.head_k_dim, lc.head_v_dim, device=dev)
+            cs = torch.empty(2, lc.conv_dim, 3, dtype=torch.bfloat16, device=dev)
+            cs2 = torch.empty_like(cs)
+            mixed, z, bb, aa = layer.project(x)
+            y = F.linear(layer.mixer(mixed, z, bb, aa, conv_state_out=cs, rec_state_out=S, token_by_token=False),
+                         layer.out_proj.weight)
+            mixed, z, bb, aa = layer.project(xd)
+            yd = F.linear(layer.mixer(mixed, z, bb, aa, conv_state=cs, rec_state=S, conv_state_out=cs2,
+                                      rec_state_out=S, token_by_token=True), layer.out_proj.weight)
+            if reduce and world > 1:
+                dist.all_reduce(y, op=dist.ReduceOp.SUM)
+                dist.all_reduce(yd, op=dist.ReduceOp.SUM)
+        return y.float(), yd.float()
+
+    y, yd = layer_out(m, local, True)
+    res = None
+    if rank == 0:
+        full, lfull = build_shard_layer(torch, 0, 1, dev)
+        ry, ryd = layer_out(full, lfull, False)
+        res = {"prefill_B2xT300_max_abs": float((y - ry).abs().max()), "decode_step_max_abs": float((yd - ryd).abs().max()),
+               "reference": "the unsharded layer (all 32 value heads, same weights) on rank 0's GPU; outputs bf16"}
+        del full
+    torch.cuda.synchronize(dev)
+    return res
+
+
+
+def run_sharded_layer(torch, dist, m, local, rank, world, dev, barrier):
+    """The value-head-sharded layer (this rank's heads, out_proj columns, one all-reduce): decode at
+    the fixed global batch 64 (strong scaling) and at 64 per GPU (weak), prefill at the fixed global
+    batch 8 x 8192 (strong) and 8 x 8192 per GPU (weak), and rank 0's output against the unsharded
+    layer."""
+    res = {"world": world,
+           "layer": "head-sharded Gated DeltaNet layer: fused input projection of this rank's rows (cuBLAS), "
+                    "token mixer on its 32/N value heads, out_proj column slice (cuBLAS), NCCL all-reduce "
+                    "(bf16 sum) of the partial outputs"}
+    res["decode_strong"] = sharded_decode(torch, dist, m, local, dev, world, barrier, 64)
+    if world > 1:
+        res["decode_weak"] = sharded_decode(torch, dist, m, local, dev, world, barrier, 64 * world)
+    res["prefill_strong"] = sharded_prefill(torch, dist, m, local, dev, world, barrier, 8, 8192)
+    if world > 1:
+        res["prefill_weak"] = sharded_prefill(torch, dist, m, local, dev, world, barrier, 8 * world, 8192)
+    par = sharded_parity(torch, dist, m, local, rank, world, dev)
+    if par is not None:
+        res["parity_vs_unsharded"] = par
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_rollback(torch, dist, m, local, dev, world, barrier, steps=1024):
