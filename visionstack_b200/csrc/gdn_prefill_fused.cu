@@ -70,9 +70,9 @@ constexpr uint32_t HROWS = 4, HATOM = HROWS * 128;
 constexpr uint32_t R_HIST = ((R_VEC + NQK * VEC_FLOATS * 4) + 1023u) & ~1023u;
 constexpr uint32_t R_HQK = R_HIST, R_HV = R_HIST + NQK * 4 * HATOM;
 constexpr uint32_t R_SCR = R_HV + NVB * 2 * HATOM;
-// scratch floats: norm weight, partial sums (output-norm partials, or the conv's norm
-// partials: q / k x 2 atoms x 64 tokens), rstd, checkpoint decay
-constexpr int S_NW = 0, S_PART = 128, S_RSTD = 384, S_F = 448, S_END = 512;
+// scratch floats: the gated-norm weight (as 128 bf16), the conv's norm partials (q / k x 2 atoms
+// x 64 tokens), checkpoint decay
+constexpr int S_PART = 128, S_F = 448, S_END = 512;
 constexpr uint32_t R_BAR = R_SCR + S_END * 4;
 constexpr int NBAR = 20;
 constexpr uint32_t SMEM_BYTES = R_BAR + NBAR * 8 + 64 + 1024;
@@ -104,6 +104,7 @@ __device__ __forceinline__ uint32_t bf2_bits(float a, float b) {
     const __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<const uint32_t*>(&t);
 }
+__device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
 __device__ __forceinline__ void round2_bf16(float& a, float& b, uint32_t* bits = nullptr) {
     const uint32_t u = bf2_bits(a, b);
     a = bf_lo(u);
@@ -169,6 +170,23 @@ __device__ __forceinline__ uint32_t img_off(int i, int j) {
     return (uint32_t)((j >> 5) * 8192 + i * 128 + ((((j & 31) >> 2) ^ (i & 7)) << 4) + ((j & 3) << 2));
 }
 
+// 2^x and 1/x on the special-function unit (PTX ex2.approx / rcp.approx, flush to zero)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// SiLU of an fp32 pair, x / (1 + e^-x) with e^-x = 2^(-x log2(e)), on packed fp32x2 arithmetic
+__device__ __forceinline__ float2 silu2(float2 x) {
+    const float2 a = __fmul2_rn(x, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+    const float2 d = __fadd2_rn(make_float2(ex2_approx(a.x), ex2_approx(a.y)), make_float2(1.f, 1.f));
+    return __fmul2_rn(x, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
+}
 // conv + SiLU of one bf16 channel pair: taps newest first, one bf16 rounding per tap (the first
 // a bf16 product, then fused multiply-adds: deltanet.py:66-80); SiLU in fp32, rounded to bf16
 __device__ __forceinline__ uint32_t conv_silu_pair(__nv_bfloat162 x0, __nv_bfloat162 x1, __nv_bfloat162 x2,
@@ -177,10 +195,62 @@ __device__ __forceinline__ uint32_t conv_silu_pair(__nv_bfloat162 x0, __nv_bfloa
     acc = __hfma2(x1, w[2], acc);
     acc = __hfma2(x2, w[1], acc);
     acc = __hfma2(x3, w[0], acc);
-    const float ca = __low2float(acc), cb = __high2float(acc);
-    return bf2_bits(__fdividef(ca, 1.0f + __expf(-ca)), __fdividef(cb, 1.0f + __expf(-cb)));
+    const float2 s = silu2(__bfloat1622float2(acc));
+    return bf2_bits(s.x, s.y);
 }
-__device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
+// conv + SiLU in place of 32 consecutive tokens of one q / k channel pair in a 128-byte swizzled
+// 64-row block (o8[r]: byte offset of the pair in row r of each 8-row group), with the raw values
+// of the three tokens before; sq[j] = sum of squares of the pair's two outputs of token j.
+// Tokens at or past `nvalid` (kGuard) are outputs 0 (past the sequence end).
+template <bool kGuard>
+__device__ __forceinline__ void conv_qk32(unsigned char* base, const uint32_t (&o8)[8], uint32_t h1, uint32_t h2,
+                                          uint32_t h3, const __nv_bfloat162 (&w)[4], int nvalid, float (&sq)[32]) {
+    __nv_bfloat162 x1 = as_bf2(h1), x2 = as_bf2(h2), x3 = as_bf2(h3);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        uint32_t* cell = reinterpret_cast<uint32_t*>(base + (j >> 3) * 1024 + o8[j & 7]);
+        const __nv_bfloat162 x0 = as_bf2(*cell);
+        const uint32_t o = (!kGuard || j < nvalid) ? conv_silu_pair(x0, x1, x2, x3, w) : 0u;
+        *cell = o;
+        x3 = x2;
+        x2 = x1;
+        x1 = x0;
+        const float2 f = make_float2(bf_lo(o), bf_hi(o));
+        const float2 f2 = __fmul2_rn(f, f);
+        sq[j] = f2.x + f2.y;
+    }
+}
+// the same for 16 tokens of one v channel pair in row-major [64][128] bf16 rows (base: the
+// first token's cell)
+template <bool kGuard>
+__device__ __forceinline__ void conv_v16(unsigned char* base, uint32_t h1, uint32_t h2, uint32_t h3,
+                                         const __nv_bfloat162 (&w)[4], int nvalid) {
+    __nv_bfloat162 x1 = as_bf2(h1), x2 = as_bf2(h2), x3 = as_bf2(h3);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        uint32_t* cell = reinterpret_cast<uint32_t*>(base + j * 256);
+        const __nv_bfloat162 x0 = as_bf2(*cell);
+        *cell = (!kGuard || j < nvalid) ? conv_silu_pair(x0, x1, x2, x3, w) : 0u;
+        x3 = x2;
+        x2 = x1;
+        x1 = x0;
+    }
+}
+// A wait expected to be long (one role waiting for the other, or for a tensor copy): polls with
+// a short sleep between tries so the waiting warps leave the issue slots to the working ones;
+// bounded like mbar_wait_bounded.
+__device__ __forceinline__ bool mbar_wait_patient(uint32_t bar, uint32_t parity, unsigned int err_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 1;; ++it) {
+        __nanosleep(it < 16 ? 20 : 100);
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63u) == 0u && global_timer_ns() - t0 > GDN_WAIT_LIMIT_NS) {
+            atomicOr(&g_device_error, err_flag);
+            return false;
+        }
+    }
+}
 
 struct FusedMaps {
     CUtensorMap qk;    // raw mixed rows, box 64 channels x 64 tokens, 128-byte swizzle
@@ -198,9 +268,7 @@ __global__ void __launch_bounds__(NT, 1)
     unsigned char* sm = raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
     const uint32_t sb = smem_u32(sm);
     float* scr = reinterpret_cast<float*>(sm + R_SCR);
-    float* sNW = scr + S_NW;
     float* sPart = scr + S_PART;
-    float* sRstd = scr + S_RSTD;
     float* sF = scr + S_F;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + R_BAR);
     uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + R_BAR + NBAR * 8);
@@ -227,7 +295,7 @@ __global__ void __launch_bounds__(NT, 1)
         prefetch_tmap(&maps.z);
         prefetch_tmap(&maps.out);
     }
-    if (tid < D) sNW[tid] = Act<TA>::ldg(static_cast<const TA*>(p.normw) + tid);
+    if (tid < D) reinterpret_cast<TA*>(sm + R_SCR)[tid] = static_cast<const TA*>(p.normw)[tid];  // bf16
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
@@ -373,8 +441,8 @@ __global__ void __launch_bounds__(NT, 1)
             bad |= !ok;
             if (ok) mma_pending = false;
         };
-        auto wait_phase = [&](uint32_t br, int phase) {
-            bad |= !mbar_wait_bounded(br, (uint32_t)phase & 1u, GDN_DEVERR_TMA_TIMEOUT);
+        auto wait_phase = [&](uint32_t br, int phase) {  // signals of the producer warps
+            bad |= !mbar_wait_patient(br, (uint32_t)phase & 1u, GDN_DEVERR_TMA_TIMEOUT);
         };
         auto stores_to_warp0 = [&]() {
             umma::fence_before_sync();
@@ -392,7 +460,7 @@ __global__ void __launch_bounds__(NT, 1)
             // ---------------- MMA-b (after the output warps released O of the last chunk) ----------------
             if (warp == 0) {
                 wait_phase(bar(B_KQ + c % NQK), c / NQK);
-                if (c > 0) bad |= !mbar_wait_bounded(bar(B_OFREE), (uint32_t)(c - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
+                if (c > 0) bad |= !mbar_wait_patient(bar(B_OFREE), (uint32_t)(c - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
                 __syncwarp();
                 umma::fence_after_sync();
                 const uint64_t d_k = umma::desc_kmajor0(sb + r_qk), d_q = umma::desc_kmajor0(sb + r_qk + 8192);
@@ -443,7 +511,7 @@ __global__ void __launch_bounds__(NT, 1)
             if (warp == 0) {
                 wait_phase(bar(B_TPR + c % NTP), c / NTP);
                 const int gp = c + 1 < NC ? c + 1 : (c == 0 ? 0 : -1);
-                if (gp >= 0) bad |= !mbar_wait_bounded(bar(B_GPFREE), (uint32_t)gp & 1u, GDN_DEVERR_MMA_TIMEOUT);
+                if (gp >= 0) bad |= !mbar_wait_patient(bar(B_GPFREE), (uint32_t)gp & 1u, GDN_DEVERR_MMA_TIMEOUT);
                 __syncwarp();
                 umma::fence_after_sync();
                 const uint64_t d_t = umma::desc_kmajor0(sb + r_tp);
@@ -615,7 +683,6 @@ __global__ void __launch_bounds__(NT, 1)
         // ================ producer and output rows (warpgroups 2-3, 256 threads) ================
         const int ptid = tid - NMAIN;
         const int owg = wg - 2, tw = 32 * owg;  // output tokens / [G; P0] columns tw .. tw + 31
-        const float nw = sNW[dv];
         const TA* convw = static_cast<const TA*>(p.convw);
         const TA* cs_in = static_cast<const TA*>(p.cs_in);
         // this thread's q / k channel pair (conv of 32 tokens) and v channel pair (16 tokens)
@@ -625,6 +692,16 @@ __global__ void __launch_bounds__(NT, 1)
         const int gqk = (isk ? p.Hk * D : 0) + kh * D + qch;
         const int qt = ptid >> 6, vch = 2 * (ptid & 63);
         const int gv = v_ch + vch;
+        // output rows: token otok, channels 32 osg .. 32 osg + 31 as four 16-byte units, visited
+        // in a per-lane rotated order (ounit[k] = byte offset in the row, nw2: the weights of the
+        // same units)
+        const int otok = ptid >> 2, osg = ptid & 3;
+        uint32_t ounit[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) ounit[k] = (uint32_t)(4 * osg + ((k + osg + (otok & 1)) & 3)) * 16u;
+        uint32_t o8[8];  // byte offset of this thread's q / k pair in row r of an 8-row swizzle group
+#pragma unroll
+        for (int r = 0; r < 8; ++r) o8[r] = sw128(r, qchl);
         __nv_bfloat162 wqk[4], wvv[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -652,9 +729,9 @@ __global__ void __launch_bounds__(NT, 1)
         //     factors, gates and per-token vectors of chunk cq; signals kq_ready(cq), v_ready(cv)
         auto prep = [&](int cq, int cv) {
             const int t0q = (c_base + cq) * C, t0v = (c_base + cv) * C;
-            if (cq >= 0) bad |= !mbar_wait_bounded(bar(B_RAWQK + cq % NQK), (uint32_t)(cq / NQK) & 1u,
+            if (cq >= 0) bad |= !mbar_wait_patient(bar(B_RAWQK + cq % NQK), (uint32_t)(cq / NQK) & 1u,
                                                    GDN_DEVERR_TMA_TIMEOUT);
-            if (cv >= 0) bad |= !mbar_wait_bounded(bar(B_RAWV + cv % NVB), (uint32_t)(cv / NVB) & 1u,
+            if (cv >= 0) bad |= !mbar_wait_patient(bar(B_RAWV + cv % NVB), (uint32_t)(cv / NVB) & 1u,
                                                    GDN_DEVERR_TMA_TIMEOUT);
             float raw_a = 0.f, raw_b = 0.f;
             if (cq >= 0 && ptid < C && t0q + ptid < p.T) {
@@ -701,21 +778,12 @@ __global__ void __launch_bounds__(NT, 1)
             nb_sync(4, NT - NMAIN);
             // phase 2: conv + SiLU in place; outputs of tokens past the sequence end are zero
             if (cq >= 0) {
-                __nv_bfloat162 x1 = as_bf2(q1), x2 = as_bf2(q2), x3 = as_bf2(q3);
                 float sq[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int t = 32 * hf + j;
-                    uint32_t* cell = reinterpret_cast<uint32_t*>(qkb + sw128(t, qchl));
-                    const __nv_bfloat162 x0 = as_bf2(*cell);
-                    const uint32_t o = t0q + t < p.T ? conv_silu_pair(x0, x1, x2, x3, wqk) : 0u;
-                    *cell = o;
-                    x3 = x2;
-                    x2 = x1;
-                    x1 = x0;
-                    const float a0 = bf_lo(o), a1 = bf_hi(o);
-                    sq[j] = fmaf(a0, a0, a1 * a1);
-                }
+                const int nval = p.T - (t0q + 32 * hf);
+                if (nval >= 32)
+                    conv_qk32<false>(qkb + 4096 * hf, o8, q1, q2, q3, wqk, nval, sq);
+                else
+                    conv_qk32<true>(qkb + 4096 * hf, o8, q1, q2, q3, wqk, nval, sq);
                 // per-token sums over this warp's 64 channels: halving exchange that leaves token
                 // 32 hf + lane in this lane
 #pragma unroll
@@ -732,17 +800,12 @@ __global__ void __launch_bounds__(NT, 1)
                 sPart[(isk ? 128 : 0) + qatom * 64 + 32 * hf + lane] = sq[0];
             }
             if (cv >= 0) {
-                __nv_bfloat162 x1 = as_bf2(v1), x2 = as_bf2(v2), x3 = as_bf2(v3);
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int t = 16 * qt + j;
-                    uint32_t* cell = reinterpret_cast<uint32_t*>(vb + t * 256 + vch * 2);
-                    const __nv_bfloat162 x0 = as_bf2(*cell);
-                    *cell = t0v + t < p.T ? conv_silu_pair(x0, x1, x2, x3, wvv) : 0u;
-                    x3 = x2;
-                    x2 = x1;
-                    x1 = x0;
-                }
+                const int nval = p.T - (t0v + 16 * qt);
+                unsigned char* vcell = vb + 16 * qt * 256 + vch * 2;
+                if (nval >= 16)
+                    conv_v16<false>(vcell, v1, v2, v3, wvv, nval);
+                else
+                    conv_v16<true>(vcell, v1, v2, v3, wvv, nval);
             }
             fence_proxy_async_smem();  // the conv outputs are read by the tensor cores next
             nb_sync(4, NT - NMAIN);
@@ -925,7 +988,7 @@ __global__ void __launch_bounds__(NT, 1)
             const int cq = c + 2 < NC ? c + 2 : -1, cv = c + 1 < NC ? c + 1 : -1;
             if (cq >= 0 || cv >= 0) prep(cq, cv);
             // b. O of chunk c out of tensor memory; [G; P0], A and P of chunk c + 2
-            bad |= !mbar_wait_bounded(bar(B_ORDY), (uint32_t)c & 1u, GDN_DEVERR_MMA_TIMEOUT);
+            bad |= !mbar_wait_patient(bar(B_ORDY), (uint32_t)c & 1u, GDN_DEVERR_MMA_TIMEOUT);
             umma::fence_after_sync();
             if (cq >= 0) issue_gp(cq);
             const float* sv = vecs(c);
@@ -940,72 +1003,74 @@ __global__ void __launch_bounds__(NT, 1)
             }
             umma::fence_before_sync();
             mbar_arrive(bar(B_OFREE));  // these tensor-memory columns may be overwritten now
+            {  // O rounded to bf16 (the reference's core output dtype), token-major, into the v
+               // buffer of chunk c (its v rows were consumed by Z before MMA-c)
+                uint16_t* col = reinterpret_cast<uint16_t*>(sm + R_V + V_BYTES * (uint32_t)(c % NVB)) + tw * D + dv;
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const uint32_t u = bf2_bits(o[j], o[j + 1]);
+                    col[j * D] = (uint16_t)(u & 0xFFFFu);
+                    col[(j + 1) * D] = (uint16_t)(u >> 16);
+                }
+            }
             if (cq >= 0) build_ap(cq);
-            // the raw rows of chunks c + 3 (q / k) and c + 2 (v) into the buffers chunk c used
-            // (every MMA and checkpoint read of them is complete: o_ready of chunk c)
+            // the raw q / k rows of chunk c + 3 into the buffer chunk c used (every MMA and
+            // checkpoint read of it is complete: o_ready of chunk c)
             if (ptid == 0 && !bad) {
                 if (c + 3 < NC) {
                     issue_qk(c + 3);
                     ++n_rqk[(c + 3) % NQK];
                 }
-                if (c + 2 < NC) {
-                    issue_v(c + 2);
-                    ++n_rv[(c + 2) % NVB];
-                }
             }
-            // c. output rows of chunk c through the gated RMSNorm (config.py:136-143)
-#pragma unroll
-            for (int j = 0; j < 32; j += 2) round2_bf16(o[j], o[j + 1]);
-            float sq[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) sq[j] = o[j] * o[j];
-#pragma unroll
-            for (int st = 0; st < 5; ++st) {
-                const int s = 16 >> st, half = 16 >> st;
-                const bool up = (lane & s) != 0;
-#pragma unroll
-                for (int k = 0; k < half; ++k) {
-                    const float send = up ? sq[k] : sq[k + half];
-                    const float keep = up ? sq[k + half] : sq[k];
-                    sq[k] = keep + __shfl_xor_sync(0xffffffffu, send, s);
-                }
-            }
-            sPart[q4 * C + tw + lane] = sq[0];
-            nb_sync(2 + owg, 128);
-            if (q4 == 0) {
-                const int t = tw + lane;
-                const float ss = (sPart[t] + sPart[C + t]) + (sPart[2 * C + t] + sPart[3 * C + t]);
-                sRstd[t] = rsqrtf(ss / (float)D + p.eps);
-            }
-            const bool zok = mbar_wait_bounded(bar(B_Z), (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            // c. output rows of chunk c through the gated RMSNorm (config.py:136-143), from O staged
+            //    token-major in the v buffer of chunk c: each thread takes one token's 32-channel
+            //    segment: the token's norm over 4 neighbouring lanes, z and the
+            //    output rows read and written in place in the z tile, by 16-byte units whose order
+            //    is rotated per lane so that a quarter-warp touches 8 different bank groups.
+            const bool zok = mbar_wait_patient(bar(B_Z), (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
             w_z += zok;
             bad |= !zok;
-            nb_sync(2 + owg, 128);
-            // the rows are assembled in the z tile's place ([64 tokens][128] bf16) and leave by one
-            // tensor store, so every z value is read before the tile is overwritten
-            float y[32], zv[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                y[j] = o[j] * sRstd[tw + j];
-                zv[j] = bf_at(sm + R_Z, (tw + j) * D + dv);
-            }
             nb_sync(4, NT - NMAIN);
-            uint16_t* tile = reinterpret_cast<uint16_t*>(sm + R_Z) + tw * D + dv;
+            {
+                const unsigned char* ost = sm + R_V + V_BYTES * (uint32_t)(c % NVB);
+                unsigned char* zrow = sm + R_Z + otok * 256;
+                uint4 ov[4], zw[4];
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) round2_bf16(y[j], y[j + 1]);
+                for (int k = 0; k < 4; ++k) {
+                    ov[k] = *reinterpret_cast<const uint4*>(ost + otok * 256 + ounit[k]);
+                    zw[k] = *reinterpret_cast<const uint4*>(zrow + ounit[k]);
+                }
+                float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) y[j] *= nw;
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t w4[4] = {ov[k].x, ov[k].y, ov[k].z, ov[k].w};
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) round2_bf16(y[j], y[j + 1]);
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = make_float2(bf_lo(w4[e]), bf_hi(w4[e]));
+                        acc = __ffma2_rn(f, f, acc);
+                    }
+                }
+                float ss = acc.x + acc.y;
+                ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+                ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+                const float rstd = rsqrtf(ss / (float)D + p.eps);
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-                const float z0 = zv[j], z1 = zv[j + 1];
-                float a0 = y[j] * __fdividef(z0, 1.0f + __expf(-z0));
-                float a1 = y[j + 1] * __fdividef(z1, 1.0f + __expf(-z1));
-                uint32_t bits;
-                round2_bf16(a0, a1, &bits);
-                tile[j * D] = (uint16_t)(bits & 0xFFFFu);
-                tile[(j + 1) * D] = (uint16_t)(bits >> 16);
+                for (int k = 0; k < 4; ++k) {
+                    uint32_t w4[4] = {ov[k].x, ov[k].y, ov[k].z, ov[k].w};
+                    const uint32_t z4[4] = {zw[k].x, zw[k].y, zw[k].z, zw[k].w};
+                    const uint4 nw4 = *reinterpret_cast<const uint4*>(sm + R_SCR + ounit[k]);  // bf16 weights
+                    const uint32_t nwk[4] = {nw4.x, nw4.y, nw4.z, nw4.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 y = __fmul2_rn(make_float2(bf_lo(w4[e]), bf_hi(w4[e])), make_float2(rstd, rstd));
+                        // normed rounded to bf16, times the bf16 weight in one rounded bf16 product
+                        const __nv_bfloat162 scaled = __hmul2(as_bf2(bf2_bits(y.x, y.y)), as_bf2(nwk[e]));
+                        const float2 g = __fmul2_rn(__bfloat1622float2(scaled),
+                                                    silu2(make_float2(bf_lo(z4[e]), bf_hi(z4[e]))));
+                        w4[e] = bf2_bits(g.x, g.y);
+                    }
+                    *reinterpret_cast<uint4*>(zrow + ounit[k]) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                }
             }
             fence_proxy_async_smem();
             // the group agrees on a wait that ran out (any thread) once per chunk, before the store
@@ -1017,6 +1082,11 @@ __global__ void __launch_bounds__(NT, 1)
                 // rows past the sequence end fall outside the tensor map and are not written
                 tma_store_3d(&maps.out, sb + R_Z, h * D, t0, b);
                 bulk_commit_group();
+                // the staged O is read: the raw v rows of chunk c + 2 may land in that buffer
+                if (c + 2 < NC) {
+                    issue_v(c + 2);
+                    ++n_rv[(c + 2) % NVB];
+                }
                 if (c + 1 < NC) {
                     bulk_wait_group_read0();  // the tile is read: the next z rows may land there
                     issue_z(c + 1);
