@@ -87,10 +87,10 @@ constexpr int B_RAWQK = 0,   // 3: raw q/k rows of buffer i landed
     B_O1 = 7,                // O1 of the chunk complete
     B_ORDY = 8,              // MMA-d complete: O (O1 + P v_new) ready for the output warps
     B_GP = 9,                // [G; P0] MMA of the producer complete
-    B_OFREE = 10,            // output warps copied O out of tensor memory (256 arrivals)
+    B_UNUSED = 10,
     B_KQ = 11,               // 3: conv'd [k;q] rows and vectors of buffer i ready (1 arrival)
     B_VR = 14,               // 2: conv'd v rows ready (1 arrival)
-    B_TPR = 16,              // 2: T / P images ready (1 arrival)
+    B_APR = 16,              // 2: A (for T) and the P image of buffer i ready (1 arrival)
     B_GPFREE = 18;           // [G; P0] copied out of tensor memory (256 arrivals)
 
 using TA = __nv_bfloat16;
@@ -205,19 +205,27 @@ __device__ __forceinline__ uint32_t conv_silu_pair(__nv_bfloat162 x0, __nv_bfloa
 template <bool kGuard>
 __device__ __forceinline__ void conv_qk32(unsigned char* base, const uint32_t (&o8)[8], uint32_t h1, uint32_t h2,
                                           uint32_t h3, const __nv_bfloat162 (&w)[4], int nvalid, float (&sq)[32]) {
+    // 16 tokens at a time: every raw value of the group is loaded before any output is stored
+    // (the stores go to the same rows, so loads and stores would otherwise serialise)
     __nv_bfloat162 x1 = as_bf2(h1), x2 = as_bf2(h2), x3 = as_bf2(h3);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        uint32_t* cell = reinterpret_cast<uint32_t*>(base + (j >> 3) * 1024 + o8[j & 7]);
-        const __nv_bfloat162 x0 = as_bf2(*cell);
-        const uint32_t o = (!kGuard || j < nvalid) ? conv_silu_pair(x0, x1, x2, x3, w) : 0u;
-        *cell = o;
-        x3 = x2;
-        x2 = x1;
-        x1 = x0;
-        const float2 f = make_float2(bf_lo(o), bf_hi(o));
-        const float2 f2 = __fmul2_rn(f, f);
-        sq[j] = f2.x + f2.y;
+    for (int g = 0; g < 32; g += 16) {
+        uint32_t xr[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            xr[j] = *reinterpret_cast<const uint32_t*>(base + ((g + j) >> 3) * 1024 + o8[(g + j) & 7]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const __nv_bfloat162 x0 = as_bf2(xr[j]);
+            const uint32_t o = (!kGuard || g + j < nvalid) ? conv_silu_pair(x0, x1, x2, x3, w) : 0u;
+            *reinterpret_cast<uint32_t*>(base + ((g + j) >> 3) * 1024 + o8[(g + j) & 7]) = o;
+            x3 = x2;
+            x2 = x1;
+            x1 = x0;
+            const float2 f = make_float2(bf_lo(o), bf_hi(o));
+            const float2 f2 = __fmul2_rn(f, f);
+            sq[g + j] = f2.x + f2.y;
+        }
     }
 }
 // the same for 16 tokens of one v channel pair in row-major [64][128] bf16 rows (base: the
@@ -226,11 +234,13 @@ template <bool kGuard>
 __device__ __forceinline__ void conv_v16(unsigned char* base, uint32_t h1, uint32_t h2, uint32_t h3,
                                          const __nv_bfloat162 (&w)[4], int nvalid) {
     __nv_bfloat162 x1 = as_bf2(h1), x2 = as_bf2(h2), x3 = as_bf2(h3);
+    uint32_t xr[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) xr[j] = *reinterpret_cast<const uint32_t*>(base + j * 256);
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-        uint32_t* cell = reinterpret_cast<uint32_t*>(base + j * 256);
-        const __nv_bfloat162 x0 = as_bf2(*cell);
-        *cell = (!kGuard || j < nvalid) ? conv_silu_pair(x0, x1, x2, x3, w) : 0u;
+        const __nv_bfloat162 x0 = as_bf2(xr[j]);
+        *reinterpret_cast<uint32_t*>(base + j * 256) = (!kGuard || j < nvalid) ? conv_silu_pair(x0, x1, x2, x3, w) : 0u;
         x3 = x2;
         x2 = x1;
         x1 = x0;
@@ -251,6 +261,81 @@ __device__ __forceinline__ bool mbar_wait_patient(uint32_t bar, uint32_t parity,
         }
     }
 }
+
+// T = (I + A)^-1 of one chunk in place over A (the K-major operand image layout of img_off), by
+// the 256 threads tix = 0..255 of a group that synchronises on named barrier bar_id: T11, T22 by
+// forward substitution (one warp per 32 x 32 block, lane = column), X = A21 T11 parked in the
+// zero upper-right block, T21 = -T22 X over A21; then every element rounded to tf32 (nearest),
+// zero above the diagonal, and fenced for the tensor cores.
+__device__ __forceinline__ void build_t_image(unsigned char* Tb, int tix, int lane, int bar_id) {
+            nb_sync(bar_id, 256);
+            const int pw = tix >> 5;
+            if (pw < 2) {
+                const int o = 32 * pw;
+                float x[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) x[i] = 0.f;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int k = 0; k < i; k += 4) {
+                        const float4 a = *reinterpret_cast<const float4*>(Tb + img_off(o + i, o + k));
+                        s01 = __ffma2_rn(make_float2(a.x, a.y), make_float2(x[k], x[k + 1]), s01);
+                        s23 = __ffma2_rn(make_float2(a.z, a.w), make_float2(x[k + 2], x[k + 3]), s23);
+                    }
+                    x[i] = (i == lane ? 1.f : 0.f) - ((s01.x + s01.y) + (s23.x + s23.y));
+                }
+#pragma unroll
+                for (int i = 0; i < 32; ++i) *reinterpret_cast<float*>(Tb + img_off(o + i, o + lane)) = x[i];
+            }
+            nb_sync(bar_id, 256);
+            const int bi = tix >> 3, jb = (tix & 7) * 4;
+            {  // X[bi][jb..] = A21[bi][:] T11[:][jb..]  (T11[k][j] = 0 for k < j)
+                float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
+                for (int k = jb; k < 32; k += 4) {
+                    const float4 a = *reinterpret_cast<const float4*>(Tb + img_off(32 + bi, k));
+                    const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const float4 r = *reinterpret_cast<const float4*>(Tb + img_off(k + kk, jb));
+                        a01 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.x, r.y), a01);
+                        a23 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.z, r.w), a23);
+                    }
+                }
+                // the upper-right block is read by nobody in this phase
+                *reinterpret_cast<float4*>(Tb + img_off(bi, 32 + jb)) = make_float4(a01.x, a01.y, a23.x, a23.y);
+            }
+            nb_sync(bar_id, 256);
+            {  // T21[bi][jb..] = -T22[bi][:] X[:][jb..]  (T22[i][k] = 0 for k > i)
+                float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
+                for (int k = 0; k <= bi; k += 4) {
+                    const float4 a = *reinterpret_cast<const float4*>(Tb + img_off(32 + bi, 32 + k));
+                    const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const float4 r = *reinterpret_cast<const float4*>(Tb + img_off(k + kk, 32 + jb));
+                        a01 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.x, r.y), a01);
+                        a23 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.z, r.w), a23);
+                    }
+                }
+                // A21 was last read in the previous phase
+                *reinterpret_cast<float4*>(Tb + img_off(32 + bi, jb)) =
+                    make_float4(-a01.x, -a01.y, -a23.x, -a23.y);
+            }
+            nb_sync(bar_id, 256);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int idx = tix + 256 * e, i = idx >> 4, j = (idx & 15) * 4;
+                float4* cell = reinterpret_cast<float4*>(Tb + img_off(i, j));
+                const float4 v = *cell;
+                *cell = make_float4(j + 0 <= i ? umma::tf32_rna(v.x) : 0.f, j + 1 <= i ? umma::tf32_rna(v.y) : 0.f,
+                                    j + 2 <= i ? umma::tf32_rna(v.z) : 0.f, j + 3 <= i ? umma::tf32_rna(v.w) : 0.f);
+            }
+            fence_proxy_async_smem();  // T is read by the tensor cores next
+            nb_sync(bar_id, 256);
+}
+
 
 struct FusedMaps {
     CUtensorMap qk;    // raw mixed rows, box 64 channels x 64 tokens, 128-byte swizzle
@@ -354,8 +439,8 @@ __global__ void __launch_bounds__(NT, 1)
     if (tid == 0) {
         if (pi > 0)
             for (int i = 0; i < NBAR; ++i) mbar_inval(bar(i));
-        // every producer / output thread arrives on o_free and gp_free; one thread on the others
-        for (int i = 0; i < NBAR; ++i) mbar_init(bar(i), (i == B_OFREE || i == B_GPFREE) ? NT - NMAIN : 1);
+        // every producer thread arrives on gp_free; one thread on the others
+        for (int i = 0; i < NBAR; ++i) mbar_init(bar(i), i == B_GPFREE ? NT - NMAIN : 1);
         fence_mbar_init();
     }
     if (c_base == 0) write_conv_windows<TA, D, D, NT>(p, ck, b, h, kh, rep);
@@ -410,7 +495,14 @@ __global__ void __launch_bounds__(NT, 1)
         mbar_arrive_expect_tx(bar(B_Z), (uint32_t)C * D * 2u);
         tma_load_3d(sb + R_Z, &maps.z, h * D, (c_base + cc) * C, b, bar(B_Z));
     };
-    if (tid == NMAIN) {
+    // every input copy is issued by one thread of the state path (warp 1, lane 0: warp 0 issues
+    // the MMAs), which counts them for the drain at the piece's end
+    constexpr int TMA_TID = 32;
+    int n_rqk[NQK] = {0, 0, 0}, n_rv[NVB] = {0, 0}, n_z = 0;
+    if (tid == TMA_TID) {
+        for (int i = 0; i < NQK && i < NC; ++i) n_rqk[i] = 1;
+        for (int i = 0; i < NVB && i < NC; ++i) n_rv[i] = 1;
+        n_z = 1;
         issue_qk(0);
         if (NC > 1) issue_qk(1);
         if (NC > 2) issue_qk(2);
@@ -434,8 +526,8 @@ __global__ void __launch_bounds__(NT, 1)
         // chunk and leave together.  Until then a bad thread keeps going on stale data: every
         // address it touches is fixed by the chunk index, never by data.
         bool bad = false;
-        auto mma_wait = [&]() {
-            const bool ok = mbar_wait_bounded(bar(B_MMA), mma_phase & 1u, GDN_DEVERR_MMA_TIMEOUT);
+        auto mma_wait = [&]() {  // patient: warps 1-7 wait here while warp 0 waits for the producer
+            const bool ok = mbar_wait_patient(bar(B_MMA), mma_phase & 1u, GDN_DEVERR_MMA_TIMEOUT);
             ++mma_phase;
             umma::fence_after_sync();
             bad |= !ok;
@@ -451,16 +543,28 @@ __global__ void __launch_bounds__(NT, 1)
             else
                 nb_arrive(1, NMAIN);
         };
+        // output rows: token otok, channels 32 osg .. 32 osg + 31 as four 16-byte units, visited in
+        // a per-lane rotated order (ounit[k]: byte offset in the row) so that a quarter-warp
+        // touches 8 different bank groups
+        const int otok = tid >> 2, osg = tid & 3;
+        uint32_t ounit[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) ounit[k] = (uint32_t)(4 * osg + ((k + osg + (otok & 1)) & 3)) * 16u;
+        int w_z = 0;  // z copies waited for
+        // T of chunks 0 and 1 (later ones are built two chunks ahead at the end of each chunk)
+        for (int cc = 0; cc < 2 && cc < NC; ++cc) {
+            wait_phase(bar(B_APR + cc), 0);
+            build_t_image(sm + R_TP + TP_BYTES * (uint32_t)cc, tid, lane, 1);
+        }
         for (int c = 0; c < NC; ++c) {
             const int t0 = (c_base + c) * C;
             const float* sv = vecs(c);
             const uint32_t r_qk = R_QK + QK_BYTES * (uint32_t)(c % NQK);
             const uint32_t r_tp = R_TP + TP_BYTES * (uint32_t)(c % NTP);
             const unsigned char* vrows = sm + R_V + V_BYTES * (uint32_t)(c % NVB);
-            // ---------------- MMA-b (after the output warps released O of the last chunk) ----------------
+            // ---------------- MMA-b (this path read O of the last chunk out of [Y | O1] already) ----------------
             if (warp == 0) {
                 wait_phase(bar(B_KQ + c % NQK), c / NQK);
-                if (c > 0) bad |= !mbar_wait_patient(bar(B_OFREE), (uint32_t)(c - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
                 __syncwarp();
                 umma::fence_after_sync();
                 const uint64_t d_k = umma::desc_kmajor0(sb + r_qk), d_q = umma::desc_kmajor0(sb + r_qk + 8192);
@@ -507,9 +611,9 @@ __global__ void __launch_bounds__(NT, 1)
                 umma::tmem_wait_st();
             }
             stores_to_warp0();
-            // ---------------- MMA-c: v_new^T = Z^T T^T (after the producer returned columns 448-511) ----------------
+            // ---------------- MMA-c: v_new^T = Z^T T^T (after the producer returned columns 448-511;
+            //                  T of this chunk was built by this path two chunks ago) ----------------
             if (warp == 0) {
-                wait_phase(bar(B_TPR + c % NTP), c / NTP);
                 const int gp = c + 1 < NC ? c + 1 : (c == 0 ? 0 : -1);
                 if (gp >= 0) bad |= !mbar_wait_patient(bar(B_GPFREE), (uint32_t)gp & 1u, GDN_DEVERR_MMA_TIMEOUT);
                 __syncwarp();
@@ -669,6 +773,101 @@ __global__ void __launch_bounds__(NT, 1)
                 if (lastc && out_slot >= 0) __threadfence();  // the hand-off state before its flag
             }
             while (ck_i < ck.n && ck.off[ck_i] - t0 == C) ++ck_i;
+            // ---------------- output rows of chunk c through the gated RMSNorm (config.py:136-143) ----------------
+            // O = e^gamma rq dk^-1/2 O1 + P v_new, rounded to bf16 (the reference's core output dtype),
+            // staged token-major in the v buffer of chunk c (its v rows were consumed by Z)
+            bad |= !mbar_wait_bounded(bar(B_ORDY), (uint32_t)c & 1u, GDN_DEVERR_MMA_TIMEOUT);
+            umma::fence_after_sync();
+            {
+                float o1[32], dd[32];
+                umma::tmem_ld32(tmem + lane_base + C_YO + 64 + 32 * wg, o1);
+                umma::tmem_ld32(tmem + lane_base + C_YO + 32 * wg, dd);
+                umma::tmem_wait_ld();
+                const float* eqv = sv + V_EQ + 32 * wg;
+                uint16_t* col = reinterpret_cast<uint16_t*>(sm + R_V + V_BYTES * (uint32_t)(c % NVB)) + 32 * wg * D + dv;
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const uint32_t u = bf2_bits(fmaf(eqv[j], o1[j], dd[j]), fmaf(eqv[j + 1], o1[j + 1], dd[j + 1]));
+                    col[j * D] = (uint16_t)(u & 0xFFFFu);
+                    col[(j + 1) * D] = (uint16_t)(u >> 16);
+                }
+            }
+            {
+                const bool zok = mbar_wait_patient(bar(B_Z), (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
+                w_z += zok;
+                bad |= !zok;
+            }
+            umma::fence_before_sync();
+            nb_sync(1, NMAIN);  // O staged, and every read of [Y | O1] done: the next MMA-b may overwrite it
+            umma::fence_after_sync();
+            {  // each thread: one token's 32-channel segment; z read and the output written in place
+                const unsigned char* ost = sm + R_V + V_BYTES * (uint32_t)(c % NVB) + otok * 256;
+                unsigned char* zrow = sm + R_Z + otok * 256;
+                uint4 ov[4], zw[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    ov[k] = *reinterpret_cast<const uint4*>(ost + ounit[k]);
+                    zw[k] = *reinterpret_cast<const uint4*>(zrow + ounit[k]);
+                }
+                float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t w4[4] = {ov[k].x, ov[k].y, ov[k].z, ov[k].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = make_float2(bf_lo(w4[e]), bf_hi(w4[e]));
+                        acc = __ffma2_rn(f, f, acc);
+                    }
+                }
+                float ss = acc.x + acc.y;
+                ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+                ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+                const float rstd = rsqrtf(ss / (float)D + p.eps);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    uint32_t w4[4] = {ov[k].x, ov[k].y, ov[k].z, ov[k].w};
+                    const uint32_t z4[4] = {zw[k].x, zw[k].y, zw[k].z, zw[k].w};
+                    const uint4 nw4 = *reinterpret_cast<const uint4*>(sm + R_SCR + ounit[k]);  // bf16 weights
+                    const uint32_t nwk[4] = {nw4.x, nw4.y, nw4.z, nw4.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 y = __fmul2_rn(make_float2(bf_lo(w4[e]), bf_hi(w4[e])), make_float2(rstd, rstd));
+                        // normed rounded to bf16, times the bf16 weight in one rounded bf16 product
+                        const __nv_bfloat162 scaled = __hmul2(as_bf2(bf2_bits(y.x, y.y)), as_bf2(nwk[e]));
+                        const float2 g = __fmul2_rn(__bfloat1622float2(scaled),
+                                                    silu2(make_float2(bf_lo(z4[e]), bf_hi(z4[e]))));
+                        w4[e] = bf2_bits(g.x, g.y);
+                    }
+                    *reinterpret_cast<uint4*>(zrow + ounit[k]) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                }
+            }
+            fence_proxy_async_smem();
+            nb_sync(1, NMAIN);  // the output rows are complete; the staged O and z are read
+            if (tid == TMA_TID && !bad) {
+                // rows past the sequence end fall outside the tensor map and are not written
+                tma_store_3d(&maps.out, sb + R_Z, h * D, t0, b);
+                bulk_commit_group();
+                // the buffers of chunk c are free (MMA-b, MMA-e, checkpoints and O staging done):
+                // raw q / k rows of chunk c + 3 and raw v rows of chunk c + 2 land there
+                if (c + 3 < NC) {
+                    issue_qk(c + 3);
+                    ++n_rqk[(c + 3) % NQK];
+                }
+                if (c + 2 < NC) {
+                    issue_v(c + 2);
+                    ++n_rv[(c + 2) % NVB];
+                }
+                if (c + 1 < NC) {
+                    bulk_wait_group_read0();  // the tile is read: the next z rows may land there
+                    issue_z(c + 1);
+                    ++n_z;
+                }
+            }
+            // ---------------- T of chunk c + 2 (its A and P come from the producer) ----------------
+            if (c + 2 < NC) {
+                wait_phase(bar(B_APR + (c + 2) % NTP), (c + 2) / NTP);
+                build_t_image(sm + R_TP + TP_BYTES * (uint32_t)((c + 2) % NTP), tid, lane, 1);
+            }
             umma::fence_before_sync();
             if (nb_any(bad, 1, NMAIN)) {
                 failed = true;
@@ -679,6 +878,19 @@ __global__ void __launch_bounds__(NT, 1)
         }
         if (tid == 0 && failed && mma_pending)  // an MMA in flight finishes (bounded) before the CTA exits
             mbar_wait_bounded(bar(B_MMA), (mma_phase - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
+        if (tid == TMA_TID) {
+            if (failed)
+                for (; w_z < n_z; ++w_z) mbar_wait_bounded(bar(B_Z), (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            bulk_wait_group0();  // output rows written before the piece ends
+            // the last copy into each buffer lands before the piece ends (bounded; every earlier one
+            // on the same barrier was waited for before the next was issued)
+            for (int i = 0; i < NQK; ++i)
+                if (n_rqk[i] > 0)
+                    mbar_wait_bounded(bar(B_RAWQK + i), (uint32_t)(n_rqk[i] - 1) & 1u, GDN_DEVERR_TMA_TIMEOUT);
+            for (int i = 0; i < NVB; ++i)
+                if (n_rv[i] > 0)
+                    mbar_wait_bounded(bar(B_RAWV + i), (uint32_t)(n_rv[i] - 1) & 1u, GDN_DEVERR_TMA_TIMEOUT);
+        }
     } else {
         // ================ producer and output rows (warpgroups 2-3, 256 threads) ================
         const int ptid = tid - NMAIN;
@@ -692,13 +904,6 @@ __global__ void __launch_bounds__(NT, 1)
         const int gqk = (isk ? p.Hk * D : 0) + kh * D + qch;
         const int qt = ptid >> 6, vch = 2 * (ptid & 63);
         const int gv = v_ch + vch;
-        // output rows: token otok, channels 32 osg .. 32 osg + 31 as four 16-byte units, visited
-        // in a per-lane rotated order (ounit[k] = byte offset in the row, nw2: the weights of the
-        // same units)
-        const int otok = ptid >> 2, osg = ptid & 3;
-        uint32_t ounit[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) ounit[k] = (uint32_t)(4 * osg + ((k + osg + (otok & 1)) & 3)) * 16u;
         uint32_t o8[8];  // byte offset of this thread's q / k pair in row r of an 8-row swizzle group
 #pragma unroll
         for (int r = 0; r < 8; ++r) o8[r] = sw128(r, qchl);
@@ -715,13 +920,8 @@ __global__ void __launch_bounds__(NT, 1)
             __nv_bfloat162 r = __halves2bfloat162(s[0], s[3]);
             return *reinterpret_cast<uint32_t*>(&r);
         };
+        const float neg_a = -expf(p.A_log[h]), dt_b = p.dt_bias[h];  // g = neg_a softplus(a + dt_b)
         bool bad = false;
-        int n_rqk[NQK] = {0, 0, 0}, n_rv[NVB] = {0, 0}, n_z = 0, w_z = 0;  // copies issued (thread 0)
-        if (ptid == 0) {
-            for (int i = 0; i < NQK && i < NC; ++i) n_rqk[i] = 1;
-            for (int i = 0; i < NVB && i < NC; ++i) n_rv[i] = 1;
-            n_z = 1;
-        }
         bool gp_pending = false;
         int n_gp = 0;  // [G; P0] MMAs issued in this piece (thread 0)
 
@@ -818,7 +1018,7 @@ __global__ void __launch_bounds__(NT, 1)
                 vv[V_RQ + t] = rsqrtf((sPart[t] + sPart[64 + t]) + 1e-6f);
                 vv[V_RK + t] = rsqrtf((sPart[128 + t] + sPart[192 + t]) + 1e-6f);
                 vv[V_B + t] = valid ? Act<TA>::round(sigmoid_f(raw_b)) : 0.f;
-                vv[V_G + t] = valid ? -expf(p.A_log[h]) * softplus_f(raw_a + p.dt_bias[h]) : 0.f;
+                vv[V_G + t] = valid ? neg_a * softplus_f(raw_a + dt_b) : 0.f;
                 nb_sync(6, C);
                 if (t == 0) {  // sequential cumsum over the chunk (the reference's torch.cumsum)
                     float acc = 0.f;
@@ -881,235 +1081,74 @@ __global__ void __launch_bounds__(NT, 1)
             const float rowf = g_row ? vv[V_B + t] * vv[V_RK + t] : vv[V_RQ + t] * p.q_scale;
             const float erow = vv[V_EG + t] * rowf;
             unsigned char* dst = sm + R_TP + TP_BYTES * (uint32_t)(cc % NTP) + (g_row ? 0u : 16384u);
+            // every value first (the column vectors read as 16-byte broadcasts), then the stores
+            if (factored) {
+                const float4* e4 = reinterpret_cast<const float4*>(vv + V_ENG + tw);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float4 e = e4[q];
+                    const float2 a = __fmul2_rn(make_float2(g[4 * q], g[4 * q + 1]),
+                                                __fmul2_rn(make_float2(erow, erow), make_float2(e.x, e.y)));
+                    const float2 b = __fmul2_rn(make_float2(g[4 * q + 2], g[4 * q + 3]),
+                                                __fmul2_rn(make_float2(erow, erow), make_float2(e.z, e.w)));
+                    g[4 * q] = a.x;
+                    g[4 * q + 1] = a.y;
+                    g[4 * q + 2] = b.x;
+                    g[4 * q + 3] = b.y;
+                }
+            } else {
+                const float4* g4 = reinterpret_cast<const float4*>(vv + V_G + tw);
+                const float4* k4 = reinterpret_cast<const float4*>(vv + V_RK + tw);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float4 gg = g4[q], rk = k4[q];
+                    g[4 * q] *= __expf(gt - gg.x) * (rowf * rk.x);
+                    g[4 * q + 1] *= __expf(gt - gg.y) * (rowf * rk.y);
+                    g[4 * q + 2] *= __expf(gt - gg.z) * (rowf * rk.z);
+                    g[4 * q + 3] *= __expf(gt - gg.w) * (rowf * rk.w);
+                }
+            }
 #pragma unroll
             for (int jj = 0; jj < 32; jj += 4) {
                 const int j = tw + jj;
                 float val[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float dec = factored ? erow * vv[V_ENG + j + e]
-                                               : __expf(gt - vv[V_G + j + e]) * (rowf * vv[V_RK + j + e]);
-                    const float x = g[jj + e] * dec;
-                    val[e] = g_row ? (j + e < t ? x : 0.f) : (j + e <= t ? umma::tf32_rna(x) : 0.f);
-                }
+                for (int e = 0; e < 4; ++e)
+                    val[e] = g_row ? (j + e < t ? g[jj + e] : 0.f) : (j + e <= t ? umma::tf32_rna(g[jj + e]) : 0.f);
                 *reinterpret_cast<float4*>(dst + img_off(t, j)) = make_float4(val[0], val[1], val[2], val[3]);
             }
+            fence_proxy_async_smem();  // P is read by MMA-d
+            nb_sync(4, NT - NMAIN);    // every [G; P0] read and A / P write of the group is done
+            if (ptid == 0) mbar_arrive(bar(B_APR + cc % NTP));
         };
-        // --- T = (I + A)^-1 of chunk cc in place over A (K-major operand image layout):
-        //     T11, T22 by forward substitution (one warp per 32 x 32 block, lane = column),
-        //     X = A21 T11 parked in the zero upper-right block, T21 = -T22 X over A21; then every
-        //     element rounded to tf32 (nearest), zero above the diagonal; signals tp_ready(cc)
-        auto build_t = [&](int cc) {
-            unsigned char* Tb = sm + R_TP + TP_BYTES * (uint32_t)(cc % NTP);
-            nb_sync(4, NT - NMAIN);
-            const int pw = ptid >> 5;
-            if (pw < 2) {
-                const int o = 32 * pw;
-                float x[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) x[i] = 0.f;
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
-#pragma unroll
-                    for (int k = 0; k < i; k += 4) {
-                        const float4 a = *reinterpret_cast<const float4*>(Tb + img_off(o + i, o + k));
-                        s01 = __ffma2_rn(make_float2(a.x, a.y), make_float2(x[k], x[k + 1]), s01);
-                        s23 = __ffma2_rn(make_float2(a.z, a.w), make_float2(x[k + 2], x[k + 3]), s23);
-                    }
-                    x[i] = (i == lane ? 1.f : 0.f) - ((s01.x + s01.y) + (s23.x + s23.y));
-                }
-#pragma unroll
-                for (int i = 0; i < 32; ++i) *reinterpret_cast<float*>(Tb + img_off(o + i, o + lane)) = x[i];
-            }
-            nb_sync(4, NT - NMAIN);
-            const int bi = ptid >> 3, jb = (ptid & 7) * 4;
-            {  // X[bi][jb..] = A21[bi][:] T11[:][jb..]  (T11[k][j] = 0 for k < j)
-                float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
-                for (int k = jb; k < 32; k += 4) {
-                    const float4 a = *reinterpret_cast<const float4*>(Tb + img_off(32 + bi, k));
-                    const float av[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const float4 r = *reinterpret_cast<const float4*>(Tb + img_off(k + kk, jb));
-                        a01 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.x, r.y), a01);
-                        a23 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.z, r.w), a23);
-                    }
-                }
-                // the upper-right block is read by nobody in this phase
-                *reinterpret_cast<float4*>(Tb + img_off(bi, 32 + jb)) = make_float4(a01.x, a01.y, a23.x, a23.y);
-            }
-            nb_sync(4, NT - NMAIN);
-            {  // T21[bi][jb..] = -T22[bi][:] X[:][jb..]  (T22[i][k] = 0 for k > i)
-                float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
-                for (int k = 0; k <= bi; k += 4) {
-                    const float4 a = *reinterpret_cast<const float4*>(Tb + img_off(32 + bi, 32 + k));
-                    const float av[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const float4 r = *reinterpret_cast<const float4*>(Tb + img_off(k + kk, 32 + jb));
-                        a01 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.x, r.y), a01);
-                        a23 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.z, r.w), a23);
-                    }
-                }
-                // A21 was last read in the previous phase
-                *reinterpret_cast<float4*>(Tb + img_off(32 + bi, jb)) =
-                    make_float4(-a01.x, -a01.y, -a23.x, -a23.y);
-            }
-            nb_sync(4, NT - NMAIN);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int idx = ptid + (NT - NMAIN) * e, i = idx >> 4, j = (idx & 15) * 4;
-                float4* cell = reinterpret_cast<float4*>(Tb + img_off(i, j));
-                const float4 v = *cell;
-                *cell = make_float4(j + 0 <= i ? umma::tf32_rna(v.x) : 0.f, j + 1 <= i ? umma::tf32_rna(v.y) : 0.f,
-                                    j + 2 <= i ? umma::tf32_rna(v.z) : 0.f, j + 3 <= i ? umma::tf32_rna(v.w) : 0.f);
-            }
-            fence_proxy_async_smem();  // T and P are read by the tensor cores next
-            nb_sync(4, NT - NMAIN);
-            if (ptid == 0) mbar_arrive(bar(B_TPR + cc % NTP));
-        };
-
-        // ---- prologue: chunks 0 and 1 convolved, their T / P images built ----
+        // ---- prologue: chunks 0 and 1 convolved, their A / P built ----
         prep(0, 0);
         if (NC > 1) prep(1, -1);
         issue_gp(0);
         build_ap(0);
-        build_t(0);
         if (NC > 1) {
             issue_gp(1);
             build_ap(1);
-            build_t(1);
         }
         if (nb_any(bad, 4, NT - NMAIN)) failed = true;
         for (int c = 0; c < NC && !failed; ++c) {
-            const int t0 = (c_base + c) * C;
-            // a. conv of the q / k rows of chunk c + 2 and the v rows of chunk c + 1
+            // conv of the q / k rows of chunk c + 2 and the v rows of chunk c + 1, then [G; P0], A and
+            // P of chunk c + 2 once MMA-d of chunk c has released the borrowed tensor-memory columns
             const int cq = c + 2 < NC ? c + 2 : -1, cv = c + 1 < NC ? c + 1 : -1;
             if (cq >= 0 || cv >= 0) prep(cq, cv);
-            // b. O of chunk c out of tensor memory; [G; P0], A and P of chunk c + 2
-            bad |= !mbar_wait_patient(bar(B_ORDY), (uint32_t)c & 1u, GDN_DEVERR_MMA_TIMEOUT);
-            umma::fence_after_sync();
-            if (cq >= 0) issue_gp(cq);
-            const float* sv = vecs(c);
-            float o[32];
-            {  // O[t][dv] = e^{gamma_t} rq dk^-1/2 O1 + P v_new
-                float o1[32], dd[32];
-                umma::tmem_ld32(tmem + lane_base + C_YO + 64 + tw, o1);
-                umma::tmem_ld32(tmem + lane_base + C_YO + tw, dd);
-                umma::tmem_wait_ld();
-#pragma unroll
-                for (int j = 0; j < 32; ++j) o[j] = fmaf(sv[V_EQ + tw + j], o1[j], dd[j]);
+            if (cq >= 0) {
+                bad |= !mbar_wait_patient(bar(B_ORDY), (uint32_t)c & 1u, GDN_DEVERR_MMA_TIMEOUT);
+                umma::fence_after_sync();
+                issue_gp(cq);
+                build_ap(cq);
             }
-            umma::fence_before_sync();
-            mbar_arrive(bar(B_OFREE));  // these tensor-memory columns may be overwritten now
-            {  // O rounded to bf16 (the reference's core output dtype), token-major, into the v
-               // buffer of chunk c (its v rows were consumed by Z before MMA-c)
-                uint16_t* col = reinterpret_cast<uint16_t*>(sm + R_V + V_BYTES * (uint32_t)(c % NVB)) + tw * D + dv;
-#pragma unroll
-                for (int j = 0; j < 32; j += 2) {
-                    const uint32_t u = bf2_bits(o[j], o[j + 1]);
-                    col[j * D] = (uint16_t)(u & 0xFFFFu);
-                    col[(j + 1) * D] = (uint16_t)(u >> 16);
-                }
-            }
-            if (cq >= 0) build_ap(cq);
-            // the raw q / k rows of chunk c + 3 into the buffer chunk c used (every MMA and
-            // checkpoint read of it is complete: o_ready of chunk c)
-            if (ptid == 0 && !bad) {
-                if (c + 3 < NC) {
-                    issue_qk(c + 3);
-                    ++n_rqk[(c + 3) % NQK];
-                }
-            }
-            // c. output rows of chunk c through the gated RMSNorm (config.py:136-143), from O staged
-            //    token-major in the v buffer of chunk c: each thread takes one token's 32-channel
-            //    segment: the token's norm over 4 neighbouring lanes, z and the
-            //    output rows read and written in place in the z tile, by 16-byte units whose order
-            //    is rotated per lane so that a quarter-warp touches 8 different bank groups.
-            const bool zok = mbar_wait_patient(bar(B_Z), (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
-            w_z += zok;
-            bad |= !zok;
-            nb_sync(4, NT - NMAIN);
-            {
-                const unsigned char* ost = sm + R_V + V_BYTES * (uint32_t)(c % NVB);
-                unsigned char* zrow = sm + R_Z + otok * 256;
-                uint4 ov[4], zw[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    ov[k] = *reinterpret_cast<const uint4*>(ost + otok * 256 + ounit[k]);
-                    zw[k] = *reinterpret_cast<const uint4*>(zrow + ounit[k]);
-                }
-                float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const uint32_t w4[4] = {ov[k].x, ov[k].y, ov[k].z, ov[k].w};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 f = make_float2(bf_lo(w4[e]), bf_hi(w4[e]));
-                        acc = __ffma2_rn(f, f, acc);
-                    }
-                }
-                float ss = acc.x + acc.y;
-                ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-                ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-                const float rstd = rsqrtf(ss / (float)D + p.eps);
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    uint32_t w4[4] = {ov[k].x, ov[k].y, ov[k].z, ov[k].w};
-                    const uint32_t z4[4] = {zw[k].x, zw[k].y, zw[k].z, zw[k].w};
-                    const uint4 nw4 = *reinterpret_cast<const uint4*>(sm + R_SCR + ounit[k]);  // bf16 weights
-                    const uint32_t nwk[4] = {nw4.x, nw4.y, nw4.z, nw4.w};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 y = __fmul2_rn(make_float2(bf_lo(w4[e]), bf_hi(w4[e])), make_float2(rstd, rstd));
-                        // normed rounded to bf16, times the bf16 weight in one rounded bf16 product
-                        const __nv_bfloat162 scaled = __hmul2(as_bf2(bf2_bits(y.x, y.y)), as_bf2(nwk[e]));
-                        const float2 g = __fmul2_rn(__bfloat1622float2(scaled),
-                                                    silu2(make_float2(bf_lo(z4[e]), bf_hi(z4[e]))));
-                        w4[e] = bf2_bits(g.x, g.y);
-                    }
-                    *reinterpret_cast<uint4*>(zrow + ounit[k]) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-                }
-            }
-            fence_proxy_async_smem();
-            // the group agrees on a wait that ran out (any thread) once per chunk, before the store
             if (nb_any(bad, 4, NT - NMAIN)) {
                 failed = true;
                 break;
             }
-            if (ptid == 0) {
-                // rows past the sequence end fall outside the tensor map and are not written
-                tma_store_3d(&maps.out, sb + R_Z, h * D, t0, b);
-                bulk_commit_group();
-                // the staged O is read: the raw v rows of chunk c + 2 may land in that buffer
-                if (c + 2 < NC) {
-                    issue_v(c + 2);
-                    ++n_rv[(c + 2) % NVB];
-                }
-                if (c + 1 < NC) {
-                    bulk_wait_group_read0();  // the tile is read: the next z rows may land there
-                    issue_z(c + 1);
-                    ++n_z;
-                }
-            }
-            // d. T of chunk c + 2
-            if (cq >= 0) build_t(cq);
         }
-        if (ptid == 0) {
-            if (failed)
-                for (; w_z < n_z; ++w_z) mbar_wait_bounded(bar(B_Z), (uint32_t)w_z & 1u, GDN_DEVERR_TMA_TIMEOUT);
-            bulk_wait_group0();  // output rows written before the piece ends
-            // the last copy into each buffer lands before the piece ends (bounded; every earlier one
-            // on the same barrier was waited for before the next was issued)
-            for (int i = 0; i < NQK; ++i)
-                if (n_rqk[i] > 0)
-                    mbar_wait_bounded(bar(B_RAWQK + i), (uint32_t)(n_rqk[i] - 1) & 1u, GDN_DEVERR_TMA_TIMEOUT);
-            for (int i = 0; i < NVB; ++i)
-                if (n_rv[i] > 0)
-                    mbar_wait_bounded(bar(B_RAWV + i), (uint32_t)(n_rv[i] - 1) & 1u, GDN_DEVERR_TMA_TIMEOUT);
-            if (gp_pending) mbar_wait_bounded(bar(B_GP), (uint32_t)(n_gp - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
-        }
+        if (ptid == 0 && gp_pending)  // a [G; P0] MMA in flight finishes (bounded) before the piece ends
+            mbar_wait_bounded(bar(B_GP), (uint32_t)(n_gp - 1) & 1u, GDN_DEVERR_MMA_TIMEOUT);
     }
     umma::fence_before_sync();
     cta_failed = __syncthreads_or(failed);
