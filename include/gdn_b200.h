@@ -51,13 +51,15 @@ extern "C" {
 
 /* gdn_mixer_args.flags: run the register-tile token-by-token kernel even
  * where the bulk-copy pipelined one applies, the CUDA-core chunked kernel even
- * where the tensor-core one applies, and (gdn_mixer_prefill_ws) the two-kernel
- * chunked form with its preparation pass through the workspace instead of the
- * single fused kernel (same results up to float rounding; for testing and
- * comparison). */
+ * where the tensor-core one applies, and (gdn_mixer_prefill_ws) the single
+ * kernel that prepares each chunk in shared memory two chunks ahead of the
+ * state pass instead of the two-kernel form with its preparation pass through
+ * the workspace (same results up to float rounding).  The single kernel needs
+ * a workspace only for state hand-offs (at most 64 KB per SM, whatever the
+ * length); the two-kernel form is faster at the prefill benchmark's size. */
 #define GDN_FLAG_REGISTER_KERNEL 1
 #define GDN_FLAG_CUDA_CORE_PREFILL 2
-#define GDN_FLAG_TWO_KERNEL_PREFILL 4
+#define GDN_FLAG_PREP_IN_KERNEL_PREFILL 4
 
 /* Bits of the device error word (gdn_device_error). */
 #define GDN_DEVERR_TMA_TIMEOUT 0x1u
@@ -67,7 +69,8 @@ extern "C" {
 
 /* Size of the library's fixed device scratch used by gdn_mixer_prefill_noalloc
  * (64 MiB per device: the two-kernel prefill's workspace for about 1.9k
- * tokens x 16 / 32 heads of 128). */
+ * tokens x 16 / 32 heads of 128; with GDN_FLAG_PREP_IN_KERNEL_PREFILL a call
+ * needs at most one 64 KB state hand-off slot per SM, so every length fits). */
 #define GDN_STATIC_SCRATCH_BYTES (64ll << 20)
 
 /* Maximum number of state checkpoints one call can record. */
@@ -260,38 +263,36 @@ int32_t gdn_mixer_prefill(const gdn_mixer_args* args, void* stream);
 /*
  * Device workspace, in bytes, that gdn_mixer_prefill_ws needs for these
  * arguments: 0 when the call takes a path without workspace, a negative
- * GDN_ERR_* code when the arguments are invalid.  The default (fused) form
- * needs workspace only when there are more (batch, value head) chains than
- * the current device has SMs: one state-sized hand-off slot (64 KB) and flag
- * per SM, about 9.7 MB on a 148-SM B200, whatever the sequence length.  With
- * GDN_FLAG_TWO_KERNEL_PREFILL it is the two-kernel form's workspace (about
- * 2.2 GB at batch 8 x 8192 tokens, 16 / 32 heads of 128: the conv outputs in
- * bf16 plus a 32 KB pair of 64x64 tf32 matrices per chunk and value head,
- * plus the hand-off slots).  Ask with the device current that will run the
- * call.
+ * GDN_ERR_* code when the arguments are invalid.  At batch 8 x 8192 tokens,
+ * 16 / 32 heads of 128 the default two-kernel form needs about 2.2 GB (the
+ * conv outputs in bf16 plus a 32 KB pair of 64x64 tf32 matrices per chunk and
+ * value head); when there are more (batch, value head) chains than the
+ * current device has SMs both forms add one state-sized hand-off slot (64 KB)
+ * and flag per SM, which is all that GDN_FLAG_PREP_IN_KERNEL_PREFILL needs
+ * (about 9.7 MB on a 148-SM B200, whatever the length).  Ask with the device
+ * current that will run the call.
  */
 int64_t gdn_prefill_workspace_bytes(const gdn_mixer_args* args);
 
 /*
  * Chunked token mixer (prefill) with a caller workspace, same arguments,
- * results and cache semantics as gdn_mixer_prefill.  By default one fused
- * kernel (one CTA per batch row and value head, or one cooperative wave of
- * one CTA per SM when there are more chains than SMs) carries the state
- * through the chunks (deltanet.py:345-389) with every state product on the
- * tensor cores, while a producer warpgroup pair in the same CTA computes, two
- * chunks ahead, what does not depend on the state - conv + SiLU, L2-norm
- * factors, gates, and each chunk's (I + A)^-1 and masked Q K^T
- * (deltanet.py:266-343) - in shared memory.  With GDN_FLAG_TWO_KERNEL_PREFILL
+ * results and cache semantics as gdn_mixer_prefill.  By default two kernels:
  * a fully parallel preparation kernel (one CTA per batch row, key head and
- * chunk of 64 tokens) writes that part to `workspace` first and a sequential
- * kernel reads it back.  `workspace` (device, 16-byte aligned, at least
- * gdn_prefill_workspace_bytes, not overlapping any other argument; may be
- * NULL when that is 0) is scratch: the call clears what must start at zero
- * and nothing in it survives the call.
- * Shapes the two-kernel form does not cover (activations other than bf16,
- * head dims other than 128, conv_kernel != 4, num_v_heads / num_k_heads not
- * in {1, 2, 4}, misaligned inputs) or GDN_FLAG_CUDA_CORE_PREFILL run
- * gdn_mixer_prefill instead and ignore the workspace.
+ * chunk of 64 tokens) computes what does not depend on the recurrent state -
+ * conv + SiLU, L2-norm factors, gates, and each chunk's (I + A)^-1 and masked
+ * Q K^T (deltanet.py:266-343) - into `workspace`; the sequential kernel (one
+ * CTA per batch row and value head, or one cooperative wave of one CTA per SM
+ * when there are more chains than SMs) then carries the state through the
+ * chunks (deltanet.py:345-389) with every state product on the tensor cores.
+ * With GDN_FLAG_PREP_IN_KERNEL_PREFILL one kernel does both: producer warps
+ * prepare each chunk in shared memory two chunks ahead of the state pass.
+ * `workspace` (device, 16-byte aligned, at least gdn_prefill_workspace_bytes,
+ * not overlapping any other argument; may be NULL when that is 0) is scratch:
+ * the call clears what must start at zero and nothing in it survives the call.
+ * Shapes neither form covers (activations other than bf16, head dims other
+ * than 128, conv_kernel != 4, num_v_heads / num_k_heads not in {1, 2, 4},
+ * misaligned inputs) or GDN_FLAG_CUDA_CORE_PREFILL run gdn_mixer_prefill
+ * instead and ignore the workspace.
  */
 int32_t gdn_mixer_prefill_ws(const gdn_mixer_args* args, void* workspace, int64_t workspace_bytes, void* stream);
 

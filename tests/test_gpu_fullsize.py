@@ -100,18 +100,19 @@ def test_full_size_prefill_composes_over_a_split(full_inputs):
 
 
 def test_full_size_prefill_forms_agree(full_inputs):
-    """The default kernel, the two-kernel form and the older single kernel on the same call."""
+    """The default two-kernel form, the prep-in-kernel single kernel and the older single kernel on the
+    same call."""
     from visionstack_b200 import _lib
     m, _, shape, mixed, z, bb, aa = full_inputs
     dev = mixed.device
     res = []
-    for kw in ({}, {"two_kernel_prefill": True}, {"fused_prefill": True}):
+    for kw in ({}, {"prep_in_kernel_prefill": True}, {"fused_prefill": True}):
         S = torch.empty(B, shape.num_v_heads, shape.head_k_dim, shape.head_v_dim, device=dev)
         o = m.mixer(mixed, z, bb, aa, rec_state_out=S, token_by_token=False, **kw)
         res.append((o, S))
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
-    for i, name in ((1, "two-kernel"), (2, "single-kernel")):
+    for i, name in ((1, "prep-in-kernel"), (2, "single-kernel")):
         assert_state_close(res[0][1], res[i][1], f"default vs {name} final state", scale=2.0)
         assert_bf16_close(res[0][0], res[i][0], f"default vs {name} outputs", scale=2.0)
 

@@ -47,7 +47,7 @@ def mixer_inputs(shape: W.LayerShape, B: int, T: int, dtype: str, seed: int, wit
 
 
 def run_ours(m, shape, d, dtype, token_by_token, offsets=(), register_kernel=False, fused_prefill=False,
-             two_kernel_prefill=False):
+             prep_in_kernel_prefill=False):
     dev = torch.device("cuda")
     t = lambda a: torch.from_numpy(a).to(dev).to(TDT[dtype])  # noqa: E731
     B, T = d["mixed"].shape[:2]
@@ -64,7 +64,7 @@ def run_ours(m, shape, d, dtype, token_by_token, offsets=(), register_kernel=Fal
                   conv_state_out=cs_out, rec_state_out=rs_out, checkpoint_offsets=offsets,
                   state_checkpoints=st_ck, conv_checkpoints=cv_ck, token_by_token=token_by_token,
                   register_kernel=register_kernel, fused_prefill=fused_prefill,
-                  two_kernel_prefill=two_kernel_prefill)
+                  prep_in_kernel_prefill=prep_in_kernel_prefill)
     torch.cuda.synchronize()
     return out, cs_out, rs_out, st_ck, cv_ck
 
@@ -248,7 +248,7 @@ def test_mixer_plan_matches_mixer():
     assert torch.equal(o1, o2) and torch.equal(S1, S2) and torch.equal(cs1, cs2)
 
 
-PREFILL_FORMS = {"default": {}, "two_kernel": {"two_kernel_prefill": True}, "single_kernel": {"fused_prefill": True}}
+PREFILL_FORMS = {"default": {}, "prep_in_kernel": {"prep_in_kernel_prefill": True}, "single_kernel": {"fused_prefill": True}}
 
 
 @pytest.mark.parametrize("form", list(PREFILL_FORMS))
@@ -262,10 +262,10 @@ PREFILL_FORMS = {"default": {}, "two_kernel": {"two_kernel_prefill": True}, "sin
 def test_tensor_core_prefill_vs_oracle(B, T, with_state, offsets, form):
     """The tcgen05 chunked kernels (bf16, head dim 128) against the oracle, with
     sub-chunk and chunk-boundary checkpoints, ragged last chunks and T < 64:
-    the default single kernel with its in-kernel preparation two chunks ahead,
-    the two-kernel form (parallel preparation pass through a workspace, then
-    the sequential pass) and the older single kernel that prepares each chunk
-    on the state's critical path."""
+    the default two-kernel form (parallel preparation pass through a
+    workspace, then the sequential pass), the single kernel whose producer
+    warps prepare each chunk two chunks ahead of the state pass, and the older
+    single kernel that prepares each chunk on the state's critical path."""
     from visionstack_b200 import _lib
     shape = W.LayerShape(256, 2, 4, 128, 128)
     m, params = make_layer(shape, "bf16")
@@ -275,7 +275,7 @@ def test_tensor_core_prefill_vs_oracle(B, T, with_state, offsets, form):
     assert _lib.device_error() == 0
 
 
-@pytest.mark.parametrize("form", ["default", "two_kernel"])
+@pytest.mark.parametrize("form", ["default", "prep_in_kernel"])
 def test_prefill_chains_split_across_ctas(form):
     """More (batch, value head) chains than SMs: the sequential kernel runs one CTA per SM,
     cuts the chains' chunks into equal runs and hands the state from one CTA to the next
@@ -292,7 +292,7 @@ def test_prefill_chains_split_across_ctas(form):
     assert _lib.device_error() == 0
 
 
-@pytest.mark.parametrize("form", ["default", "two_kernel"])
+@pytest.mark.parametrize("form", ["default", "prep_in_kernel"])
 @pytest.mark.parametrize("rep", [1, 4])
 def test_prefill_gqa_groupings(rep, form):
     """Key heads shared by 1 or 4 value heads (the preparation pass handles
@@ -315,13 +315,13 @@ def test_tensor_core_prefill_matches_cuda_core_kernel():
     t = lambda a: torch.from_numpy(a).to(dev).to(torch.bfloat16)  # noqa: E731
     S0 = torch.from_numpy(d["rec_state"]).to(dev)
     outs = []
-    for kw in ({}, {"fused_prefill": True}, {"cuda_core_prefill": True}, {"two_kernel_prefill": True}):
+    for kw in ({}, {"fused_prefill": True}, {"cuda_core_prefill": True}, {"prep_in_kernel_prefill": True}):
         S = torch.empty_like(S0)
         o = m.mixer(t(d["mixed"]), t(d["z"]), t(d["b"]), t(d["a"]), conv_state=t(d["conv_state"]), rec_state=S0,
                     rec_state_out=S, token_by_token=False, **kw)
         outs.append((o, S))
     torch.cuda.synchronize()
-    for i, name in ((1, "single-kernel"), (2, "cuda-core"), (3, "two-kernel")):
+    for i, name in ((1, "single-kernel"), (2, "cuda-core"), (3, "prep-in-kernel")):
         assert_bf16_close(outs[0][0], outs[i][0], f"default vs {name} out", scale=2.0)
         assert_state_close(outs[0][1], outs[i][1], f"default vs {name} state", scale=2.0)
 

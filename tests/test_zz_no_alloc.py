@@ -37,17 +37,17 @@ def _fake_args(B: int, T: int):
 
 def test_noalloc_rejects_calls_larger_than_the_static_scratch():
     lib = _lib.load()
-    # the default (fused) prefill needs at most one hand-off state per SM, at any length
-    assert 0 <= lib.gdn_prefill_workspace_bytes(ctypes.byref(_fake_args(8, 8192))) <= 148 * (64 << 10) + 4096
-    # the two-kernel form keeps every chunk's preparation in the workspace: far beyond the scratch
+    # the prep-in-kernel prefill needs at most one hand-off state per SM, at any length
+    fused = _fake_args(8, 8192)
+    fused.flags = _lib.GDN_FLAG_PREP_IN_KERNEL_PREFILL
+    assert 0 <= lib.gdn_prefill_workspace_bytes(ctypes.byref(fused)) <= 148 * (64 << 10) + 4096
+    # the default two-kernel form keeps every chunk's preparation in the workspace: far beyond the scratch
     big = _fake_args(8, 8192)
-    big.flags = _lib.GDN_FLAG_TWO_KERNEL_PREFILL
     need = lib.gdn_prefill_workspace_bytes(ctypes.byref(big))
     assert need > _lib.GDN_STATIC_SCRATCH_BYTES
     assert lib.gdn_mixer_prefill_noalloc(ctypes.byref(big), None) == -1
     assert b"static scratch" in lib.gdn_last_error_string()
     small = _fake_args(1, 512)
-    small.flags = _lib.GDN_FLAG_TWO_KERNEL_PREFILL
     assert 0 < lib.gdn_prefill_workspace_bytes(ctypes.byref(small)) <= _lib.GDN_STATIC_SCRATCH_BYTES
     bad = _fake_args(1, 512)
     bad.batch = 0
@@ -55,7 +55,7 @@ def test_noalloc_rejects_calls_larger_than_the_static_scratch():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("flags", [0, _lib.GDN_FLAG_TWO_KERNEL_PREFILL], ids=["fused", "two_kernel"])
+@pytest.mark.parametrize("flags", [0, _lib.GDN_FLAG_PREP_IN_KERNEL_PREFILL], ids=["two_kernel", "prep_in_kernel"])
 @pytest.mark.parametrize("B,T", [(1, 700), (5, 256)])
 def test_noalloc_matches_workspace_entry_on_two_calls_in_a_row(B, T, flags):
     from tests.helpers import assert_bit_exact

@@ -44,7 +44,7 @@ EXPORTED_SYMBOLS = (
 )
 GDN_FLAG_REGISTER_KERNEL = 1
 GDN_FLAG_CUDA_CORE_PREFILL = 2
-GDN_FLAG_TWO_KERNEL_PREFILL = 4
+GDN_FLAG_PREP_IN_KERNEL_PREFILL = 4
 GDN_DEVERR_TMA_TIMEOUT = 0x1
 GDN_DEVERR_BAD_SLOT = 0x4
 GDN_DEVERR_HANDOFF_TIMEOUT = 0x8

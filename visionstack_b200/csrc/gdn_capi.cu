@@ -80,7 +80,7 @@ int32_t validate_mixer(const gdn_mixer_args* a, gdn::MixParams* p, gdn::CkptList
     if (a->act_dtype != GDN_DTYPE_F32 && a->act_dtype != GDN_DTYPE_BF16)
         return fail(GDN_ERR_UNSUPPORTED, "act_dtype %d", a->act_dtype);
     if (!(a->norm_eps >= 0.0f)) return fail(GDN_ERR_INVALID_ARG, "norm_eps must be >= 0");
-    if (a->flags & ~(GDN_FLAG_REGISTER_KERNEL | GDN_FLAG_CUDA_CORE_PREFILL | GDN_FLAG_TWO_KERNEL_PREFILL))
+    if (a->flags & ~(GDN_FLAG_REGISTER_KERNEL | GDN_FLAG_CUDA_CORE_PREFILL | GDN_FLAG_PREP_IN_KERNEL_PREFILL))
         return fail(GDN_ERR_INVALID_ARG, "unknown flags 0x%x", a->flags);
     if (!a->mixed_qkv || !a->z || !a->a || !a->b || !a->conv_weight || !a->A_log || !a->dt_bias ||
         !a->norm_weight || !a->out)
@@ -263,7 +263,7 @@ int64_t gdn_prefill_workspace_bytes(const gdn_mixer_args* args) {
                                                                                  args->act_dtype))
         return 0;
     ok();
-    if (args->flags & GDN_FLAG_TWO_KERNEL_PREFILL) {
+    if (!(args->flags & GDN_FLAG_PREP_IN_KERNEL_PREFILL)) {
         size_t off[6];
         return (int64_t)gdn::prefill_ws_layout(args->batch, args->seq_len, args->num_k_heads, args->num_v_heads,
                                                args->head_k_dim, handoff_slots(args), off);
@@ -281,8 +281,8 @@ int32_t gdn_mixer_prefill_ws(const gdn_mixer_args* args, void* workspace, int64_
     if ((args->flags & GDN_FLAG_CUDA_CORE_PREFILL) || !gdn::prefill_prep_supported(p, args->head_k_dim,
                                                                                  args->act_dtype))
         return gdn_mixer_prefill(args, stream);  // needs no workspace
-    if (!(args->flags & GDN_FLAG_TWO_KERNEL_PREFILL)) {
-        // the fused kernel: workspace only for the state hand-offs of split mode
+    if (args->flags & GDN_FLAG_PREP_IN_KERNEL_PREFILL) {
+        // the single kernel: workspace only for the state hand-offs of split mode
         const int n_hs = handoff_slots(args);
         size_t off[2];
         const size_t need = n_hs > 0 ? gdn::prefill_fused_ws_layout(n_hs, off) : 0;

@@ -263,79 +263,115 @@ __device__ __forceinline__ bool mbar_wait_patient(uint32_t bar, uint32_t parity,
 }
 
 // T = (I + A)^-1 of one chunk in place over A (the K-major operand image layout of img_off), by
-// the 256 threads tix = 0..255 of a group that synchronises on named barrier bar_id: T11, T22 by
-// forward substitution (one warp per 32 x 32 block, lane = column), X = A21 T11 parked in the
-// zero upper-right block, T21 = -T22 X over A21; then every element rounded to tf32 (nearest),
-// zero above the diagonal, and fenced for the tensor cores.
-__device__ __forceinline__ void build_t_image(unsigned char* Tb, int tix, int lane, int bar_id) {
-            nb_sync(bar_id, 256);
-            const int pw = tix >> 5;
-            if (pw < 2) {
-                const int o = 32 * pw;
-                float x[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) x[i] = 0.f;
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
-#pragma unroll
-                    for (int k = 0; k < i; k += 4) {
-                        const float4 a = *reinterpret_cast<const float4*>(Tb + img_off(o + i, o + k));
-                        s01 = __ffma2_rn(make_float2(a.x, a.y), make_float2(x[k], x[k + 1]), s01);
-                        s23 = __ffma2_rn(make_float2(a.z, a.w), make_float2(x[k + 2], x[k + 3]), s23);
-                    }
-                    x[i] = (i == lane ? 1.f : 0.f) - ((s01.x + s01.y) + (s23.x + s23.y));
-                }
-#pragma unroll
-                for (int i = 0; i < 32; ++i) *reinterpret_cast<float*>(Tb + img_off(o + i, o + lane)) = x[i];
-            }
-            nb_sync(bar_id, 256);
-            const int bi = tix >> 3, jb = (tix & 7) * 4;
-            {  // X[bi][jb..] = A21[bi][:] T11[:][jb..]  (T11[k][j] = 0 for k < j)
-                float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
-                for (int k = jb; k < 32; k += 4) {
-                    const float4 a = *reinterpret_cast<const float4*>(Tb + img_off(32 + bi, k));
-                    const float av[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const float4 r = *reinterpret_cast<const float4*>(Tb + img_off(k + kk, jb));
-                        a01 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.x, r.y), a01);
-                        a23 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.z, r.w), a23);
-                    }
-                }
-                // the upper-right block is read by nobody in this phase
-                *reinterpret_cast<float4*>(Tb + img_off(bi, 32 + jb)) = make_float4(a01.x, a01.y, a23.x, a23.y);
-            }
-            nb_sync(bar_id, 256);
-            {  // T21[bi][jb..] = -T22[bi][:] X[:][jb..]  (T22[i][k] = 0 for k > i)
-                float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
-                for (int k = 0; k <= bi; k += 4) {
-                    const float4 a = *reinterpret_cast<const float4*>(Tb + img_off(32 + bi, 32 + k));
-                    const float av[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const float4 r = *reinterpret_cast<const float4*>(Tb + img_off(k + kk, 32 + jb));
-                        a01 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.x, r.y), a01);
-                        a23 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.z, r.w), a23);
-                    }
-                }
-                // A21 was last read in the previous phase
-                *reinterpret_cast<float4*>(Tb + img_off(32 + bi, jb)) =
-                    make_float4(-a01.x, -a01.y, -a23.x, -a23.y);
-            }
-            nb_sync(bar_id, 256);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int idx = tix + 256 * e, i = idx >> 4, j = (idx & 15) * 4;
-                float4* cell = reinterpret_cast<float4*>(Tb + img_off(i, j));
-                const float4 v = *cell;
-                *cell = make_float4(j + 0 <= i ? umma::tf32_rna(v.x) : 0.f, j + 1 <= i ? umma::tf32_rna(v.y) : 0.f,
-                                    j + 2 <= i ? umma::tf32_rna(v.z) : 0.f, j + 3 <= i ? umma::tf32_rna(v.w) : 0.f);
-            }
-            fence_proxy_async_smem();  // T is read by the tensor cores next
-            nb_sync(bar_id, 256);
+// the 256 threads tix = 0..255 of a group that synchronises on named barrier bar_id, doubling up
+// from the diagonal as the reference's block solve does (deltanet.py:112-162):
+//   1. the four 16 x 16 diagonal blocks by forward substitution (two warps, a half-warp per
+//      block, lane = column);
+//   2. 16 -> 32: X = A21 T11 parked in the zero upper-right 16 x 16 of each 32 x 32 diagonal
+//      block, then T21 = -T22 X over A21;
+//   3. 32 -> 64: the same with the 32 x 32 blocks (X in the upper-right 32 x 32);
+// then every element rounded to tf32 (nearest), zero above the diagonal (the parked products
+// included), and fenced for the tensor cores.  The block products skip the known zeros of the
+// triangular factors; every loop has a fixed trip count (predicated) so the loads pipeline.
+__device__ __forceinline__ float4 ld_img4(const unsigned char* Tb, int i, int j) {
+    return *reinterpret_cast<const float4*>(Tb + img_off(i, j));
 }
-
+__device__ __forceinline__ float2 ld_img2(const unsigned char* Tb, int i, int j) {
+    return *reinterpret_cast<const float2*>(Tb + img_off(i, j));
+}
+__device__ __forceinline__ void build_t_image(unsigned char* Tb, int tix, int lane, int bar_id) {
+    nb_sync(bar_id, 256);
+    if (tix < 64) {  // 1. diagonal 16 x 16 blocks
+        const int blk = (tix >> 4), o = 16 * blk, jl = lane & 15;
+        float x[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) x[i] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < i; k += 4) {
+                const float4 a = ld_img4(Tb, o + i, o + k);
+                s01 = __ffma2_rn(make_float2(a.x, a.y), make_float2(x[k], x[k + 1]), s01);
+                s23 = __ffma2_rn(make_float2(a.z, a.w), make_float2(x[k + 2], x[k + 3]), s23);
+            }
+            x[i] = (i == jl ? 1.f : 0.f) - ((s01.x + s01.y) + (s23.x + s23.y));
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) *reinterpret_cast<float*>(Tb + img_off(o + i, o + jl)) = x[i];
+    }
+    nb_sync(bar_id, 256);
+    {  // 2. 16 -> 32 in both 32 x 32 diagonal blocks: item = (block, row r, two columns c2)
+        const int o = 32 * (tix >> 7), r = (tix >> 3) & 15, c2 = (tix & 7) * 2;
+        float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {  // X[r][c2..] = A21[r][k] T11[k][c2..], T11[k][c] = 0 for k < c
+            if (k >= c2) {
+                const float a = *reinterpret_cast<const float*>(Tb + img_off(o + 16 + r, o + k));
+                acc = __ffma2_rn(make_float2(a, a), ld_img2(Tb, o + k, o + c2), acc);
+            }
+        }
+        *reinterpret_cast<float2*>(Tb + img_off(o + r, o + 16 + c2)) = acc;  // upper-right 16 x 16: free
+        nb_sync(bar_id, 256);
+        acc = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {  // T21[r][c2..] = -T22[r][k] X[k][c2..], T22[r][k] = 0 for k > r
+            if (k <= r) {
+                const float a = *reinterpret_cast<const float*>(Tb + img_off(o + 16 + r, o + 16 + k));
+                acc = __ffma2_rn(make_float2(a, a), ld_img2(Tb, o + k, o + 16 + c2), acc);
+            }
+        }
+        *reinterpret_cast<float2*>(Tb + img_off(o + 16 + r, o + c2)) = make_float2(-acc.x, -acc.y);
+    }
+    nb_sync(bar_id, 256);
+    const int bi = tix >> 3, jb = (tix & 7) * 4;
+    {  // 3. X[bi][jb..] = A21[bi][:] T11[:][jb..] (T11[k][j] = 0 for k < j), into the upper-right 32 x 32
+        float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 32; k += 4) {
+            if (k >= jb) {
+                const float4 a = ld_img4(Tb, 32 + bi, k);
+                const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const float4 r = ld_img4(Tb, k + kk, jb);
+                    a01 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.x, r.y), a01);
+                    a23 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.z, r.w), a23);
+                }
+            }
+        }
+        *reinterpret_cast<float4*>(Tb + img_off(bi, 32 + jb)) = make_float4(a01.x, a01.y, a23.x, a23.y);
+    }
+    nb_sync(bar_id, 256);
+    {  // T21[bi][jb..] = -T22[bi][:] X[:][jb..] (T22[i][k] = 0 for k > i), over A21
+        float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 32; k += 4) {
+            if (k <= bi) {
+                const float4 a = ld_img4(Tb, 32 + bi, 32 + k);
+                const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const float4 r = ld_img4(Tb, k + kk, 32 + jb);
+                    a01 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.x, r.y), a01);
+                    a23 = __ffma2_rn(make_float2(av[kk], av[kk]), make_float2(r.z, r.w), a23);
+                }
+            }
+        }
+        *reinterpret_cast<float4*>(Tb + img_off(32 + bi, jb)) = make_float4(-a01.x, -a01.y, -a23.x, -a23.y);
+    }
+    nb_sync(bar_id, 256);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int idx = tix + 256 * e, i = idx >> 4, j = (idx & 15) * 4;
+        float4* cell = reinterpret_cast<float4*>(Tb + img_off(i, j));
+        const float4 v = *cell;
+        *cell = make_float4(j + 0 <= i ? umma::tf32_rna(v.x) : 0.f, j + 1 <= i ? umma::tf32_rna(v.y) : 0.f,
+                            j + 2 <= i ? umma::tf32_rna(v.z) : 0.f, j + 3 <= i ? umma::tf32_rna(v.w) : 0.f);
+    }
+    fence_proxy_async_smem();  // T is read by the tensor cores next
+    nb_sync(bar_id, 256);
+}
 
 struct FusedMaps {
     CUtensorMap qk;    // raw mixed rows, box 64 channels x 64 tokens, 128-byte swizzle
@@ -1018,16 +1054,17 @@ __global__ void __launch_bounds__(NT, 1)
                 vv[V_RQ + t] = rsqrtf((sPart[t] + sPart[64 + t]) + 1e-6f);
                 vv[V_RK + t] = rsqrtf((sPart[128 + t] + sPart[192 + t]) + 1e-6f);
                 vv[V_B + t] = valid ? Act<TA>::round(sigmoid_f(raw_b)) : 0.f;
-                vv[V_G + t] = valid ? neg_a * softplus_f(raw_a + dt_b) : 0.f;
-                nb_sync(6, C);
-                if (t == 0) {  // sequential cumsum over the chunk (the reference's torch.cumsum)
-                    float acc = 0.f;
-#pragma unroll 8
-                    for (int i = 0; i < C; ++i) {
-                        acc += vv[V_G + i];
-                        vv[V_G + i] = acc;
-                    }
+                // gamma = cumsum(g) over the chunk (the reference's torch.cumsum): an inclusive scan
+                // per warp by shuffles, then the second warp adds the first one's total
+                float gs = valid ? neg_a * softplus_f(raw_a + dt_b) : 0.f;
+#pragma unroll
+                for (int d = 1; d < 32; d <<= 1) {
+                    const float y = __shfl_up_sync(0xffffffffu, gs, d);
+                    if (lane >= d) gs += y;
                 }
+                vv[V_G + t] = gs;
+                nb_sync(6, C);
+                if (t >= 32) vv[V_G + t] = gs + vv[V_G + 31];
                 nb_sync(6, C);
                 const float gt = vv[V_G + t], gC = vv[V_G + C - 1], rk = vv[V_RK + t];
                 const float eg = expf(gt);

@@ -330,29 +330,28 @@ class Qwen3_5GatedDeltaNet(nn.Module):
               state_checkpoints: Optional[torch.Tensor] = None, conv_checkpoints: Optional[torch.Tensor] = None,
               token_by_token: Optional[bool] = None, register_kernel: bool = False,
               cuda_core_prefill: bool = False, fused_prefill: bool = False,
-              two_kernel_prefill: bool = False) -> torch.Tensor:
+              prep_in_kernel_prefill: bool = False) -> torch.Tensor:
         """One launch of the fused token mixer on projection outputs
         (deltanet.py:489-561): returns the gated-norm output [B, T, Hv*dv].
 
         ``token_by_token`` picks the decode kernel (T <= 8) or the chunked
         kernel; by default the reference's rule applies (a state and T <= 8).
-        The chunked form runs as one kernel that prepares each chunk (conv,
-        norms, gates, T and P) in shared memory two chunks ahead of the state
-        pass (a workspace from torch's caching allocator holds the state
-        hand-offs when there are more chains than SMs).  ``register_kernel``
-        forces the register-tile decode kernel instead of the bulk-copy
-        pipelined one, ``two_kernel_prefill`` the two-kernel chunked form
-        (a parallel preparation pass through the workspace, then the
-        sequential pass), ``fused_prefill`` the older single-kernel
-        tensor-core chunked form that prepares each chunk on the state's
-        critical path, ``cuda_core_prefill`` the CUDA-core chunked kernel
-        (same results up to float rounding; used by the tests).
+        The chunked form runs as two kernels (a parallel preparation pass into
+        a workspace from torch's caching allocator, then the sequential
+        pass).  ``register_kernel`` forces the register-tile decode kernel
+        instead of the bulk-copy pipelined one, ``prep_in_kernel_prefill``
+        the single kernel whose producer warps prepare each chunk in shared
+        memory two chunks ahead of the state pass (workspace only for state
+        hand-offs), ``fused_prefill`` the older single kernel that prepares
+        each chunk on the state's critical path (no workspace),
+        ``cuda_core_prefill`` the CUDA-core chunked kernel (same results up to
+        float rounding; used by the tests).
         """
         if token_by_token is None:
             token_by_token = rec_state is not None and mixed_qkv.shape[1] <= _lib.GDN_MAX_DECODE_TOKENS
         flags = (_lib.GDN_FLAG_REGISTER_KERNEL if register_kernel else 0) | \
             (_lib.GDN_FLAG_CUDA_CORE_PREFILL if cuda_core_prefill else 0) | \
-            (_lib.GDN_FLAG_TWO_KERNEL_PREFILL if two_kernel_prefill else 0)
+            (_lib.GDN_FLAG_PREP_IN_KERNEL_PREFILL if prep_in_kernel_prefill else 0)
         args, out, keep = self._mixer_args(mixed_qkv, z, b, a, conv_state, rec_state, conv_state_out,
                                            rec_state_out, out, flags)
         offs = list(checkpoint_offsets)
