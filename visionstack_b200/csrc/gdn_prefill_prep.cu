@@ -222,24 +222,32 @@ __global__ void __launch_bounds__(NT, 3)
             x1 = __halves2bfloat162(sa ? sa[2] : zero, sb2 ? sb2[2] : zero);
         }
         const bool full_window = cs_in != nullptr || c > 0;  // every token has 3 predecessors
-#pragma unroll 4
-        for (int t = 0; t < C; ++t) {
-            __nv_bfloat162* cell = reinterpret_cast<__nv_bfloat162*>(gbase + (t + HIST) * D * 2 + ch * 2);
-            const __nv_bfloat162 x0 = *cell;
-            const int tg = t0 + t;
-            uint32_t outv = 0u;
-            if (tg < T) {
-                __nv_bfloat162 acc = __hmul2(x0, w[3]);
-                if (full_window || tg >= 1) acc = __hfma2(x1, w[2], acc);
-                if (full_window || tg >= 2) acc = __hfma2(x2, w[1], acc);
-                if (full_window || tg >= 3) acc = __hfma2(x3, w[0], acc);
-                const float ca = __low2float(acc), cb = __high2float(acc);
-                outv = pack_bf2(__fdividef(ca, 1.0f + __expf(-ca)), __fdividef(cb, 1.0f + __expf(-cb)));
+        // 16 tokens at a time: every raw value of the group is loaded before any output is stored
+        // (the outputs overwrite the same rows, so interleaved loads and stores would serialise)
+        for (int tb = 0; tb < C; tb += 16) {
+            __nv_bfloat162 xr[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                xr[j] = *reinterpret_cast<const __nv_bfloat162*>(gbase + (tb + j + HIST) * D * 2 + ch * 2);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int t = tb + j;
+                const __nv_bfloat162 x0 = xr[j];
+                const int tg = t0 + t;
+                uint32_t outv = 0u;
+                if (tg < T) {
+                    __nv_bfloat162 acc = __hmul2(x0, w[3]);
+                    if (full_window || tg >= 1) acc = __hfma2(x1, w[2], acc);
+                    if (full_window || tg >= 2) acc = __hfma2(x2, w[1], acc);
+                    if (full_window || tg >= 3) acc = __hfma2(x3, w[0], acc);
+                    const float ca = __low2float(acc), cb = __high2float(acc);
+                    outv = pack_bf2(__fdividef(ca, 1.0f + __expf(-ca)), __fdividef(cb, 1.0f + __expf(-cb)));
+                }
+                x3 = x2;
+                x2 = x1;
+                x1 = x0;
+                *reinterpret_cast<uint32_t*>(gbase + (t + HIST) * D * 2 + ch * 2) = outv;
             }
-            x3 = x2;
-            x2 = x1;
-            x1 = x0;
-            *reinterpret_cast<uint32_t*>(cell) = outv;
         }
     }
     // conv outputs (staging rows 3..66 of every group) to the workspace: one tensor store per group
