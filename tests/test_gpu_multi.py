@@ -119,9 +119,10 @@ def _mixer_worker(rank, world, port, q):
         S0 = torch.from_numpy(d["rec_state"][:, h0:h1]).to(dev)
         S = torch.empty_like(S0)
         cs_out = torch.empty_like(cs)
-        core = layer.mixer(mixed, z, b, a, conv_state=cs, rec_state=S0, conv_state_out=cs_out, rec_state_out=S,
-                           token_by_token=False)
-        y = F.linear(core, layer.out_proj.weight)
+        with torch.no_grad():
+            core = layer.mixer(mixed, z, b, a, conv_state=cs, rec_state=S0, conv_state_out=cs_out, rec_state_out=S,
+                               token_by_token=False)
+            y = F.linear(core, layer.out_proj.weight)
         dist.all_reduce(y, op=dist.ReduceOp.SUM)
         torch.cuda.synchronize()
         outs = [torch.empty_like(core) for _ in range(world)]
