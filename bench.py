@@ -65,6 +65,8 @@ def parse():
                          "run at 1 GPU only)")
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the head-sharded layer measurement (projections, mixer, out_proj, all-reduce)")
+    ap.add_argument("--no-prefix-snapshot", action="store_true",
+                    help="skip the prefix-cache snapshot/restore measurement (run at 1 GPU only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-s", type=float, default=12.0, help="seconds of CPU work for the CPU baseline")
     return ap.parse_args()
@@ -563,6 +565,10 @@ def run_ours(args, rank: int, world: int) -> None:
     if not args.no_sharded:
         sharded = run_sharded_layer(torch, dist, m, local, rank, world, dev, barrier)
 
+    prefix_snap = None
+    if not args.no_prefix_snapshot and world == 1:
+        prefix_snap = run_prefix_snapshot(torch, m, local, dev)
+
     stack = None
     if not args.no_stack and world == 1:
         try:
@@ -601,6 +607,8 @@ def run_ours(args, rank: int, world: int) -> None:
         line["rollback"] = rollback
     if sharded is not None:
         line["sharded_layer"] = sharded
+    if prefix_snap is not None:
+        line["prefix_snapshot"] = prefix_snap
     if stack is not None:
         line["stack"] = stack
     if world == 1 and not args.no_cpu_baseline:
@@ -609,6 +617,103 @@ def run_ours(args, rank: int, world: int) -> None:
             prefill["cpu_baseline"] = base.pop("prefill")
         line["cpu_baseline"] = base
     print(json.dumps(line), flush=True)
+
+
+def run_prefix_snapshot(torch, m, local, dev, layers=36, prefix=4096, checkpoints=(1024, 2048, 3072)):
+    """Prefix-cache snapshot and splice of the DeltaNet states of a 36-layer stack at B1 (current
+    states at 4096 tokens + checkpoints at 1024/2048/3072: 4 x 36 x (2 MiB recurrent + 48 KiB conv)),
+    seeded random states.  The snapshot's device-to-host copies run on the copy stream into one
+    pinned arena; the restore copies host-to-device on the same stream.  Also timed: 64 B64 decode
+    steps (one CUDA graph) alone and with a snapshot in flight beside them."""
+    from visionstack_b200 import Qwen3_5HybridCache, snapshot_prefix_state
+    from visionstack_b200.prefix import copy_stream
+    hv, d = local.num_v_heads, local.head_k_dim
+    g = torch.Generator(device=dev)
+    g.manual_seed(9)
+    cache = Qwen3_5HybridCache()
+    for l in range(layers):
+        cache.conv_states[l] = torch.randn(1, local.conv_dim, 3, generator=g, device=dev).to(torch.bfloat16)
+        cache.recurrent_states[l] = 0.02 * torch.randn(1, hv, d, d, generator=g, device=dev)
+        for cp in checkpoints:
+            cache.conv_checkpoints.setdefault(cp, {})[l] = cache.conv_states[l].clone()
+            cache.recurrent_checkpoints.setdefault(cp, {})[l] = cache.recurrent_states[l].clone()
+    toks = list(range(prefix))
+    cs = copy_stream(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+
+    def snap_once():
+        torch.cuda.synchronize(dev)
+        ev[0].record(cs)
+        st = snapshot_prefix_state(toks, None, cache)
+        ev[1].record(cs)
+        st.synchronize()
+        return st, ev[0].elapsed_time(ev[1])
+
+    for _ in range(2):
+        st, _ = snap_once()
+    st, d2h_ms = min((snap_once() for _ in range(3)), key=lambda r: r[1])
+    nbytes = sum(t.numel() * t.element_size() for mp in st.recurrent_checkpoints.values() for t in mp.values()) + \
+        sum(t.numel() * t.element_size() for mp in st.conv_checkpoints.values() for t in mp.values())
+    # restore at 3072: every layer's checkpoint states back on the device
+    h2d = []
+    for _ in range(4):
+        torch.cuda.synchronize(dev)
+        ev[2].record(cs)
+        rc, _, off = st.restore(dev, snap_len=3072)
+        ev[3].record(cs)
+        torch.cuda.synchronize(dev)
+        h2d.append(ev[2].elapsed_time(ev[3]))
+    restore_ms = min(h2d[1:])
+    rbytes = sum(t.numel() * t.element_size() for t in list(rc.recurrent_states.values()) +
+                 list(rc.conv_states.values()))
+    ok = all(torch.equal(rc.recurrent_states[l].cpu(), st.recurrent_checkpoints[3072][l]) for l in (0, layers - 1))
+
+    # overlap: 64 decode steps at B64 alone, then with a snapshot of the same states in flight
+    Bd = 64
+    with torch.no_grad():
+        x = torch.randn(Bd, 1, W.SHAPE_QWEN.hidden_size, generator=g, device=dev).to(torch.bfloat16)
+        mixed, z, bb, aa = m.project(x)
+    S = 0.02 * torch.randn(Bd, hv, d, d, generator=g, device=dev)
+    cv = [torch.zeros(Bd, local.conv_dim, 3, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            m.mixer(mixed, z, bb, aa, conv_state=cv[i % 2], rec_state=S, conv_state_out=cv[(i + 1) % 2],
+                    rec_state_out=S, token_by_token=True)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(64):
+            m.mixer(mixed, z, bb, aa, conv_state=cv[i % 2], rec_state=S, conv_state_out=cv[(i + 1) % 2],
+                    rec_state_out=S, token_by_token=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def decode_ms(with_snapshot):
+        torch.cuda.synchronize(dev)
+        with torch.cuda.stream(stream):
+            if with_snapshot:
+                snap = snapshot_prefix_state(toks, None, cache)
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        if with_snapshot:
+            snap.synchronize()
+        return e0.elapsed_time(e1)
+
+    decode_ms(False)
+    alone = min(decode_ms(False) for _ in range(3))
+    beside = min(decode_ms(True) for _ in range(3))
+    del graph
+    return {"workload": f"prefix snapshot of {layers} DeltaNet layers at B1: current states at {prefix} tokens + "
+                        f"checkpoints at {list(checkpoints)} (2 MiB recurrent + 48 KiB conv per layer and offset); "
+                        f"restore at 3072",
+            "snapshot_bytes": nbytes, "d2h_ms": d2h_ms, "d2h_gbs": nbytes / (d2h_ms * 1e-3) / 1e9,
+            "restore_bytes": rbytes, "h2d_ms": restore_ms, "h2d_gbs": rbytes / (restore_ms * 1e-3) / 1e9,
+            "restore_bit_exact": bool(ok),
+            "decode_64_steps_ms": {"alone": alone, "with_snapshot_in_flight": beside, "ratio": beside / alone},
+            "path": "visionstack_b200.prefix.snapshot_prefix_state / PinnedPrefixState.restore: copies on a "
+                    "dedicated copy stream, one pinned arena per snapshot, no host synchronisation"}
 
 
 def run_prefill(torch, dist, m, local, dev, world, barrier, B=8, T=8192):

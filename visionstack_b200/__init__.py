@@ -15,6 +15,7 @@ from .deltanet import (
     _recurrent_gated_delta_rule,
     _solve_unit_lower_triangular,
 )
+from .prefix import PinnedPrefixState, PrefixStateCache, snapshot_prefix_state
 from .slots import StateSlots
 
 __all__ = [
@@ -23,6 +24,9 @@ __all__ = [
     "Qwen3_5TextConfig",
     "Qwen3_5GatedDeltaNet",
     "StateSlots",
+    "PinnedPrefixState",
+    "PrefixStateCache",
+    "snapshot_prefix_state",
     "_causal_conv1d_fn",
     "_chunk_gated_delta_rule",
     "_extract_conv_state_at_offset",

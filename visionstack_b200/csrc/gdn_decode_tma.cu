@@ -6,13 +6,19 @@
 // of its q/k/v channels and z for every token, its conv-state and
 // conv-weight rows - arrive in the group's shared-memory stage through bulk
 // asynchronous copies (cp.async.bulk; the state and the small inputs complete
-// on two mbarriers).  As soon as the group has moved the state into registers
-// it issues the copy of its next tile's state, and after the conv the copies
-// of the next tile's inputs, so those copies overlap the rest of the
-// computation.  The two groups interleave, keeping two state
-// tiles in flight per SM while the SMs do the conv / norm / delta-rule /
-// gated-norm work.  The new state leaves from registers with streaming
-// 128-bit stores (in place when state_out == state_in).
+// on two mbarriers), issued by the lanes of the group's first warp.  The pool
+// slots, gate inputs and decay constants of the next tile are looked up one
+// tile ahead.  The two groups interleave, keeping two state tiles in flight
+// per SM while the SMs do the conv / norm / delta-rule / gated-norm work.
+//
+// The state lives in registers and leaves with streaming 128-bit stores (in
+// place when state_out == state_in).  An SM sustains only ~30 B/clk of such
+// stores, so a multi-token call (speculative verify: a 64 KB checkpoint per
+// token) is store-bound; its stores are therefore spread in quarters over the
+// work that follows each update (the next token's norms, products and
+// reduction, or the next tile's conv phase), instead of stalling every warp
+// on the store queue at once.  The single-token step loads its next state as
+// early as possible instead and stores its final state at the end of the tile.
 //
 // With a slot table (gdn_mixer_verify_slots) the state and conv state of row b
 // come from pool slot slot_table[b][0] and the state after token t goes to
@@ -26,6 +32,8 @@
 #include "gdn_common.cuh"
 #include "gdn_kernels.cuh"
 
+#include <type_traits>
+
 namespace gdn {
 namespace dtma {
 
@@ -34,6 +42,9 @@ constexpr int NG = 2;       // consumer groups per CTA
 constexpr int NT = GT * NG;
 constexpr int KC = 4;       // conv taps of the streaming kernel
 constexpr int LC = KC - 1;  // conv-state length
+// Checkpoints whose pool slots are looked up one tile ahead and kept in shared
+// memory (slot mode); later ones look the table up where they are written.
+constexpr int NCKS = 16;
 
 template <int D, int TMAX, typename TA>
 struct GroupLayout {
@@ -57,7 +68,8 @@ struct GroupLayout {
     static constexpr int OFF_O = OFF_U + D * 4;                  // [D]
     static constexpr int OFF_RED = OFF_O + D * 4;                // [2][RG][D]
     static constexpr int OFF_GATE = OFF_RED + 2 * RG * D * 4;    // [2][TMAX]
-    static constexpr int OFF_BAR = (OFF_GATE + 2 * TMAX * 4 + 7) / 8 * 8;
+    static constexpr int OFF_SLOT = OFF_GATE + 2 * TMAX * 4;     // [2][NCKS] checkpoint pool slots
+    static constexpr int OFF_BAR = (OFF_SLOT + 2 * NCKS * 4 + 7) / 8 * 8;
     static constexpr int BYTES = (OFF_BAR + 16 + 127) / 128 * 128;  // two mbarriers: inputs, state
 };
 
@@ -70,11 +82,6 @@ __device__ __forceinline__ int row_slot(const MixParams& p, int b, int col) {
         return -1;
     }
     return s;
-}
-
-// Output slot of checkpoint i of row b: the caller's index, or the pool slot.
-__device__ __forceinline__ int ckpt_slot(const MixParams& p, const CkptList& ck, int i, int b) {
-    return p.slot_table ? row_slot(p, b, ck.slot[i]) : ck.slot[i];
 }
 
 __device__ __forceinline__ void group_sync(int id) {
@@ -100,6 +107,11 @@ __global__ void __launch_bounds__(NT, 1)
     using GL = GroupLayout<D, TMAX, TA>;
     constexpr int CG = GL::CG, RG = GL::RG, RPT = D / RG;
     static_assert(D % RG == 0 && RPT >= 4 && RPT % 4 == 0, "bad tiling");
+
+    // Multi-token calls (TMAX > 1) defer the last token's state stores into the next tile's
+    // conv phase, so its state is loaded after that phase; the single-token step loads the
+    // next state first (its copy then starts earliest) and stores the final state at once.
+    constexpr bool DEFER = TMAX > 1;
 
     extern __shared__ __align__(128) unsigned char smem[];
     const int grp = threadIdx.x / GT, tid = threadIdx.x % GT, lane = tid & 31;
@@ -129,65 +141,82 @@ __global__ void __launch_bounds__(NT, 1)
     }
     __syncthreads();
 
-    // Thread 0 of the group issues the copies of one tile into the group's stage: the state
-    // (on bar_s: it refills as soon as the state is in registers) and the small inputs (on bar:
-    // they refill after the conv).
-    auto start_slot = [&](int b) -> size_t {  // pool slot of the starting state (slot mode)
-        if (!p.slot_table) return 0;
-        const int s0 = row_slot(p, b, 0);
-        return s0 < 0 ? 0 : (size_t)s0;
-    };
-    auto issue_state = [&](int tile) {
-        const size_t slot0 = start_slot(tile / p.Hv);
+    // Warp 0 of the group issues the copies of one tile into the group's stage: the state (on
+    // bar_s, one copy by lane 0: it refills as soon as the state is in registers) and the small
+    // inputs (on bar, spread over the lanes: they refill after the conv).  `slot0` is the pool
+    // slot of the tile's starting state (0 without a slot table).
+    auto issue_state = [&](int tile, size_t slot0) {
         mbar_arrive_expect_tx(bar_s, (uint32_t)GL::S_BYTES);
         bulk_load(smem_u32(gbase + GL::OFF_S), p.S_in + (slot0 * p.B * p.Hv + tile) * D * D, GL::S_BYTES, bar_s);
     };
-    auto issue = [&](int tile) {
+    auto issue = [&](int tile, size_t slot0) {
         const int b = tile / p.Hv, h = tile - (tile / p.Hv) * p.Hv, kh = h / rep;
-        const uint32_t mrow = D * sizeof(TA);
+        constexpr uint32_t mrow = D * sizeof(TA);
         const int c0 = kh * D, c1 = p.Hk * D + kh * D, c2 = 2 * p.Hk * D + h * D;
-        const size_t slot0 = start_slot(b);
-        uint32_t bytes = 4u * T * mrow + 3u * D * KC * sizeof(TA);
-        if (has_cs) bytes += 3u * D * LC * sizeof(TA);
-        mbar_arrive_expect_tx(bar, bytes);
-        for (int t = 0; t < T; ++t) {
-            const TA* row = gmixed + (size_t)b * p.ms_b + (size_t)t * p.ms_t;
-            bulk_load(smem_u32(gbase + GL::OFF_MQ + t * mrow), row + c0, mrow, bar);
-            bulk_load(smem_u32(gbase + GL::OFF_MK + t * mrow), row + c1, mrow, bar);
-            bulk_load(smem_u32(gbase + GL::OFF_MV + t * mrow), row + c2, mrow, bar);
-            bulk_load(smem_u32(gbase + GL::OFF_Z + t * mrow), gz + (size_t)b * p.zs_b + (size_t)t * p.zs_t + h * D,
-                      mrow, bar);
+        if (lane == 0) {
+            uint32_t bytes = 4u * T * mrow + 3u * D * KC * sizeof(TA);
+            if (has_cs) bytes += 3u * D * LC * sizeof(TA);
+            mbar_arrive_expect_tx(bar, bytes);
         }
-        const TA* cw = static_cast<const TA*>(p.convw);
-        const int chans[3] = {c0, c1, c2};
-#pragma unroll
-        for (int g = 0; g < 3; ++g) {
-            if (has_cs)
-                bulk_load(smem_u32(gbase + GL::OFF_CS + g * D * LC * (int)sizeof(TA)),
-                          static_cast<const TA*>(p.cs_in) + ((slot0 * p.B + b) * conv_dim + chans[g]) * LC,
-                          D * LC * sizeof(TA), bar);
-            bulk_load(smem_u32(gbase + GL::OFF_CW + g * D * KC * (int)sizeof(TA)), cw + (size_t)chans[g] * KC,
-                      D * KC * sizeof(TA), bar);
+        __syncwarp();
+        // copy i < 4T: token i / 4, stream i % 4 (q, k, v rows of the projections, z); then the
+        // conv weights and the conv states of the three channel groups
+        const int nrow = 4 * T;
+        for (int i = lane; i < nrow + 6; i += 32) {
+            if (i < nrow) {
+                const int t = i >> 2, st = i & 3;
+                const TA* src = st == 3 ? gz + (size_t)b * p.zs_b + (size_t)t * p.zs_t + h * D
+                                        : gmixed + (size_t)b * p.ms_b + (size_t)t * p.ms_t +
+                                              (st == 0 ? c0 : (st == 1 ? c1 : c2));
+                bulk_load(smem_u32(gbase + GL::OFF_MQ + st * GL::M_BYTES + t * mrow), src, mrow, bar);
+            } else {
+                const int j = i - nrow, g = j % 3;
+                const int ch = g == 0 ? c0 : (g == 1 ? c1 : c2);
+                if (j < 3)
+                    bulk_load(smem_u32(gbase + GL::OFF_CW + g * D * KC * (int)sizeof(TA)),
+                              static_cast<const TA*>(p.convw) + (size_t)ch * KC, D * KC * sizeof(TA), bar);
+                else if (has_cs)
+                    bulk_load(smem_u32(gbase + GL::OFF_CS + g * D * LC * (int)sizeof(TA)),
+                              static_cast<const TA*>(p.cs_in) + ((slot0 * p.B + b) * conv_dim + ch) * LC,
+                              D * LC * sizeof(TA), bar);
+            }
         }
+    };
+    auto start_slot = [&](int tile) -> int {  // pool slot of the tile's starting state (slot mode)
+        if (!p.slot_table) return 0;
+        const int s0 = row_slot(p, tile / p.Hv, 0);
+        return s0 < 0 ? 0 : s0;
     };
 
     const int worker = blockIdx.x * NG + grp, nworkers = gridDim.x * NG;
-    if (tid == 0 && worker < num_tiles) {
-        if (has_S) issue_state(worker);
-        issue(worker);
+    if (tid < 32 && worker < num_tiles) {
+        const size_t s0 = (size_t)start_slot(worker);
+        if (has_S && lane == 0) issue_state(worker, s0);
+        issue(worker, s0);
     }
 
-    // gate inputs of the next tile are loaded one tile ahead into registers
-    float na = 0.f, nb = 0.f;
-    auto load_gates = [&](int tile) {
-        if (tid < T && tile < num_tiles) {
-            const int b = tile / p.Hv, h = tile - (tile / p.Hv) * p.Hv;
+    // Looked up one tile ahead into registers: the gate inputs and decay constants of the next
+    // tile's head, and in slot mode the pool slots of its starting state and of its checkpoints.
+    float na = 0.f, nb = 0.f, nalog = 0.f, ndtb = 0.f;
+    int nslot0 = 0, nck = -1;
+    auto prefetch = [&](int tile) {
+        if (tile >= num_tiles) return;
+        const int b = tile / p.Hv, h = tile - (tile / p.Hv) * p.Hv;
+        if (tid < T) {
             const size_t ai = (size_t)b * p.as_b + (size_t)tid * p.as_t + h;
             na = Act<TA>::ld(static_cast<const TA*>(p.a) + ai);
             nb = Act<TA>::ld(static_cast<const TA*>(p.b) + ai);
+            nalog = p.A_log[h];
+            ndtb = p.dt_bias[h];
+        }
+        if (p.slot_table) {
+            if (tid < 32) nslot0 = start_slot(tile);
+            if (tid < ck.n && tid < NCKS) nck = row_slot(p, b, ck.slot[tid]);
         }
     };
-    load_gates(worker);
+    prefetch(worker);
+    static_assert(D <= GT, "one output column per thread");
+    const float nw = tid < D ? Act<TA>::ldg(static_cast<const TA*>(p.normw) + tid) : 0.f;
 
     const TA* sMQ = reinterpret_cast<const TA*>(gbase + GL::OFF_MQ);
     const TA* sZ = reinterpret_cast<const TA*>(gbase + GL::OFF_Z);
@@ -195,94 +224,222 @@ __global__ void __launch_bounds__(NT, 1)
     const TA* sCW = reinterpret_cast<const TA*>(gbase + GL::OFF_CW);
     const float* sS = reinterpret_cast<const float*>(gbase + GL::OFF_S);
 
+    // The state lives in registers: rows rg*RPT .. +RPT-1, columns cg*4 .. cg*4+3.  Its stores
+    // (checkpoints, final state) are not issued in one burst after the update, which stalls
+    // every warp on the store queue at the same moment, but in four quarters spread over the
+    // work that follows: the end of the token's gated norm, then the next token's norms,
+    // products and reduction, or for the last token of a tile the next tile's conv phase.
+    // pend0 / pend1 are the destinations of the state held in S that are still owed a store
+    // (null when none; the same for every thread of the group).
+    float4 S[RPT];
+    float4* pend0 = nullptr;
+    float4* pend1 = nullptr;
+    auto flush = [&](auto quarter) {
+        constexpr int Q = decltype(quarter)::value, R0 = Q * (RPT / 4), R1 = R0 + RPT / 4;
+        if (pend0 == nullptr) return;
+#pragma unroll
+        for (int r = R0; r < R1; ++r) {
+            __stcs(pend0 + (rg * RPT + r) * CG + cg, S[r]);
+            if (pend1) __stcs(pend1 + (rg * RPT + r) * CG + cg, S[r]);
+        }
+        if (Q == 3) pend0 = pend1 = nullptr;
+    };
+    auto owe = [&](float4* dst) {  // the state in S must also go to dst
+        if (!pend0) pend0 = dst;
+        else if (!pend1) pend1 = dst;
+        else {
+#pragma unroll
+            for (int r = 0; r < RPT; ++r) __stcs(dst + (rg * RPT + r) * CG + cg, S[r]);
+        }
+    };
+    using Q0 = std::integral_constant<int, 0>;
+    using Q1 = std::integral_constant<int, 1>;
+    using Q2 = std::integral_constant<int, 2>;
+    using Q3 = std::integral_constant<int, 3>;
+
     uint32_t k = 0;
     bool failed = false;
     for (int tile = worker; tile < num_tiles; tile += nworkers, ++k) {
         const int b = tile / p.Hv, h = tile - (tile / p.Hv) * p.Hv, kh = h / rep;
-        const float cur_a = na, cur_b = nb;
-        load_gates(tile + nworkers);
+        const float cur_a = na, cur_b = nb, cur_alog = nalog, cur_dtb = ndtb;
+        const int cur_ck = nck;
+        prefetch(tile + nworkers);
         if (tid < T) {
             sgate[tid] = Act<TA>::round(sigmoid_f(cur_b));
-            sgate[TMAX + tid] = expf(-expf(p.A_log[h]) * softplus_f(cur_a + p.dt_bias[h]));
+            sgate[TMAX + tid] = expf(-expf(cur_alog) * softplus_f(cur_a + cur_dtb));
         }
+        // checkpoint slots of this tile, double-buffered by tile parity: the previous tile's last
+        // readers may still be in its final token (no barrier ends a tile), and the group_any
+        // barrier below publishes these before any reader of this tile
+        int* sck = reinterpret_cast<int*>(gbase + GL::OFF_SLOT) + (k & 1u) * NCKS;
+        if (p.slot_table && tid < ck.n && tid < NCKS) sck[tid] = cur_ck;
+        auto ck_slot = [&](int i) -> int {  // output slot of checkpoint i of this tile
+            if (!p.slot_table) return ck.slot[i];
+            return i < NCKS ? sck[i] : row_slot(p, b, ck.slot[i]);
+        };
 
         const bool ok = (!has_S || mbar_wait_bounded(bar_s, k & 1u, GDN_DEVERR_TMA_TIMEOUT)) &&
                         mbar_wait_bounded(bar, k & 1u, GDN_DEVERR_TMA_TIMEOUT);
 
-        // ---- consume the stage: state to registers, conv windows, conv of every token, z ----
-        // The state is read before the group agrees on the waits (a thread whose wait gave up
-        // reads stale, in-bounds data that is then discarded), so one barrier both agrees on
-        // failure and releases the state region for the next tile's state.
-        float4 S[RPT];  // rows rg*RPT .. +RPT-1, columns cg*4 .. cg*4+3
-#pragma unroll
-        for (int r = 0; r < RPT; ++r)
-            S[r] = has_S ? *reinterpret_cast<const float4*>(sS + (rg * RPT + r) * D + cg * 4)
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-        if (group_any(!ok, bar_id)) {
-            failed = true;
-            break;
-        }
-        if (has_S && tid == 0 && tile + nworkers < num_tiles) {
-            fence_proxy_async_smem();
-            issue_state(tile + nworkers);
-        }
-
         const bool own_qk = (h % rep) == 0;
         const int cbeg = own_qk ? 0 : 2 * D;
-        {
-            // conv windows (raw inputs, bit-exact copies): final state + checkpoints
+        // destination of window w: -1 the final conv state, else checkpoint w (null: bad slot)
+        auto window_dst = [&](int w) -> TA* {
+            if (w < 0) return static_cast<TA*>(p.cs_out) + (size_t)b * conv_dim * LC;
+            const int slot = ck_slot(w);
+            return slot < 0 ? nullptr : static_cast<TA*>(p.cs_ckpt) + ((size_t)slot * p.B + b) * conv_dim * LC;
+        };
+        // One conv window, one channel per thread: the single-token step writes only the final
+        // conv state, and spreading its 3D channels over every thread beats fewer, wider stores.
+        auto write_window_per_channel = [&](TA* dst, int off) {
+            for (int c = cbeg + tid; c < 3 * D; c += GT) {
+                const int g = c / D, ci = c % D;
+                const int gc = (g == 0 ? kh * D : (g == 1 ? p.Hk * D + kh * D : 2 * p.Hk * D + h * D)) + ci;
+                const TA* mg = sMQ + g * (GL::M_BYTES / (int)sizeof(TA));
+#pragma unroll
+                for (int i = 0; i < LC; ++i) {
+                    const int pos = off - LC + i;
+                    TA val;
+                    if (pos >= 0) val = mg[pos * D + ci];
+                    else if (has_cs) val = sCS[(g * D + ci) * LC + (LC + pos)];
+                    else val = TA(0.0f);
+                    dst[(size_t)gc * LC + i] = val;
+                }
+            }
+        };
+        // Conv windows (raw inputs, bit-exact copies) in one pass: the final conv state (offset T)
+        // and the conv checkpoints.  A work item is (window, channel group, block of 8 channels):
+        // it reads each tap's 8 channels with one 16-byte load (taps before the first token from
+        // the conv state) and writes the block's [8][LC] span, contiguous in the conv state,
+        // with 16-byte stores.
+        auto write_windows = [&]() {
+            constexpr int CB = 8, NB = D / CB;
             const int nwin = (p.cs_out ? 1 : 0) + (p.cs_ckpt ? ck.n : 0);
-            for (int w = 0; w < nwin; ++w) {
+            const int g0 = cbeg / D, ng = 3 - g0;
+            for (int it = tid; it < nwin * ng * NB; it += GT) {
+                const int w = it / (ng * NB), rem = it - w * (ng * NB);
+                const int g = g0 + rem / NB, ci0 = (rem % NB) * CB;
                 const bool fin = p.cs_out && w == 0;
                 const int ci_idx = p.cs_out ? w - 1 : w;
+                TA* dst = window_dst(fin ? -1 : ci_idx);
+                if (!dst) continue;
                 const int off = fin ? T : ck.off[ci_idx];
-                const int slot = fin ? 0 : ckpt_slot(p, ck, ci_idx, b);
-                if (slot < 0) continue;
-                TA* dst = fin ? static_cast<TA*>(p.cs_out) + (size_t)b * conv_dim * LC
-                              : static_cast<TA*>(p.cs_ckpt) + ((size_t)slot * p.B + b) * conv_dim * LC;
-                for (int c = cbeg + tid; c < 3 * D; c += GT) {
-                    const int g = c / D, ci = c % D;
-                    const int gc = (g == 0 ? kh * D : (g == 1 ? p.Hk * D + kh * D : 2 * p.Hk * D + h * D)) + ci;
-                    const TA* mg = sMQ + g * (GL::M_BYTES / (int)sizeof(TA));
+                const int gch = g == 0 ? kh * D : (g == 1 ? p.Hk * D + kh * D : 2 * p.Hk * D + h * D);
+                const TA* mg = sMQ + g * (GL::M_BYTES / (int)sizeof(TA));
+                const TA* cs = sCS + (g * D + ci0) * LC;
+                uint4* d4 = reinterpret_cast<uint4*>(dst + (size_t)(gch + ci0) * LC);
+                if constexpr (sizeof(TA) == 2) {
+                    uint32_t r[LC][4];  // tap i: channels ci0 .. ci0+7 as bf16 pairs
 #pragma unroll
                     for (int i = 0; i < LC; ++i) {
                         const int pos = off - LC + i;
-                        TA val;
-                        if (pos >= 0) val = mg[pos * D + ci];
-                        else if (has_cs) val = sCS[(g * D + ci) * LC + (LC + pos)];
-                        else val = TA(0.0f);
-                        dst[(size_t)gc * LC + i] = val;
+                        if (pos >= 0) {
+                            const uint4 v = *reinterpret_cast<const uint4*>(mg + pos * D + ci0);
+                            r[i][0] = v.x; r[i][1] = v.y; r[i][2] = v.z; r[i][3] = v.w;
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const uint32_t lo = has_cs ? __bfloat16_as_ushort(cs[(2 * k) * LC + LC + pos]) : 0u;
+                                const uint32_t hi = has_cs ? __bfloat16_as_ushort(cs[(2 * k + 1) * LC + LC + pos]) : 0u;
+                                r[i][k] = lo | (hi << 16);
+                            }
+                        }
                     }
+                    // (channel, tap) order: c0t0 c0t1 | c0t2 c1t0 | c1t1 c1t2 | c2t0 ...
+                    uint32_t o[12];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        o[3 * k] = __byte_perm(r[0][k], r[1][k], 0x5410);
+                        o[3 * k + 1] = __byte_perm(r[2][k], r[0][k], 0x7610);
+                        o[3 * k + 2] = __byte_perm(r[1][k], r[2][k], 0x7632);
+                    }
+                    d4[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                    d4[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                    d4[2] = make_uint4(o[8], o[9], o[10], o[11]);
+                } else {
+                    float v[CB * LC];
+#pragma unroll
+                    for (int e = 0; e < CB * LC; ++e) {
+                        const int c = e / LC, i = e % LC, pos = off - LC + i;
+                        v[e] = pos >= 0 ? Act<TA>::ld(mg + pos * D + ci0 + c)
+                                        : (has_cs ? Act<TA>::ld(cs + c * LC + LC + pos) : 0.f);
+                    }
+#pragma unroll
+                    for (int q = 0; q < CB * LC / 4; ++q)
+                        d4[q] = make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]),
+                                           __float_as_uint(v[4 * q + 2]), __float_as_uint(v[4 * q + 3]));
                 }
             }
-        }
-        // conv + SiLU of every token, sliding a 4-tap window along the sequence;
-        // indices past the conv channels copy z (balances the two phases)
-        for (int c = tid; c < 3 * D + D; c += GT) {
+        };
+        // conv + SiLU of channel c < 3D for token t; c in [3D, 4D) copies z column c - 3D
+        auto conv_one = [&](int c, int t) {
             if (c >= 3 * D) {
                 const int j = c - 3 * D;
-                for (int t = 0; t < T; ++t) zbuf[t * D + j] = Act<TA>::ld(sZ + t * D + j);
-                continue;
+                zbuf[t * D + j] = Act<TA>::ld(sZ + t * D + j);
+                return;
             }
             const int g = c / D, ci = c % D;
             const TA* mg = sMQ + g * (GL::M_BYTES / (int)sizeof(TA));
-            float w[KC], win[KC];
+            float w[KC], win[KC];  // win[j]: the input j tokens back
 #pragma unroll
-            for (int j = 0; j < KC; ++j) w[j] = Act<TA>::ld(sCW + (g * D + ci) * KC + j);
-            win[0] = 0.f;
-#pragma unroll
-            for (int j = 1; j < KC; ++j) win[j] = has_cs ? Act<TA>::ld(sCS + (g * D + ci) * LC + (LC - j)) : 0.f;
-            for (int t = 0; t < T; ++t) {
-                win[0] = Act<TA>::ld(mg + t * D + ci);
-                cbuf[t * 3 * D + c] = Act<TA>::round(silu_f(conv_taps<TA>(win, w, KC, has_cs ? LC : t)));
-#pragma unroll
-                for (int j = KC - 1; j > 0; --j) win[j] = win[j - 1];
+            for (int j = 0; j < KC; ++j) {
+                w[j] = Act<TA>::ld(sCW + (g * D + ci) * KC + j);
+                const int pos = t - j;
+                win[j] = pos >= 0 ? Act<TA>::ld(mg + pos * D + ci)
+                                  : (has_cs ? Act<TA>::ld(sCS + (g * D + ci) * LC + (LC + pos)) : 0.f);
             }
-        }
-        group_sync(bar_id);  // stage consumed: refill it with this group's next tile
-        if (tid == 0 && tile + nworkers < num_tiles) {
-            fence_proxy_async_smem();
-            issue(tile + nworkers);
+            cbuf[t * 3 * D + c] = Act<TA>::round(silu_f(conv_taps<TA>(win, w, KC, has_cs ? LC : t)));
+        };
+
+        if constexpr (!DEFER) {
+            // ---- consume the stage: state to registers, conv windows, conv of every token, z ----
+            // The state is read before the group agrees on the waits (a thread whose wait gave up
+            // reads stale, in-bounds data that is then discarded), so one barrier both agrees on
+            // failure and releases the state region for the next tile's state.
+#pragma unroll
+            for (int r = 0; r < RPT; ++r)
+                S[r] = has_S ? *reinterpret_cast<const float4*>(sS + (rg * RPT + r) * D + cg * 4)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (group_any(!ok, bar_id)) {
+                failed = true;
+                break;
+            }
+            if (has_S && tid == 0 && tile + nworkers < num_tiles) {
+                fence_proxy_async_smem();
+                issue_state(tile + nworkers, (size_t)nslot0);
+            }
+            if (p.cs_out && !p.cs_ckpt) write_window_per_channel(window_dst(-1), T);
+            else write_windows();
+            for (int c = tid; c < 4 * D; c += GT)
+                for (int t = 0; t < T; ++t) conv_one(c, t);
+            group_sync(bar_id);  // stage consumed: refill it with this group's next tile
+            if (tid < 32 && tile + nworkers < num_tiles) {
+                fence_proxy_async_smem();
+                issue(tile + nworkers, (size_t)nslot0);
+            }
+        } else {
+            // ---- conv windows and every token's conv while the previous tile's last state stores
+            // drain, then the state (its registers are free once those stores are issued) ----
+            if (group_any(!ok, bar_id)) {
+                failed = true;
+                break;
+            }
+            flush(Q1{});
+            write_windows();
+            flush(Q2{});
+            for (int c = tid; c < 4 * D; c += GT)
+                for (int t = 0; t < T; ++t) conv_one(c, t);
+            flush(Q3{});
+#pragma unroll
+            for (int r = 0; r < RPT; ++r)
+                S[r] = has_S ? *reinterpret_cast<const float4*>(sS + (rg * RPT + r) * D + cg * 4)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+            group_sync(bar_id);  // stage consumed (inputs and state): refill it with this group's next tile
+            if (tid < 32 && tile + nworkers < num_tiles) {
+                fence_proxy_async_smem();
+                if (has_S && lane == 0) issue_state(tile + nworkers, (size_t)nslot0);
+                issue(tile + nworkers, (size_t)nslot0);
+            }
         }
 
         int ck_i = 0;
@@ -305,6 +462,7 @@ __global__ void __launch_bounds__(NT, 1)
             const float rq = rsqrtf(aq + 1e-6f), rk = rsqrtf(ak + 1e-6f);
             const float qk = aqk * rq * p.q_scale * rk;
             const float beta = sgate[t], alpha = sgate[TMAX + t];
+            flush(Q1{});
 
             float kr[RPT], qr[RPT];
             const float2 rk2 = make_float2(rk, rk), rq2 = make_float2(rq, rq), qs2 = make_float2(p.q_scale, p.q_scale);
@@ -329,6 +487,7 @@ __global__ void __launch_bounds__(NT, 1)
                 pq01 = __ffma2_rn(qv, s01, pq01);
                 pq23 = __ffma2_rn(qv, s23, pq23);
             }
+            flush(Q2{});
             const float4 pk = make_float4(pk01.x, pk01.y, pk23.x, pk23.y);
             const float4 pq = make_float4(pq01.x, pq01.y, pq23.x, pq23.y);
             reinterpret_cast<float4*>(red + rg * D)[cg] = pk;
@@ -344,6 +503,7 @@ __global__ void __launch_bounds__(NT, 1)
                 else so[j] = alpha * acc;
             }
             group_sync(bar_id);
+            flush(Q3{});  // the state after the previous token is stored: S may change
 
             {
                 const float4 u4 = reinterpret_cast<const float4*>(su)[cg];
@@ -358,15 +518,12 @@ __global__ void __launch_bounds__(NT, 1)
                 }
             }
             while (ck_i < ck.n && ck.off[ck_i] == t + 1) {
-                const int slot = p.S_ckpt ? ckpt_slot(p, ck, ck_i, b) : -1;
-                if (slot >= 0) {
-                    float4* dst = reinterpret_cast<float4*>(p.S_ckpt + ((size_t)slot * p.B * p.Hv + tile) *
-                                                                           (size_t)(D * D));
-#pragma unroll
-                    for (int r = 0; r < RPT; ++r) __stcs(dst + (rg * RPT + r) * CG + cg, S[r]);
-                }
+                const int slot = p.S_ckpt ? ck_slot(ck_i) : -1;
+                if (slot >= 0)
+                    owe(reinterpret_cast<float4*>(p.S_ckpt + ((size_t)slot * p.B * p.Hv + tile) * (size_t)(D * D)));
                 ++ck_i;
             }
+            if (t + 1 == T && p.S_out) owe(reinterpret_cast<float4*>(p.S_out + (size_t)tile * D * D));
 
             // gated RMSNorm of token t (sum of squares recomputed by every warp);
             // o = alpha q.S + (q.k) u
@@ -378,23 +535,28 @@ __global__ void __launch_bounds__(NT, 1)
             }
             ss = warp_sum(ss);
             const float rstd = rsqrtf(ss / (float)D + p.eps);
-            const TA* normw = static_cast<const TA*>(p.normw);
-            TA* out = static_cast<TA*>(p.out) + ((size_t)b * T + t) * (size_t)(p.Hv * D) + h * D;
-            for (int j = tid; j < D; j += GT) {
+            if (tid < D) {
+                const int j = tid;
+                TA* out = static_cast<TA*>(p.out) + ((size_t)b * T + t) * (size_t)(p.Hv * D) + h * D;
                 const float o = Act<TA>::round(fmaf(qk, su[j], so[j]));
-                const float y = Act<TA>::round(Act<TA>::ldg(normw + j) * Act<TA>::round(o * rstd));
+                const float y = Act<TA>::round(nw * Act<TA>::round(o * rstd));
                 Act<TA>::st(out + j, y * silu_f(zbuf[t * D + j]));
             }
+            flush(Q0{});
             // su / so / red are rewritten by the next token; after the last token the next
             // tile's first two barriers come before any thread writes them (or the gates)
             if (t + 1 < T) group_sync(bar_id);
         }
-
-        if (p.S_out) {
-            float4* dst = reinterpret_cast<float4*>(p.S_out + (size_t)tile * D * D);
-#pragma unroll
-            for (int r = 0; r < RPT; ++r) __stcs(dst + (rg * RPT + r) * CG + cg, S[r]);
+        if constexpr (!DEFER) {  // the state is reloaded at the next tile's start
+            flush(Q1{});
+            flush(Q2{});
+            flush(Q3{});
         }
+    }
+    if (!failed) {  // the last tile's final stores
+        flush(Q1{});
+        flush(Q2{});
+        flush(Q3{});
     }
 
     if (failed && tid == 0) {
@@ -437,6 +599,9 @@ bool aligned_for_bulk(const MixParams& p, int d) {
     if ((p.ms_b * es) % 16 || (p.ms_t * es) % 16 || (p.zs_b * es) % 16 || (p.zs_t * es) % 16) return false;
     if ((d * es) % 16 || (d * KC * es) % 16) return false;
     if (p.cs_in && (!al(p.cs_in) || (conv_dim * LC * es) % 16 || (d * LC * es) % 16)) return false;
+    // conv windows leave in 16-byte chunks
+    if ((p.cs_out || p.cs_ckpt) && ((conv_dim * LC * es) % 16 || (d * LC * es) % 16)) return false;
+    if ((p.cs_out && !al(p.cs_out)) || (p.cs_ckpt && !al(p.cs_ckpt))) return false;
     return true;
 }
 
