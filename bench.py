@@ -4,10 +4,14 @@
 
 Headline workload (one GPU): the single-token decode step of one DeltaNet
 layer at batch 64, hidden 2048, 16 key heads / 32 value heads, d_k = d_v = 128,
-bf16 activations and an fp32 recurrent state (128 MiB).  One bench step = one
-fused kernel launch that takes the step's projection outputs to the gated
-RMSNorm output, updating the recurrent state in place.  Four rotating state
-slots (4 x 134 MB) keep every step's state traffic out of the 126 MB L2.
+bf16 activations and an fp32 recurrent state (128 MiB).  Every decode step is
+one fused kernel launch that takes the step's projection outputs to the gated
+RMSNorm output, updating the recurrent state in place.  One bench step is a
+run of 512 such decode steps, captured once as a CUDA graph and replayed; K
+bench steps are timed.  ``value`` is decode steps per second, ``ms_per_step``
+the time of one bench step (512 launches), ``ms_per_decode_step`` that of one
+launch, ``gpu_launches`` K x 512.  Four rotating state slots (4 x 134 MB) keep
+every step's state traffic out of the 126 MB L2.
 
 With ``--gpus N`` (torchrun, one rank per GPU) the value heads are sharded:
 rank r owns value heads [r*32/N, (r+1)*32/N) and the key heads they read; the
@@ -17,10 +21,14 @@ rows, 16 N rollback rows), so every GPU keeps the single-GPU amount of work
 (weak scaling), and ``value`` is the whole job's rate in units of the
 single-GPU workload (B64 decode steps per second).
 
-Also reported: the chunked-prefill workload (batch 8 x 8192 tokens) and the
-speculative verify + rollback workload (batch 16, 4-token drafts) as secondary
-objects, the roofline of the dominant kernel, an end-to-end number
-through the public API with host buffers, the CPU oracle timed on the host,
+Also reported, as objects of the same line: the chunked-prefill workload
+(batch 8 x 8192 tokens), the speculative verify + rollback workload (batch 16,
+4-token drafts), the whole head-sharded layer with its NCCL all-reduce at
+strong and weak scaling (``sharded_layer``), at one GPU the prefix-cache
+snapshot / restore of a 36-layer stack's states (``prefix_snapshot``) and the
+48-layer hybrid stack (``stack``); the roofline of the dominant kernel; an
+end-to-end number through the public API with host buffers; the CPU oracle
+timed on the host's cores (decode, prefill and the configs[0] layer case);
 and SM clocks sampled during the timed region.
 
 ``--impl reference`` times the CPU restatement of the reference path (the

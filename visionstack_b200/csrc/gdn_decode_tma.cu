@@ -140,6 +140,10 @@ __global__ void __launch_bounds__(NT, 1)
         fence_mbar_init();
     }
     __syncthreads();
+    // launched as a programmatic dependent: the next kernel may start as CTAs retire, and
+    // nothing below touches global memory before the previous kernel has completed
+    pdl_launch_dependents();
+    pdl_wait();
 
     // Warp 0 of the group issues the copies of one tile into the group's stage: the state (on
     // bar_s, one copy by lane 0: it refills as soon as the state is in registers) and the small
@@ -371,24 +375,28 @@ __global__ void __launch_bounds__(NT, 1)
                 }
             }
         };
-        // conv + SiLU of channel c < 3D for token t; c in [3D, 4D) copies z column c - 3D
-        auto conv_one = [&](int c, int t) {
+        // conv + SiLU of channel c < 3D for every token, sliding a 4-tap window along the
+        // sequence; c in [3D, 4D) copies z column c - 3D for every token
+        auto conv_channel = [&](int c) {
             if (c >= 3 * D) {
                 const int j = c - 3 * D;
-                zbuf[t * D + j] = Act<TA>::ld(sZ + t * D + j);
+                for (int t = 0; t < T; ++t) zbuf[t * D + j] = Act<TA>::ld(sZ + t * D + j);
                 return;
             }
             const int g = c / D, ci = c % D;
             const TA* mg = sMQ + g * (GL::M_BYTES / (int)sizeof(TA));
             float w[KC], win[KC];  // win[j]: the input j tokens back
 #pragma unroll
-            for (int j = 0; j < KC; ++j) {
-                w[j] = Act<TA>::ld(sCW + (g * D + ci) * KC + j);
-                const int pos = t - j;
-                win[j] = pos >= 0 ? Act<TA>::ld(mg + pos * D + ci)
-                                  : (has_cs ? Act<TA>::ld(sCS + (g * D + ci) * LC + (LC + pos)) : 0.f);
+            for (int j = 0; j < KC; ++j) w[j] = Act<TA>::ld(sCW + (g * D + ci) * KC + j);
+            win[0] = 0.f;
+#pragma unroll
+            for (int j = 1; j < KC; ++j) win[j] = has_cs ? Act<TA>::ld(sCS + (g * D + ci) * LC + (LC - j)) : 0.f;
+            for (int t = 0; t < T; ++t) {
+                win[0] = Act<TA>::ld(mg + t * D + ci);
+                cbuf[t * 3 * D + c] = Act<TA>::round(silu_f(conv_taps<TA>(win, w, KC, has_cs ? LC : t)));
+#pragma unroll
+                for (int j = KC - 1; j > 0; --j) win[j] = win[j - 1];
             }
-            cbuf[t * 3 * D + c] = Act<TA>::round(silu_f(conv_taps<TA>(win, w, KC, has_cs ? LC : t)));
         };
 
         if constexpr (!DEFER) {
@@ -410,8 +418,7 @@ __global__ void __launch_bounds__(NT, 1)
             }
             if (p.cs_out && !p.cs_ckpt) write_window_per_channel(window_dst(-1), T);
             else write_windows();
-            for (int c = tid; c < 4 * D; c += GT)
-                for (int t = 0; t < T; ++t) conv_one(c, t);
+            for (int c = tid; c < 4 * D; c += GT) conv_channel(c);
             group_sync(bar_id);  // stage consumed: refill it with this group's next tile
             if (tid < 32 && tile + nworkers < num_tiles) {
                 fence_proxy_async_smem();
@@ -427,8 +434,7 @@ __global__ void __launch_bounds__(NT, 1)
             flush(Q1{});
             write_windows();
             flush(Q2{});
-            for (int c = tid; c < 4 * D; c += GT)
-                for (int t = 0; t < T; ++t) conv_one(c, t);
+            for (int c = tid; c < 4 * D; c += GT) conv_channel(c);
             flush(Q3{});
 #pragma unroll
             for (int r = 0; r < RPT; ++r)
@@ -586,8 +592,7 @@ cudaError_t launch_one(const MixParams& p, const CkptList& ck, cudaStream_t s) {
     const int tiles = p.B * p.Hv;
     int grid = (tiles + NG - 1) / NG;
     if (grid > sm_count[dev]) grid = sm_count[dev];
-    decode_tma_kernel<D, TMAX, TA><<<grid, NT, bytes, s>>>(p, ck, tiles);
-    return cudaGetLastError();
+    return launch_pdl(decode_tma_kernel<D, TMAX, TA>, dim3(grid), dim3(NT), bytes, s, p, ck, tiles);
 }
 
 template <typename TA>

@@ -16,6 +16,8 @@ namespace {
 
 __global__ void accept_slots_kernel(const int* __restrict__ accepted, int* __restrict__ table, int B, int n,
                                     int T) {
+    pdl_launch_dependents();
+    pdl_wait();  // the verify launch before this one reads the table
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     const int a = accepted[b];
@@ -34,8 +36,8 @@ __global__ void accept_slots_kernel(const int* __restrict__ accepted, int* __res
 
 cudaError_t launch_accept_slots(const int* accepted, int* table, int B, int n_slots, int T, cudaStream_t s) {
     const int threads = 128;
-    accept_slots_kernel<<<(B + threads - 1) / threads, threads, 0, s>>>(accepted, table, B, n_slots, T);
-    return cudaGetLastError();
+    return launch_pdl(accept_slots_kernel, dim3((B + threads - 1) / threads), dim3(threads), 0, s, accepted, table, B,
+                      n_slots, T);
 }
 
 unsigned int slots_device_error(bool clear) {
