@@ -209,9 +209,9 @@ int32_t gdn_device_error(uint32_t* flags_out, int32_t clear);
 
 /*
  * Tensor-core self-test: D[128][N] = A * B with the 5th-generation tensor
- * core (tf32 in, fp32 out; modes 7..8 bf16 in) for operand-layout combination
- * `mode` (0..8, see gdn_umma_selftest.cu; modes 4..8 read A from tensor
- * memory), in plain
+ * core (tf32 in, fp32 out; modes 7..10 bf16 in) for operand-layout combination
+ * `mode` (0..10, see gdn_umma_selftest.cu; modes 4..8 read A from tensor
+ * memory, 9..10 both operands from shared memory), in plain
  * row-major fp32 device buffers.  Checks the shared-memory layouts,
  * descriptors and tensor-memory operands the chunked kernels rely on.  No
  * counterpart in the reference.

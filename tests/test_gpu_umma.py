@@ -15,11 +15,12 @@ from visionstack_b200 import _lib
 pytestmark = pytest.mark.gpu
 
 # mode: (K, N, A MN-major, B MN-major); modes 4-8 read A from tensor memory,
-# modes 7-8 take bf16 operands
+# modes 7-10 take bf16 operands (9-10 with both operands in shared memory)
 SHAPES = {0: (128, 64, False, False), 1: (128, 128, False, True), 2: (64, 128, False, True),
           3: (64, 128, True, True), 4: (128, 128, False, False), 5: (64, 64, False, False),
-          6: (64, 128, False, True), 7: (128, 128, False, False), 8: (64, 128, False, True)}
-BF16_MODES = (7, 8)
+          6: (64, 128, False, True), 7: (128, 128, False, False), 8: (64, 128, False, True),
+          9: (128, 64, False, True), 10: (64, 64, True, True)}
+BF16_MODES = (7, 8, 9, 10)
 
 
 def _bf16(x):

@@ -402,7 +402,7 @@ int32_t gdn_selftest_expired_wait(int32_t kind, int32_t* flag, void* stream) {
 }
 
 int32_t gdn_selftest_umma(int32_t mode, const float* A, const float* B, float* D, void* stream) {
-    if (mode < 0 || mode > 8) return fail(GDN_ERR_INVALID_ARG, "mode %d not in 0..8", mode);
+    if (mode < 0 || mode > 10) return fail(GDN_ERR_INVALID_ARG, "mode %d not in 0..10", mode);
     if (!A || !B || !D) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
     const void* ptrs[] = {A, B, D};
     for (const void* ptr : ptrs)

@@ -16,8 +16,12 @@
 //   mode 7: A in tensor memory [128][128], B K-major [128][128] (D = A B^T, N = 128)
 //   mode 8: A in tensor memory [128][64],  B MN-major [64][128] (D = A B, K = 64;
 //           64-element mn atoms 16 KB apart)
+// and kind::f16 with both bf16 operands in shared memory:
+//   mode 9:  A K-major [128][128] (the [k;q] rows), B MN-major [128][64] (D = A B, N = 64)
+//   mode 10: A MN-major [64][128] (k rows read as A^T, 64-element mn atoms 16 KB apart),
+//            B MN-major [64][64] (D = A B, K = 64, N = 64)
 // Inputs are plain row-major fp32 in global memory: A is [M][K] except for
-// mode 3 ([K][M]); B is [N][K] for K-major B and [K][N] for MN-major B.
+// the MN-major A of modes 3 and 10 ([K][M]); B is [N][K] for K-major B and [K][N] for MN-major B.
 #include <cuda_bf16.h>
 
 #include "gdn_kernels.cuh"
@@ -42,7 +46,9 @@ __host__ __device__ inline SelfTestShape selftest_shape(int mode) {
         case 5: return {64, 64, 0, 0, 1, 0};
         case 6: return {64, 128, 0, 1, 1, 0};
         case 7: return {128, 128, 0, 0, 1, 1};
-        default: return {64, 128, 0, 1, 1, 1};
+        case 8: return {64, 128, 0, 1, 1, 1};
+        case 9: return {128, 64, 0, 1, 0, 1};
+        default: return {64, 64, 1, 1, 0, 1};
     }
 }
 
@@ -60,7 +66,17 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const f
     uint32_t* tslot = reinterpret_cast<uint32_t*>(base + 2 * 128 * 128 * 4 + 8);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-    for (int i = tid; i < M * K && !sh.a_tmem; i += 128) {
+    for (int i = tid; i < M * K && !sh.a_tmem && sh.bf16; i += 128) {
+        const __nv_bfloat16 v = __float2bfloat16_rn(A[i]);
+        if (!sh.a_mn) {
+            const int m = i / K, k = i % K;
+            *reinterpret_cast<__nv_bfloat16*>(sA + umma::kmajor_off16(m, k, M)) = v;
+        } else {
+            const int k = i / M, m = i % M;
+            *reinterpret_cast<__nv_bfloat16*>(sA + umma::mnmajor_off16(k, m, MN_ATOM16)) = v;
+        }
+    }
+    for (int i = tid; i < M * K && !sh.a_tmem && !sh.bf16; i += 128) {
         if (!sh.a_mn) {
             const int m = i / K, k = i % K;
             *reinterpret_cast<float*>(sA + umma::kmajor_off(m, k, M)) = A[i];
@@ -131,11 +147,17 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int mode, const f
     umma::fence_after_sync();
 
     if (tid == 0 && sh.bf16) {
-        const uint32_t idesc = umma::idesc_bf16(M, N, 0, sh.b_mn);
+        const uint32_t idesc = umma::idesc_bf16(M, N, sh.a_mn, sh.b_mn);
         const uint64_t d0 = sh.b_mn ? umma::desc_mnmajor16_0(smem_u32(sB), MN_ATOM16) : umma::desc_kmajor0(smem_u32(sB));
+        const uint64_t a0 = sh.a_mn ? umma::desc_mnmajor16_0(smem_u32(sA), MN_ATOM16) : umma::desc_kmajor0(smem_u32(sA));
         for (int kk = 0; kk < K / 16; ++kk) {
             const uint32_t step = sh.b_mn ? umma::mnmajor16_kstep(kk) : umma::kmajor_kstep(kk, N);
-            umma::mma_bf16_ta(tbase, tbase + A_COL + kk * 8, umma::desc_add(d0, step), idesc, kk > 0 ? 1u : 0u);
+            if (sh.a_tmem) {
+                umma::mma_bf16_ta(tbase, tbase + A_COL + kk * 8, umma::desc_add(d0, step), idesc, kk > 0 ? 1u : 0u);
+            } else {
+                const uint32_t astep = sh.a_mn ? umma::mnmajor16_kstep(kk) : umma::kmajor_kstep(kk, M);
+                umma::mma_bf16(tbase, umma::desc_add(a0, astep), umma::desc_add(d0, step), idesc, kk > 0 ? 1u : 0u);
+            }
         }
         umma::mma_commit(smem_u32(bar));
     } else if (tid == 0) {
