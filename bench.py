@@ -25,8 +25,8 @@ Also reported, as objects of the same line: the chunked-prefill workload
 (batch 8 x 8192 tokens), the speculative verify + rollback workload (batch 16,
 4-token drafts), the whole head-sharded layer with its NCCL all-reduce at
 strong and weak scaling (``sharded_layer``), at one GPU the prefix-cache
-snapshot / restore of a 36-layer stack's states (``prefix_snapshot``) and the
-48-layer hybrid stack (``stack``); the roofline of the dominant kernel; an
+snapshot / restore of a 36-layer stack's states (``prefix_snapshot``), and the
+48-layer hybrid stack (``stack``, tensor-parallel over the run's GPUs); the roofline of the dominant kernel; an
 end-to-end number through the public API with host buffers; the CPU oracle
 timed on the host's cores (decode, prefill and the configs[0] layer case);
 and SM clocks sampled during the timed region.
@@ -70,7 +70,7 @@ def parse():
     ap.add_argument("--no-rollback", action="store_true", help="skip the secondary rollback measurement")
     ap.add_argument("--no-stack", action="store_true",
                     help="skip the secondary 48-layer hybrid stack measurement (B32: prefill 4096, decode 256; "
-                         "run at 1 GPU only)")
+                         "tensor-parallel over the GPUs of the run)")
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the head-sharded layer measurement (projections, mixer, out_proj, all-reduce)")
     ap.add_argument("--no-prefix-snapshot", action="store_true",
@@ -578,11 +578,14 @@ def run_ours(args, rank: int, world: int) -> None:
         prefix_snap = run_prefix_snapshot(torch, m, local, dev)
 
     stack = None
-    if not args.no_stack and world == 1:
-        try:
-            stack = run_stack(torch, dev)
-        except Exception as e:  # the stack is a secondary measurement: never lose the line to it
-            stack = {"error": f"{type(e).__name__}: {e}"[:300]}
+    if not args.no_stack:
+        if world == 1:
+            try:
+                stack = run_stack(torch, dist, dev, rank, world, barrier)
+            except Exception as e:  # the stack is a secondary measurement: never lose the line to it
+                stack = {"error": f"{type(e).__name__}: {e}"[:300]}
+        else:  # every rank takes the same collective steps; an error ends the job
+            stack = run_stack(torch, dist, dev, rank, world, barrier)
 
     if rank != 0:
         return
@@ -765,14 +768,18 @@ def run_prefill(torch, dist, m, local, dev, world, barrier, B=8, T=8192):
                          "kernel": "gdn::pseq::prefill_seq_kernel (tcgen05 bf16 hi+lo and tf32, state in tensor memory, 1 CTA per (batch, head)) after gdn::pprep::prefill_prep_kernel"}}
 
 
-def run_stack(torch, dev):
+def run_stack(torch, dist, dev, rank, world, barrier):
     """The 48-layer hybrid stack (36 Gated DeltaNet layers on the CUDA token mixer, 12 gated
     attention layers and all MLPs on library kernels), random bf16 weights, B32: a 4096-token
     prefill into a hybrid cache, then 256 decode steps of random token ids.  The prefill is eager
     PyTorch around the mixer; the decode steps replay one captured CUDA graph (static KV buffers,
-    the position on the device); the decode time is that of the replayed steps."""
+    the position on the device); the decode time is that of the replayed steps.  With N ranks the
+    stack is tensor-parallel (``stack_tp.shard_stack``: DeltaNet value heads, attention query
+    heads with the KV heads they read, MLP columns; two NCCL all-reduces per layer, inside the
+    decode graph too) at the same batch (strong scaling); times are the max over ranks."""
     from visionstack_b200 import Qwen3_5HybridCache, Qwen3_5TextConfig
     from visionstack_b200.stack import Qwen3_5TextModel, StackDecodeGraph
+    from visionstack_b200.stack_tp import shard_stack
     cfg = Qwen3_5TextConfig(**W.STACK_48)
     R = W.STACK_48_RUN
     B, P, D = R["batch"], R["prefill"], R["decode"]
@@ -800,12 +807,16 @@ def run_stack(torch, dev):
                     t.mul_(0.5)
                 p.data = t
     ids = torch.randint(0, cfg.vocab_size, (B, P + D), generator=g, device=dev)
+    if world > 1:
+        shard_stack(model, rank, world)
+        torch.cuda.empty_cache()
 
     def run(n_pre, n_dec):
         cache = Qwen3_5HybridCache()
         cache.kv_capacity = n_pre + n_dec
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
         torch.cuda.synchronize(dev)
+        barrier()
         ev[0].record()
         model(input_ids=ids[:, :n_pre], past_key_values=cache, use_cache=True)
         ev[1].record()
@@ -814,13 +825,17 @@ def run_stack(torch, dev):
         dg = StackDecodeGraph(model, cache, ids)
         dg.step()
         torch.cuda.synchronize(dev)
+        barrier()
         ev[2].record()
         for _ in range(n_dec - 1):
             dg.step()
         ev[3].record()
         torch.cuda.synchronize(dev)
         dg.finish()
-        return ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3]) / (n_dec - 1) * n_dec
+        del dg
+        t = _max_over_ranks(torch, dist, world, dev, ev[0].elapsed_time(ev[1]),
+                            ev[2].elapsed_time(ev[3]) / (n_dec - 1) * n_dec)
+        return t[0], t[1]
 
     with torch.inference_mode():
         run(256, 4)
@@ -829,32 +844,40 @@ def run_stack(torch, dev):
     peak_mem = torch.cuda.max_memory_allocated(dev)
     nl = sum(1 for t in cfg.layer_types if t == "linear_attention")
     na = cfg.num_hidden_layers - nl
+    # per rank: its weight shard (embedding excluded: one row per token is read), its DeltaNet
+    # heads' states, its KV heads' cache; FLOPs of the whole job over the GPUs (each does 1/N)
     params = sum(p.numel() for n, p in model.named_parameters() if not n.endswith("embed_tokens.weight"))
     wbytes = sum(p.numel() * p.element_size() for n, p in model.named_parameters()
                  if not n.endswith("embed_tokens.weight"))
-    hv, dk = cfg.linear_num_value_heads, cfg.linear_key_head_dim
-    conv_dim = 2 * cfg.linear_num_key_heads * dk + hv * cfg.linear_value_head_dim
+    hv, dk = cfg.linear_num_value_heads // world, cfg.linear_key_head_dim
+    conv_dim = (2 * cfg.linear_num_key_heads * dk + cfg.linear_num_value_heads * cfg.linear_value_head_dim) // world
     state_rw = nl * (2 * B * hv * dk * dk * 4 + 2 * B * conv_dim * 3 * 2)
-    kv_read = na * B * 2 * (P + D // 2) * cfg.num_key_value_heads * cfg.head_dim * 2
+    kv_heads = max(1, cfg.num_key_value_heads // world)
+    kv_read = na * B * 2 * (P + D // 2) * kv_heads * cfg.head_dim * 2
     dec_bytes = wbytes + state_rw + kv_read
     ms_dec = t_dec / D
     hbm, tflops, src = measured_peaks()
-    attn_fl = na * B * cfg.num_attention_heads * (P * P / 2) * cfg.head_dim * 4
-    pre_fl = 2.0 * params * B * P + attn_fl + nl * prefill_flops(B, P, hv, dk)
+    attn_fl = na * B * (cfg.num_attention_heads // world) * (P * P / 2) * cfg.head_dim * 4
+    pre_fl = 2.0 * params * B * P + attn_fl + nl * prefill_flops(B, P, hv, dk)  # per rank
     del model
     torch.cuda.empty_cache()
     return {"workload": f"48-layer hybrid stack (36 Gated DeltaNet + 12 gated attention, hidden 2048, MLP 12288, "
                         f"vocab 151936), random bf16 weights, B{B}: prefill {P} tokens then {D} decode steps",
+            "world": world,
+            "parallelism": "single GPU" if world == 1 else
+            f"tensor-parallel over {world} GPUs (DeltaNet value heads, attention query heads with their KV "
+            f"heads, MLP columns; NCCL all-reduce after every mixer and MLP), global batch fixed (strong)",
             "prefill_tokens_per_s": B * P / (t_pre * 1e-3), "prefill_ms": t_pre,
             "decode_steps_per_s": 1000.0 / ms_dec, "decode_tokens_per_s": B * 1000.0 / ms_dec,
             "decode_ms_per_step": ms_dec, "peak_memory_gb": peak_mem / 1e9,
             "prefill_roofline": {"bound": "tensor", "achieved": pre_fl / (t_pre * 1e-3) / 1e12, "peak": tflops,
                                  "unit": "TFLOP/s", "frac": pre_fl / (t_pre * 1e-3) / 1e12 / tflops,
-                                 "flops": pre_fl, "peak_source": src},
+                                 "flops_per_gpu": pre_fl, "peak_source": src},
             "decode_roofline": {"bound": "hbm", "achieved": dec_bytes / (ms_dec * 1e-3) / 1e9, "peak": hbm,
                                 "unit": "GB/s", "frac": dec_bytes / (ms_dec * 1e-3) / 1e9 / hbm,
-                                "bytes_per_step": dec_bytes, "peak_source": src},
-            "path": "visionstack_b200.stack.Qwen3_5TextModel (prefill eager, decode from one CUDA graph); "
+                                "bytes_per_step_per_gpu": dec_bytes, "peak_source": src},
+            "path": "visionstack_b200.stack.Qwen3_5TextModel (prefill eager, decode from one CUDA graph; with N "
+                    "GPUs cut by visionstack_b200.stack_tp.shard_stack); "
                     "DeltaNet layers on gdn_mixer_prefill_ws / gdn_mixer_decode, decode attention on "
                     "gdn_attn_decode, prefill attention on torch SDPA, GEMMs on cuBLAS"}
 

@@ -165,3 +165,103 @@ def test_two_gpu_sharded_mixer_matches_oracle():
     assert_state_close(states, r_S, "sharded mixer final state (2 GPUs)")
     ry = O.cast(np.matmul(core, full["out_proj.weight"].T.astype(np.float32)), "bf16")
     assert_bf16_close(y, ry, "all-reduced out_proj partials", scale=2.0)
+
+
+STACK_CFG = dict(vocab_size=256, hidden_size=512, intermediate_size=1024, num_hidden_layers=4, num_attention_heads=4,
+                 num_key_value_heads=2, head_dim=128, linear_num_key_heads=4, linear_num_value_heads=8,
+                 linear_key_head_dim=128, linear_value_head_dim=128, linear_conv_kernel_dim=4, rms_norm_eps=1e-6)
+
+
+def _stack_model(dev):
+    """4 layers (3 DeltaNet + 1 gated attention), seeded random bf16 weights, the same on every rank."""
+    from visionstack_b200 import Qwen3_5TextConfig
+    from visionstack_b200.stack import Qwen3_5TextModel
+    cfg = Qwen3_5TextConfig(**STACK_CFG)
+    with torch.device("meta"):
+        m = Qwen3_5TextModel(cfg)
+    m = m.to_empty(device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(17)
+    with torch.no_grad():
+        for name, p in m.named_parameters():
+            if name.endswith("A_log"):
+                p.data = torch.empty(p.shape, device=dev).uniform_(-1.0, 1.0, generator=g)
+            elif name.endswith("dt_bias"):
+                p.data = torch.zeros(p.shape, device=dev)
+            elif name.endswith("linear_attn.norm.weight"):
+                p.data = torch.ones(p.shape, device=dev, dtype=torch.bfloat16)
+            elif "norm" in name:
+                p.data = 0.1 * torch.randn(p.shape, generator=g, device=dev).to(torch.bfloat16)
+            else:
+                t = torch.randn(p.shape, generator=g, device=dev, dtype=torch.bfloat16)
+                if p.dim() == 2 and not name.endswith("embed_tokens.weight"):
+                    t.mul_(p.shape[1] ** -0.5)
+                elif name.endswith("conv1d.weight"):
+                    t.mul_(0.5)
+                p.data = t
+    return m
+
+
+def _stack_worker(rank, world, port, q):
+    """Every rank runs the unsharded stack and its tensor-parallel shard on the same inputs: a
+    prefill, then 3 decode steps from one captured CUDA graph (all-reduces inside)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from visionstack_b200 import Qwen3_5HybridCache
+        from visionstack_b200.stack import StackDecodeGraph
+        from visionstack_b200.stack_tp import shard_stack
+        dev = torch.device("cuda", rank)
+        g = torch.Generator(device=dev)
+        g.manual_seed(23)
+        ids = torch.randint(0, STACK_CFG["vocab_size"], (2, 100), generator=g, device=dev)
+
+        def run(m):
+            cache = Qwen3_5HybridCache()
+            cache.kv_capacity = 100
+            outs = [m(input_ids=ids[:, :96], past_key_values=cache, use_cache=True).last_hidden_state.clone()]
+            dg = StackDecodeGraph(m, cache, ids)
+            for _ in range(3):
+                outs.append(dg.step().clone())
+            torch.cuda.synchronize()
+            dg.finish()
+            return outs, cache
+
+        with torch.inference_mode():
+            ref, rc = run(_stack_model(dev))
+            dist.barrier()
+            shd, sc = run(shard_stack(_stack_model(dev), rank, world))
+        errs = [(float((a.float() - b.float()).abs().max()), float((a.float() - b.float()).abs().mean()),
+                 float(b.float().abs().max())) for a, b in zip(shd, ref)]
+        hv = STACK_CFG["linear_num_value_heads"] // world
+        s_ref = rc.recurrent_states[0][:, rank * hv:(rank + 1) * hv]
+        s_err = float((sc.recurrent_states[0] - s_ref).abs().max() / s_ref.abs().max())
+        q.put((rank, errs, s_err))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_tensor_parallel_stack_matches_unsharded():
+    """The 4-layer stack cut over 2 GPUs (DeltaNet value heads, attention query heads with their KV
+    head, MLP columns, NCCL all-reduce after every mixer and MLP) against the unsharded stack: the
+    prefill's and three graph-replayed decode steps' final hidden states, and the first DeltaNet
+    layer's recurrent state (the same inputs on both sides) as the head slice of the unsharded one.
+    bf16 GEMMs cut in N and sums of bf16 partials round differently, so the hidden states are held
+    to the stack tests' bf16 bounds (max 0.125, mean 0.01)."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_stack_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, errs, s_err in res:
+        for i, (mx, mean, scale) in enumerate(errs):
+            assert mx <= 0.125 and mean <= 0.01, f"rank {rank} step {i}: max {mx}, mean {mean} (|ref| {scale})"
+        assert s_err <= 1e-2, f"rank {rank}: first DeltaNet state differs from its head slice by {s_err}"
