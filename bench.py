@@ -807,8 +807,11 @@ def run_stack(torch, dist, dev, rank, world, barrier):
                     t.mul_(0.5)
                 p.data = t
     ids = torch.randint(0, cfg.vocab_size, (B, P + D), generator=g, device=dev)
+    peer = None
     if world > 1:
-        shard_stack(model, rank, world)
+        from visionstack_b200.peer import PeerAllReduce
+        peer = PeerAllReduce(max_elems=B * cfg.hidden_size, nblocks=32, device=dev)  # the decode steps' sums
+        shard_stack(model, rank, world, peer=peer)
         torch.cuda.empty_cache()
 
     def run(n_pre, n_dec):
@@ -860,13 +863,16 @@ def run_stack(torch, dist, dev, rank, world, barrier):
     attn_fl = na * B * (cfg.num_attention_heads // world) * (P * P / 2) * cfg.head_dim * 4
     pre_fl = 2.0 * params * B * P + attn_fl + nl * prefill_flops(B, P, hv, dk)  # per rank
     del model
+    if peer is not None:
+        peer.close()
     torch.cuda.empty_cache()
     return {"workload": f"48-layer hybrid stack (36 Gated DeltaNet + 12 gated attention, hidden 2048, MLP 12288, "
                         f"vocab 151936), random bf16 weights, B{B}: prefill {P} tokens then {D} decode steps",
             "world": world,
             "parallelism": "single GPU" if world == 1 else
             f"tensor-parallel over {world} GPUs (DeltaNet value heads, attention query heads with their KV "
-            f"heads, MLP columns; NCCL all-reduce after every mixer and MLP), global batch fixed (strong)",
+            f"heads, MLP columns; an all-reduce after every mixer and MLP: the one-shot NVLink peer kernel "
+            f"for the decode steps, NCCL for the prefill), global batch fixed (strong)",
             "prefill_tokens_per_s": B * P / (t_pre * 1e-3), "prefill_ms": t_pre,
             "decode_steps_per_s": 1000.0 / ms_dec, "decode_tokens_per_s": B * 1000.0 / ms_dec,
             "decode_ms_per_step": ms_dec, "peak_memory_gb": peak_mem / 1e9,
@@ -910,12 +916,14 @@ def _max_over_ranks(torch, dist, world, dev, *vals):
     return [float(v) for v in t.tolist()]
 
 
-def sharded_decode(torch, dist, m, local, dev, world, barrier, Bg: int, steps: int = 256, graph_steps: int = 32):
+def sharded_decode(torch, dist, m, local, dev, world, barrier, Bg: int, steps: int = 256, graph_steps: int = 32,
+                   peer=None):
     """One decode step of the value-head-sharded layer at global batch Bg: this rank's fused input
     projection, the token mixer on its heads (state in place), its out_proj column slice, and the
-    all-reduce (NCCL, bf16 sum) of the [Bg, 1, hidden] partial outputs.  Steps replay from CUDA
-    graphs of ``graph_steps`` steps; state slots rotate so the states never sit in L2."""
-    import torch.nn.functional as F
+    all-reduce (bf16 sum) of the [Bg, 1, hidden] partial outputs: NCCL, or with ``peer`` the
+    one-shot NVLink kernel (gdn_peer_allreduce_bf16).  Steps replay from CUDA graphs of
+    ``graph_steps`` steps; state slots rotate so the states never sit in L2."""
+    from visionstack_b200.peer import sum_partials
     hv, d, H = local.num_v_heads, local.head_k_dim, W.SHAPE_QWEN.hidden_size
     state_bytes = Bg * hv * d * d * 4
     nslot = max(2, -(-300_000_000 // state_bytes))
@@ -940,7 +948,7 @@ def sharded_decode(torch, dist, m, local, dev, world, barrier, Bg: int, steps: i
              states[slot], core)
         torch.matmul(core, w_out.t(), out=y)
         if reduce and world > 1:
-            dist.all_reduce(y, op=dist.ReduceOp.SUM)
+            sum_partials(y, peer)
 
     stream = torch.cuda.Stream(device=dev)
     with torch.no_grad(), torch.cuda.stream(stream):
@@ -978,8 +986,18 @@ def sharded_decode(torch, dist, m, local, dev, world, barrier, Bg: int, steps: i
         barrier()
         ms_local = _ev_time(torch, lambda: run(False), reps) / graph_steps
         barrier()
-        # the all-reduce of one step's partial outputs, alone
-        ms_ar = _ev_time(torch, lambda: dist.all_reduce(y, op=dist.ReduceOp.SUM), 64) if world > 1 else 0.0
+        # the all-reduce of one step's partial outputs, alone: 32 calls replayed from one CUDA graph
+        # (as inside the step; an eager loop would time the host's launch path)
+        ms_ar = 0.0
+        if world > 1:
+            gar = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gar, stream=stream):
+                for _ in range(32):
+                    sum_partials(y, peer)
+            gar.replay()
+            barrier()
+            ms_ar = _ev_time(torch, gar.replay, 8) / 32
+            del gar
         barrier()
     graphs.clear()
     ms_full, ms_local, ms_ar = _max_over_ranks(torch, dist, world, dev, ms_full, ms_local, ms_ar)
@@ -993,6 +1011,8 @@ def sharded_decode(torch, dist, m, local, dev, world, barrier, Bg: int, steps: i
             "roofline": {"bound": "hbm", "bytes_per_gpu_per_step": hbm_bytes,
                          "achieved": hbm_bytes / (ms_full * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
                          "frac": hbm_bytes / (ms_full * 1e-3) / 1e9 / hbm, "peak_source": src},
+            "allreduce": "one-shot over NVLink peer memory (gdn_peer_allreduce_bf16)" if peer is not None and
+            world > 1 else ("NCCL" if world > 1 else None),
             "timing": mode}
 
 
@@ -1104,11 +1124,17 @@ def run_sharded_layer(torch, dist, m, local, rank, world, dev, barrier):
     layer."""
     res = {"world": world,
            "layer": "head-sharded Gated DeltaNet layer: fused input projection of this rank's rows (cuBLAS), "
-                    "token mixer on its 32/N value heads, out_proj column slice (cuBLAS), NCCL all-reduce "
-                    "(bf16 sum) of the partial outputs"}
+                    "token mixer on its 32/N value heads, out_proj column slice (cuBLAS), all-reduce (bf16 sum) "
+                    "of the partial outputs: NCCL, and for decode also the one-shot NVLink peer kernel "
+                    "(*_peer)"}
     res["decode_strong"] = sharded_decode(torch, dist, m, local, dev, world, barrier, 64)
     if world > 1:
+        from visionstack_b200.peer import PeerAllReduce
+        peer = PeerAllReduce(max_elems=64 * world * W.SHAPE_QWEN.hidden_size, nblocks=32, device=dev)
+        res["decode_strong_peer"] = sharded_decode(torch, dist, m, local, dev, world, barrier, 64, peer=peer)
         res["decode_weak"] = sharded_decode(torch, dist, m, local, dev, world, barrier, 64 * world)
+        res["decode_weak_peer"] = sharded_decode(torch, dist, m, local, dev, world, barrier, 64 * world, peer=peer)
+        peer.close()
     res["prefill_strong"] = sharded_prefill(torch, dist, m, local, dev, world, barrier, 8, 8192)
     if world > 1:
         res["prefill_weak"] = sharded_prefill(torch, dist, m, local, dev, world, barrier, 8 * world, 8192)

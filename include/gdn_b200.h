@@ -66,6 +66,7 @@ extern "C" {
 #define GDN_DEVERR_MMA_TIMEOUT 0x2u
 #define GDN_DEVERR_BAD_SLOT 0x4u   /* slot-table entry or accepted count out of range */
 #define GDN_DEVERR_HANDOFF_TIMEOUT 0x8u  /* chunked prefill: a chain's state hand-off never arrived */
+#define GDN_DEVERR_PEER_TIMEOUT 0x10u    /* peer all-reduce: another rank's flag never arrived */
 
 /* Size of the library's fixed device scratch used by gdn_mixer_prefill_noalloc
  * (64 MiB per device: the two-kernel prefill's workspace for about 1.9k
@@ -376,6 +377,49 @@ int32_t gdn_solve_unit_lower_triangular(const float* ut, const float* rhs, float
 int32_t gdn_rms_norm_gated(const void* x, const void* gate, const void* weight, void* out, int64_t rows,
                            int32_t dim, float eps, int32_t x_dtype, int32_t gate_dtype,
                            int32_t weight_dtype, void* stream);
+
+/*
+ * One-shot all-reduce (sum) of a small bf16 tensor across the GPUs of one node
+ * over NVLink peer memory, for the exchange step of the value-head-sharded
+ * layers: the sum of the row-parallel out_proj partials after the token
+ * mixer (and, in the sharded stack, of o_proj and down_proj), a few hundred
+ * KB per decode step, where a ring all-reduce is bound by its latency.  No
+ * counterpart in the reference (its engine runs on one GPU); it replaces the
+ * NCCL all-reduce of that step for messages up to the staging capacity.
+ *
+ * Set-up, once per group (every rank, same arguments):
+ *   1. gdn_peer_staging_bytes(world, nblocks, cap) bytes from
+ *      gdn_peer_staging_alloc (cudaMalloc on the current device, zeroed;
+ *      synchronous): two slots of every rank's partial (cap elements each),
+ *      the flags and epochs;
+ *   2. gdn_ipc_get_handle on it, the GDN_IPC_HANDLE_BYTES handles exchanged
+ *      between the ranks (any host channel), gdn_ipc_open_handle on every
+ *      other rank's handle: gdn_peer_group.staging[r] = rank r's allocation
+ *      as mapped into this process (staging[rank] = the own pointer).
+ * gdn_peer_allreduce_bf16 then sums `in` (n elements, n a multiple of 8,
+ * n <= cap, 16-byte aligned; `out` may equal `in`) over the ranks into `out`,
+ * on `stream`.  Every rank calls it the same number of times in the same
+ * order (it can be captured in a CUDA graph: the call's epoch lives on the
+ * device).  Every rank gets the same bits (fp32 sum in rank order, rounded to
+ * bf16).  A rank that never arrives makes the others give up after 1 s with
+ * GDN_DEVERR_PEER_TIMEOUT (gdn_device_error); the group must then be rebuilt.
+ * Tear-down: gdn_ipc_close_handle on the opened mappings (after a barrier),
+ * gdn_peer_staging_free on the own allocation.
+ */
+#define GDN_IPC_HANDLE_BYTES 64
+#define GDN_PEER_MAX_RANKS 8
+typedef struct gdn_peer_group {
+    int32_t rank, world, nblocks; /* nblocks: thread blocks per call, 1..1024, the same on every rank */
+    int64_t cap;                  /* elements per staging slot */
+    void* staging[GDN_PEER_MAX_RANKS];
+} gdn_peer_group;
+int64_t gdn_peer_staging_bytes(int32_t world, int32_t nblocks, int64_t cap);
+int32_t gdn_peer_staging_alloc(int64_t bytes, void** ptr_out);
+int32_t gdn_peer_staging_free(void* ptr);
+int32_t gdn_ipc_get_handle(const void* dev_ptr, void* handle_out);
+int32_t gdn_ipc_open_handle(const void* handle, void** dev_ptr_out);
+int32_t gdn_ipc_close_handle(void* dev_ptr);
+int32_t gdn_peer_allreduce_bf16(const gdn_peer_group* group, const void* in, void* out, int64_t n, void* stream);
 
 #ifdef __cplusplus
 }

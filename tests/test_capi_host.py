@@ -194,3 +194,33 @@ def test_attn_decode_validation():
     assert lib.gdn_attn_decode(p + 2, p, p, p, p, 2, 2, 8, 256, 64, 0.0625, p, n, None) < 0
     assert lib.gdn_attn_decode(p, p, p, p, p, 2, 2, 8, 256, 64, 0.0625, p, n - 16, None) == -1
     assert lib.gdn_last_error_string()
+
+
+def test_peer_allreduce_validation():
+    """The peer all-reduce's size rules and argument checks, on the host (nothing launches)."""
+    import ctypes
+    lib = _lib.load()
+    assert lib.gdn_peer_staging_bytes(2, 32, 1 << 20) >= 4 * (1 << 20)
+    assert lib.gdn_peer_staging_bytes(9, 32, 1024) == -1   # more ranks than GDN_PEER_MAX_RANKS
+    assert lib.gdn_peer_staging_bytes(2, 0, 1024) == -1    # no blocks
+    assert lib.gdn_peer_staging_bytes(2, 32, 1001) == -1   # capacity not a multiple of 8
+    ptr = ctypes.c_void_p()
+    assert lib.gdn_peer_staging_alloc(0, ctypes.byref(ptr)) == -1
+    assert lib.gdn_ipc_get_handle(None, ctypes.create_string_buffer(64)) == -1
+    assert lib.gdn_ipc_open_handle(None, ctypes.byref(ptr)) == -1
+    g = _lib.PeerGroup()
+    g.rank, g.world, g.nblocks, g.cap = 0, 2, 32, 1024
+    g.staging[0], g.staging[1] = 0x100000, 0x200000
+    p = 0x300000
+    call = lambda x, y, n: lib.gdn_peer_allreduce_bf16(ctypes.byref(g), x, y, n, None)  # noqa: E731
+    assert lib.gdn_peer_allreduce_bf16(None, p, p, 8, None) == -1
+    assert call(p, p, 12) == -1          # not a multiple of 8
+    assert call(p, p, 2048) == -1        # above the capacity
+    assert call(p + 2, p, 8) == -3       # misaligned
+    assert call(p, p, 0) == 0            # nothing to sum
+    g.rank = 2
+    assert call(p, p, 8) == -1           # rank outside the group
+    g.rank = 0
+    g.staging[1] = None
+    assert call(p, p, 8) == -1           # a rank's staging memory is missing
+    assert b"staging" in lib.gdn_last_error_string()

@@ -228,12 +228,20 @@ def _stack_worker(rank, world, port, q):
             dg.finish()
             return outs, cache
 
+        from visionstack_b200.peer import PeerAllReduce
+        peer = PeerAllReduce(max_elems=2 * STACK_CFG["hidden_size"], nblocks=8, device=dev)
         with torch.inference_mode():
             ref, rc = run(_stack_model(dev))
             dist.barrier()
             shd, sc = run(shard_stack(_stack_model(dev), rank, world))
+            dist.barrier()
+            shp, _ = run(shard_stack(_stack_model(dev), rank, world, peer=peer))
+        peer.close()
         errs = [(float((a.float() - b.float()).abs().max()), float((a.float() - b.float()).abs().mean()),
                  float(b.float().abs().max())) for a, b in zip(shd, ref)]
+        # decode steps through the peer kernel against the NCCL-sharded stack (both round the sum of the
+        # bf16 partials once to bf16; the graph-replayed steps may still order the work differently)
+        errs += [(float((a.float() - b.float()).abs().max()), 0.0, 0.0) for a, b in zip(shp[1:], shd[1:])]
         hv = STACK_CFG["linear_num_value_heads"] // world
         s_ref = rc.recurrent_states[0][:, rank * hv:(rank + 1) * hv]
         s_err = float((sc.recurrent_states[0] - s_ref).abs().max() / s_ref.abs().max())
@@ -245,7 +253,8 @@ def _stack_worker(rank, world, port, q):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_two_gpu_tensor_parallel_stack_matches_unsharded():
     """The 4-layer stack cut over 2 GPUs (DeltaNet value heads, attention query heads with their KV
-    head, MLP columns, NCCL all-reduce after every mixer and MLP) against the unsharded stack: the
+    head, MLP columns, NCCL all-reduce after every mixer and MLP; again with the decode steps' sums
+    on the one-shot peer all-reduce) against the unsharded stack: the
     prefill's and three graph-replayed decode steps' final hidden states, and the first DeltaNet
     layer's recurrent state (the same inputs on both sides) as the head slice of the unsharded one.
     bf16 GEMMs cut in N and sums of bf16 partials round differently, so the hidden states are held
@@ -262,6 +271,90 @@ def test_two_gpu_tensor_parallel_stack_matches_unsharded():
         p.join(timeout=120)
         assert p.exitcode == 0
     for rank, errs, s_err in res:
-        for i, (mx, mean, scale) in enumerate(errs):
+        for i, (mx, mean, scale) in enumerate(errs[:4]):
             assert mx <= 0.125 and mean <= 0.01, f"rank {rank} step {i}: max {mx}, mean {mean} (|ref| {scale})"
+        for i, (mx, _, _) in enumerate(errs[4:]):
+            assert mx <= 0.125, f"rank {rank} decode step {i}: peer all-reduce vs NCCL differ by {mx}"
         assert s_err <= 1e-2, f"rank {rank}: first DeltaNet state differs from its head slice by {s_err}"
+
+
+def _peer_worker(rank, world, port, q):
+    """Every rank sums seeded partials with the one-shot peer all-reduce: out of place, in place,
+    several sizes, and replayed from a CUDA graph; each result must equal, bit for bit, the fp32
+    sum in rank order rounded to bf16 (computed here from every rank's seeded partial)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from visionstack_b200 import _lib
+        from visionstack_b200.peer import PeerAllReduce
+        dev = torch.device("cuda", rank)
+        peer = PeerAllReduce(max_elems=1 << 17, nblocks=8, device=dev)
+
+        def parts(n, salt):
+            return [torch.randn(n, generator=torch.Generator().manual_seed(1000 * salt + 17 * r + n))
+                    .to(torch.bfloat16) for r in range(world)]
+
+        def expect(ps):
+            acc = torch.zeros(ps[0].shape, dtype=torch.float32)
+            for p in ps:
+                acc += p.float()
+            return acc.to(torch.bfloat16)
+
+        bad = []
+        for salt, n in enumerate((8, 8000, 65536, 1 << 17)):
+            ps = parts(n, salt)
+            x = ps[rank].to(dev)
+            out = torch.empty_like(x)
+            peer(x, out)
+            y = x.clone()
+            peer(y)
+            torch.cuda.synchronize()
+            e = expect(ps)
+            if not (torch.equal(out.cpu(), e) and torch.equal(y.cpu(), e)):
+                bad.append(f"n={n}")
+        # three calls captured in one graph, replayed twice with fresh inputs
+        bufs = [torch.empty(4096, dtype=torch.bfloat16, device=dev) for _ in range(3)]
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for b in bufs:
+                peer(b)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for b in bufs:
+                peer(b)
+        for rep in range(2):
+            pss = [parts(4096, 10 + 3 * rep + i) for i in range(3)]
+            for b, ps in zip(bufs, pss):
+                b.copy_(ps[rank].to(dev))
+            graph.replay()
+            torch.cuda.synchronize()
+            for i, (b, ps) in enumerate(zip(bufs, pss)):
+                if not torch.equal(b.cpu(), expect(ps)):
+                    bad.append(f"graph replay {rep} call {i}")
+        del graph
+        err = _lib.device_error()
+        peer.close()
+        q.put((rank, bad, err))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_peer_allreduce_is_exact():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, bad, err in res:
+        assert not bad and err == 0, f"rank {rank}: {bad}, device error {err:#x}"

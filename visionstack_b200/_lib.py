@@ -41,6 +41,13 @@ EXPORTED_SYMBOLS = (
     "gdn_attn_decode",
     "gdn_solve_unit_lower_triangular",
     "gdn_rms_norm_gated",
+    "gdn_peer_staging_bytes",
+    "gdn_peer_staging_alloc",
+    "gdn_peer_staging_free",
+    "gdn_ipc_get_handle",
+    "gdn_ipc_open_handle",
+    "gdn_ipc_close_handle",
+    "gdn_peer_allreduce_bf16",
 )
 GDN_FLAG_REGISTER_KERNEL = 1
 GDN_FLAG_CUDA_CORE_PREFILL = 2
@@ -48,6 +55,9 @@ GDN_FLAG_PREP_IN_KERNEL_PREFILL = 4
 GDN_DEVERR_TMA_TIMEOUT = 0x1
 GDN_DEVERR_BAD_SLOT = 0x4
 GDN_DEVERR_HANDOFF_TIMEOUT = 0x8
+GDN_DEVERR_PEER_TIMEOUT = 0x10
+GDN_IPC_HANDLE_BYTES = 64
+GDN_PEER_MAX_RANKS = 8
 GDN_STATIC_SCRATCH_BYTES = 64 << 20
 
 _c_void_p = ctypes.c_void_p
@@ -72,6 +82,12 @@ class MixerArgs(ctypes.Structure):
         ("checkpoint_offsets", ctypes.POINTER(_i32)),
         ("state_checkpoints", _c_void_p), ("conv_checkpoints", _c_void_p),
     ]
+
+
+class PeerGroup(ctypes.Structure):
+    """Mirror of ``gdn_peer_group`` (include/gdn_b200.h)."""
+    _fields_ = [("rank", _i32), ("world", _i32), ("nblocks", _i32), ("cap", _i64),
+                ("staging", _c_void_p * GDN_PEER_MAX_RANKS)]
 
 
 class GDNError(RuntimeError):
@@ -142,6 +158,20 @@ def load() -> ctypes.CDLL:
         lib.gdn_rms_norm_gated.restype = _i32
         lib.gdn_rms_norm_gated.argtypes = [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i32, ctypes.c_float,
                                            _i32, _i32, _i32, _c_void_p]
+        lib.gdn_peer_staging_bytes.restype = _i64
+        lib.gdn_peer_staging_bytes.argtypes = [_i32, _i32, _i64]
+        lib.gdn_peer_staging_alloc.restype = _i32
+        lib.gdn_peer_staging_alloc.argtypes = [_i64, ctypes.POINTER(_c_void_p)]
+        lib.gdn_peer_staging_free.restype = _i32
+        lib.gdn_peer_staging_free.argtypes = [_c_void_p]
+        lib.gdn_ipc_get_handle.restype = _i32
+        lib.gdn_ipc_get_handle.argtypes = [_c_void_p, _c_void_p]
+        lib.gdn_ipc_open_handle.restype = _i32
+        lib.gdn_ipc_open_handle.argtypes = [_c_void_p, ctypes.POINTER(_c_void_p)]
+        lib.gdn_ipc_close_handle.restype = _i32
+        lib.gdn_ipc_close_handle.argtypes = [_c_void_p]
+        lib.gdn_peer_allreduce_bf16.restype = _i32
+        lib.gdn_peer_allreduce_bf16.argtypes = [ctypes.POINTER(PeerGroup), _c_void_p, _c_void_p, _i64, _c_void_p]
         lib.gdn_device_error.restype = _i32
         lib.gdn_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32), _i32]
         _lib = lib

@@ -233,7 +233,8 @@ int32_t gdn_device_error(uint32_t* flags_out, int32_t clear) {
                                   gdn::prefill_tc_device_error(clear != 0), gdn::slots_device_error(clear != 0),
                                   gdn::prefill_prep_device_error(clear != 0),
                                   gdn::prefill_seq_device_error(clear != 0),
-                                  gdn::prefill_fused_device_error(clear != 0)};
+                                  gdn::prefill_fused_device_error(clear != 0),
+                                  gdn::peer_allreduce_device_error(clear != 0)};
     uint32_t all = 0;
     for (unsigned int w : words) {
         if (w == 0xFFFFFFFFu) return fail(GDN_ERR_CUDA, "could not read the device error word");
@@ -549,3 +550,107 @@ int32_t gdn_mixer_prefill_noalloc(const gdn_mixer_args* args, void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// peer all-reduce: staging memory, IPC mappings, the call
+// ---------------------------------------------------------------------------
+namespace {
+size_t up256(size_t x) { return (x + 255) & ~(size_t)255; }
+// byte offsets of the flags and the epochs inside a staging allocation
+void peer_layout(int world, int nblocks, int64_t cap, size_t* flags_off, size_t* counters_off, size_t* total) {
+    *flags_off = up256((size_t)cap * world * 2 * 2);
+    *counters_off = *flags_off + up256((size_t)world * nblocks * 4);
+    *total = *counters_off + up256((size_t)nblocks * 4);
+}
+bool peer_shape_ok(int world, int nblocks, int64_t cap) {
+    return world >= 1 && world <= GDN_PEER_MAX_RANKS && nblocks >= 1 && nblocks <= 1024 && cap >= 8 && cap % 8 == 0 &&
+           cap <= (1ll << 34);
+}
+}  // namespace
+
+int64_t gdn_peer_staging_bytes(int32_t world, int32_t nblocks, int64_t cap) {
+    if (!peer_shape_ok(world, nblocks, cap))
+        return fail(GDN_ERR_INVALID_ARG, "world 1..%d, nblocks 1..1024, cap a positive multiple of 8",
+                    GDN_PEER_MAX_RANKS);
+    size_t f, c, t;
+    peer_layout(world, nblocks, cap, &f, &c, &t);
+    ok();
+    return (int64_t)t;
+}
+
+int32_t gdn_peer_staging_alloc(int64_t bytes, void** ptr_out) {
+    if (!ptr_out || bytes <= 0) return fail(GDN_ERR_INVALID_ARG, "bytes must be positive and ptr_out non-NULL");
+    *ptr_out = nullptr;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+    if (e != cudaSuccess) return cuda_status(e, "gdn_peer_staging_alloc cudaMalloc");
+    e = cudaMemset(p, 0, (size_t)bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_status(e, "gdn_peer_staging_alloc cudaMemset");
+    }
+    *ptr_out = p;
+    return ok();
+}
+
+int32_t gdn_peer_staging_free(void* ptr) {
+    if (!ptr) return ok();
+    return cuda_status(cudaFree(ptr), "gdn_peer_staging_free");
+}
+
+int32_t gdn_ipc_get_handle(const void* dev_ptr, void* handle_out) {
+    static_assert(sizeof(cudaIpcMemHandle_t) == GDN_IPC_HANDLE_BYTES, "IPC handle size");
+    if (!dev_ptr || !handle_out) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr));
+    if (e != cudaSuccess) return cuda_status(e, "gdn_ipc_get_handle");
+    memcpy(handle_out, &h, sizeof(h));
+    return ok();
+}
+
+int32_t gdn_ipc_open_handle(const void* handle, void** dev_ptr_out) {
+    if (!handle || !dev_ptr_out) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
+    *dev_ptr_out = nullptr;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    return cuda_status(cudaIpcOpenMemHandle(dev_ptr_out, h, cudaIpcMemLazyEnablePeerAccess), "gdn_ipc_open_handle");
+}
+
+int32_t gdn_ipc_close_handle(void* dev_ptr) {
+    if (!dev_ptr) return ok();
+    return cuda_status(cudaIpcCloseMemHandle(dev_ptr), "gdn_ipc_close_handle");
+}
+
+int32_t gdn_peer_allreduce_bf16(const gdn_peer_group* g, const void* in, void* out, int64_t n, void* stream) {
+    if (!g || !in || !out) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
+    if (!peer_shape_ok(g->world, g->nblocks, g->cap) || g->rank < 0 || g->rank >= g->world)
+        return fail(GDN_ERR_INVALID_ARG, "bad group: rank %d of %d, nblocks %d, cap %lld", g->rank, g->world,
+                    g->nblocks, (long long)g->cap);
+    if (n < 0 || n % 8 != 0 || n > g->cap)
+        return fail(GDN_ERR_INVALID_ARG, "n = %lld must be a multiple of 8 and at most cap = %lld", (long long)n,
+                    (long long)g->cap);
+    if (!aligned16(in) || !aligned16(out)) return fail(GDN_ERR_ALIGNMENT, "in / out must be 16-byte aligned");
+    for (int r = 0; r < g->world; ++r)
+        if (!g->staging[r] || !aligned16(g->staging[r]))
+            return fail(GDN_ERR_INVALID_ARG, "staging[%d] is NULL or misaligned", r);
+    if (n == 0) return ok();
+    size_t f, c, t;
+    peer_layout(g->world, g->nblocks, g->cap, &f, &c, &t);
+    gdn::PeerAllReduceArgs a;
+    memset(&a, 0, sizeof(a));
+    a.in = in;
+    a.out = out;
+    a.n = n;
+    a.cap = g->cap;
+    a.rank = g->rank;
+    a.world = g->world;
+    a.nblocks = g->nblocks;
+    for (int r = 0; r < g->world; ++r) {
+        unsigned char* base = static_cast<unsigned char*>(g->staging[r]);
+        a.data[r] = reinterpret_cast<uint16_t*>(base);
+        a.flags[r] = reinterpret_cast<int*>(base + f);
+    }
+    a.counters = reinterpret_cast<int*>(static_cast<unsigned char*>(g->staging[g->rank]) + c);
+    return cuda_status(gdn::launch_peer_allreduce(a, static_cast<cudaStream_t>(stream)), "gdn_peer_allreduce_bf16");
+}

@@ -98,6 +98,20 @@ cudaError_t launch_prefill_fused(const MixParams& p, const CkptList& ck, float* 
 unsigned int prefill_fused_device_error(bool clear);
 // address of the fixed prefill scratch on the current device (looked up once per device)
 cudaError_t static_prefill_scratch(void** addr);
+// one-shot all-reduce over NVLink peer memory (gdn_peer_allreduce.cu)
+constexpr int PEER_MAX_RANKS = 8;
+struct PeerAllReduceArgs {
+    const void* in;  // local partial, bf16 [n]
+    void* out;       // sum, bf16 [n] (may be `in`)
+    long long n;     // elements, a multiple of 8
+    long long cap;   // elements per staging slot
+    int rank, world, nblocks;
+    uint16_t* data[PEER_MAX_RANKS];  // every rank's staging slots [2][world][cap] (peer-mapped)
+    int* flags[PEER_MAX_RANKS];      // every rank's flags [world][nblocks] (peer-mapped)
+    int* counters;                   // this rank's epochs [nblocks]
+};
+cudaError_t launch_peer_allreduce(const PeerAllReduceArgs& a, cudaStream_t s);
+unsigned int peer_allreduce_device_error(bool clear);
 cudaError_t launch_prefill(const MixParams& p, const CkptList& ck, int d, int dtype, bool mixer,
                            cudaStream_t s, bool* supported);
 cudaError_t launch_conv1d(int B, int C, int T, int K, int dtype, const void* x, const void* w,

@@ -72,12 +72,13 @@ class HeadShardedGatedDeltaNet:
 
     ``forward`` runs the rank's projections, the fused token mixer on its
     heads, its slice of ``out_proj``, and one all-reduce (sum) of the partial
-    outputs over ``group`` (NCCL on GPUs).  The cache passed in holds this
+    outputs over ``group`` (NCCL on GPUs, or the one-shot peer all-reduce of
+    ``peer`` where the output fits it).  The cache passed in holds this
     rank's shard of the states.
     """
 
     def __init__(self, full_state_dict, shape: LayerShape, layer_idx: int, rank: int, world: int,
-                 group=None, device=None, dtype=None):
+                 group=None, device=None, dtype=None, peer=None):
         import torch
 
         from .config import Qwen3_5TextConfig
@@ -100,10 +101,13 @@ class HeadShardedGatedDeltaNet:
         self.local_shape = local
         self.group = group
         self.world = world
+        self.peer = peer  # optional peer.PeerAllReduce: the one-shot NVLink sum for decode-sized outputs
 
     def __call__(self, hidden_states, attention_mask=None, cache=None, async_op: bool = False):
         import torch.distributed as dist
         partial = self.layer(hidden_states, attention_mask=attention_mask, cache=cache)
+        if self.world > 1 and not async_op and self.peer is not None and self.peer.fits(partial):
+            return self.peer(partial)
         if self.world > 1:
             work = dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group, async_op=async_op)
             if async_op:

@@ -15,10 +15,11 @@ one all-reduce per sub-block (two per layer):
   column slice; summed.
 * Embedding, RMSNorms and the rotary embedding: replicated.
 
-Each sum is an all-reduce (NCCL on GPUs) of the sub-block's [B, T, hidden] output in place, run
-by a forward hook, so every shard keeps the reference's parameter names (with local shapes) and
-the decoder layer, the cache and ``StackDecodeGraph`` work unchanged (a captured decode step
-holds the all-reduces).  Caches hold each rank's own states: its DeltaNet heads and its KV heads.
+Each sum is an all-reduce of the sub-block's [B, T, hidden] output in place, run by a forward
+hook (with a ``peer.PeerAllReduce`` the decode-sized ones take its one-shot NVLink kernel, the
+rest the process group's all-reduce, NCCL on GPUs), so every shard keeps the reference's
+parameter names (with local shapes) and the decoder layer, the cache and ``StackDecodeGraph``
+work unchanged (a captured decode step holds the all-reduces).  Caches hold each rank's own states: its DeltaNet heads and its KV heads.
 The reference has no tensor parallelism; this is the multi-GPU form of its stack.
 """
 from __future__ import annotations
@@ -53,10 +54,11 @@ def attention_head_ranges(num_heads: int, num_kv_heads: int, rank: int, world: i
     return h0, h1, kv0, kv1
 
 
-def _sum_hook(group, world):
+def _sum_hook(group, peer):
+    from .peer import sum_partials
+
     def hook(module, args, output):
-        dist.all_reduce(output, op=dist.ReduceOp.SUM, group=group)
-        return output
+        return sum_partials(output, peer, group)
     return hook
 
 
@@ -116,14 +118,16 @@ def _shard_mlp(old: nn.Module, cfg, rank: int, world: int) -> nn.Module:
     return new
 
 
-def shard_stack(model: nn.Module, rank: int, world: int, group: Optional[object] = None) -> nn.Module:
+def shard_stack(model: nn.Module, rank: int, world: int, group: Optional[object] = None,
+                peer: Optional[object] = None) -> nn.Module:
     """Cut a loaded ``Qwen3_5TextModel`` down to ``rank``'s shard of a ``world``-way tensor-parallel
-    group, in place, and attach the all-reduces; returns the model.  Every rank passes the same
-    full weights.  With ``world`` = 1 the model is returned unchanged."""
+    group, in place, and attach the all-reduces (``peer``: an optional ``PeerAllReduce`` of the
+    group for the outputs that fit it); returns the model.  Every rank passes the same full
+    weights.  With ``world`` = 1 the model is returned unchanged."""
     if world == 1:
         return model
     cfg = model.config
-    hook = _sum_hook(group, world)
+    hook = _sum_hook(group, peer)
     for idx, layer in enumerate(model.layers):
         if layer.block_type == "linear_attention":
             layer.linear_attn = _shard_deltanet(layer.linear_attn, cfg, idx, rank, world)
