@@ -421,6 +421,28 @@ int32_t gdn_ipc_open_handle(const void* handle, void** dev_ptr_out);
 int32_t gdn_ipc_close_handle(void* dev_ptr);
 int32_t gdn_peer_allreduce_bf16(const gdn_peer_group* group, const void* in, void* out, int64_t n, void* stream);
 
+/*
+ * Fused elementwise steps of the hybrid stack's layers (bf16 only), each one
+ * launch in place of PyTorch's chain of dtype copies and elementwise kernels:
+ *
+ * gdn_rms_norm_zc: the zero-centred RMSNorm of Qwen3_5RMSNorm
+ * (config.py:118-127), out = bf16(x * rsqrt(mean(x^2) + eps) * (1 + weight))
+ * in fp32 per row of `dim` elements; with `delta` (and `res_out`) the residual
+ * add of the decoder layer (text.py:233-276) comes first: res_out =
+ * bf16(x + delta), normalised in its place.  x rows `x_row_stride` elements
+ * apart (>= dim, a multiple of 8: strided rows such as the per-head q / k norms
+ * are allowed), delta likewise; res_out and out contiguous [rows, dim];
+ * pointers 16-byte aligned; dim a multiple of 8.  Outputs may alias inputs.
+ *
+ * gdn_silu_mul: the gated MLP's act(gate) * up (text.py:215-230) for SiLU,
+ * with torch's roundings: out = bf16(bf16(silu(gate)) * up), n elements, a
+ * multiple of 8, 16-byte aligned.
+ */
+int32_t gdn_rms_norm_zc(const void* x, int64_t x_row_stride, const void* delta, int64_t delta_row_stride,
+                        void* res_out, const void* weight, void* out, int64_t rows, int32_t dim, float eps,
+                        void* stream);
+int32_t gdn_silu_mul(const void* gate, const void* up, void* out, int64_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

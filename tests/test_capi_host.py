@@ -224,3 +224,17 @@ def test_peer_allreduce_validation():
     g.staging[1] = None
     assert call(p, p, 8) == -1           # a rank's staging memory is missing
     assert b"staging" in lib.gdn_last_error_string()
+
+
+def test_stack_ops_validation():
+    lib = _lib.load()
+    p = 0x100000
+    assert lib.gdn_rms_norm_zc(None, 2048, None, 0, None, p, p, 4, 2048, 1e-6, None) == -1
+    assert lib.gdn_rms_norm_zc(p, 2048, p, 2048, None, p, p, 4, 2048, 1e-6, None) == -1   # delta without res_out
+    assert lib.gdn_rms_norm_zc(p, 2048, None, 0, None, p, p, 4, 2044, 1e-6, None) == -1   # dim not a multiple of 8
+    assert lib.gdn_rms_norm_zc(p, 1024, None, 0, None, p, p, 4, 2048, 1e-6, None) == -1   # stride below dim
+    assert lib.gdn_rms_norm_zc(p + 2, 2048, None, 0, None, p, p, 4, 2048, 1e-6, None) == -3
+    assert lib.gdn_rms_norm_zc(p, 2048, None, 0, None, p, p, 0, 2048, 1e-6, None) == 0    # no rows
+    assert lib.gdn_silu_mul(p, p, p, 12, None) == -1
+    assert lib.gdn_silu_mul(p, p + 8, p, 16, None) == -3
+    assert lib.gdn_silu_mul(p, p, p, 0, None) == 0

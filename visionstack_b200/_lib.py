@@ -48,6 +48,8 @@ EXPORTED_SYMBOLS = (
     "gdn_ipc_open_handle",
     "gdn_ipc_close_handle",
     "gdn_peer_allreduce_bf16",
+    "gdn_rms_norm_zc",
+    "gdn_silu_mul",
 )
 GDN_FLAG_REGISTER_KERNEL = 1
 GDN_FLAG_CUDA_CORE_PREFILL = 2
@@ -172,6 +174,11 @@ def load() -> ctypes.CDLL:
         lib.gdn_ipc_close_handle.argtypes = [_c_void_p]
         lib.gdn_peer_allreduce_bf16.restype = _i32
         lib.gdn_peer_allreduce_bf16.argtypes = [ctypes.POINTER(PeerGroup), _c_void_p, _c_void_p, _i64, _c_void_p]
+        lib.gdn_rms_norm_zc.restype = _i32
+        lib.gdn_rms_norm_zc.argtypes = [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _i64, _i32,
+                                        ctypes.c_float, _c_void_p]
+        lib.gdn_silu_mul.restype = _i32
+        lib.gdn_silu_mul.argtypes = [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]
         lib.gdn_device_error.restype = _i32
         lib.gdn_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32), _i32]
         _lib = lib

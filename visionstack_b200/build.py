@@ -20,7 +20,8 @@ LIB = os.path.join(HERE, "libgdn_b200.so")
 SOURCES = ["gdn_capi.cu", "gdn_decode.cu", "gdn_decode_tma.cu", "gdn_prefill.cu", "gdn_conv.cu",
            "gdn_umma_selftest.cu", "gdn_prefill_tc.cu", "gdn_tmap.cu", "gdn_slots.cu",
            "gdn_prefill_prep.cu", "gdn_prefill_seq.cu", "gdn_prefill_static.cu", "stack_attn_decode.cu",
-           "gdn_functional.cu", "gdn_prefill_fused.cu", "gdn_peer_allreduce.cu"]
+           "gdn_functional.cu", "gdn_prefill_fused.cu", "gdn_peer_allreduce.cu",
+           "stack_ops.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

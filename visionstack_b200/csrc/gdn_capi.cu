@@ -654,3 +654,46 @@ int32_t gdn_peer_allreduce_bf16(const gdn_peer_group* g, const void* in, void* o
     a.counters = reinterpret_cast<int*>(static_cast<unsigned char*>(g->staging[g->rank]) + c);
     return cuda_status(gdn::launch_peer_allreduce(a, static_cast<cudaStream_t>(stream)), "gdn_peer_allreduce_bf16");
 }
+
+// ---------------------------------------------------------------------------
+// fused elementwise steps of the stack's layers
+// ---------------------------------------------------------------------------
+int32_t gdn_rms_norm_zc(const void* x, int64_t x_row_stride, const void* delta, int64_t delta_row_stride,
+                        void* res_out, const void* weight, void* out, int64_t rows, int32_t dim, float eps,
+                        void* stream) {
+    if (!x || !weight || !out) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
+    if ((delta == nullptr) != (res_out == nullptr))
+        return fail(GDN_ERR_INVALID_ARG, "delta and res_out are given together or not at all");
+    if (rows < 0 || dim < 8 || dim > 16384 || dim % 8 != 0)
+        return fail(GDN_ERR_INVALID_ARG, "rows >= 0, dim a multiple of 8 in 8..16384");
+    if (rows > (1ll << 31) * 8) return fail(GDN_ERR_INVALID_ARG, "too many rows");
+    if (x_row_stride < dim || x_row_stride % 8 != 0 || (delta && (delta_row_stride < dim || delta_row_stride % 8 != 0)))
+        return fail(GDN_ERR_INVALID_ARG, "row strides must be multiples of 8 of at least dim");
+    const void* ptrs[] = {x, delta, res_out, weight, out};
+    for (const void* p : ptrs)
+        if (p && !aligned16(p)) return fail(GDN_ERR_ALIGNMENT, "pointers must be 16-byte aligned");
+    if (rows == 0) return ok();
+    gdn::RmsNormArgs a;
+    a.x = x;
+    a.x_stride = x_row_stride;
+    a.delta = delta;
+    a.delta_stride = delta_row_stride;
+    a.res = res_out;
+    a.res_stride = dim;
+    a.w = weight;
+    a.out = out;
+    a.out_stride = dim;
+    a.rows = rows;
+    a.dim = dim;
+    a.eps = eps;
+    return cuda_status(gdn::launch_rms_norm_zc(a, static_cast<cudaStream_t>(stream)), "gdn_rms_norm_zc");
+}
+
+int32_t gdn_silu_mul(const void* gate, const void* up, void* out, int64_t n, void* stream) {
+    if (!gate || !up || !out) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
+    if (n < 0 || n % 8 != 0) return fail(GDN_ERR_INVALID_ARG, "n = %lld must be a multiple of 8", (long long)n);
+    if (!aligned16(gate) || !aligned16(up) || !aligned16(out))
+        return fail(GDN_ERR_ALIGNMENT, "pointers must be 16-byte aligned");
+    if (n == 0) return ok();
+    return cuda_status(gdn::launch_silu_mul(gate, up, out, n, static_cast<cudaStream_t>(stream)), "gdn_silu_mul");
+}

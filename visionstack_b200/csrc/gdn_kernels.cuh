@@ -112,6 +112,23 @@ struct PeerAllReduceArgs {
 };
 cudaError_t launch_peer_allreduce(const PeerAllReduceArgs& a, cudaStream_t s);
 unsigned int peer_allreduce_device_error(bool clear);
+// fused elementwise steps of the stack's layers (stack_ops.cu), bf16
+struct RmsNormArgs {
+    const void* x;       // [rows] x [dim], row stride x_stride elements
+    long long x_stride;
+    const void* delta;   // optional residual added first (row stride delta_stride); NULL: none
+    long long delta_stride;
+    void* res;           // with delta: bf16(x + delta), row stride res_stride
+    long long res_stride;
+    const void* w;       // [dim] zero-centred weight (the norm multiplies by 1 + w)
+    void* out;           // [rows] x [dim], row stride out_stride
+    long long out_stride;
+    long long rows;
+    int dim;
+    float eps;
+};
+cudaError_t launch_rms_norm_zc(const RmsNormArgs& a, cudaStream_t s);
+cudaError_t launch_silu_mul(const void* gate, const void* up, void* out, long long n, cudaStream_t s);
 cudaError_t launch_prefill(const MixParams& p, const CkptList& ck, int d, int dtype, bool mixer,
                            cudaStream_t s, bool* supported);
 cudaError_t launch_conv1d(int B, int C, int T, int K, int dtype, const void* x, const void* w,

@@ -25,18 +25,66 @@ from .config import Qwen3_5TextConfig, _linear
 from .deltanet import Qwen3_5GatedDeltaNet
 
 
+def _rows(x: torch.Tensor) -> Optional[Tuple[int, int]]:
+    """(rows, row stride) of ``x`` seen as rows of its last dimension, or None when its rows are not
+    evenly spaced (the last dimension must be contiguous)."""
+    if x.dim() < 2 or x.stride(-1) != 1:
+        return None
+    for i in range(x.dim() - 2):
+        if x.stride(i) != x.stride(i + 1) * x.shape[i + 1]:
+            return None
+    return x.numel() // x.shape[-1], x.stride(-2)
+
+
+def _bf16_kernel_ok(*ts: torch.Tensor) -> bool:
+    return all(t.is_cuda and t.dtype == torch.bfloat16 and t.data_ptr() % 16 == 0 for t in ts)
+
+
+def _rms_norm_zc(x: torch.Tensor, delta: Optional[torch.Tensor], w: torch.Tensor, eps: float):
+    """The fused RMSNorm kernel (gdn_rms_norm_zc): returns (bf16(x + delta) or None, the norm)."""
+    from . import _lib
+    rx = _rows(x)
+    rows, dim = rx[0], x.shape[-1]
+    out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    res = torch.empty(x.shape, dtype=x.dtype, device=x.device) if delta is not None else None
+    ds = _rows(delta)[1] if delta is not None else 0
+    _lib.check("gdn_rms_norm_zc", _lib.load().gdn_rms_norm_zc(
+        x.data_ptr(), rx[1], delta.data_ptr() if delta is not None else None, ds,
+        res.data_ptr() if res is not None else None, w.data_ptr(), out.data_ptr(), rows, dim, float(eps),
+        torch.cuda.current_stream(x.device).cuda_stream))
+    return res, out
+
+
 class Qwen3_5RMSNorm(nn.Module):
-    """RMSNorm with a zero-centred weight, x / rms(x) * (1 + w), in fp32 (config.py:118-127)."""
+    """RMSNorm with a zero-centred weight, x / rms(x) * (1 + w), in fp32 (config.py:118-127).
+
+    For bf16 CUDA tensors it runs the fused kernel ``gdn_rms_norm_zc`` (one launch instead of
+    PyTorch's dtype copies, weight offset, norm and copy back); ``add_forward`` also fuses the
+    decoder layer's residual add in front of it."""
 
     def __init__(self, dim: int, eps: float = 1e-6):
         super().__init__()
         self.eps = eps
         self.weight = nn.Parameter(torch.zeros(dim))
 
+    def _kernel_ok(self, *ts: torch.Tensor) -> bool:
+        dim = self.weight.shape[0]
+        return (dim % 8 == 0 and self.weight.is_contiguous() and _bf16_kernel_ok(self.weight, *ts) and
+                all(t.shape[-1] == dim and _rows(t) is not None and _rows(t)[1] % 8 == 0 for t in ts))
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self._kernel_ok(x):
+            return _rms_norm_zc(x, None, self.weight, self.eps)[1]
         # one fused normalisation kernel in fp32 (same math, one pass) instead of six elementwise ones
         w = 1.0 + self.weight.float()
         return F.rms_norm(x.float(), (x.shape[-1],), weight=w, eps=self.eps).to(x.dtype)
+
+    def add_forward(self, x: torch.Tensor, delta: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """(x + delta, this norm of it), the residual stream kept in the activation dtype."""
+        if x.shape == delta.shape and self._kernel_ok(x, delta):
+            return _rms_norm_zc(x, delta, self.weight, self.eps)
+        h = x + delta
+        return h, self(h)
 
 
 def _act(x: torch.Tensor, name: str) -> torch.Tensor:
@@ -268,7 +316,16 @@ class Qwen3_5MLP(nn.Module):
         self.act_name = config.hidden_act
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return _linear(self.down_proj, _act(_linear(self.gate_proj, x), self.act_name) * _linear(self.up_proj, x))
+        g, u = _linear(self.gate_proj, x), _linear(self.up_proj, x)
+        if self.act_name not in ("gelu_pytorch_tanh", "gelu") and g.shape == u.shape and g.is_contiguous() and \
+                u.is_contiguous() and g.numel() % 8 == 0 and _bf16_kernel_ok(g, u):
+            from . import _lib
+            h = torch.empty_like(g)  # act(gate) * up in one launch (gdn_silu_mul), torch's two roundings
+            _lib.check("gdn_silu_mul", _lib.load().gdn_silu_mul(g.data_ptr(), u.data_ptr(), h.data_ptr(), g.numel(),
+                                                               torch.cuda.current_stream(g.device).cuda_stream))
+        else:
+            h = _act(g, self.act_name) * u
+        return _linear(self.down_proj, h)
 
 
 class Qwen3_5DecoderLayer(nn.Module):
@@ -294,8 +351,8 @@ class Qwen3_5DecoderLayer(nn.Module):
             h = self.linear_attn(h, attention_mask=linear_mask, cache=cache)
         else:
             h = self.self_attn(h, position_embeddings=position_embeddings, attention_mask=full_attn_mask, cache=cache)
-        hidden_states = hidden_states + h
-        return hidden_states + self.mlp(self.post_attention_layernorm(hidden_states))
+        hidden_states, h = self.post_attention_layernorm.add_forward(hidden_states, h)  # residual + norm
+        return hidden_states + self.mlp(h)
 
 
 @dataclass
