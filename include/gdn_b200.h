@@ -443,6 +443,35 @@ int32_t gdn_rms_norm_zc(const void* x, int64_t x_row_stride, const void* delta, 
                         void* stream);
 int32_t gdn_silu_mul(const void* gate, const void* up, void* out, int64_t n, void* stream);
 
+/*
+ * The gated attention's steps around its attention kernel (bf16 only):
+ *
+ * gdn_qk_norm_rope: the per-head q / k RMSNorm (Qwen3_5RMSNorm, config.py:
+ * 118-127, weights q_weight / k_weight [head_dim]) followed by the partial
+ * rotary embedding of text.py:76-86 with torch's roundings:
+ * bf16(bf16(x * cos) + bf16(rotate_half(x) * sin)) on the first rotary_dim
+ * channels, the rest passed through.  qg [batch, seq_len, num_heads,
+ * 2 head_dim] is the q_proj output (query, then gate, per head), k
+ * [batch, seq_len, num_kv_heads, head_dim] the k_proj output, cos / sin
+ * [batch, seq_len, rotary_dim]; q_out [batch, num_heads, seq_len, head_dim]
+ * and k_out [batch, num_kv_heads, seq_len, head_dim] are the layouts the
+ * attention reads.  head_dim a multiple of 8 up to 256, rotary_dim a multiple
+ * of 16 up to head_dim, everything contiguous and 16-byte aligned.
+ *
+ * gdn_attn_gate_out: out = attn.transpose(1, 2).reshape(batch, seq_len,
+ * num_heads * head_dim) * sigmoid(gate) (text.py:204-209), i.e.
+ * bf16(o * bf16(sigmoid(g))), with o [batch, num_heads, seq_len, head_dim]
+ * given by its element strides (last dimension contiguous) and the gate read
+ * from qg.
+ */
+int32_t gdn_qk_norm_rope(const void* qg, const void* k, const void* q_weight, const void* k_weight, const void* cos,
+                         const void* sin, void* q_out, void* k_out, int32_t batch, int32_t seq_len,
+                         int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t rotary_dim, float eps,
+                         void* stream);
+int32_t gdn_attn_gate_out(const void* o, int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_t, const void* qg,
+                          void* out, int32_t batch, int32_t seq_len, int32_t num_heads, int32_t head_dim,
+                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif

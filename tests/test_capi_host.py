@@ -238,3 +238,11 @@ def test_stack_ops_validation():
     assert lib.gdn_silu_mul(p, p, p, 12, None) == -1
     assert lib.gdn_silu_mul(p, p + 8, p, 16, None) == -3
     assert lib.gdn_silu_mul(p, p, p, 0, None) == 0
+    # attention steps: head_dim / rotary_dim limits, NULL / misaligned pointers
+    args = [p] * 8
+    assert lib.gdn_qk_norm_rope(*args, 2, 3, 4, 2, 512, 64, 1e-6, None) == -2
+    assert lib.gdn_qk_norm_rope(*args, 2, 3, 4, 2, 256, 24, 1e-6, None) == -2
+    assert lib.gdn_qk_norm_rope(None, *args[1:], 2, 3, 4, 2, 256, 64, 1e-6, None) == -1
+    assert lib.gdn_qk_norm_rope(*args, 0, 3, 4, 2, 256, 64, 1e-6, None) == 0   # no rows
+    assert lib.gdn_attn_gate_out(p, 8, 8, 4, p, p, 2, 3, 4, 256, None) == -3  # stride not a multiple of 8
+    assert lib.gdn_attn_gate_out(p, 8, 8, 8, p, p, 0, 3, 4, 256, None) == 0   # no rows

@@ -99,3 +99,43 @@ def test_silu_mul_matches_torch():
     diff = (out.float() - r.float()).abs()
     assert int((diff > 0).sum()) <= a.numel() // 1000, "more than 0.1% of the elements differ from torch's"
     assert bool((diff <= r.float().abs() * 2.0 ** -7 + 1e-30).all())
+
+
+def test_qk_norm_rope_and_gate_match_torch():
+    """The attention's fused steps against torch's ops on the same bf16 tensors: q / k norms and
+    the partial rotary embedding (head dim 256, 64 rotary channels as in the stack), and the gated
+    output for a contiguous and a transposed (flash-attention-like) attention output."""
+    from visionstack_b200 import Qwen3_5TextConfig
+    from visionstack_b200.stack import Qwen3_5Attention, Qwen3_5TextRotaryEmbedding, _apply_rotary_pos_emb_partial
+    g = torch.Generator(device="cuda")
+    g.manual_seed(4)
+    cfg = Qwen3_5TextConfig(hidden_size=512, num_attention_heads=4, num_key_value_heads=2, head_dim=256)
+    attn = Qwen3_5Attention(cfg, 3).cuda().to(torch.bfloat16)
+    B, T, hd = 2, 5, 256
+    with torch.no_grad():
+        attn.q_norm.weight.copy_(0.1 * torch.randn(hd, generator=g, device="cuda"))
+        attn.k_norm.weight.copy_(0.1 * torch.randn(hd, generator=g, device="cuda"))
+        qg = torch.randn(B, T, 4, 2 * hd, generator=g, device="cuda").to(torch.bfloat16)
+        kr = torch.randn(B, T, 2, hd, generator=g, device="cuda").to(torch.bfloat16)
+        pos = (torch.arange(T, device="cuda") + 37)[None, None].expand(3, B, T)
+        cos, sin = Qwen3_5TextRotaryEmbedding(cfg)(qg, pos)
+        assert attn._fused_ok(qg, kr, cos, sin)
+        q, k = attn._qk_norm_rope(qg, kr, cos, sin)
+        qn = _ref_norm(qg[..., :hd], attn.q_norm.weight, attn.q_norm.eps).transpose(1, 2)
+        kn = _ref_norm(kr, attn.k_norm.weight, attn.k_norm.eps).transpose(1, 2)
+        rq, rk = _apply_rotary_pos_emb_partial(qn, kn, cos, sin)
+    assert q.shape == rq.shape and k.shape == rk.shape
+    for got, ref, name in ((q, rq, "q"), (k, rk, "k")):
+        d = (got.float() - ref.float()).abs()
+        # the norm's mean is summed in another order: a normed value may round to the
+        # neighbouring bf16, which the rotation carries (at most a couple of roundings)
+        assert bool((d <= ref.float().abs() * 2.0 ** -6 + 2.0 ** -12).all()), f"{name}: max diff {float(d.max())}"
+        assert int((d > 0).sum()) <= ref.numel() // 100, f"{name}: too many elements differ"
+    with torch.no_grad():
+        for o in (torch.randn(B, 4, T, hd, generator=g, device="cuda").to(torch.bfloat16),
+                  torch.randn(B, T, 4, hd, generator=g, device="cuda").to(torch.bfloat16).transpose(1, 2)):
+            out = attn._gated(o, qg, None)
+            ref = o.transpose(1, 2).reshape(B, T, -1).contiguous() * torch.sigmoid(qg[..., hd:].reshape(B, T, -1))
+            d = (out.float() - ref.float()).abs()
+            assert bool((d <= ref.float().abs() * 2.0 ** -7 + 1e-30).all())
+            assert int((d > 0).sum()) <= ref.numel() // 1000

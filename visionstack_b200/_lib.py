@@ -50,6 +50,8 @@ EXPORTED_SYMBOLS = (
     "gdn_peer_allreduce_bf16",
     "gdn_rms_norm_zc",
     "gdn_silu_mul",
+    "gdn_qk_norm_rope",
+    "gdn_attn_gate_out",
 )
 GDN_FLAG_REGISTER_KERNEL = 1
 GDN_FLAG_CUDA_CORE_PREFILL = 2
@@ -179,6 +181,11 @@ def load() -> ctypes.CDLL:
                                         ctypes.c_float, _c_void_p]
         lib.gdn_silu_mul.restype = _i32
         lib.gdn_silu_mul.argtypes = [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]
+        lib.gdn_qk_norm_rope.restype = _i32
+        lib.gdn_qk_norm_rope.argtypes = [_c_void_p] * 8 + [_i32] * 6 + [ctypes.c_float, _c_void_p]
+        lib.gdn_attn_gate_out.restype = _i32
+        lib.gdn_attn_gate_out.argtypes = [_c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32,
+                                          _c_void_p]
         lib.gdn_device_error.restype = _i32
         lib.gdn_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32), _i32]
         _lib = lib

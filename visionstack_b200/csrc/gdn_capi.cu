@@ -697,3 +697,60 @@ int32_t gdn_silu_mul(const void* gate, const void* up, void* out, int64_t n, voi
     if (n == 0) return ok();
     return cuda_status(gdn::launch_silu_mul(gate, up, out, n, static_cast<cudaStream_t>(stream)), "gdn_silu_mul");
 }
+
+int32_t gdn_qk_norm_rope(const void* qg, const void* k, const void* q_weight, const void* k_weight, const void* cos,
+                         const void* sin, void* q_out, void* k_out, int32_t batch, int32_t seq_len,
+                         int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t rotary_dim, float eps,
+                         void* stream) {
+    const void* ptrs[] = {qg, k, q_weight, k_weight, cos, sin, q_out, k_out};
+    for (const void* p : ptrs) {
+        if (!p) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
+        if (!aligned16(p)) return fail(GDN_ERR_ALIGNMENT, "pointers must be 16-byte aligned");
+    }
+    if (batch < 0 || seq_len < 0 || num_heads < 1 || num_kv_heads < 1)
+        return fail(GDN_ERR_INVALID_ARG, "bad sizes");
+    if (head_dim < 8 || head_dim > 256 || head_dim % 8 != 0 || rotary_dim < 0 || rotary_dim % 16 != 0 ||
+        rotary_dim > head_dim)
+        return fail(GDN_ERR_UNSUPPORTED, "head_dim a multiple of 8 up to 256, rotary_dim a multiple of 16 up to it");
+    if ((long long)batch * seq_len == 0) return ok();
+    gdn::QkRopeArgs a;
+    a.qg = qg;
+    a.k = k;
+    a.qw = q_weight;
+    a.kw = k_weight;
+    a.cos = cos;
+    a.sin = sin;
+    a.q_out = q_out;
+    a.k_out = k_out;
+    a.B = batch;
+    a.T = seq_len;
+    a.H = num_heads;
+    a.KVH = num_kv_heads;
+    a.hd = head_dim;
+    a.rot = rotary_dim;
+    a.eps = eps;
+    return cuda_status(gdn::launch_qk_norm_rope(a, static_cast<cudaStream_t>(stream)), "gdn_qk_norm_rope");
+}
+
+int32_t gdn_attn_gate_out(const void* o, int64_t o_stride_b, int64_t o_stride_h, int64_t o_stride_t, const void* qg,
+                          void* out, int32_t batch, int32_t seq_len, int32_t num_heads, int32_t head_dim,
+                          void* stream) {
+    if (!o || !qg || !out) return fail(GDN_ERR_INVALID_ARG, "a required pointer is NULL");
+    if (!aligned16(o) || !aligned16(qg) || !aligned16(out) || o_stride_b % 8 || o_stride_h % 8 || o_stride_t % 8)
+        return fail(GDN_ERR_ALIGNMENT, "pointers 16-byte aligned, strides multiples of 8 elements");
+    if (batch < 0 || seq_len < 0 || num_heads < 1 || head_dim < 8 || head_dim % 8 != 0)
+        return fail(GDN_ERR_INVALID_ARG, "bad sizes");
+    if ((long long)batch * seq_len == 0) return ok();
+    gdn::GateOutArgs a;
+    a.o = o;
+    a.o_sb = o_stride_b;
+    a.o_sh = o_stride_h;
+    a.o_st = o_stride_t;
+    a.qg = qg;
+    a.out = out;
+    a.B = batch;
+    a.T = seq_len;
+    a.H = num_heads;
+    a.hd = head_dim;
+    return cuda_status(gdn::launch_gate_out(a, static_cast<cudaStream_t>(stream)), "gdn_attn_gate_out");
+}

@@ -129,6 +129,27 @@ struct RmsNormArgs {
 };
 cudaError_t launch_rms_norm_zc(const RmsNormArgs& a, cudaStream_t s);
 cudaError_t launch_silu_mul(const void* gate, const void* up, void* out, long long n, cudaStream_t s);
+struct QkRopeArgs {
+    const void* qg;   // [B][T][H][2 hd]: query (first hd) and gate of each head
+    const void* k;    // [B][T][KVH][hd]
+    const void* qw;   // [hd] zero-centred q-norm weight
+    const void* kw;   // [hd] k-norm weight
+    const void* cos;  // [B][T][rot]
+    const void* sin;
+    void* q_out;      // [B][H][T][hd]
+    void* k_out;      // [B][KVH][T][hd]
+    int B, T, H, KVH, hd, rot;
+    float eps;
+};
+cudaError_t launch_qk_norm_rope(const QkRopeArgs& a, cudaStream_t s);
+struct GateOutArgs {
+    const void* o;                // attention output [B][H][T][hd], strides in elements (last dim contiguous)
+    long long o_sb, o_sh, o_st;
+    const void* qg;               // [B][T][H][2 hd] (the gate is the second hd of each head)
+    void* out;                    // [B][T][H hd]
+    int B, T, H, hd;
+};
+cudaError_t launch_gate_out(const GateOutArgs& a, cudaStream_t s);
 cudaError_t launch_prefill(const MixParams& p, const CkptList& ck, int d, int dtype, bool mixer,
                            cudaStream_t s, bool* supported);
 cudaError_t launch_conv1d(int B, int C, int T, int K, int dtype, const void* x, const void* w,

@@ -14,6 +14,14 @@
 //   256-element run of the query projection).
 // * silu_mul: the gated MLP's act(gate) * up (text.py:215-230) with torch's
 //   two roundings: bf16( bf16(silu(gate)) * up ).
+// * qk_norm_rope: the gated attention's per-head q / k RMSNorm followed by the
+//   partial rotary embedding (text.py:76-86, 140-156), one warp per (token,
+//   head) row: the norm rounded to bf16, then for the first `rot` channels
+//   bf16(bf16(x * cos) + bf16(rotate_half(x) * sin)) (rotate_half: the
+//   partner half-range, negated in the first half; the partner's values come
+//   by warp shuffle), written in the [B, heads, T, hd] layout the attention reads.
+// * gate_out: attn.transpose(1, 2).reshape(B, T, H hd) * sigmoid(gate)
+//   (text.py:204-209): bf16(o * bf16(sigmoid(g))) in the [B, T, H hd] layout.
 #include <cuda_bf16.h>
 
 #include "gdn_kernels.cuh"
@@ -120,7 +128,105 @@ __global__ void __launch_bounds__(NT) silu_mul_kernel(const uint4* __restrict__ 
     }
 }
 
+__global__ void __launch_bounds__(NT) qk_norm_rope_kernel(const QkRopeArgs a) {
+    const long long row = (long long)blockIdx.x * (NT / 32) + (threadIdx.x >> 5);
+    const long long q_rows = (long long)a.B * a.T * a.H, k_rows = (long long)a.B * a.T * a.KVH;
+    if (row >= q_rows + k_rows) return;
+    const int lane = threadIdx.x & 31, units = a.hd / 8, half_u = a.rot / 16;
+    const bool is_q = row < q_rows;
+    const long long rr = is_q ? row : row - q_rows;
+    const int heads = is_q ? a.H : a.KVH;
+    const int h = (int)(rr % heads);
+    const long long bt = rr / heads;  // b * T + t
+    const int t = (int)(bt % a.T), b = (int)(bt / a.T);
+    const __nv_bfloat16* src = is_q ? static_cast<const __nv_bfloat16*>(a.qg) + rr * (2 * a.hd)
+                                    : static_cast<const __nv_bfloat16*>(a.k) + rr * a.hd;
+    const uint4* w = static_cast<const uint4*>(is_q ? a.qw : a.kw);
+    float f[8];
+    float ss = 0.f;
+    if (lane < units) {
+        unpack8(reinterpret_cast<const uint4*>(src)[lane], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float r = rsqrtf(ss / (float)a.hd + a.eps);
+    uint4 y = make_uint4(0u, 0u, 0u, 0u);
+    if (lane < units) {
+        float g[8];
+        unpack8(w[lane], g);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = (f[e] * r) * (1.0f + g[e]);
+        y = pack8(f);  // the norm's output, rounded to bf16
+    }
+    // rotary: units below rot / 8 pair unit u with u +- rot / 16
+    const int partner = lane < half_u ? lane + half_u : (lane < 2 * half_u ? lane - half_u : lane);
+    uint4 pv;
+    pv.x = __shfl_sync(0xffffffffu, y.x, partner);
+    pv.y = __shfl_sync(0xffffffffu, y.y, partner);
+    pv.z = __shfl_sync(0xffffffffu, y.z, partner);
+    pv.w = __shfl_sync(0xffffffffu, y.w, partner);
+    if (lane >= units) return;
+    if (lane < 2 * half_u) {
+        float x[8], p[8], c[8], sn[8];
+        unpack8(y, x);
+        unpack8(pv, p);
+        const long long cs = ((long long)b * a.T + t) * a.rot + 8 * lane;
+        unpack8(*reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.cos) + cs), c);
+        unpack8(*reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.sin) + cs), sn);
+        const float sign = lane < half_u ? -1.0f : 1.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float t1 = __bfloat162float(__float2bfloat16_rn(x[e] * c[e]));
+            const float t2 = __bfloat162float(__float2bfloat16_rn((sign * p[e]) * sn[e]));
+            x[e] = t1 + t2;
+        }
+        y = pack8(x);
+    }
+    __nv_bfloat16* dst = is_q ? static_cast<__nv_bfloat16*>(a.q_out) + (((long long)b * a.H + h) * a.T + t) * a.hd
+                              : static_cast<__nv_bfloat16*>(a.k_out) + (((long long)b * a.KVH + h) * a.T + t) * a.hd;
+    reinterpret_cast<uint4*>(dst)[lane] = y;
+}
+
+__global__ void __launch_bounds__(NT) gate_out_kernel(const GateOutArgs a) {
+    const int units = a.hd / 8;
+    const long long total = (long long)a.B * a.T * a.H * units;
+    for (long long i = (long long)blockIdx.x * NT + threadIdx.x; i < total; i += (long long)gridDim.x * NT) {
+        const int u = (int)(i % units);
+        const long long rest = i / units;
+        const int h = (int)(rest % a.H);
+        const long long bt = rest / a.H;
+        const int t = (int)(bt % a.T), b = (int)(bt / a.T);
+        float o[8], g[8];
+        unpack8(*reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.o) + b * a.o_sb + h * a.o_sh +
+                                                t * a.o_st + 8 * u),
+                o);
+        unpack8(*reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.qg) + bt * (2LL * a.H * a.hd) +
+                                                (long long)h * 2 * a.hd + a.hd + 8 * u),
+                g);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] *= __bfloat162float(__float2bfloat16_rn(1.0f / (1.0f + expf(-g[e]))));
+        reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + bt * ((long long)a.H * a.hd) +
+                                 (long long)h * a.hd)[u] = pack8(o);
+    }
+}
+
 }  // namespace sops
+
+cudaError_t launch_qk_norm_rope(const QkRopeArgs& a, cudaStream_t s) {
+    const long long rows = (long long)a.B * a.T * (a.H + a.KVH);
+    sops::qk_norm_rope_kernel<<<(unsigned)((rows + sops::NT / 32 - 1) / (sops::NT / 32)), sops::NT, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gate_out(const GateOutArgs& a, cudaStream_t s) {
+    const long long units = (long long)a.B * a.T * a.H * (a.hd / 8);
+    long long blocks = (units + sops::NT - 1) / sops::NT;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    sops::gate_out_kernel<<<(unsigned)blocks, sops::NT, 0, s>>>(a);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_rms_norm_zc(const RmsNormArgs& a, cudaStream_t s) {
     // threads per row: the row's 16-byte units rounded up to a power of two, 32..256

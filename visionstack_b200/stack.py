@@ -257,22 +257,64 @@ class Qwen3_5Attention(nn.Module):
                                            scale=self.scaling)
         return o.reshape(B, self.num_heads, 1, hd)
 
+    def _fused_ok(self, qg: torch.Tensor, kr: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> bool:
+        hd, rot = self.head_dim, cos.shape[-1]
+        ws = (self.q_norm.weight, self.k_norm.weight)
+        return (hd % 8 == 0 and hd <= 256 and rot % 16 == 0 and rot <= hd and qg.is_contiguous() and
+                kr.is_contiguous() and cos.is_contiguous() and sin.is_contiguous() and
+                cos.shape == (qg.shape[0], qg.shape[1], rot) and sin.shape == cos.shape and
+                all(w.is_contiguous() for w in ws) and _bf16_kernel_ok(qg, kr, cos, sin, *ws))
+
+    def _qk_norm_rope(self, qg: torch.Tensor, kr: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
+        """q / k norms and the partial rotary embedding in one launch (gdn_qk_norm_rope): q
+        [B, H, T, hd] and k [B, KVH, T, hd], the layouts the torch path's rotation produces."""
+        from . import _lib
+        B, T, hd = qg.shape[0], qg.shape[1], self.head_dim
+        q = torch.empty(B, self.num_heads, T, hd, dtype=qg.dtype, device=qg.device)
+        k = torch.empty(B, self.num_kv_heads, T, hd, dtype=qg.dtype, device=qg.device)
+        _lib.check("gdn_qk_norm_rope", _lib.load().gdn_qk_norm_rope(
+            qg.data_ptr(), kr.data_ptr(), self.q_norm.weight.data_ptr(), self.k_norm.weight.data_ptr(),
+            cos.data_ptr(), sin.data_ptr(), q.data_ptr(), k.data_ptr(), B, T, self.num_heads, self.num_kv_heads, hd,
+            cos.shape[-1], float(self.q_norm.eps), torch.cuda.current_stream(qg.device).cuda_stream))
+        return q, k
+
+    def _gated(self, o: torch.Tensor, qg: torch.Tensor, gate: Optional[torch.Tensor]) -> torch.Tensor:
+        """attn.transpose(1, 2).reshape(B, T, H hd) * sigmoid(gate) (text.py:204-209): one launch
+        (gdn_attn_gate_out) when the fused path produced q, else torch's ops on ``gate``."""
+        B, H, T, hd = o.shape
+        if gate is None and o.stride(-1) == 1 and all(st % 8 == 0 for st in o.stride()[:3]) and \
+                _bf16_kernel_ok(o, qg):
+            from . import _lib
+            out = torch.empty(B, T, H * hd, dtype=o.dtype, device=o.device)
+            _lib.check("gdn_attn_gate_out", _lib.load().gdn_attn_gate_out(
+                o.data_ptr(), o.stride(0), o.stride(1), o.stride(2), qg.data_ptr(), out.data_ptr(), B, T, H, hd,
+                torch.cuda.current_stream(o.device).cuda_stream))
+            return out
+        if gate is None:
+            gate = qg[..., hd:].reshape(B, T, H * hd)
+        return o.transpose(1, 2).reshape(B, T, -1).contiguous() * torch.sigmoid(gate)
+
     def forward(self, hidden_states: torch.Tensor, position_embeddings: Tuple[torch.Tensor, torch.Tensor],
                 attention_mask: Optional[torch.Tensor] = None,
                 cache: Optional[Qwen3_5HybridCache] = None) -> torch.Tensor:
         B, T = hidden_states.shape[:2]
         hd = self.head_dim
         qg = _linear(self.q_proj, hidden_states).view(B, T, self.num_heads, 2 * hd)
-        q, gate = qg[..., :hd], qg[..., hd:].reshape(B, T, self.num_heads * hd)
-        q = self.q_norm(q).transpose(1, 2)
-        k = self.k_norm(_linear(self.k_proj, hidden_states).view(B, T, self.num_kv_heads, hd)).transpose(1, 2)
+        kr = _linear(self.k_proj, hidden_states).view(B, T, self.num_kv_heads, hd)
         v = _linear(self.v_proj, hidden_states).view(B, T, self.num_kv_heads, hd).transpose(1, 2)
-        q, k = _apply_rotary_pos_emb_partial(q, k, *position_embeddings)
+        cos, sin = position_embeddings
+        gate = None
+        if self._fused_ok(qg, kr, cos, sin):
+            q, k = self._qk_norm_rope(qg, kr, cos, sin)
+        else:
+            q, gate = qg[..., :hd], qg[..., hd:].reshape(B, T, self.num_heads * hd)
+            q = self.q_norm(q).transpose(1, 2)
+            k = self.k_norm(kr).transpose(1, 2)
+            q, k = _apply_rotary_pos_emb_partial(q, k, cos, sin)
         static_pos = getattr(cache, "static_pos", None) if cache is not None else None
         if static_pos is not None:
             o = self._static_decode(cache, q, k, v, static_pos, attention_mask)
-            o = o.transpose(1, 2).reshape(B, T, -1).contiguous() * torch.sigmoid(gate)
-            return _linear(self.o_proj, o)
+            return _linear(self.o_proj, self._gated(o, qg, gate))
         has_past = False
         if cache is not None:
             k, v, has_past = self._store_kv(cache, k, v)
@@ -301,8 +343,7 @@ class Qwen3_5Attention(nn.Module):
         else:
             o = F.scaled_dot_product_attention(q, k, v, is_causal=(T > 1 and not has_past), scale=self.scaling,
                                                enable_gqa=gqa)
-        o = o.transpose(1, 2).reshape(B, T, -1).contiguous() * torch.sigmoid(gate)
-        return _linear(self.o_proj, o)
+        return _linear(self.o_proj, self._gated(o, qg, gate))
 
 
 class Qwen3_5MLP(nn.Module):
