@@ -69,11 +69,11 @@ class PeerAllReduce:
         dist.barrier(group)
 
     def fits(self, x: torch.Tensor) -> bool:
-        """True when ``x`` can go through the peer path (bf16, contiguous, on this rank's device,
-        a multiple of 8 elements up to the capacity, 16-byte aligned)."""
+        """True when ``x`` goes through the peer path: bf16 on this rank's device, a multiple of 8
+        elements up to the capacity.  Every input of the decision is the same on every rank of a
+        sharded layer (dtype, size), so the ranks never split between this path and another."""
         n = x.numel()
-        return (x.dtype == torch.bfloat16 and x.is_contiguous() and x.device == self.device and n % 8 == 0 and
-                0 < n <= self.cap and x.data_ptr() % 16 == 0)
+        return x.dtype == torch.bfloat16 and x.device == self.device and n % 8 == 0 and 0 < n <= self.cap
 
     def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Sum ``x`` over the ranks into ``out`` (default: in place) on the current stream."""
@@ -84,12 +84,19 @@ class PeerAllReduce:
                 out.copy_(x)
             return out
         if not self.fits(x) or out.shape != x.shape or not self.fits(out):
-            raise ValueError("PeerAllReduce takes contiguous, 16-byte aligned bf16 tensors of a multiple of 8 "
-                             f"elements up to {self.cap} on {self.device}")
+            raise ValueError(f"PeerAllReduce takes bf16 tensors of a multiple of 8 elements up to {self.cap} "
+                             f"on {self.device}")
+
+        def direct(t: torch.Tensor) -> bool:
+            return t.is_contiguous() and t.data_ptr() % 16 == 0
+        src = x if direct(x) else x.contiguous().clone()  # a fresh allocation is 16-byte aligned
+        dst = out if direct(out) else torch.empty(out.shape, dtype=out.dtype, device=out.device)
         lib = _lib.load()
         stream = torch.cuda.current_stream(self.device).cuda_stream
         _lib.check("gdn_peer_allreduce_bf16", lib.gdn_peer_allreduce_bf16(
-            ctypes.byref(self._group), x.data_ptr(), out.data_ptr(), x.numel(), stream))
+            ctypes.byref(self._group), src.data_ptr(), dst.data_ptr(), src.numel(), stream))
+        if dst is not out:
+            out.copy_(dst)
         return out
 
     def close(self) -> None:
