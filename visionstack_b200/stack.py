@@ -387,13 +387,28 @@ class Qwen3_5DecoderLayer(nn.Module):
     def forward(self, hidden_states: torch.Tensor, position_embeddings: Tuple[torch.Tensor, torch.Tensor],
                 linear_mask: Optional[torch.Tensor] = None, full_attn_mask: Optional[torch.Tensor] = None,
                 cache: Optional[Qwen3_5HybridCache] = None) -> torch.Tensor:
-        h = self.input_layernorm(hidden_states)
+        hidden_states, pending = self.forward_pending(hidden_states, None, position_embeddings, linear_mask,
+                                                      full_attn_mask, cache)
+        return hidden_states + pending
+
+    def forward_pending(self, hidden_states: torch.Tensor, pending: Optional[torch.Tensor],
+                        position_embeddings: Tuple[torch.Tensor, torch.Tensor],
+                        linear_mask: Optional[torch.Tensor] = None, full_attn_mask: Optional[torch.Tensor] = None,
+                        cache: Optional[Qwen3_5HybridCache] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """The block with its last residual add left to the caller: takes the residual stream and the
+        previous block's not yet added MLP output (or None) and returns the stream and this block's
+        MLP output.  The add then runs inside the next norm's kernel (`add_forward`); the result is
+        that of `forward` bit for bit (both round the sum to the activation dtype)."""
+        if pending is None:
+            h = self.input_layernorm(hidden_states)
+        else:
+            hidden_states, h = self.input_layernorm.add_forward(hidden_states, pending)
         if self.block_type == "linear_attention":
             h = self.linear_attn(h, attention_mask=linear_mask, cache=cache)
         else:
             h = self.self_attn(h, position_embeddings=position_embeddings, attention_mask=full_attn_mask, cache=cache)
         hidden_states, h = self.post_attention_layernorm.add_forward(hidden_states, h)  # residual + norm
-        return hidden_states + self.mlp(h)
+        return hidden_states, self.mlp(h)
 
 
 @dataclass
@@ -455,11 +470,13 @@ class Qwen3_5TextModel(nn.Module):
 
         h = inputs_embeds
         pe = self.rotary_emb(h, position_ids)
+        pending = None  # each block's MLP output is added inside the next norm's kernel
         for layer in self.layers:
-            h = layer(h, position_embeddings=pe, linear_mask=linear_mask, full_attn_mask=full_mask, cache=cache)
+            h, pending = layer.forward_pending(h, pending, pe, linear_mask, full_mask, cache)
         if cache is not None:
             cache.past_seen_tokens = past + T
-        return Qwen3_5ModelOutput(last_hidden_state=self.norm(h), past_key_values=cache)
+        out = self.norm(h) if pending is None else self.norm.add_forward(h, pending)[1]
+        return Qwen3_5ModelOutput(last_hidden_state=out, past_key_values=cache)
 
 
 class StackDecodeGraph:
