@@ -246,3 +246,4 @@ def test_stack_ops_validation():
     assert lib.gdn_qk_norm_rope(*args, 0, 3, 4, 2, 256, 64, 1e-6, None) == 0   # no rows
     assert lib.gdn_attn_gate_out(p, 8, 8, 4, p, p, 2, 3, 4, 256, None) == -3  # stride not a multiple of 8
     assert lib.gdn_attn_gate_out(p, 8, 8, 8, p, p, 0, 3, 4, 256, None) == 0   # no rows
+    assert lib.gdn_rms_norm_zc(p, 2048, None, 0, None, p, p, 1 << 31, 2048, 1e-6, None) == -1  # grid limit

@@ -666,7 +666,7 @@ int32_t gdn_rms_norm_zc(const void* x, int64_t x_row_stride, const void* delta, 
         return fail(GDN_ERR_INVALID_ARG, "delta and res_out are given together or not at all");
     if (rows < 0 || dim < 8 || dim > 16384 || dim % 8 != 0)
         return fail(GDN_ERR_INVALID_ARG, "rows >= 0, dim a multiple of 8 in 8..16384");
-    if (rows > (1ll << 31) * 8) return fail(GDN_ERR_INVALID_ARG, "too many rows");
+    if (rows > 0x7FFFFFFFll) return fail(GDN_ERR_INVALID_ARG, "rows = %lld: at most 2^31 - 1", (long long)rows);
     if (x_row_stride < dim || x_row_stride % 8 != 0 || (delta && (delta_row_stride < dim || delta_row_stride % 8 != 0)))
         return fail(GDN_ERR_INVALID_ARG, "row strides must be multiples of 8 of at least dim");
     const void* ptrs[] = {x, delta, res_out, weight, out};
@@ -713,6 +713,8 @@ int32_t gdn_qk_norm_rope(const void* qg, const void* k, const void* q_weight, co
         rotary_dim > head_dim)
         return fail(GDN_ERR_UNSUPPORTED, "head_dim a multiple of 8 up to 256, rotary_dim a multiple of 16 up to it");
     if ((long long)batch * seq_len == 0) return ok();
+    if ((long long)batch * seq_len * (num_heads + num_kv_heads) > 0x7FFFFFFFll * 8)
+        return fail(GDN_ERR_INVALID_ARG, "too many (token, head) rows for one launch");
     gdn::QkRopeArgs a;
     a.qg = qg;
     a.k = k;
