@@ -473,20 +473,23 @@ def run_ours(args, rank: int, world: int) -> None:
     # end to end through the public API: every step copies its projection
     # outputs (packed [mixed | z | b | a] rows, one copy) from pinned host memory,
     # calls the mixer, and copies the gated-norm output back to pinned host
-    # memory.  Copies run on two copy streams, double-buffered, so the transfers
-    # of neighbouring steps overlap the kernel.
+    # memory.  Copies run on two copy streams over NB device buffers, so step i's
+    # input copy starts once step i - NB's kernel is done with its buffer: with four
+    # buffers every copy a step's kernel waits for finished a step earlier, and the
+    # kernels follow one another as in the device-timed loop.
     K_e2e = min(K, 1000)
     wdt = conv_dim + vdim + 2 * hv
     with torch.no_grad():
         packed = torch.cat([mixed[:, :, 0], z[:, :, 0], bb[:, :, 0], aa[:, :, 0]], dim=-1)  # [NIN, B, wdt]
     h_in = packed.cpu().pin_memory()
-    d_in = [torch.empty(B, 1, wdt, dtype=torch.bfloat16, device=dev) for _ in range(2)]
-    d_out = [torch.empty(B, 1, vdim, dtype=torch.bfloat16, device=dev) for _ in range(2)]
-    h_out = [torch.empty(B, 1, vdim, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    NB = 8
+    d_in = [torch.empty(B, 1, wdt, dtype=torch.bfloat16, device=dev) for _ in range(NB)]
+    d_out = [torch.empty(B, 1, vdim, dtype=torch.bfloat16, device=dev) for _ in range(NB)]
+    h_out = [torch.empty(B, 1, vdim, dtype=torch.bfloat16).pin_memory() for _ in range(NB)]
     s_h2d, s_d2h = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-    ev_ready = [torch.cuda.Event() for _ in range(2)]
-    ev_used = [torch.cuda.Event() for _ in range(2)]
-    ev_back = [torch.cuda.Event() for _ in range(2)]
+    ev_ready = [torch.cuda.Event() for _ in range(NB)]
+    ev_used = [torch.cuda.Event() for _ in range(NB)]
+    ev_back = [torch.cuda.Event() for _ in range(NB)]
     h2d = wdt * B * 2
     d2h = B * vdim * 2
 
@@ -506,14 +509,14 @@ def run_ours(args, rank: int, world: int) -> None:
         s_h2d.wait_event(ev_fork)
         s_d2h.wait_event(ev_fork)
         for i in range(n):
-            jb, slot = i % 2, (first + i) % NSLOT
+            jb, slot = i % NB, (first + i) % NSLOT
             with torch.cuda.stream(s_h2d):
-                if i >= 2:
+                if i >= NB:
                     s_h2d.wait_event(ev_used[jb])
                 d_in[jb][:, 0].copy_(h_in[(first + i) % NIN], non_blocking=True)
                 ev_ready[jb].record(s_h2d)
             stream.wait_event(ev_ready[jb])
-            if i >= 2:
+            if i >= NB:
                 stream.wait_event(ev_back[jb])
             x = d_in[jb]
             cin = convs[slot][((first + i) // NSLOT) % 2]
@@ -525,9 +528,8 @@ def run_ours(args, rank: int, world: int) -> None:
                 s_d2h.wait_event(ev_used[jb])
                 h_out[jb].copy_(d_out[jb], non_blocking=True)
                 ev_back[jb].record(s_d2h)
-        stream.wait_event(ev_back[(n - 1) % 2])
-        if n >= 2:
-            stream.wait_event(ev_back[(n - 2) % 2])
+        for j in range(max(0, n - NB), n):  # every output copy of the run has landed
+            stream.wait_event(ev_back[j % NB])
 
     plan = m.mixer_plan(B, 1, torch.bfloat16, dev, token_by_token=True)
     views = [bind(x) for x in d_in]
@@ -536,7 +538,8 @@ def run_ours(args, rank: int, world: int) -> None:
     # Serving-style decode loop: GE steps captured into one CUDA graph (each step still copies
     # its own inputs from pinned host memory, calls the plan, and copies its output back), the
     # graph replayed to cover the timed steps; this takes the host's per-step issue cost out.
-    GE = 32  # a multiple of 2 x NSLOT: every replay leaves the conv-state ping-pong where it began
+    GE = 64  # a multiple of 2 x NSLOT and of NB: every replay leaves the conv-state ping-pong and the
+    # buffer rotation where they began
     g_e2e = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_e2e, stream=stream):
         e2e_run(GE, 4)
@@ -607,9 +610,9 @@ def run_ours(args, rank: int, world: int) -> None:
                      "peak_source": src, "bytes_per_launch": bytes_launch,
                      "kernel": "gdn::dtma::decode_tma_kernel<128,1,bf16> (2 groups x 256 threads, 1 CTA/SM)"},
         "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "path": "Qwen3_5GatedDeltaNet.mixer_plan -> gdn_mixer_decode in CUDA graphs of 32 steps; every "
+                "path": "Qwen3_5GatedDeltaNet.mixer_plan -> gdn_mixer_decode in CUDA graphs of 64 steps; every "
                         "step: H2D of its packed inputs from pinned host memory, the plan call, D2H of its "
-                        "output; copies on two copy streams, double-buffered"},
+                        "output; copies on two copy streams over 8 device buffers"},
         "clocks": sampler.summary(),
     }
     if prefill is not None:
