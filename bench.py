@@ -474,7 +474,7 @@ def run_ours(args, rank: int, world: int) -> None:
     # outputs (packed [mixed | z | b | a] rows, one copy) from pinned host memory,
     # calls the mixer, and copies the gated-norm output back to pinned host
     # memory.  Copies run on two copy streams over NB device buffers, so step i's
-    # input copy starts once step i - NB's kernel is done with its buffer: with four
+    # input copy starts once step i - NB's kernel is done with its buffer: with eight
     # buffers every copy a step's kernel waits for finished a step earlier, and the
     # kernels follow one another as in the device-timed loop.
     K_e2e = min(K, 1000)
